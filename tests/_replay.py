@@ -1,0 +1,193 @@
+"""Shared helpers for tests: load golden fixtures and replay them through
+the oracle (test infrastructure; imports oracle/)."""
+from __future__ import annotations
+
+import json
+import math
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+from oracle import oracle as O  # noqa: E402
+
+ADAMW_DEFAULTS = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, fisher_wd=False,
+                      cautious_wd=False, use_bias_correction=True, stochastic_rounding=True,
+                      use_atan2=False, nesterov=False, nesterov_coef=None, normed_momentum=False,
+                      centered_wd=0.0, centered_wd_mode="float8", state_precision="auto",
+                      factored_2nd=False)
+MUON_DEFAULTS = dict(lr=1e-3, beta1=0.95, weight_decay=0.0, cautious_wd=False, nesterov=True,
+                     nesterov_coef=None, ns_steps=5, ns_eps=1e-7, ns_coeffs=(3.4445, -4.7750, 2.0315),
+                     stochastic_rounding=True, rms_rescaling=True, state_precision="auto",
+                     accelerated_ns=False, cns_a_bound=None, centered_wd=0.0, centered_wd_mode="float8",
+                     adam_betas=(0.9, 0.99), adam_eps=1e-8, adam_weight_decay=0.0, adam_fisher_wd=False,
+                     adam_use_bias_correction=True, adam_use_atan2=False, adam_nesterov=False,
+                     adam_nesterov_coef=None, adam_state_precision="auto", adam_factored_2nd=False)
+ADAMUON_DEFAULTS = dict(MUON_DEFAULTS, betas=(0.95, 0.95), eps=1e-8, use_atan2=False, factored_2nd=False,
+                        kappa_p=1.0, auto_projection=True)
+PRODIGY_DEFAULTS = dict(lr=1.0, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, fisher_wd=False,
+                        cautious_wd=False, stochastic_rounding=True, use_atan2=False, nesterov=False,
+                        nesterov_coef=None, state_precision="auto", factored_2nd=False, beta3=None,
+                        d0=1e-6, d_coef=1.0, growth_rate=float("inf"), safeguard_warmup=False,
+                        slice_p=11, prodigy_steps=0, d_limiter=False, centered_wd=0.0,
+                        centered_wd_mode="float8")
+LION_DEFAULTS = dict(lr=1e-4, betas=(0.9, 0.99), weight_decay=0.0, cautious_wd=False, stochastic_rounding=True)
+
+
+def list_cases():
+    return sorted(f[:-4] for f in os.listdir(GOLDEN) if f.endswith(".npz"))
+
+
+def load(name):
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    meta = json.loads(str(z["meta"]))
+    return meta, z
+
+
+def values(arr, dt):
+    """fixture array -> float32 values."""
+    return O.from_bf16_bits(arr) if dt == "bf16" else np.asarray(arr, np.float32)
+
+
+def draws(z, step, i):
+    out = {}
+    pre = f"r_{step}_{i}_"
+    for k in z.files:
+        if k.startswith(pre):
+            out[k[len(pre):]] = z[k].astype(np.int32)
+    return out
+
+
+def _adam_hp(kw, aux=False, precision=None):
+    if aux:
+        d = {k: v for k, v in MUON_DEFAULTS.items()}
+        d.update(kw)
+        return dict(lr=d["lr"], betas=tuple(d["adam_betas"]), eps=d["adam_eps"],
+                    weight_decay=d["adam_weight_decay"], fisher_wd=d["adam_fisher_wd"],
+                    cautious_wd=d["cautious_wd"], use_bias_correction=d["adam_use_bias_correction"],
+                    stochastic_rounding=d["stochastic_rounding"], use_atan2=d["adam_use_atan2"],
+                    nesterov=d["adam_nesterov"], nesterov_coef=d["adam_nesterov_coef"],
+                    centered_wd=d["centered_wd"], centered_wd_mode=d["centered_wd_mode"],
+                    precision=d["adam_state_precision"], factored_2nd=d["adam_factored_2nd"])
+    d = dict(ADAMW_DEFAULTS)
+    d.update(kw)
+    d["betas"] = tuple(d["betas"])
+    d["precision"] = d["state_precision"]
+    return d
+
+
+def replay(name, steps=None, pin_d=False, teacher=False):
+    """Run the oracle over a golden case.  Yields (step, i, p_values, state)
+    after every param update, in the reference's loop order."""
+    meta, z = load(name)
+    dt = meta["dtype"]
+    shapes = [tuple(s) for s in meta["shapes"]]
+    kw = meta["kw"]
+    cls = meta["cls"]
+    nsteps = meta["steps"] if steps is None else steps
+    ps = [values(z[f"p0_{i}"], dt).reshape(shapes[i]) for i in range(len(shapes))]
+    kinds = []
+    if meta["groups"]:
+        for g in meta["groups"]:
+            kinds += [g["optim_type"]] * g["n"]
+    else:
+        kinds = ["main"] * len(shapes)
+    states = []
+    group = None
+    if cls == "AdamW_adv":
+        hp = _adam_hp(kw)
+        for i, sh in enumerate(shapes):
+            st = O.adamw_init_state(sh, dt, hp["precision"], hp["factored_2nd"], hp["betas"][0])
+            if hp["centered_wd"]:
+                st.update(O.init_anchor(ps[i], dt, hp["centered_wd_mode"]))
+            states.append(st)
+    elif cls in ("Muon_adv", "AdaMuon_adv"):
+        base = dict(MUON_DEFAULTS if cls == "Muon_adv" else ADAMUON_DEFAULTS)
+        base.update(kw)
+        base["precision"] = base["state_precision"]
+        base["betas"] = tuple(base.get("betas", (0.95, 0.95)))
+        aux = _adam_hp(kw, aux=True)
+        for i, sh in enumerate(shapes):
+            if kinds[i] == "muon":
+                st = {}
+                O.init_state_tensor(st, "momentum_buffer", sh, base["precision"], dt)
+                if cls == "AdaMuon_adv":
+                    O.init_state_tensor(st, "second_momentum_buffer", sh, base["precision"], dt, non_neg=True)
+                states.append(st)
+            else:
+                states.append(O.adamw_init_state(sh, dt, aux["precision"], aux["factored_2nd"], aux["betas"][0]))
+    elif cls == "Prodigy_adv":
+        hp = dict(PRODIGY_DEFAULTS)
+        hp.update(kw)
+        hp["betas"] = tuple(hp["betas"])
+        hp["precision"] = hp["state_precision"]
+        group = dict(d=hp["d0"], d0=hp["d0"], d_max=hp["d0"], d_numerator=0.0, d_coef=hp["d_coef"],
+                     growth_rate=hp["growth_rate"], d_limiter=hp["d_limiter"], k=0,
+                     prodigy_steps=hp["prodigy_steps"],
+                     beta3=hp["beta3"] if hp["beta3"] is not None else math.sqrt(hp["betas"][1]))
+        for i, sh in enumerate(shapes):
+            st = O.adamw_init_state(sh, dt, hp["precision"], hp["factored_2nd"], hp["betas"][0])
+            sl = ps[i].reshape(-1)[::hp["slice_p"]]
+            st["s"] = np.zeros(sl.shape, np.uint16) if dt == "bf16" else np.zeros(sl.shape, np.float32)
+            if np.any(ps[i] != 0):
+                st["p0"] = O.bf16_bits(sl) if dt == "bf16" else sl.astype(np.float32).copy()
+            else:
+                st["p0"] = np.zeros((), np.uint16 if dt == "bf16" else np.float32)
+            states.append(st)
+    elif cls == "Lion_adv":
+        hp = dict(LION_DEFAULTS)
+        hp.update(kw)
+        hp["betas"] = tuple(hp["betas"])
+        for i, sh in enumerate(shapes):
+            states.append({"step": 0, "exp_avg": np.zeros(sh, np.uint16 if dt == "bf16" else np.float32)})
+    else:
+        raise KeyError(cls)
+
+    d_num_carry = np.float32(0.0)
+    for s in range(nsteps):
+        if cls == "Prodigy_adv":
+            d_num = np.float32(d_num_carry)
+            d_den = np.float32(0.0)
+        if teacher and s > 0:
+            # start every step from the reference's own params and states so
+            # that each step's comparison measures that step alone
+            for i, sh in enumerate(shapes):
+                ps[i] = values(z[f"p_{s - 1}_{i}"], dt).reshape(sh)
+                for key in list(states[i].keys()):
+                    fk = f"st_{s - 1}_{i}_{key}"
+                    if fk in z.files and isinstance(states[i][key], np.ndarray):
+                        states[i][key] = np.array(z[fk]).astype(states[i][key].dtype).reshape(states[i][key].shape)
+        for i, sh in enumerate(shapes):
+            g = values(z[f"g_{s}_{i}"], dt).reshape(sh)
+            r = draws(z, s, i)
+            if cls == "AdamW_adv":
+                ps[i] = O.adam_family_step(ps[i], dt, g, states[i], hp, r, algo="adamw")
+            elif cls in ("Muon_adv", "AdaMuon_adv"):
+                if kinds[i] == "muon":
+                    fn = O.muon_step if cls == "Muon_adv" else O.adamuon_step
+                    ps[i] = fn(ps[i], dt, g, states[i], base, r)
+                else:
+                    ps[i] = O.adam_family_step(ps[i], dt, g, states[i], aux, r, algo="auxadam")
+            elif cls == "Prodigy_adv":
+                hp_s = dict(hp, d=group["d"], k=group["k"], beta3=group["beta3"])
+                ps[i], stats = O.adam_family_step(ps[i], dt, g, states[i], hp_s, r, algo="prodigy")
+                if stats is not None:
+                    d_num = np.float32(d_num + np.float32(stats[0]))
+                    d_den = np.float32(d_den + np.float32(stats[1]))
+            elif cls == "Lion_adv":
+                ps[i] = O.lion_step(ps[i], dt, g, states[i], hp, r)
+            yield s, i, ps[i], states[i], group
+        if cls == "Prodigy_adv":
+            d_num_carry = O.prodigy_calculate_d(group, d_num, d_den)
+            yield s, -1, None, None, dict(group)
+            if pin_d:
+                # continue from the reference's own d so that per-step
+                # comparisons do not accumulate d's summation-order error
+                ref = z[f"d_{s}"]
+                group["d"], group["d_max"], group["d_numerator"] = float(ref[0]), float(ref[1]), float(ref[2])
+                d_num_carry = float(np.float32(group["d_numerator"] * group["beta3"]))
