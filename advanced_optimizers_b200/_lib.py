@@ -1,0 +1,144 @@
+"""ctypes binding of libadvopt.so (the C ABI declared in include/advopt.h).
+
+The library is built in-tree by ``python -m advanced_optimizers_b200.build``
+(or ``__graft_entry__.build()``).  There is no fallback: every optimizer
+step runs through these entry points, and a missing library or a missing
+CUDA device raises immediately.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import numpy as np
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libadvopt.so")
+ABI_VERSION = 1
+
+# ---- constants mirrored from include/advopt.h ----
+DT_F32, DT_BF16 = 0, 1
+PREC = {"fp32": 0, "bf16_sr": 1, "int8_sr": 2, "auto": 3}
+ALGO_ADAMW, ALGO_AUXADAM, ALGO_PRODIGY = 0, 1, 2
+F_NESTEROV = 1 << 0
+F_ATAN2 = 1 << 1
+F_NORMED = 1 << 2
+F_CAUTIOUS = 1 << 3
+F_SR = 1 << 4
+F_NOISE_IN = 1 << 5
+F_HAS_M = 1 << 6
+F_PRODIGY_STATS = 1 << 7
+F_FISHER = 1 << 8
+F_FISHER_STATS = 1 << 9
+F_ANCHORS = 1 << 10
+T_FACTORED = 1 << 0
+T_VEC = 1 << 1
+T_P0_SCALAR = 1 << 2
+T_ANCHOR_SHIFT = 4
+ANCHOR = {"none": 0, "full": 1, "float8": 2, "int8": 3, "int4": 4}
+
+# advopt_adam_tensor (192 bytes)
+ADAM_TENSOR_DT = np.dtype([
+    ("param", "<u8"), ("grad", "<u8"), ("exp_avg", "<u8"), ("exp_avg_scale", "<u8"),
+    ("exp_avg_sq", "<u8"), ("exp_avg_sq_scale", "<u8"), ("row_factor", "<u8"), ("col_factor", "<u8"),
+    ("col_partial", "<u8"), ("aux0", "<u8"), ("aux1", "<u8"), ("aux2", "<u8"),
+    ("noise_v", "<u8"), ("noise_m", "<u8"), ("noise_p", "<u8"),
+    ("numel", "<i8"), ("d1", "<i8"), ("d2", "<i8"),
+    ("step_size", "<f4"), ("sqrt_bc2", "<f4"), ("eps", "<f4"), ("wd", "<f4"), ("cwd", "<f4"),
+    ("fisher_clip", "<f4"),
+    ("tensor_id", "<u4"), ("step", "<u4"), ("flags", "<u4"), ("slice_p", "<u4"),
+    ("slot_base", "<i4"), ("n_slots", "<i4"),
+])
+PIECE_DT = np.dtype([("begin", "<i8"), ("end", "<i8"), ("tensor", "<i4"), ("slot", "<i4")])
+LION_TENSOR_DT = np.dtype([
+    ("param", "<u8"), ("grad", "<u8"), ("exp_avg", "<u8"), ("noise_p", "<u8"), ("numel", "<i8"),
+    ("lr", "<f4"), ("wd", "<f4"), ("tensor_id", "<u4"), ("step", "<u4"), ("flags", "<u4"), ("pad", "<u4"),
+])
+
+
+class AdamLaunch(ctypes.Structure):
+    _fields_ = [
+        ("tensors", ctypes.c_uint64), ("pieces", ctypes.c_uint64), ("cta_offsets", ctypes.c_uint64),
+        ("piece_stats", ctypes.c_uint64),
+        ("n_tensors", ctypes.c_int32), ("n_pieces", ctypes.c_int32), ("grid", ctypes.c_int32),
+        ("smem_floats", ctypes.c_int32), ("gen_offset", ctypes.c_int32), ("algo", ctypes.c_int32),
+        ("precision", ctypes.c_int32), ("param_dtype", ctypes.c_int32), ("flags", ctypes.c_uint32),
+        ("beta1", ctypes.c_float), ("beta2", ctypes.c_float), ("w_m", ctypes.c_float),
+        ("w_nest", ctypes.c_float), ("c_v", ctypes.c_float), ("c_m", ctypes.c_float),
+        ("d_eps", ctypes.c_float), ("beta3", ctypes.c_float), ("s_alpha", ctypes.c_float),
+        ("d", ctypes.c_float), ("pad0", ctypes.c_float), ("seed", ctypes.c_uint64),
+    ]
+
+
+_LIB = None
+_LOCK = threading.Lock()
+
+
+class AdvOptError(RuntimeError):
+    pass
+
+
+def lib():
+    """Load libadvopt.so once; raise if it is missing or its layout differs."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        if not os.path.exists(LIB_PATH):
+            raise AdvOptError(f"{LIB_PATH} is missing: build it with `python -m advanced_optimizers_b200.build` "
+                              "(there is no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        P, I32, U32, F, U64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_uint32, ctypes.c_float, ctypes.c_uint64
+        sig = {
+            "advopt_adam_step": ([ctypes.POINTER(AdamLaunch), P], ctypes.c_int),
+            "advopt_factored_finish": ([ctypes.POINTER(AdamLaunch), P, I32, I32, P], ctypes.c_int),
+            "advopt_prodigy_finish": ([ctypes.POINTER(AdamLaunch), P, F, I32, P], ctypes.c_int),
+            "advopt_fisher_finish": ([ctypes.POINTER(AdamLaunch), P, P], ctypes.c_int),
+            "advopt_lion_step": ([P, I32, P, I32, I32, F, F, U32, U64, P], ctypes.c_int),
+            "advopt_sizeof": ([ctypes.c_int], ctypes.c_size_t),
+            "advopt_abi_version": ([], ctypes.c_int),
+            "advopt_last_error": ([], ctypes.c_char_p),
+            "advopt_adam_occupancy": ([I32, I32, I32, I32, ctypes.POINTER(I32), ctypes.POINTER(I32)], ctypes.c_int),
+        }
+        for name, (args, res) in sig.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        if L.advopt_abi_version() != ABI_VERSION:
+            raise AdvOptError("libadvopt.so ABI version mismatch; rebuild the library")
+        for which, size in ((0, ADAM_TENSOR_DT.itemsize), (1, PIECE_DT.itemsize),
+                            (2, ctypes.sizeof(AdamLaunch)), (3, LION_TENSOR_DT.itemsize)):
+            got = L.advopt_sizeof(which)
+            if got != size:
+                raise AdvOptError(f"struct layout mismatch (#{which}: C {got} bytes, Python {size})")
+        _LIB = L
+        return L
+
+
+def check(rc: int, what: str):
+    if rc != 0:
+        msg = lib().advopt_last_error().decode(errors="replace")
+        raise AdvOptError(f"{what} failed ({rc}): {msg}")
+
+
+def exported_symbols():
+    """Names the header declares (used by the load test)."""
+    return ["advopt_adam_step", "advopt_factored_finish", "advopt_prodigy_finish", "advopt_fisher_finish",
+            "advopt_lion_step", "advopt_sizeof", "advopt_abi_version", "advopt_last_error",
+            "advopt_adam_occupancy"]
+
+
+_OCC_CACHE = {}
+
+
+def adam_occupancy(precision: int, param_dtype: int, algo: int, smem_floats: int):
+    key = (precision, param_dtype, algo, smem_floats)
+    if key not in _OCC_CACHE:
+        sms, ctas = ctypes.c_int32(0), ctypes.c_int32(0)
+        check(lib().advopt_adam_occupancy(precision, param_dtype, algo, smem_floats,
+                                          ctypes.byref(sms), ctypes.byref(ctas)), "advopt_adam_occupancy")
+        _OCC_CACHE[key] = (sms.value, max(1, ctas.value))
+    return _OCC_CACHE[key]

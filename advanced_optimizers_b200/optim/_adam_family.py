@@ -1,0 +1,462 @@
+"""Host side of the Adam-family step (AdamW_adv, Muon's auxiliary Adam,
+Prodigy_adv): state creation with the reference's keys and dtypes, the
+per-group plan (device descriptor table + pieces), and the launches.
+
+State layout follows AdamW_adv.py:221-277, Muon_AuxAdam.py:15-67 and
+Prodigy_adv.py:271-331 key for key, so checkpoints cross-load with the
+reference.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import torch
+
+from .. import _lib as L
+from .._device import DeviceTable, aligned16, dtype_code, ptr, require_cuda_tensor, stream_handle, upload_static
+from .._plan import effective_shape, plan as plan_pieces
+
+A_ATAN2 = 4 / math.pi
+SHIFTER = [1, 2, 4, 8, 16, 32, 64, 128]
+BLOCK = 2048
+SUPPORTED_PRECISIONS = ("auto", "fp32", "bf16_sr", "int8_sr")
+
+
+def f32(x) -> float:
+    """The float32 value a Python scalar takes as an ATen op argument."""
+    return float(np.float32(x))
+
+
+# ---------------------------------------------------------------------------
+# state creation (state_util.init_state_tensor, state_util.py:13-37)
+# ---------------------------------------------------------------------------
+
+def init_state_tensor(state, key, p, precision, non_neg=False):
+    if precision == "fp32":
+        dt = torch.float32
+    elif precision == "bf16_sr":
+        dt = torch.bfloat16
+    elif precision == "int8_sr":
+        dt = torch.uint8 if non_neg else torch.int8
+    elif precision == "auto":
+        dt = p.dtype
+    else:
+        raise NotImplementedError(f"state_precision '{precision}' is not supported by the B200 kernels")
+    state[key] = torch.zeros(p.shape, dtype=dt, device=p.device)
+    if dt in (torch.uint8, torch.int8):
+        nb = (p.numel() + BLOCK - 1) // BLOCK
+        state[f"{key}_scale"] = torch.ones(nb, dtype=torch.float32, device=p.device)
+
+
+def is_wd_centered(p) -> bool:
+    """centered_decay.is_wd_centered (centered_decay.py:4-12)."""
+    return bool(getattr(p, "_is_lora_A", False) or getattr(p, "_is_lora_B", False) or getattr(p, "_is_oft", False))
+
+
+def adjust_wds(wd, cwd, p):
+    """scaled_optm.adjust_wds (scaled_optm.py:84-105)."""
+    if getattr(p, "_is_dora_scale", False):
+        return wd, cwd
+    if getattr(p, "_is_oft", False):
+        return wd, 0.0
+    if p.ndim >= 2 and (getattr(p, "_is_lora_A", False) or getattr(p, "_is_lora_B", False)):
+        return wd, 0.0
+    return wd, cwd
+
+
+@torch.no_grad()
+def init_anchor(p, state, centered_wd, mode):
+    """centered_decay._init_anchor (centered_decay.py:184-217)."""
+    if not centered_wd or is_wd_centered(p) or "anchor_data" in state:
+        return
+    if mode == "float8":
+        state["anchor_data"] = p.to(torch.float8_e4m3fn)
+    elif mode in ("int8", "int4"):
+        blk, bits = (128, 8) if mode == "int8" else (32, 4)
+        flat = p.flatten()
+        n = flat.numel()
+        pad = (blk - n % blk) % blk
+        vals = torch.nn.functional.pad(flat.unsqueeze(0), (0, pad), mode="replicate").squeeze(0) if pad else flat.clone()
+        vb = vals.view(-1, blk).float()
+        mn, mx = torch.aminmax(vb, dim=1, keepdim=True)
+        qmin, qmax = -(1 << (bits - 1)), (1 << (bits - 1)) - 1
+        scales = (mx - mn).div_(float(qmax - qmin))
+        scales.masked_fill_(scales == 0, 1.0)
+        q = vb.sub_(mn).div_(scales).add_(qmin).round_().clamp_(qmin, qmax).to(torch.int8)
+        if mode == "int4":
+            qf = q.view(-1)
+            q = (((qf[0::2] & 0x0F) << 4) | (qf[1::2] & 0x0F)).to(torch.int8)
+        state["anchor_data"] = q
+        state["anchor_scale"] = scales.squeeze(1).to(p.dtype)
+        state["anchor_min"] = mn.squeeze(1).to(p.dtype)
+    elif mode == "full":
+        state["anchor_data"] = p.clone()
+
+
+def anchor_code(state, mode) -> int:
+    """Storage of the centered-WD anchor, as dequantize_anchor reads it
+    (centered_decay.py:219-252): by dtype, with the group's mode telling
+    int8 from int4 codes."""
+    if "anchor_data" not in state:
+        return 0
+    d = state["anchor_data"]
+    if d.dtype == torch.float8_e4m3fn:
+        return L.ANCHOR["float8"]
+    if d.dtype == torch.int8:
+        if mode == "int4":
+            return L.ANCHOR["int4"]
+        if mode == "int8":
+            return L.ANCHOR["int8"]
+        raise NotImplementedError(f"int8 anchor data with centered_wd_mode '{mode}'")
+    return L.ANCHOR["full"]
+
+
+@torch.no_grad()
+def init_adam_state(p, state, *, precision, factored_2nd, beta1, vector_reshape, centered_wd, centered_wd_mode,
+                    fisher_wd):
+    """AdamW_adv.__init_state for the non-'factored' precisions (AdamW_adv.py:221-277);
+    Muon_AuxAdam._init_auxadam_state is the same with adam_* keys (Muon_AuxAdam.py:15-67)."""
+    state["step"] = 0
+    is_vector = p.dim() == 1 and not vector_reshape
+    state["factored"] = False
+    state["factored_2nd"] = bool(factored_2nd and not is_vector)
+    if beta1 > 0:
+        init_state_tensor(state, "exp_avg", p, precision)
+    if state["factored_2nd"]:
+        d1, d2 = effective_shape(p.numel())
+        state["effective_shape"] = (d1, d2)
+        state["mu_v_nmf"] = torch.zeros(d1, device=p.device, dtype=torch.float32)
+        state["mv_v_nmf"] = torch.zeros(d2, device=p.device, dtype=torch.float32)
+        state["shifter"] = torch.tensor(SHIFTER, device=p.device, dtype=torch.uint8)
+    else:
+        init_state_tensor(state, "exp_avg_sq", p, precision, non_neg=True)
+    init_anchor(p, state, centered_wd, centered_wd_mode)
+    if fisher_wd:
+        state["wd_scaler"] = torch.tensor(1.0, device=p.device)
+
+
+# ---------------------------------------------------------------------------
+# launch configuration
+# ---------------------------------------------------------------------------
+
+class AdamCfg:
+    """Group-level hyperparameters of one launch, already in the reference's
+    scalar semantics.  `algo` is L.ALGO_*."""
+
+    def __init__(self, *, algo, lr, betas, eps, weight_decay, precision, nesterov=False, nesterov_coef=None,
+                 use_bias_correction=True, use_atan2=False, normed_momentum=False, cautious_wd=False,
+                 fisher_wd=False, centered_wd=0.0, centered_wd_mode="float8", stochastic_rounding=True,
+                 prodigy=None):
+        self.algo = algo
+        self.lr = float(lr)
+        self.beta1, self.beta2 = float(betas[0]), float(betas[1])
+        self.eps = eps
+        self.weight_decay = float(weight_decay)
+        self.precision = precision
+        self.nesterov = bool(nesterov)
+        self.nesterov_coef = nesterov_coef
+        self.use_bias_correction = bool(use_bias_correction)
+        self.use_atan2 = bool(use_atan2)
+        self.normed = bool(normed_momentum) and algo == L.ALGO_ADAMW
+        self.cautious = bool(cautious_wd)
+        self.fisher = bool(fisher_wd)
+        self.centered_wd = float(centered_wd)
+        self.centered_wd_mode = centered_wd_mode
+        self.sr = bool(stochastic_rounding)
+        self.prodigy = prodigy   # dict: d, d0, beta3, safeguard_warmup, slice_p, stats (bool)
+
+
+class GroupPlan:
+    """Static part of one launch: the tensors (params with grads, one dtype),
+    their descriptor table, the pieces and the scratch buffers."""
+
+    def __init__(self, params, states, tensor_ids, cfg: AdamCfg):
+        self.params = list(params)
+        self.states = list(states)
+        p0 = self.params[0]
+        self.device = p0.device
+        self.pdt = dtype_code(p0.dtype)
+        n = len(self.params)
+        self.n = n
+        prec = cfg.precision
+        if prec == "auto" and self.pdt == L.DT_F32:
+            prec = "fp32"
+        self.precision = L.PREC[prec]
+        self.descs = np.zeros(n, L.ADAM_TENSOR_DT)
+        d = self.descs
+        numels, d2s = [], []
+        max_d2 = 0
+        any_generic = False
+        self.has_anchor = False
+        vec_ok = []
+        for i, (p, st) in enumerate(zip(self.params, self.states)):
+            numel = p.numel()
+            numels.append(numel)
+            flags = 0
+            fact = bool(st.get("factored_2nd", False))
+            m = st.get("exp_avg")
+            v = st.get("exp_avg_sq")
+            tensors = [p, m, v]
+            if fact:
+                d1, d2 = st["effective_shape"]
+                flags |= L.T_FACTORED
+                d["d1"][i], d["d2"][i] = d1, d2
+                d["row_factor"][i] = ptr(st["mu_v_nmf"])
+                d["col_factor"][i] = ptr(st["mv_v_nmf"])
+                d2s.append(d2)
+                max_d2 = max(max_d2, d2)
+                if d2 < 2048 or d2 % 8 != 0:
+                    any_generic = True
+                tensors += [st["mu_v_nmf"], st["mv_v_nmf"]]
+            else:
+                d2s.append(0)
+            d["param"][i] = ptr(p)
+            d["exp_avg"][i] = ptr(m)
+            d["exp_avg_scale"][i] = ptr(st.get("exp_avg_scale"))
+            d["exp_avg_sq"][i] = ptr(v)
+            d["exp_avg_sq_scale"][i] = ptr(st.get("exp_avg_sq_scale"))
+            d["numel"][i] = numel
+            d["tensor_id"][i] = tensor_ids[i]
+            d["fisher_clip"][i] = 1.0
+            ac = anchor_code(st, cfg.centered_wd_mode)
+            if ac:
+                self.has_anchor = True
+                flags |= ac << L.T_ANCHOR_SHIFT
+                d["aux0"][i] = ptr(st["anchor_data"])
+                d["aux1"][i] = ptr(st.get("anchor_scale"))
+                d["aux2"][i] = ptr(st.get("anchor_min"))
+            if cfg.prodigy is not None:
+                d["aux0"][i] = ptr(st["s"])
+                d["aux1"][i] = ptr(st["p0"])
+                d["slice_p"][i] = cfg.prodigy["slice_p"]
+                if st["p0"].dim() == 0:
+                    flags |= L.T_P0_SCALAR
+            vec_ok.append(aligned16(*tensors))
+            if vec_ok[-1]:
+                flags |= L.T_VEC
+            d["flags"][i] = flags
+        self.numels = numels
+        self.vec_ok = vec_ok
+        self.max_d2 = max_d2
+        self.gen_offset = ((max_d2 + 3) // 4) * 4
+        self.smem_floats = self.gen_offset + (2 * 2048 + 4 if any_generic else 0)
+        sms, ctas = L.adam_occupancy(self.precision, self.pdt, cfg.algo, self.smem_floats)
+        total_chunks = sum((x + 2047) // 2048 for x in numels)
+        self.grid = max(1, min(sms * ctas, total_chunks))
+        pieces, offsets, n_slots = plan_pieces(numels, d2s, self.grid)
+        self.n_pieces = len(pieces)
+        # factored scratch: one row of column partials per piece
+        self.scratch = []
+        fact_idx = []
+        for i in range(n):
+            if d["flags"][i] & L.T_FACTORED:
+                d2 = int(d["d2"][i])
+                buf = torch.empty(max(1, n_slots[i]) * d2, dtype=torch.float32, device=self.device)
+                self.scratch.append(buf)
+                d["col_partial"][i] = ptr(buf)
+                d["n_slots"][i] = n_slots[i]
+                fact_idx.append(i)
+        self.fact_idx = fact_idx
+        self.fact_idx_dev = upload_static(np.asarray(fact_idx, np.int32), self.device) if fact_idx else None
+        self.pieces_dev = upload_static(pieces, self.device)
+        self.offsets_dev = upload_static(offsets, self.device)
+        need_stats = cfg.prodigy is not None or cfg.fisher
+        self.stats = torch.zeros(max(1, 2 * self.n_pieces), dtype=torch.float64, device=self.device) \
+            if need_stats else None
+        self.table = DeviceTable(self.descs.nbytes, self.device)
+        self.eps_cache = [None] * n
+
+    def launch_struct(self, cfg: AdamCfg, flags: int, seed: int) -> L.AdamLaunch:
+        s = L.AdamLaunch()
+        s.tensors = self.table.ptr
+        s.pieces = int(self.pieces_dev.data_ptr())
+        s.cta_offsets = int(self.offsets_dev.data_ptr())
+        s.piece_stats = int(self.stats.data_ptr()) if self.stats is not None else 0
+        s.n_tensors = self.n
+        s.n_pieces = self.n_pieces
+        s.grid = self.grid
+        s.smem_floats = self.smem_floats
+        s.gen_offset = self.gen_offset
+        s.algo = cfg.algo
+        s.precision = self.precision
+        s.param_dtype = self.pdt
+        s.flags = flags
+        s.seed = seed
+        return s
+
+
+def grads_of(params):
+    return [p.grad for p in params]
+
+
+class AdamFamilyRunner:
+    """Owns the plans of one optimizer and performs group launches."""
+
+    def __init__(self, seed: int = 42):
+        self.plans = {}
+        self.seed = int(seed)
+        self.test_noise = None   # {id(param): {label: int32 CUDA tensor}} for the next step only
+        self.kernel_events = None  # list to collect (start, end) CUDA events around the main launch
+        self.launch_count = 0      # kernels launched so far (for launch accounting)
+
+    def invalidate(self):
+        self.plans.clear()
+
+    def get_plan(self, key, params, states, ids, cfg):
+        pl = self.plans.get(key)
+        if pl is None or any(pl.descs["param"][i] != ptr(p) for i, p in enumerate(params)):
+            pl = GroupPlan(params, states, ids, cfg)
+            self.plans[key] = pl
+        return pl
+
+    @torch.no_grad()
+    def run(self, key, params, states, ids, cfg: AdamCfg, prodigy_sums=None):
+        """One launch over `params` (same dtype and device, all with grads)."""
+        for p in params:
+            require_cuda_tensor(p, "param")
+            require_cuda_tensor(p.grad, "grad")
+        pl = self.get_plan(key, params, states, ids, cfg)
+        d = pl.descs
+        for i, p in enumerate(params):
+            gp = p.grad.data_ptr()
+            d["grad"][i] = gp
+            if gp % 16:
+                d["flags"][i] &= ~L.T_VEC
+            elif pl.vec_ok[i]:
+                d["flags"][i] |= L.T_VEC
+        # per-tensor scalars in the reference's arithmetic (Python floats, cast to fp32)
+        lr = cfg.lr
+        step_cache = {}
+        for i, (p, st) in enumerate(zip(params, states)):
+            t = st["step"]
+            if cfg.algo == L.ALGO_PRODIGY:
+                dd = cfg.prodigy["d"]
+                dlr = dd * lr
+                ss = dlr * A_ATAN2 if cfg.use_atan2 else dlr
+                sbc2 = 1.0
+                lr_wd = dlr
+            else:
+                sc = step_cache.get(t)
+                if sc is None:
+                    if cfg.use_bias_correction:
+                        s1 = t + 1
+                        bc1 = 1.0 - cfg.beta1 ** s1
+                        sbc2 = (1.0 - cfg.beta2 ** s1) ** 0.5
+                    else:
+                        bc1, sbc2 = 1, 1
+                    step_size = lr / bc1
+                    sc = (step_size * A_ATAN2 if cfg.use_atan2 else step_size, sbc2)
+                    step_cache[t] = sc
+                ss, sbc2 = sc
+                lr_wd = lr
+            eps = cfg.eps if cfg.eps is not None else 1.0 / math.sqrt(p.numel())
+            if cfg.algo == L.ALGO_PRODIGY:
+                eps = cfg.prodigy["d"] * eps
+            wd, cwd = adjust_wds(cfg.weight_decay, cfg.centered_wd, p)
+            d["step_size"][i] = ss
+            d["sqrt_bc2"][i] = sbc2
+            d["eps"][i] = eps
+            d["wd"][i] = wd * lr_wd if wd != 0 else 0.0
+            d["cwd"][i] = cwd * lr_wd if cwd != 0 else 0.0
+            d["step"][i] = t & 0xFFFFFFFF
+        flags = 0
+        if cfg.beta1 > 0:
+            flags |= L.F_HAS_M
+        if cfg.nesterov:
+            flags |= L.F_NESTEROV
+        if cfg.use_atan2:
+            flags |= L.F_ATAN2
+        if cfg.normed:
+            flags |= L.F_NORMED
+        if cfg.cautious:
+            flags |= L.F_CAUTIOUS
+        if cfg.sr and pl.pdt == L.DT_BF16:
+            flags |= L.F_SR
+        if pl.has_anchor:
+            flags |= L.F_ANCHORS
+        noise_keep = []
+        if self.test_noise is not None:
+            flags |= L.F_NOISE_IN
+            for i, p in enumerate(params):
+                nz = self.test_noise.get(id(p), {})
+                n = p.numel()
+                padded = ((n + BLOCK - 1) // BLOCK) * BLOCK
+                for label, field in (("exp_avg_sq", "noise_v"), ("exp_avg", "noise_m"), ("param", "noise_p")):
+                    t = nz.get(label)
+                    if t is not None:
+                        t = t.to(device=p.device, dtype=torch.int32).contiguous()
+                        need = padded if (label != "param" and cfg.precision == "int8_sr") else n
+                        if t.numel() < need:
+                            raise ValueError(f"injected noise '{label}' has {t.numel()} entries, {need} needed")
+                        noise_keep.append(t)
+                        d[field][i] = t.data_ptr()
+                    else:
+                        d[field][i] = 0
+        if self.test_noise is not None:
+            need = []
+            if cfg.sr and pl.pdt == L.DT_BF16:
+                need.append("noise_p")
+            if cfg.precision in ("int8_sr", "bf16_sr") and cfg.beta1 > 0:
+                need.append("noise_m")
+            for i in range(pl.n):
+                for field in need + (["noise_v"] if cfg.precision in ("int8_sr", "bf16_sr")
+                                     and not (d["flags"][i] & L.T_FACTORED) else []):
+                    if d[field][i] == 0:
+                        raise ValueError(f"injected noise missing for tensor {i} ({field})")
+        pl.table.upload(d)
+        s = pl.launch_struct(cfg, flags, self.seed)
+        nc = cfg.nesterov_coef
+        nv_coef = cfg.beta1 if nc is None else nc
+        s.beta1 = f32(cfg.beta1)
+        s.beta2 = f32(cfg.beta2)
+        s.w_m = f32(1.0 - cfg.beta1)
+        s.w_nest = f32(1 - nv_coef)
+        if cfg.algo == L.ALGO_PRODIGY:
+            pd = cfg.prodigy
+            dd, d0 = pd["d"], pd["d0"]
+            s.c_v = f32(dd * dd * (1.0 - cfg.beta2))
+            s.c_m = f32(dd * (1.0 - cfg.beta1))
+            s.d = f32(dd)
+            s.beta3 = f32(pd["beta3"])
+            dlr = dd * lr
+            s.s_alpha = f32(((dd / d0) * dd) if pd["safeguard_warmup"] else ((dd / d0) * dlr))
+            if pd["stats"]:
+                s.flags |= L.F_PRODIGY_STATS
+        else:
+            s.c_v = f32(1.0 - cfg.beta2)
+        stream = stream_handle(pl.device)
+        lib = L.lib()
+        if cfg.fisher:
+            if not cfg.use_atan2:
+                st_s = L.AdamLaunch.from_buffer_copy(s)
+                st_s.flags = (s.flags | L.F_FISHER_STATS) & ~L.F_PRODIGY_STATS
+                L.check(lib.advopt_adam_step(ctypes.byref(st_s), stream), "advopt_adam_step (Fisher statistics)")
+                L.check(lib.advopt_fisher_finish(ctypes.byref(st_s), pl.table.ptr, stream), "advopt_fisher_finish")
+                self.launch_count += 2
+            s.flags |= L.F_FISHER
+        if self.kernel_events is not None:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(torch.cuda.current_stream(pl.device))
+        L.check(lib.advopt_adam_step(ctypes.byref(s), stream), "advopt_adam_step")
+        self.launch_count += 1
+        if self.kernel_events is not None:
+            ev1.record(torch.cuda.current_stream(pl.device))
+            self.kernel_events.append((ev0, ev1, pl))
+        if pl.fact_idx:
+            self.launch_count += 2
+            L.check(lib.advopt_factored_finish(ctypes.byref(s), int(pl.fact_idx_dev.data_ptr()), len(pl.fact_idx),
+                                               pl.max_d2, stream), "advopt_factored_finish")
+        if cfg.algo == L.ALGO_PRODIGY and cfg.prodigy["stats"]:
+            pd = cfg.prodigy
+            coef = f32((pd["d"] / pd["d0"]) * (pd["d"] * lr))
+            s_bf16 = 1 if (pl.pdt == L.DT_BF16) else 0
+            L.check(lib.advopt_prodigy_finish(ctypes.byref(s), int(prodigy_sums.data_ptr()), coef, s_bf16, stream),
+                    "advopt_prodigy_finish")
+            self.launch_count += 1
+        for st in states:
+            st["step"] += 1
+        if noise_keep:
+            # keep the injected arrays alive until the kernels that read them are done
+            torch.cuda.current_stream(pl.device).synchronize()

@@ -1,0 +1,73 @@
+"""Pieces shared by the optimizer classes."""
+from __future__ import annotations
+
+import torch
+
+
+def reject(cond, what: str):
+    """Options the B200 kernels do not implement fail loudly (no fallback)."""
+    if cond:
+        raise NotImplementedError(f"{what} is not supported by the B200 optimizer kernels")
+
+
+def fix_loaded_state_dtype(state: dict, p: torch.Tensor, group: dict) -> None:
+    """state_util.fix_loaded_state_dtype (state_util.py:181-263): undo
+    torch's load_state_dict casting of quantised / factored states."""
+    mode = group.get("centered_wd_mode", "full")
+    actual = group.get("actual_state_precision", group.get("state_precision", "auto"))
+    is_factored = state.get("factored", False) or actual == "factored"
+    if actual == "fp32":
+        base = torch.float32
+    elif actual == "bf16_sr":
+        base = torch.bfloat16
+    elif actual == "int8_sr":
+        base = torch.uint8
+    else:
+        base = torch.float32 if is_factored else p.dtype
+    skipped = p.numel() == 0 or getattr(p, "_is_dora_scale", False)
+    uint8_keys = {"sign", "sign_slow", "sign_buf", "shifter"}
+    fp32_keys = {"mu_m_nmf", "mv_m_nmf", "mu_v_nmf", "mv_v_nmf", "mu_m_slow_nmf", "mv_m_slow_nmf",
+                 "mu_mbuf_nmf", "mv_mbuf_nmf", "mu_b_nmf", "normuon_v", "mu_vbuf_nmf", "mv_vbuf_nmf"}
+    for key, val in list(state.items()):
+        if not isinstance(val, torch.Tensor):
+            continue
+        if key == "anchor_data":
+            if skipped or mode == "full":
+                if val.dtype != p.dtype:
+                    state[key] = val.to(p.dtype)
+            elif mode in ("int8", "int4"):
+                if val.dtype != torch.int8:
+                    state[key] = val.to(torch.int8)
+            elif mode == "float8":
+                if val.dtype != torch.float8_e4m3fn:
+                    state[key] = val.to(torch.float8_e4m3fn)
+        elif key in ("anchor_scale", "anchor_min"):
+            if val.dtype != p.dtype:
+                state[key] = val.to(p.dtype)
+        elif key in uint8_keys:
+            if val.dtype != torch.uint8:
+                state[key] = val.to(torch.uint8)
+        elif key in fp32_keys or (key.endswith("_scale") and key != "anchor_scale"):
+            if val.dtype != torch.float32:
+                state[key] = val.to(torch.float32)
+        elif val.is_floating_point():
+            if key in ("s", "p0"):
+                if val.dtype != p.dtype:
+                    state[key] = val.to(p.dtype)
+            elif val.dtype != base and key != "wd_scaler":
+                state[key] = val.to(base)
+        elif actual == "int8_sr" and val.dtype not in (torch.int8, torch.uint8):
+            state[key] = val.to(torch.uint8 if key in ("exp_avg_sq", "second_momentum_buffer") else torch.int8)
+        if state[key].device != p.device:
+            state[key] = state[key].to(p.device)
+        if not state[key].is_contiguous():
+            state[key] = state[key].contiguous()
+
+
+def post_process_loaded_state(optimizer) -> None:
+    """param_update.post_process_loaded_state (param_update.py:395-409)."""
+    for group in optimizer.param_groups:
+        for p in group["params"]:
+            st = optimizer.state.get(p)
+            if st:
+                fix_loaded_state_dtype(st, p, group)

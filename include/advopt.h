@@ -1,0 +1,213 @@
+/*
+ * advopt.h — C ABI of the B200 (sm_100a) optimizer-step library
+ * (libadvopt.so, built from advanced_optimizers_b200/csrc).
+ *
+ * The library replaces the per-parameter eager step of adv_optm 2.5.4
+ * (Koratahiu/Advanced_Optimizers).  The reference has no native interface of
+ * its own: its boundary is the Python method `Optimizer.step()` of each class,
+ * which loops `step_parameter(p, group, i)` over the parameters.  Each entry
+ * point below replaces one cluster of that loop's tensor ops for a whole
+ * parameter group at once; the Python classes in advanced_optimizers_b200/
+ * call them through ctypes (the binding INTEGRATION.md shows).
+ *
+ * Conventions
+ *  - All pointers inside the structs are DEVICE pointers unless stated.
+ *  - Every entry point is asynchronous on `stream` (a cudaStream_t passed as
+ *    void*), allocates nothing, and returns 0 on success or a negative
+ *    ADVOPT_E* code; advopt_last_error() then describes the failure.
+ *  - Tensors are contiguous; parameters and their gradients share a dtype.
+ */
+#ifndef ADVOPT_H_
+#define ADVOPT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ADVOPT_ABI_VERSION 1
+
+/* ---- error codes ---- */
+#define ADVOPT_OK 0
+#define ADVOPT_E_INVALID (-1)   /* bad argument (null table, unsupported mode, size) */
+#define ADVOPT_E_CUDA (-2)      /* a CUDA runtime call failed */
+#define ADVOPT_E_UNSUPPORTED (-3)
+
+/* ---- element / storage codes ---- */
+#define ADVOPT_DT_F32 0
+#define ADVOPT_DT_BF16 1
+
+/* state precision (group['actual_state_precision'] of the reference) */
+#define ADVOPT_PREC_FP32 0     /* fp32 states, fp32 math                      */
+#define ADVOPT_PREC_BF16_SR 1  /* bf16 states written by stochastic rounding  */
+#define ADVOPT_PREC_INT8_SR 2  /* int8 m / uint8 v, 2048-element block scales */
+#define ADVOPT_PREC_AUTO 3     /* states in the param dtype, math in it too   */
+
+/* algorithm */
+#define ADVOPT_ALGO_ADAMW 0    /* AdamW_adv._step_parameter (v before m)           */
+#define ADVOPT_ALGO_AUXADAM 1  /* Muon_AuxAdam._adam_step_parameter (m before v)   */
+#define ADVOPT_ALGO_PRODIGY 2  /* Prodigy_adv._step_parameter (d-scaled moments)   */
+
+/* launch flags */
+#define ADVOPT_F_NESTEROV (1u << 0)
+#define ADVOPT_F_ATAN2 (1u << 1)
+#define ADVOPT_F_NORMED (1u << 2)      /* normed_momentum (AdamW only) */
+#define ADVOPT_F_CAUTIOUS (1u << 3)
+#define ADVOPT_F_SR (1u << 4)          /* stochastic rounding of bf16 params */
+#define ADVOPT_F_NOISE_IN (1u << 5)    /* read SR noise from the tensors' noise_* arrays */
+#define ADVOPT_F_HAS_M (1u << 6)       /* betas[0] > 0 */
+#define ADVOPT_F_PRODIGY_STATS (1u << 7)
+#define ADVOPT_F_FISHER (1u << 8)      /* Fisher weight decay (needs a stats pass) */
+#define ADVOPT_F_FISHER_STATS (1u << 9)/* this launch only accumulates sum((p*ws)^2) */
+#define ADVOPT_F_ANCHORS (1u << 10)    /* some tensor carries a centered-WD anchor */
+
+/* per-tensor flags */
+#define ADVOPT_T_FACTORED (1u << 0)    /* second moment as rank-1 factors (factored_2nd) */
+#define ADVOPT_T_VEC (1u << 1)         /* all pointers 16-byte aligned: vector path allowed */
+#define ADVOPT_T_P0_SCALAR (1u << 2)   /* Prodigy p0 is the scalar 0 (all-zero param at init) */
+#define ADVOPT_T_ANCHOR_SHIFT 4        /* 3 bits: centered-WD anchor storage */
+#define ADVOPT_ANCHOR_NONE 0
+#define ADVOPT_ANCHOR_FULL 1           /* anchor in the param dtype      */
+#define ADVOPT_ANCHOR_FP8 2            /* float8_e4m3fn                   */
+#define ADVOPT_ANCHOR_INT8 3           /* int8, block 128, scale/min in the param dtype */
+#define ADVOPT_ANCHOR_INT4 4           /* int4 pairs (high, low), block 32 */
+
+/*
+ * One parameter tensor of an Adam-family group (AdamW_adv, Muon's auxiliary
+ * Adam, Prodigy_adv).  Field order is fixed: 8-byte fields, then 4-byte ones.
+ * Replaces the per-tensor state of AdamW_adv.py:221-277 / Prodigy_adv.py:271-331.
+ */
+typedef struct advopt_adam_tensor {
+  void* param;               /* p (f32 or bf16), updated in place             */
+  const void* grad;          /* p.grad                                        */
+  void* exp_avg;             /* m: f32 / bf16 / int8, NULL without momentum   */
+  float* exp_avg_scale;      /* int8 block scales [ceil(n/2048)]              */
+  void* exp_avg_sq;          /* v: f32 / bf16 / uint8, NULL when factored     */
+  float* exp_avg_sq_scale;   /* uint8 block scales                            */
+  float* row_factor;         /* factored: mu_v_nmf [d1] (rewritten in place)  */
+  float* col_factor;         /* factored: mv_v_nmf [d2] (rewritten by finish) */
+  float* col_partial;        /* factored: scratch [n_slots][d2]               */
+  void* aux0;                /* Prodigy s | anchor data                       */
+  void* aux1;                /* Prodigy p0 | anchor scale                     */
+  void* aux2;                /* anchor min                                    */
+  const int32_t* noise_v;    /* injected SR noise for v  (ADVOPT_F_NOISE_IN)  */
+  const int32_t* noise_m;    /* injected SR noise for m                       */
+  const int32_t* noise_p;    /* injected SR noise for the param               */
+  int64_t numel;
+  int64_t d1;                /* factored effective shape (d1, d2)             */
+  int64_t d2;
+  float step_size;           /* lr/bc1 (AdamW), dlr (Prodigy); x4/pi under atan2 */
+  float sqrt_bc2;            /* sqrt(1 - beta2^t), 1 without bias correction  */
+  float eps;                 /* eps or 1/sqrt(numel) (eps=None); Prodigy: d*eps */
+  float wd;                  /* weight_decay * lr (0: none)                   */
+  float cwd;                 /* centered_wd * lr (0: none)                    */
+  float fisher_clip;         /* Fisher: max(1, rms(p/denom)) written by advopt_fisher_finish */
+  uint32_t tensor_id;        /* stable id of the param inside the optimizer   */
+  uint32_t step;             /* Philox counter word (per-tensor step)         */
+  uint32_t flags;            /* ADVOPT_T_*                                    */
+  uint32_t slice_p;          /* Prodigy slice stride                          */
+  int32_t slot_base;         /* first partial slot of this tensor             */
+  int32_t n_slots;           /* partial slots of this tensor                  */
+} advopt_adam_tensor;
+
+/* A contiguous run [begin, end) of one tensor's flat elements, processed by
+ * one CTA.  begin is a multiple of 2048; for factored tensors both ends sit on
+ * row boundaries of the effective shape.  `slot` indexes the tensor's
+ * col_partial rows (factored) and the launch's per-piece statistics. */
+typedef struct advopt_piece {
+  int64_t begin;
+  int64_t end;
+  int32_t tensor;
+  int32_t slot;
+} advopt_piece;
+
+/* One launch over one parameter group (all scalars already rounded to fp32
+ * the way the reference's scalar arguments are). */
+typedef struct advopt_adam_launch {
+  const advopt_adam_tensor* tensors;  /* [n_tensors]                          */
+  const advopt_piece* pieces;         /* [n_pieces], grouped by CTA           */
+  const int32_t* cta_offsets;         /* [grid + 1]: CTA c runs pieces [off[c], off[c+1]) */
+  double* piece_stats;                /* [n_pieces * 2] Prodigy / Fisher partials */
+  int32_t n_tensors;
+  int32_t n_pieces;
+  int32_t grid;                       /* CTAs (= length of cta_offsets - 1)   */
+  int32_t smem_floats;                /* dynamic shared memory, floats        */
+  int32_t gen_offset;                 /* float offset of the generic-path buffers (>= max d2) */
+  int32_t algo;                       /* ADVOPT_ALGO_*                        */
+  int32_t precision;                  /* ADVOPT_PREC_*                        */
+  int32_t param_dtype;                /* ADVOPT_DT_*                          */
+  uint32_t flags;                     /* ADVOPT_F_*                           */
+  float beta1;                        /* mul_(beta1) (Prodigy m)              */
+  float beta2;                        /* mul_(beta2)                          */
+  float w_m;                          /* lerp weight 1 - beta1                */
+  float w_nest;                       /* lerp weight 1 - nesterov coef        */
+  float c_v;                          /* addcmul value: 1-beta2 (Prodigy: d*d*(1-beta2)) */
+  float c_m;                          /* Prodigy add alpha d*(1-beta1)        */
+  float d_eps;                        /* unused (Prodigy's d*eps is per tensor) */
+  float beta3;                        /* Prodigy s decay                      */
+  float s_alpha;                      /* Prodigy s add alpha                  */
+  float d;                            /* Prodigy d (grad.mul(d) without momentum) */
+  float pad0;
+  uint64_t seed;                      /* Philox key                           */
+} advopt_adam_launch;
+
+/* Adam-family step for one group.  Replaces AdamW_adv.step/_step_parameter
+ * (AdamW_adv.py:279-465), Muon_AuxAdam._adam_step_parameter
+ * (Muon_AuxAdam.py:70-192), Prodigy_adv._step_parameter
+ * (Prodigy_adv.py:372-519), and param_update.apply_parameter_update
+ * (param_update.py:77-156) for every tensor of the group. */
+int advopt_adam_step(const advopt_adam_launch* launch, void* stream);
+
+/* Second half of factored_2nd: reduce the column partials into mv_v_nmf and
+ * normalise one factor (factorization_util.py:60-80).  `tensor_index` lists
+ * the factored tensors of the launch. */
+int advopt_factored_finish(const advopt_adam_launch* launch, const int32_t* tensor_index,
+                           int32_t n_factored, int32_t max_d2, void* stream);
+
+/* Prodigy: fold the per-piece statistics into the group's running sums in
+ * parameter order (Prodigy_adv.py:505-509).  `sums` (device, 2 floats) holds
+ * d_numerator (already decayed by beta3) and d_denom on entry and exit.
+ * `coef` = (d/d0)*dlr as float, `s_is_bf16` says whether s is stored in bf16. */
+int advopt_prodigy_finish(const advopt_adam_launch* launch, float* sums, float coef,
+                          int32_t s_is_bf16, void* stream);
+
+/* Fisher weight decay: turn the per-piece sums of (p/denom)^2 into each
+ * tensor's 1/max(1, rms) (update_util.py:26-36), written to fisher_clip of a
+ * device copy of the tensor table. */
+int advopt_fisher_finish(const advopt_adam_launch* launch, advopt_adam_tensor* tensors_rw, void* stream);
+
+/* Lion_adv step for one group (Lion_adv.py:213-278, lion_k.py:23-24). */
+typedef struct advopt_lion_tensor {
+  void* param;
+  const void* grad;
+  void* exp_avg;             /* param dtype */
+  const int32_t* noise_p;
+  int64_t numel;
+  float lr;
+  float wd;                  /* weight_decay * lr */
+  uint32_t tensor_id;
+  uint32_t step;
+  uint32_t flags;            /* ADVOPT_T_VEC */
+  uint32_t pad;
+} advopt_lion_tensor;
+
+int advopt_lion_step(const advopt_lion_tensor* tensors, int32_t n_tensors, const advopt_piece* pieces,
+                     int32_t n_pieces, int32_t param_dtype, float w1, float w2, uint32_t flags,
+                     uint64_t seed, void* stream);
+
+/* Layout checks for bindings: sizeof of each struct. */
+size_t advopt_sizeof(int which); /* 0 adam_tensor, 1 piece, 2 adam_launch, 3 lion_tensor */
+int advopt_abi_version(void);
+/* Last error message of the calling thread ("" if none). */
+const char* advopt_last_error(void);
+/* Number of SMs and the Adam kernel's resident CTAs per SM for a given
+ * dynamic shared-memory size (floats); used by the host planner. */
+int advopt_adam_occupancy(int32_t precision, int32_t param_dtype, int32_t algo, int32_t smem_floats,
+                          int32_t* sm_count, int32_t* ctas_per_sm);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ADVOPT_H_ */

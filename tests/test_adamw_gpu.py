@@ -1,0 +1,130 @@
+"""AdamW_adv on the GPU against (1) the reference's own outputs recorded in
+the golden fixtures, with the reference's random integers injected, and (2)
+the oracle at sizes that exercise the fast factored path (d2 >= 2048).
+
+Tolerances (stated per check): int8/uint8 codes and block scales bit-exact;
+bf16 params within 1 bf16 ulp; fp32 values within 1e-6 relative (params) /
+2e-6 (states; factored row/column factors are sums whose float32 order
+differs from the reference's)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from _compare import check_bf16_param, check_fp32, check_state
+from _gpu import load_state, to_numpy, to_torch
+from _replay import O, list_cases, load, values
+
+pytestmark = pytest.mark.gpu
+
+ADAMW_CASES = [c for c in list_cases() if c.startswith("adamw_")]
+
+
+def _draws(z, s, i):
+    pre = f"r_{s}_{i}_"
+    return {k[len(pre):]: torch.from_numpy(z[k].astype(np.int32)).cuda() for k in z.files if k.startswith(pre)}
+
+
+@pytest.mark.parametrize("name", ADAMW_CASES)
+def test_adamw_matches_reference_golden(name):
+    import advanced_optimizers_b200 as A
+    meta, z = load(name)
+    dt = meta["dtype"]
+    shapes = [tuple(s) for s in meta["shapes"]]
+    params = [torch.nn.Parameter(to_torch(z[f"p0_{i}"], dt).reshape(sh)) for i, sh in enumerate(shapes)]
+    opt = A.AdamW_adv(params, **meta["kw"])
+    for s in range(meta["steps"]):
+        # teacher forcing: start each step from the reference's params and states
+        for i, p in enumerate(params):
+            if s > 0:
+                p.data.copy_(to_torch(z[f"p_{s - 1}_{i}"], dt).reshape(p.shape))
+            load_state(opt, p, z, s - 1 if s > 0 else -1, i)
+            p.grad = to_torch(z[f"g_{s}_{i}"], dt).reshape(p.shape)
+        opt.set_test_noise({p: _draws(z, s, i) for i, p in enumerate(params)})
+        opt.step()
+        torch.cuda.synchronize()
+        for i, p in enumerate(params):
+            what = f"{name} step {s} param {i}"
+            ref_p = z[f"p_{s}_{i}"]
+            if dt == "bf16":
+                check_bf16_param(to_numpy(p), ref_p, what)
+            else:
+                prev = z[f"p_{s - 1}_{i}"] if s > 0 else z[f"p0_{i}"]
+                check_fp32(to_numpy(p), ref_p, 1e-6, what, prev)
+            for key, val in opt.state[p].items():
+                rk = f"st_{s}_{i}_{key}"
+                if torch.is_tensor(val) and rk in z.files:
+                    pk = f"st_{s - 1}_{i}_{key}" if s > 0 else f"st0_{i}_{key}"
+                    prev = z[pk] if pk in z.files and z[pk].shape == z[rk].shape else None
+                    check_state(key, to_numpy(val), z[rk], f"{what} {key}", prev)
+            assert opt.state[p]["step"] == int(z[f"st_{s}_{i}_step"])
+
+
+def _oracle_state_from_torch(st):
+    out = {}
+    for k, v in st.items():
+        out[k] = to_numpy(v) if torch.is_tensor(v) else v
+    return out
+
+
+@pytest.mark.parametrize("case", [
+    # (shapes, dtype, kwargs) — effective shapes hit d2 = 2048, 4096, 7168 (fast path) and small d2
+    ([(4096, 1024), (2048, 2048), (4096,), (777, 3)], "bf16",
+     dict(state_precision="int8_sr", factored_2nd=True, nesterov=True)),
+    ([(14336, 4096)], "bf16", dict(state_precision="int8_sr", factored_2nd=True, nesterov=True)),
+    ([(1024, 4096), (4096,), (33, 65)], "bf16", dict(state_precision="int8_sr", weight_decay=0.1, lr=1e-2)),
+    ([(768, 2304), (2304,), (50257, 64)], "f32",
+     dict(state_precision="fp32", weight_decay=0.01)),
+])
+def test_adamw_matches_oracle_large(case):
+    import advanced_optimizers_b200 as A
+    shapes, dt, kw = case
+    g = torch.Generator().manual_seed(0)
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float32
+    p_host = [(torch.randn(sh, generator=g) * 0.02).to(tdt) for sh in shapes]
+    params = [torch.nn.Parameter(t.cuda()) for t in p_host]
+    opt = A.AdamW_adv(params, **kw)
+    ostate = [_oracle_state_from_torch(opt.state[p]) for p in params]
+    hp = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, nesterov=False, use_bias_correction=True,
+              stochastic_rounding=True, precision=kw.get("state_precision", "auto"))
+    hp.update({k: v for k, v in kw.items() if k != "state_precision"})
+    p_o = [to_numpy(t) for t in p_host]
+    p_o = [O.from_bf16_bits(x) if dt == "bf16" else x for x in p_o]
+    for s in range(2):
+        grads = []
+        for sh in shapes:
+            t = torch.randn(sh, generator=g) * 1e-3
+            mask = torch.rand(sh, generator=g) < 0.01
+            grads.append(torch.where(mask, t * 100, t).to(tdt))
+        noise = {}
+        for p, sh in zip(params, shapes):
+            n = math.prod(sh)
+            pad = ((n + 2047) // 2048) * 2048
+            noise[p] = {"exp_avg": torch.randint(0, 65536, (pad,), generator=g, dtype=torch.int32),
+                        "exp_avg_sq": torch.randint(0, 65536, (pad,), generator=g, dtype=torch.int32),
+                        "param": torch.randint(0, 65536, (n,), generator=g, dtype=torch.int32)}
+        for p, gr in zip(params, grads):
+            p.grad = gr.cuda()
+        opt.set_test_noise({p: {k: v.cuda() for k, v in nz.items()} for p, nz in noise.items()})
+        opt.step()
+        torch.cuda.synchronize()
+        for i, (p, sh) in enumerate(zip(params, shapes)):
+            gnp = to_numpy(grads[i])
+            gv = O.from_bf16_bits(gnp).reshape(sh) if dt == "bf16" else gnp
+            nz = {k: v.numpy() for k, v in noise[p].items()}
+            prev = p_o[i].copy()
+            p_o[i] = O.adam_family_step(p_o[i], dt, gv, ostate[i], hp, nz, algo="adamw")
+            what = f"{shapes[i]} step {s}"
+            if dt == "bf16":
+                check_bf16_param(to_numpy(p), O.bf16_bits(p_o[i]), what)
+            else:
+                check_fp32(to_numpy(p), p_o[i], 1e-6, what, prev)
+            for key, val in opt.state[p].items():
+                if torch.is_tensor(val) and key in ostate[i] and isinstance(ostate[i][key], np.ndarray):
+                    check_state(key, to_numpy(val), ostate[i][key], f"{what} {key}")
+            # keep the oracle on the device's factors so later steps compare one step each
+            for key in ("mu_v_nmf", "mv_v_nmf"):
+                if key in ostate[i]:
+                    ostate[i][key] = to_numpy(opt.state[p][key])
+            p_o[i] = O.from_bf16_bits(to_numpy(p)).reshape(sh) if dt == "bf16" else to_numpy(p).reshape(sh)
