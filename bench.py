@@ -31,10 +31,10 @@ sys.path.insert(0, ROOT)
 WORKLOAD = "adamw_adv int8_sr+factored_2nd+nesterov, llama-3-8b shapes, bf16"
 
 
-def llama3_8b_shapes():
-    d, L, kv, ffn, V = 4096, 32, 1024, 14336, 128256
-    s = [(V, d), (V, d)]
-    for _ in range(L):
+def llama3_8b_shapes(layers=32, embed=True):
+    d, kv, ffn, V = 4096, 1024, 14336, 128256
+    s = [(V, d), (V, d)] if embed else []
+    for _ in range(layers):
         s += [(d, d), (kv, d), (kv, d), (d, d), (ffn, d), (ffn, d), (d, ffn), (d,), (d,)]
     return s + [(d,)]
 
@@ -203,7 +203,7 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     import advanced_optimizers_b200 as A
 
-    shapes = llama3_8b_shapes()
+    shapes = llama3_8b_shapes(args.layers, not args.no_embed)
     total = sum(math.prod(s) for s in shapes)
     owner = lpt_shard(shapes, world)
     mine = [i for i in range(len(shapes)) if owner[i] == rank]
@@ -327,7 +327,9 @@ def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, la
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "params": total, "tensors": len(shapes),
+            "config": {"workload": WORKLOAD if (args.layers == 32 and not args.no_embed) else
+                       f"profiling subset: {args.layers} layers" + ("" if not args.no_embed else ", no embeddings"),
+                       "params": total, "tensors": len(shapes),
                        "parallelism": f"per-tensor sharding x{world}" + (" + bf16 param all-gather" if world > 1 else ""),
                        "l2": "inputs larger than L2 (about 40 GB resident per step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -351,6 +353,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--layers", type=int, default=32, help="decoder layers (32 = the full model; fewer for profiling)")
+    ap.add_argument("--no-embed", action="store_true", help="leave out embed/lm_head (profiling only)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
