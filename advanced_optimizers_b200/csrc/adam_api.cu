@@ -1,0 +1,183 @@
+// Adam-family host dispatch, the factored/Prodigy/Fisher finishing kernels
+// and the C entry points (include/advopt.h).
+#include "adam_impl.cuh"
+
+namespace advopt {
+
+// ---------------------------------------------------------------------------
+// factored_2nd finish: column sums from the partials, then normalise one
+// factor (factorization_util.py:60-80).  Kernel A sums partial rows in slot
+// order (float64) into mv; kernel B normalises mu (d1 < d2) or mv by its total.
+// ---------------------------------------------------------------------------
+__global__ void factored_cols_kernel(const advopt_adam_tensor* tensors, const int32_t* index) {
+  const advopt_adam_tensor* t = tensors + index[blockIdx.y];
+  const int64_t d2 = t->d2;
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= d2) return;
+  double acc = 0.0;
+  const float* src = t->col_partial + j;
+  for (int s = 0; s < t->n_slots; ++s) acc += (double)src[(int64_t)s * d2];
+  t->col_factor[j] = (float)acc;
+}
+
+__global__ void factored_norm_kernel(const advopt_adam_tensor* tensors, const int32_t* index) {
+  const advopt_adam_tensor* t = tensors + index[blockIdx.x];
+  const int64_t d1 = t->d1, d2 = t->d2;
+  float* vec = d1 < d2 ? t->row_factor : t->col_factor;
+  const int64_t n = d1 < d2 ? d1 : d2;
+  __shared__ double part[32];
+  double acc = 0.0;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) acc += (double)vec[i];
+  acc = warp_sum_d(acc);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  __shared__ float scale_s;
+  if (threadIdx.x == 0) {
+    double tot = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += part[w];
+    float sc = (float)tot;
+    scale_s = sc < 1e-12f ? 1e-12f : sc;     // scale.clamp_min_(1e-12)
+  }
+  __syncthreads();
+  const float sc = scale_s;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) vec[i] = __fdiv_rn(vec[i], sc);
+}
+
+// Prodigy: per-tensor sums of the piece statistics, folded in param order.
+__global__ void prodigy_finish_kernel(const advopt_adam_launch L, float* sums, float coef, int s_is_bf16) {
+  __shared__ double dot_s[256], abs_s[256];
+  float num = sums[0], den = sums[1];
+  // pieces of tensor t are found by scanning all pieces (launch sizes are small)
+  for (int t = 0; t < L.n_tensors; ++t) {
+    double a = 0.0, b = 0.0;
+    for (int i = threadIdx.x; i < L.n_pieces; i += blockDim.x) {
+      if (L.pieces[i].tensor == t) {
+        a += L.piece_stats[2 * i];
+        b += L.piece_stats[2 * i + 1];
+      }
+    }
+    dot_s[threadIdx.x] = a;
+    abs_s[threadIdx.x] = b;
+    __syncthreads();
+    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+      if ((int)threadIdx.x < o) {
+        dot_s[threadIdx.x] += dot_s[threadIdx.x + o];
+        abs_s[threadIdx.x] += abs_s[threadIdx.x + o];
+      }
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+      const float dot = (float)dot_s[0];
+      num = __fadd_rn(num, __fmul_rn(coef, dot));              // d_numerator.add_((d/d0)*dlr*dot)
+      float sabs = (float)abs_s[0];
+      if (s_is_bf16) sabs = round_bf16(sabs);                 // s.abs().sum() is bf16 for bf16 s
+      den = __fadd_rn(den, sabs);
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    sums[0] = num;
+    sums[1] = den;
+  }
+}
+
+// Fisher: rms of p*ws per tensor -> 1/max(1, rms) stored as fisher_clip (the
+// divisor clip_coef itself; update_util.py:26-36).
+__global__ void fisher_finish_kernel(const advopt_adam_launch L, advopt_adam_tensor* tensors_rw) {
+  const int t = blockIdx.x;
+  __shared__ double part[256];
+  double a = 0.0;
+  for (int i = threadIdx.x; i < L.n_pieces; i += blockDim.x)
+    if (L.pieces[i].tensor == t) a += L.piece_stats[2 * i];
+  part[threadIdx.x] = a;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if ((int)threadIdx.x < o) part[threadIdx.x] += part[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const double n = (double)tensors_rw[t].numel;
+    const float mean = (float)(part[0] / n);
+    const float rms = __fsqrt_rn(mean);
+    tensors_rw[t].fisher_clip = rms > 1.0f ? rms : 1.0f;
+  }
+}
+
+
+static cudaError_t run_adam(const advopt_adam_launch& L, cudaStream_t s) {
+  switch (L.precision) {
+    case ADVOPT_PREC_FP32: return launch_adam_fp32(L, s);
+    case ADVOPT_PREC_BF16_SR: return launch_adam_bf16sr(L, s);
+    case ADVOPT_PREC_INT8_SR: return launch_adam_int8(L, s);
+    default:  // AUTO: f32 params are exactly the FP32 path
+      return L.param_dtype == ADVOPT_DT_BF16 ? launch_adam_auto(L, s) : launch_adam_fp32(L, s);
+  }
+}
+
+static cudaError_t run_occupancy(int prec, int pdt, int algo, int smem_floats, int* ctas) {
+  switch (prec) {
+    case ADVOPT_PREC_FP32: return occupancy_adam_fp32(pdt, algo, smem_floats, ctas);
+    case ADVOPT_PREC_BF16_SR: return occupancy_adam_bf16sr(pdt, algo, smem_floats, ctas);
+    case ADVOPT_PREC_INT8_SR: return occupancy_adam_int8(pdt, algo, smem_floats, ctas);
+    default: return pdt == ADVOPT_DT_BF16 ? occupancy_adam_auto(pdt, algo, smem_floats, ctas)
+                                          : occupancy_adam_fp32(pdt, algo, smem_floats, ctas);
+  }
+}
+
+}  // namespace advopt
+
+using namespace advopt;
+
+extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
+  if (!L || !L->tensors || !L->pieces || !L->cta_offsets || L->grid <= 0)
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: null table or empty grid");
+  if (L->precision < 0 || L->precision > 3 || L->algo < 0 || L->algo > 2 || L->param_dtype < 0 || L->param_dtype > 1)
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: bad precision/algo/dtype code");
+  if ((L->flags & (ADVOPT_F_PRODIGY_STATS | ADVOPT_F_FISHER_STATS)) && !L->piece_stats)
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: statistics requested without piece_stats");
+  if (L->smem_floats < 0 || L->smem_floats > 49152)
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: factored d2 above 49152 columns is not supported");
+  return check_cuda(run_adam(*L, static_cast<cudaStream_t>(stream)), "advopt_adam_step");
+}
+
+extern "C" int advopt_factored_finish(const advopt_adam_launch* L, const int32_t* index, int32_t n_factored,
+                                      int32_t max_d2, void* stream) {
+  if (!L || (n_factored > 0 && !index)) return set_error(ADVOPT_E_INVALID, "advopt_factored_finish: null argument");
+  if (n_factored <= 0) return ADVOPT_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  dim3 ga((unsigned)((max_d2 + 255) / 256), (unsigned)n_factored);
+  factored_cols_kernel<<<ga, 256, 0, s>>>(L->tensors, index);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return check_cuda(e, "advopt_factored_finish");
+  factored_norm_kernel<<<n_factored, 1024, 0, s>>>(L->tensors, index);
+  return check_cuda(cudaGetLastError(), "advopt_factored_finish");
+}
+
+extern "C" int advopt_prodigy_finish(const advopt_adam_launch* L, float* sums, float coef, int32_t s_is_bf16,
+                                     void* stream) {
+  if (!L || !sums || !L->piece_stats) return set_error(ADVOPT_E_INVALID, "advopt_prodigy_finish: null argument");
+  prodigy_finish_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(*L, sums, coef, s_is_bf16);
+  return check_cuda(cudaGetLastError(), "advopt_prodigy_finish");
+}
+
+extern "C" int advopt_fisher_finish(const advopt_adam_launch* L, advopt_adam_tensor* tensors_rw, void* stream) {
+  if (!L || !tensors_rw || !L->piece_stats) return set_error(ADVOPT_E_INVALID, "advopt_fisher_finish: null argument");
+  fisher_finish_kernel<<<L->n_tensors, 256, 0, static_cast<cudaStream_t>(stream)>>>(*L, tensors_rw);
+  return check_cuda(cudaGetLastError(), "advopt_fisher_finish");
+}
+
+extern "C" int advopt_adam_occupancy(int32_t precision, int32_t param_dtype, int32_t algo, int32_t smem_floats,
+                                     int32_t* sm_count, int32_t* ctas_per_sm) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return check_cuda(e, "advopt_adam_occupancy");
+  int sms = 0;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return check_cuda(e, "advopt_adam_occupancy");
+  int ctas = 0;
+  e = run_occupancy(precision, param_dtype, algo, smem_floats, &ctas);
+  if (e != cudaSuccess) return check_cuda(e, "advopt_adam_occupancy");
+  if (sm_count) *sm_count = sms;
+  if (ctas_per_sm) *ctas_per_sm = ctas;
+  return ADVOPT_OK;
+}

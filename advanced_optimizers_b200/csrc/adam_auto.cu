@@ -1,0 +1,9 @@
+// Adam-family kernels instantiated for state precision ADVOPT_PREC_AUTO.
+#include "adam_impl.cuh"
+
+namespace advopt {
+cudaError_t launch_adam_auto(const advopt_adam_launch& L, cudaStream_t s) { return launch_adam_prec<ADVOPT_PREC_AUTO>(L, s); }
+cudaError_t occupancy_adam_auto(int pdt, int algo, int smem_floats, int* ctas) {
+  return occupancy_adam_prec<ADVOPT_PREC_AUTO>(pdt, algo, smem_floats, ctas);
+}
+}  // namespace advopt

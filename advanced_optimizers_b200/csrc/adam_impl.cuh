@@ -1,4 +1,4 @@
-// Multi-tensor Adam-family step (AdamW_adv, Muon's auxiliary Adam, Prodigy_adv)
+// Multi-tensor Adam-family step kernel template (included by adam_<precision>.cu) (AdamW_adv, Muon's auxiliary Adam, Prodigy_adv)
 // for sm_100a.  One persistent launch covers a whole parameter group: the host
 // planner cuts the group's tensors into "pieces" (contiguous, 2048-aligned
 // element ranges; row-aligned for factored tensors) and gives every CTA a
@@ -15,9 +15,11 @@
 //   sums and column partials of factored_2nd (factorization_util.py:60-80),
 //   weight decay incl. cautious/centered/Fisher (param_update.py:15-156), and
 //   Prodigy's slice statistics (Prodigy_adv.py:495-511).
+#pragma once
+
 #include "advopt.h"
-#include "common.cuh"
 #include "capi_internal.h"
+#include "common.cuh"
 
 namespace advopt {
 
@@ -64,17 +66,6 @@ __device__ __forceinline__ void load_tensor(const advopt_adam_tensor* t, TensorR
   r.step_size = t->step_size; r.sqrt_bc2 = t->sqrt_bc2; r.eps = t->eps; r.wd = t->wd; r.cwd = t->cwd;
   r.fisher_clip = t->fisher_clip;
   r.tensor_id = t->tensor_id; r.step = t->step; r.flags = t->flags; r.slice_p = t->slice_p;
-}
-
-// Noise for 8 elements: injected int32 array or Philox.
-__device__ __forceinline__ void noise8(const advopt_adam_launch& L, const TensorRegs& T, const int32_t* arr,
-                                       uint32_t stream, int64_t k0, int nv, uint32_t (&r)[8]) {
-  if (L.flags & ADVOPT_F_NOISE_IN) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) r[e] = e < nv ? (uint32_t)arr[k0 + e] : 0u;
-  } else {
-    philox_u16x8(L.seed, T.tensor_id, T.step, stream, k0, r);
-  }
 }
 
 // Centered-WD anchor value of element k as float (centered_decay.py:219-261).
@@ -168,20 +159,169 @@ __device__ __forceinline__ float fisher_den(float v, float den_u, const TensorRe
   return __fadd_rn(__fdiv_rn(den, T.sqrt_bc2), T.eps);
 }
 
+
+// ---------------------------------------------------------------------------
+// Raw words of one thread's 8 elements of one chunk, as loaded from HBM; the
+// next chunk's words are loaded while the current chunk is computed.
+// ---------------------------------------------------------------------------
+template <int BPE>
+struct Words {
+  static constexpr int N = 2 * BPE;  // 32-bit words for 8 elements
+  uint32_t w[N];
+};
+
+template <int BPE>
+__device__ __forceinline__ void ld_words(const void* base, int64_t k0, int nv, bool v8, Words<BPE>& out) {
+  const unsigned char* p = static_cast<const unsigned char*>(base) + k0 * BPE;
+  if (v8) {
+    if (BPE == 1) {
+      const uint2 q = __ldg(reinterpret_cast<const uint2*>(p));
+      out.w[0] = q.x; out.w[1] = q.y;
+    } else if (BPE == 2) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(p));
+      out.w[0] = q.x; out.w[1] = q.y; out.w[2] = q.z; out.w[3] = q.w;
+    } else {
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+      const uint4 b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+      out.w[0] = a.x; out.w[1] = a.y; out.w[2] = a.z; out.w[3] = a.w;
+      out.w[4] = b.x; out.w[5] = b.y; out.w[6] = b.z; out.w[7] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < Words<BPE>::N; ++i) out.w[i] = 0u;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (e < nv) {
+        if (BPE == 1) out.w[e >> 2] |= (uint32_t)p[e] << (8 * (e & 3));
+        else if (BPE == 2) out.w[e >> 1] |= (uint32_t)reinterpret_cast<const uint16_t*>(p)[e] << (16 * (e & 1));
+        else out.w[e] = reinterpret_cast<const uint32_t*>(p)[e];
+      }
+    }
+  }
+}
+
+// Unpack 8 elements to float: BPE 4 = f32, 2 = bf16, 1 = int8 (SIGNED) / uint8.
+template <int BPE, bool SIGNED = true>
+__device__ __forceinline__ void unpack8(const Words<BPE>& in, float (&x)[8]) {
+  if (BPE == 4) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[e] = __uint_as_float(in.w[e]);
+  } else if (BPE == 2) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = __uint_as_float(in.w[i] << 16);
+      x[2 * i + 1] = __uint_as_float(in.w[i] & 0xFFFF0000u);
+    }
+  } else {
+    codes4_to_f<SIGNED>(in.w[0], x);
+    codes4_to_f<SIGNED>(in.w[1], x + 4);
+  }
+}
+
+template <int kStore>
+struct StoreBytes {
+  static constexpr int v = kStore == 2 ? 1 : (kStore == 1 ? 2 : 4);
+};
+
+// Per-thread raw data of one chunk.
+template <bool PBF, int kStore>
+struct Raw {
+  Words<PBF ? 2 : 4> g, p;
+  Words<StoreBytes<kStore>::v> m, v;
+  float mv[8];
+  float mu, ms, vs;
+};
+
+struct ChunkPos {
+  int64_t cs;    // first element of the chunk
+  int clen;      // elements in the chunk
+  int64_t r0;    // factored: row of the chunk's first element
+  int64_t c0;    // factored: its column
+};
+
 template <int PREC, bool PBF, int ALGO, bool EXT>
-__global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_launch L) {
+__device__ __forceinline__ void load_raw(const TensorRegs& T, const ChunkPos& cp, int tid, bool fact, bool ffast,
+                                         bool has_m, bool vec, Raw<PBF, StateTraits<PREC, PBF>::kStore>& R) {
+  constexpr int kStore = StateTraits<PREC, PBF>::kStore;
+  constexpr int SB = StoreBytes<kStore>::v;
+  const int64_t k0 = cp.cs + tid * kVec;
+  const int nv = max(0, min(kVec, cp.clen - tid * kVec));
+  const bool v8 = vec && nv == kVec;
+  const int64_t blk = cp.cs >> 11;
+  ld_words<PBF ? 2 : 4>(T.grad, k0, nv, v8, R.g);
+  ld_words<PBF ? 2 : 4>(T.param, k0, nv, v8, R.p);
+  if (has_m) {
+    ld_words<SB>(T.m, k0, nv, v8, R.m);
+    if (kStore == 2) R.ms = T.m_scale[blk];
+  }
+  if (fact) {
+    if (ffast) {
+      const int64_t cc = cp.c0 + tid * kVec;
+      const bool second = cc >= T.d2;
+      const int64_t col = second ? cc - T.d2 : cc;
+      R.mu = nv > 0 ? T.row[cp.r0 + (second ? 1 : 0)] : 0.0f;
+      const float4 a = *reinterpret_cast<const float4*>(T.col + col);
+      const float4 b = *(reinterpret_cast<const float4*>(T.col + col) + 1);
+      R.mv[0] = a.x; R.mv[1] = a.y; R.mv[2] = a.z; R.mv[3] = a.w;
+      R.mv[4] = b.x; R.mv[5] = b.y; R.mv[6] = b.z; R.mv[7] = b.w;
+    }
+  } else {
+    ld_words<SB>(T.v, k0, nv, v8, R.v);
+    if (kStore == 2) R.vs = T.v_scale[blk];
+  }
+}
+
+template <bool NOISE_IN>
+__device__ __forceinline__ U4 noise_words(const advopt_adam_launch& L, const TensorRegs& T, const int32_t* arr,
+                                          uint32_t stream, int64_t k0, int nv) {
+  if (NOISE_IN) {
+    uint32_t r[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) r[e] = e < nv ? ((uint32_t)arr[k0 + e] & 0xFFFFu) : 0u;
+    return U4{r[0] | (r[1] << 16), r[2] | (r[3] << 16), r[4] | (r[5] << 16), r[6] | (r[7] << 16)};
+  }
+  const uint64_t grp = (uint64_t)k0 >> 3;
+  U4 c{(uint32_t)grp, (uint32_t)(grp >> 32) | (stream << 24), T.tensor_id, T.step};
+  return philox4x32_10(c, (uint32_t)L.seed, (uint32_t)(L.seed >> 32));
+}
+__device__ __forceinline__ uint32_t noise_at(const U4& n, int e) {
+  const uint32_t w = (e >> 1) == 0 ? n.x : (e >> 1) == 1 ? n.y : (e >> 1) == 2 ? n.z : n.w;
+  return (e & 1) ? (w >> 16) : (w & 0xFFFFu);
+}
+
+// Stochastic quantisation of 8 values with a per-block divisor (set_state,
+// state_util.py:124-157 and param_update.py:271-363), packed into 2 words.
+template <bool SIGNED>
+__device__ __forceinline__ uint2 quantize8(const float (&x)[8], float bmax, const U4& nz) {
+  const float scale = __fdiv_rn(bmax, SIGNED ? 127.0f : 255.0f);
+  const float safe = scale < 1e-12f ? 1e-12f : scale;
+  const float rs = __frcp_rn(safe);
+  int c[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float y = __fadd_rn(div_const(x[e], safe, rs), noise_unit(noise_at(nz, e)));
+    const int f = floor_int(y);
+    c[e] = SIGNED ? min(max(f, -127), 127) : min(max(f, 0), 255);
+  }
+  return make_uint2(pack4_bytes(c[0], c[1], c[2], c[3]), pack4_bytes(c[4], c[5], c[6], c[7]));
+}
+
+template <int PREC, bool PBF, int ALGO, bool EXT, bool NOISE_IN>
+__global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_launch L) {
   using TR = StateTraits<PREC, PBF>;
   constexpr int kStore = TR::kStore;
   constexpr bool kMBF = TR::kMathBF;
+  constexpr int SB = StoreBytes<kStore>::v;
   // dynamic shared memory: [0, max d2) column accumulators of the factored
   // tensor in progress; from gen_offset, the generic factored path's staged
   // chunk (2048 floats) and row-segment sums (2049 floats)
-  extern __shared__ float dsm[];
-  float* colacc = dsm;
-  float* vbuf = dsm + L.gen_offset;
+  extern __shared__ float4 dsm4[];
+  float* colacc = reinterpret_cast<float*>(dsm4);
+  float* vbuf = colacc + L.gen_offset;
   float* segs = vbuf + kChunk;
   __shared__ float red[2][kWarps][4];         // per-chunk block reductions (double-buffered)
   __shared__ double dred[kWarps][2];
+  __shared__ TensorRegs Ts;                   // the piece's tensor descriptor
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t F = L.flags;
@@ -195,69 +335,86 @@ __global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_lau
   const bool fstats = EXT && (F & ADVOPT_F_FISHER_STATS);
   // the Fisher statistics pass writes nothing but piece_stats
   const bool pstats = (ALGO == ADVOPT_ALGO_PRODIGY) && (F & ADVOPT_F_PRODIGY_STATS) && !fstats;
+  const float beta1 = L.beta1, beta2 = L.beta2, w_m = L.w_m, w_nest = L.w_nest, c_v = L.c_v, c_m = L.c_m;
   auto Rm = [](float x) { return kMBF ? round_bf16(x) : x; };  // rounding of m / update / grad ops
   int parity = 0;
 
   const int pbeg = L.cta_offsets[blockIdx.x], pend = L.cta_offsets[blockIdx.x + 1];
-  __shared__ TensorRegs T;  // descriptor of the piece's tensor, read field by field when needed
   for (int pi = pbeg; pi < pend; ++pi) {
     const advopt_piece pc = L.pieces[pi];
-    __syncthreads();  // previous piece finished with T
-    if (tid == 0) load_tensor(L.tensors + pc.tensor, T);
+    __syncthreads();  // the previous piece is done with Ts
+    if (tid == 0) load_tensor(L.tensors + pc.tensor, Ts);
     __syncthreads();
+    const TensorRegs& T = Ts;  // fields are re-read from shared memory where registers are short
     const bool fact = T.flags & ADVOPT_T_FACTORED;
     const bool vec = T.flags & ADVOPT_T_VEC;
     const bool has_anchor = EXT && (((T.flags >> ADVOPT_T_ANCHOR_SHIFT) & 7u) != 0);
-    // factored row/column sums are skipped in the Fisher statistics pass
-    const bool fact_sums = fact && !fstats;
+    const bool fact_sums = fact && !fstats;   // factored row/column sums (skipped by the Fisher pass)
     const int64_t d2 = fact ? T.d2 : 1;
-    // fast factored path: every chunk holds each column at most once and each
-    // thread's 8 elements sit in one row with 8 aligned factor columns
-    const bool ffast = fact && d2 >= kChunk && (d2 % 8) == 0;
+    // fast factored path: each column at most once per chunk, each thread's 8
+    // elements in one row, 8-aligned factor columns
+    const bool ffast = fact && d2 >= kChunk && (d2 % 8) == 0 && ((reinterpret_cast<uintptr_t>(T.col) & 15) == 0);
     const bool vbf = kMBF && !fact;  // v math in bf16 ('auto' bf16, not factored)
+    const float rcp_sbc2 = __frcp_rn(T.sqrt_bc2);
+    const float step_size = T.step_size, eps = T.eps, sbc2 = T.sqrt_bc2, wd = T.wd, cwd = T.cwd;
     if (fact_sums) {
       for (int j = tid; j < (int)d2; j += kThreads) colacc[j] = 0.0f;
       __syncthreads();
     }
-    int64_t r0 = fact ? pc.begin / d2 : 0;
-    int64_t c0 = fact ? pc.begin - r0 * d2 : 0;
     double row_carry = 0.0;  // thread 0: running sum of the row in progress
     double st0 = 0.0, st1 = 0.0;
     const uint32_t slice_p = T.slice_p ? T.slice_p : 1u;
 
-    for (int64_t cs = pc.begin; cs < pc.end; cs += kChunk) {
-      const int clen = (int)min((int64_t)kChunk, pc.end - cs);
-      const int64_t k0 = cs + tid * kVec;
+    ChunkPos cp;
+    cp.cs = pc.begin;
+    cp.clen = (int)min((int64_t)kChunk, pc.end - pc.begin);
+    cp.r0 = fact ? pc.begin / d2 : 0;
+    cp.c0 = fact ? pc.begin - cp.r0 * d2 : 0;
+    Raw<PBF, kStore> cur;
+    load_raw<PREC, PBF, ALGO, EXT>(T, cp, tid, fact, ffast, has_m, vec, cur);
+
+    while (true) {
+      // next chunk's position, and its loads in flight during this chunk
+      ChunkPos np = cp;
+      np.cs = cp.cs + kChunk;
+      const bool has_next = np.cs < pc.end;
+      if (fact) {
+        np.c0 = cp.c0 + cp.clen;
+        if (ffast) {
+          if (np.c0 >= d2) { np.c0 -= d2; np.r0 += 1; }
+        } else if (np.c0 >= d2) {
+          const int64_t dr = np.c0 / d2;
+          np.r0 += dr;
+          np.c0 -= dr * d2;
+        }
+      }
+      Raw<PBF, kStore> nxt;
+      if (has_next) {
+        np.clen = (int)min((int64_t)kChunk, pc.end - np.cs);
+        load_raw<PREC, PBF, ALGO, EXT>(T, np, tid, fact, ffast, has_m, vec, nxt);
+      }
+
+      const int clen = cp.clen;
+      const int64_t k0 = cp.cs + tid * kVec;
       const int nv = max(0, min(kVec, clen - tid * kVec));
       const bool v8 = vec && nv == kVec;
-      const int64_t blk = cs / kChunk;
+      const int64_t blk = cp.cs >> 11;
+      const int64_t r0 = cp.r0, c0 = cp.c0;
 
       float g[8], p[8], m[8], vh[8];
-      load8<PBF>(T.grad, k0, nv, v8, g);
-      load8<PBF>(T.param, k0, nv, v8, p);
+      unpack8<PBF ? 2 : 4>(cur.g, g);
+      unpack8<PBF ? 2 : 4>(cur.p, p);
       if (has_m) {
+        unpack8<SB, true>(cur.m, m);
         if (kStore == 2) {
-          const float sc = T.m_scale[blk];
-          load8_q<true>(T.m, k0, nv, v8, m);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) m[e] = __fmul_rn(m[e], sc);
-        } else if (kStore == 1) {
-          load8<true>(T.m, k0, nv, v8, m);
-        } else {
-          load8<false>(T.m, k0, nv, v8, m);
+          for (int e = 0; e < 8; ++e) m[e] = __fmul_rn(m[e], cur.ms);
         }
       }
       if (fact) {
-        // v_hat = outer(mu, mv) (factorization_util.py:53-57)
         if (ffast) {
-          const int64_t cc = c0 + tid * kVec;
-          const bool second = cc >= d2;
-          const int64_t col = second ? cc - d2 : cc;
-          float mv[8];
-          load8<false>(T.col, col, 8, (reinterpret_cast<uintptr_t>(T.col) & 15) == 0, mv);
-          const float mu = nv > 0 ? T.row[r0 + (second ? 1 : 0)] : 0.0f;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) vh[e] = __fmul_rn(mu, mv[e]);
+          for (int e = 0; e < 8; ++e) vh[e] = __fmul_rn(cur.mu, cur.mv[e]);   // outer(mu, mv)
         } else {
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -270,36 +427,30 @@ __global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_lau
           }
         }
       } else {
+        unpack8<SB, false>(cur.v, vh);
         if (kStore == 2) {
-          const float sc = T.v_scale[blk];
-          load8_q<false>(T.v, k0, nv, v8, vh);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) vh[e] = __fmul_rn(vh[e], sc);
-        } else if (kStore == 1) {
-          load8<true>(T.v, k0, nv, v8, vh);
-        } else {
-          load8<false>(T.v, k0, nv, v8, vh);
+          for (int e = 0; e < 8; ++e) vh[e] = __fmul_rn(vh[e], cur.vs);
         }
       }
-      uint32_t rp[8];
-      if (sr && !fstats) noise8(L, T, T.nz_p, kNoiseP, k0, nv, rp);
+      U4 nzp{0u, 0u, 0u, 0u};
+      if (sr && !fstats) nzp = noise_words<NOISE_IN>(L, T, T.nz_p, kNoiseP, k0, nv);
       int slice_off = 0;  // offset of the next Prodigy slice point from k0
       if (pstats) slice_off = (int)((slice_p - (uint32_t)(k0 % slice_p)) % slice_p);
 
-      // ---- per-element arithmetic, in the reference's op order; the param
-      // update does not depend on the block statistics and is done here ----
+      // ---- per-element arithmetic in the reference's op order; the param
+      // update does not need the block statistics and happens here ----
       float m_new[8], v[8];
       float amax_m = 0.0f, vmax = 0.0f;
       uint32_t pout[8];
-      float pout_f[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const bool ok = e < nv;
         float gi = g[e];
         // v = v*beta2 + c_v*g*g   (mul_ then addcmul_, AdamW_adv.py:417, Prodigy_adv.py:469)
-        float vi = __fmul_rn(vh[e], L.beta2);
+        float vi = __fmul_rn(vh[e], beta2);
         if (vbf) vi = round_bf16(vi);
-        vi = __fmaf_rn(__fmul_rn(L.c_v, gi), gi, vi);
+        vi = __fmaf_rn(__fmul_rn(c_v, gi), gi, vi);
         if (vbf) vi = round_bf16(vi);
         if (fact) vi = fabsf(vi);       // _factorize_state's abs_ (factorization_util.py:35)
         v[e] = ok ? vi : 0.0f;
@@ -307,11 +458,11 @@ __global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_lau
         float den = __fsqrt_rn(vi);
         if (vbf) den = round_bf16(den);
         if (ALGO != ADVOPT_ALGO_PRODIGY) {
-          den = __fdiv_rn(den, T.sqrt_bc2);
+          den = div_rcp(den, sbc2, rcp_sbc2);   // den >= 2^-75 or 0: always in div_rcp's exact range
           if (vbf) den = round_bf16(den);
         }
         if (!atan2m) {
-          den = __fadd_rn(den, T.eps);   // Prodigy: T.eps holds d*eps
+          den = __fadd_rn(den, eps);   // Prodigy: eps holds d*eps
           if (vbf) den = round_bf16(den);
         }
         const float du = kMBF ? round_bf16(den) : den;   // denom.to(update.dtype)
@@ -321,18 +472,18 @@ __global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_lau
         if (has_m) {
           float mi;
           if (ALGO == ADVOPT_ALGO_PRODIGY) {
-            mi = Rm(__fmaf_rn(gi, L.c_m, Rm(__fmul_rn(m[e], L.beta1))));
+            mi = Rm(__fmaf_rn(gi, c_m, Rm(__fmul_rn(m[e], beta1))));
           } else {
-            mi = Rm(lerp_t(m[e], gi, L.w_m));
+            mi = Rm(lerp_t(m[e], gi, w_m));
           }
           m_new[e] = ok ? mi : 0.0f;
-          ui = nest ? Rm(lerp_t(mi, gi, L.w_nest)) : mi;
+          ui = nest ? Rm(lerp_t(mi, gi, w_nest)) : mi;
         } else {
           m_new[e] = 0.0f;
           ui = (ALGO == ADVOPT_ALGO_PRODIGY) ? Rm(__fmul_rn(gi, L.d)) : gi;
         }
         if (!normed) ui = atan2m ? Rm(atan2f(ui, du)) : Rm(__fdiv_rn(ui, du));
-        ui = Rm(__fmul_rn(ui, T.step_size));
+        ui = Rm(__fmul_rn(ui, step_size));
         amax_m = fmaxf(amax_m, fabsf(m_new[e]));
         vmax = fmaxf(vmax, v[e]);
 
@@ -374,18 +525,46 @@ __global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_lau
         // parameter update (param_update.py:77-156)
         const float anc = (has_anchor && ok) ? anchor_value(T, k0 + e, PBF) : 0.0f;
         if (PBF && !sr) {
-          const float pcv = weight_decay<true>(p[e], ui, T.wd, T.cwd, cautious, has_anchor, anc, fisher, ws);
+          const float pcv = weight_decay<true>(p[e], ui, wd, cwd, cautious, has_anchor, anc, fisher, ws);
           pout[e] = f_to_bf16_rne(__fadd_rn(pcv, -ui));
         } else {
-          const float pcv = weight_decay<false>(p[e], ui, T.wd, T.cwd, cautious, has_anchor, anc, fisher, ws);
+          const float pcv = weight_decay<false>(p[e], ui, wd, cwd, cautious, has_anchor, anc, fisher, ws);
           const float pn = __fadd_rn(pcv, -ui);
-          if (PBF) pout[e] = f_to_bf16_sr(pn, rp[e]);
-          else pout_f[e] = pn;
+          // bf16 + SR: add the noise to the bit pattern; the pack below keeps the high half
+          pout[e] = PBF ? (__float_as_uint(pn) + noise_at(nzp, e)) : __float_as_uint(pn);
         }
       }
       if (!fstats) {
-        if (PBF) store8_bf16(T.param, k0, nv, v8, pout);
-        else store8_f32(T.param, k0, nv, v8, pout_f);
+        if (PBF) {
+          Words<2> o;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o.w[i] = sr ? __byte_perm(pout[2 * i], pout[2 * i + 1], 0x7632) : (pout[2 * i] | (pout[2 * i + 1] << 16));
+          uint16_t* dst = static_cast<uint16_t*>(T.param) + k0;
+          if (v8) {
+            *reinterpret_cast<uint4*>(dst) = make_uint4(o.w[0], o.w[1], o.w[2], o.w[3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (e < nv) dst[e] = (uint16_t)(o.w[e >> 1] >> (16 * (e & 1)));
+          }
+        } else {
+          float* dst = static_cast<float*>(T.param) + k0;
+          if (v8) {
+            reinterpret_cast<uint4*>(dst)[0] = make_uint4(pout[0], pout[1], pout[2], pout[3]);
+            reinterpret_cast<uint4*>(dst)[1] = make_uint4(pout[4], pout[5], pout[6], pout[7]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (e < nv) dst[e] = __uint_as_float(pout[e]);
+          }
+        }
+      }
+      // noise for the quantised / SR'd states, drawn before the barrier
+      U4 nzm{0u, 0u, 0u, 0u}, nzv{0u, 0u, 0u, 0u};
+      if (!fstats && TR::kStore != 0 && (kStore == 2 || TR::kSRStates)) {
+        if (has_m) nzm = noise_words<NOISE_IN>(L, T, T.nz_m, kNoiseM, k0, nv);
+        if (!fact) nzv = noise_words<NOISE_IN>(L, T, T.nz_v, kNoiseV, k0, nv);
       }
 
       // ---- factored second moment: row sums and column partials ----
@@ -395,14 +574,16 @@ __global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_lau
           const int64_t cc = c0 + tid * kVec;
           const bool second = cc >= d2;
           const int64_t col = second ? cc - d2 : cc;
-          float s = 0.0f;
           if (nv > 0) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              s = __fadd_rn(s, v[e]);
-              colacc[col + e] = __fadd_rn(colacc[col + e], v[e]);
-            }
+            float4* ca = reinterpret_cast<float4*>(colacc + col);
+            float4 a = ca[0], b = ca[1];
+            a.x = __fadd_rn(a.x, v[0]); a.y = __fadd_rn(a.y, v[1]); a.z = __fadd_rn(a.z, v[2]); a.w = __fadd_rn(a.w, v[3]);
+            b.x = __fadd_rn(b.x, v[4]); b.y = __fadd_rn(b.y, v[5]); b.z = __fadd_rn(b.z, v[6]); b.w = __fadd_rn(b.w, v[7]);
+            ca[0] = a;
+            ca[1] = b;
           }
+          const float s = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])),
+                                    __fadd_rn(__fadd_rn(v[4], v[5]), __fadd_rn(v[6], v[7])));
           if (second) rsum1 = s; else rsum0 = s;
         } else {
 #pragma unroll
@@ -413,7 +594,10 @@ __global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_lau
 
       // ---- block reductions (one barrier per chunk) ----
       {
-        const float a = warp_max(amax_m), b = warp_max(vmax), c = warp_sum(rsum0), d = warp_sum(rsum1);
+        const float a = (has_m && kStore == 2) ? warp_max(amax_m) : 0.0f;
+        const float b = (!fact && kStore == 2) ? warp_max(vmax) : 0.0f;
+        const float c = ffast ? warp_sum(rsum0) : 0.0f;
+        const float d = ffast ? warp_sum(rsum1) : 0.0f;
         if (lane == 0) {
           red[parity][warp][0] = a;
           red[parity][warp][1] = b;
@@ -480,25 +664,20 @@ __global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_lau
             float bmax = 0.0f;
 #pragma unroll
             for (int w = 0; w < kWarps; ++w) bmax = fmaxf(bmax, red[parity][w][0]);
-            const float scale = __fdiv_rn(bmax, 127.0f);
-            const float safe = scale < 1e-12f ? 1e-12f : scale;
-            uint32_t r[8], c[8];
-            noise8(L, T, T.nz_m, kNoiseM, k0, nv, r);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) c[e] = quant_code(m_new[e], safe, r[e], false);
-            store8_q(T.m, k0, nv, v8, c);
-            if (tid == 0) T.m_scale[blk] = scale;
-          } else if (kStore == 1) {
-            uint32_t b[8];
-            if (TR::kSRStates) {
-              uint32_t r[8];
-              noise8(L, T, T.nz_m, kNoiseM, k0, nv, r);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) b[e] = f_to_bf16_sr(m_new[e], r[e]);
+            const uint2 q = quantize8<true>(m_new, bmax, nzm);
+            uint8_t* dst = static_cast<uint8_t*>(T.m) + k0;
+            if (v8) {
+              *reinterpret_cast<uint2*>(dst) = q;
             } else {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) b[e] = f_to_bf16_rne(m_new[e]);
+              for (int e = 0; e < 8; ++e)
+                if (e < nv) dst[e] = (uint8_t)((e < 4 ? q.x : q.y) >> (8 * (e & 3)));
             }
+            if (tid == 0) T.m_scale[blk] = __fdiv_rn(bmax, 127.0f);
+          } else if (kStore == 1) {
+            uint32_t b[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) b[e] = TR::kSRStates ? f_to_bf16_sr(m_new[e], noise_at(nzm, e)) : f_to_bf16_rne(m_new[e]);
             store8_bf16(T.m, k0, nv, v8, b);
           } else {
             store8_f32(T.m, k0, nv, v8, m_new);
@@ -509,42 +688,30 @@ __global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_lau
             float bmax = 0.0f;
 #pragma unroll
             for (int w = 0; w < kWarps; ++w) bmax = fmaxf(bmax, red[parity][w][1]);
-            const float scale = __fdiv_rn(bmax, 255.0f);
-            const float safe = scale < 1e-12f ? 1e-12f : scale;
-            uint32_t r[8], c[8];
-            noise8(L, T, T.nz_v, kNoiseV, k0, nv, r);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) c[e] = quant_code(v[e], safe, r[e], true);
-            store8_q(T.v, k0, nv, v8, c);
-            if (tid == 0) T.v_scale[blk] = scale;
-          } else if (kStore == 1) {
-            uint32_t b[8];
-            if (TR::kSRStates) {
-              uint32_t r[8];
-              noise8(L, T, T.nz_v, kNoiseV, k0, nv, r);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) b[e] = f_to_bf16_sr(v[e], r[e]);
+            const uint2 q = quantize8<false>(v, bmax, nzv);
+            uint8_t* dst = static_cast<uint8_t*>(T.v) + k0;
+            if (v8) {
+              *reinterpret_cast<uint2*>(dst) = q;
             } else {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) b[e] = f_to_bf16_rne(v[e]);
+              for (int e = 0; e < 8; ++e)
+                if (e < nv) dst[e] = (uint8_t)((e < 4 ? q.x : q.y) >> (8 * (e & 3)));
             }
+            if (tid == 0) T.v_scale[blk] = __fdiv_rn(bmax, 255.0f);
+          } else if (kStore == 1) {
+            uint32_t b[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) b[e] = TR::kSRStates ? f_to_bf16_sr(v[e], noise_at(nzv, e)) : f_to_bf16_rne(v[e]);
             store8_bf16(T.v, k0, nv, v8, b);
           } else {
             store8_f32(T.v, k0, nv, v8, v);
           }
         }
       }
-
-      // advance the factored row/column position by one chunk
-      if (fact) {
-        c0 += clen;
-        if (c0 >= d2) {
-          const int64_t dr = c0 / d2;
-          r0 += dr;
-          c0 -= dr * d2;
-        }
-      }
       parity ^= 1;
+      if (!has_next) break;
+      cp = np;
+      cur = nxt;
     }
 
     // ---- end of piece: flush column partials and statistics ----
@@ -575,114 +742,14 @@ __global__ void __launch_bounds__(kThreads, 3) adam_kernel(const advopt_adam_lau
   }
 }
 
-
-// ---------------------------------------------------------------------------
-// factored_2nd finish: column sums from the partials, then normalise one
-// factor (factorization_util.py:60-80).  Kernel A sums partial rows in slot
-// order (float64) into mv; kernel B normalises mu (d1 < d2) or mv by its total.
-// ---------------------------------------------------------------------------
-__global__ void factored_cols_kernel(const advopt_adam_tensor* tensors, const int32_t* index) {
-  const advopt_adam_tensor* t = tensors + index[blockIdx.y];
-  const int64_t d2 = t->d2;
-  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= d2) return;
-  double acc = 0.0;
-  const float* src = t->col_partial + j;
-  for (int s = 0; s < t->n_slots; ++s) acc += (double)src[(int64_t)s * d2];
-  t->col_factor[j] = (float)acc;
-}
-
-__global__ void factored_norm_kernel(const advopt_adam_tensor* tensors, const int32_t* index) {
-  const advopt_adam_tensor* t = tensors + index[blockIdx.x];
-  const int64_t d1 = t->d1, d2 = t->d2;
-  float* vec = d1 < d2 ? t->row_factor : t->col_factor;
-  const int64_t n = d1 < d2 ? d1 : d2;
-  __shared__ double part[32];
-  double acc = 0.0;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) acc += (double)vec[i];
-  acc = warp_sum_d(acc);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
-  __syncthreads();
-  __shared__ float scale_s;
-  if (threadIdx.x == 0) {
-    double tot = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += part[w];
-    float sc = (float)tot;
-    scale_s = sc < 1e-12f ? 1e-12f : sc;     // scale.clamp_min_(1e-12)
-  }
-  __syncthreads();
-  const float sc = scale_s;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) vec[i] = __fdiv_rn(vec[i], sc);
-}
-
-// Prodigy: per-tensor sums of the piece statistics, folded in param order.
-__global__ void prodigy_finish_kernel(const advopt_adam_launch L, float* sums, float coef, int s_is_bf16) {
-  __shared__ double dot_s[256], abs_s[256];
-  float num = sums[0], den = sums[1];
-  // pieces of tensor t are found by scanning all pieces (launch sizes are small)
-  for (int t = 0; t < L.n_tensors; ++t) {
-    double a = 0.0, b = 0.0;
-    for (int i = threadIdx.x; i < L.n_pieces; i += blockDim.x) {
-      if (L.pieces[i].tensor == t) {
-        a += L.piece_stats[2 * i];
-        b += L.piece_stats[2 * i + 1];
-      }
-    }
-    dot_s[threadIdx.x] = a;
-    abs_s[threadIdx.x] = b;
-    __syncthreads();
-    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
-      if ((int)threadIdx.x < o) {
-        dot_s[threadIdx.x] += dot_s[threadIdx.x + o];
-        abs_s[threadIdx.x] += abs_s[threadIdx.x + o];
-      }
-      __syncthreads();
-    }
-    if (threadIdx.x == 0) {
-      const float dot = (float)dot_s[0];
-      num = __fadd_rn(num, __fmul_rn(coef, dot));              // d_numerator.add_((d/d0)*dlr*dot)
-      float sabs = (float)abs_s[0];
-      if (s_is_bf16) sabs = round_bf16(sabs);                 // s.abs().sum() is bf16 for bf16 s
-      den = __fadd_rn(den, sabs);
-    }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    sums[0] = num;
-    sums[1] = den;
-  }
-}
-
-// Fisher: rms of p*ws per tensor -> 1/max(1, rms) stored as fisher_clip (the
-// divisor clip_coef itself; update_util.py:26-36).
-__global__ void fisher_finish_kernel(const advopt_adam_launch L, advopt_adam_tensor* tensors_rw) {
-  const int t = blockIdx.x;
-  __shared__ double part[256];
-  double a = 0.0;
-  for (int i = threadIdx.x; i < L.n_pieces; i += blockDim.x)
-    if (L.pieces[i].tensor == t) a += L.piece_stats[2 * i];
-  part[threadIdx.x] = a;
-  __syncthreads();
-  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
-    if ((int)threadIdx.x < o) part[threadIdx.x] += part[threadIdx.x + o];
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    const double n = (double)tensors_rw[t].numel;
-    const float mean = (float)(part[0] / n);
-    const float rms = __fsqrt_rn(mean);
-    tensors_rw[t].fisher_clip = rms > 1.0f ? rms : 1.0f;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// host side
-// ---------------------------------------------------------------------------
+// Host launchers, instantiated per precision in adam_<precision>.cu.
 template <int PREC, bool PBF, int ALGO>
-static cudaError_t launch_one(const advopt_adam_launch& L, cudaStream_t s) {
+cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
   const bool ext = L.flags & (ADVOPT_F_ATAN2 | ADVOPT_F_NORMED | ADVOPT_F_FISHER | ADVOPT_F_FISHER_STATS |
                               ADVOPT_F_ANCHORS);
-  auto k = ext ? adam_kernel<PREC, PBF, ALGO, true> : adam_kernel<PREC, PBF, ALGO, false>;
+  const bool nin = L.flags & ADVOPT_F_NOISE_IN;
+  auto k = ext ? (nin ? adam_kernel<PREC, PBF, ALGO, true, true> : adam_kernel<PREC, PBF, ALGO, true, false>)
+               : (nin ? adam_kernel<PREC, PBF, ALGO, false, true> : adam_kernel<PREC, PBF, ALGO, false, false>);
   const size_t smem = (size_t)L.smem_floats * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -691,118 +758,48 @@ static cudaError_t launch_one(const advopt_adam_launch& L, cudaStream_t s) {
 }
 
 template <int PREC, bool PBF, int ALGO>
-static cudaError_t occupancy_one(int smem_floats, int* ctas) {
-  auto k = adam_kernel<PREC, PBF, ALGO, false>;
+cudaError_t occupancy_adam_algo(int smem_floats, int* ctas) {
+  auto k = adam_kernel<PREC, PBF, ALGO, false, false>;
   const size_t smem = (size_t)smem_floats * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas, k, kThreads, smem);
 }
 
-#define ADVOPT_DISPATCH(FN, PREC, PBF, ALGO, ...)                                                  \
-  [&]() -> cudaError_t {                                                                           \
-    switch (ALGO) {                                                                                \
-      case ADVOPT_ALGO_ADAMW: return FN<PREC, PBF, ADVOPT_ALGO_ADAMW>(__VA_ARGS__);                \
-      case ADVOPT_ALGO_AUXADAM: return FN<PREC, PBF, ADVOPT_ALGO_AUXADAM>(__VA_ARGS__);            \
-      default: return FN<PREC, PBF, ADVOPT_ALGO_PRODIGY>(__VA_ARGS__);                             \
-    }                                                                                              \
-  }()
-
-template <class Fn>
-static cudaError_t dispatch(int prec, int pdt, Fn&& fn) {
-  return fn(prec, pdt);
-}
-
-static cudaError_t run_adam(const advopt_adam_launch& L, cudaStream_t s) {
+template <int PREC>
+cudaError_t launch_adam_prec(const advopt_adam_launch& L, cudaStream_t s) {
   const bool pbf = L.param_dtype == ADVOPT_DT_BF16;
-  switch (L.precision) {
-    case ADVOPT_PREC_FP32:
-      return pbf ? ADVOPT_DISPATCH(launch_one, ADVOPT_PREC_FP32, true, L.algo, L, s)
-                 : ADVOPT_DISPATCH(launch_one, ADVOPT_PREC_FP32, false, L.algo, L, s);
-    case ADVOPT_PREC_BF16_SR:
-      return pbf ? ADVOPT_DISPATCH(launch_one, ADVOPT_PREC_BF16_SR, true, L.algo, L, s)
-                 : ADVOPT_DISPATCH(launch_one, ADVOPT_PREC_BF16_SR, false, L.algo, L, s);
-    case ADVOPT_PREC_INT8_SR:
-      return pbf ? ADVOPT_DISPATCH(launch_one, ADVOPT_PREC_INT8_SR, true, L.algo, L, s)
-                 : ADVOPT_DISPATCH(launch_one, ADVOPT_PREC_INT8_SR, false, L.algo, L, s);
-    default:  // AUTO: f32 params are exactly the FP32 path
-      return pbf ? ADVOPT_DISPATCH(launch_one, ADVOPT_PREC_AUTO, true, L.algo, L, s)
-                 : ADVOPT_DISPATCH(launch_one, ADVOPT_PREC_FP32, false, L.algo, L, s);
+  switch (L.algo) {
+    case ADVOPT_ALGO_ADAMW:
+      return pbf ? launch_adam_algo<PREC, true, ADVOPT_ALGO_ADAMW>(L, s) : launch_adam_algo<PREC, false, ADVOPT_ALGO_ADAMW>(L, s);
+    case ADVOPT_ALGO_AUXADAM:
+      return pbf ? launch_adam_algo<PREC, true, ADVOPT_ALGO_AUXADAM>(L, s) : launch_adam_algo<PREC, false, ADVOPT_ALGO_AUXADAM>(L, s);
+    default:
+      return pbf ? launch_adam_algo<PREC, true, ADVOPT_ALGO_PRODIGY>(L, s) : launch_adam_algo<PREC, false, ADVOPT_ALGO_PRODIGY>(L, s);
   }
 }
 
-static cudaError_t run_occupancy(int prec, int pdt, int algo, int smem_floats, int* ctas) {
+template <int PREC>
+cudaError_t occupancy_adam_prec(int pdt, int algo, int smem_floats, int* ctas) {
   const bool pbf = pdt == ADVOPT_DT_BF16;
-  switch (prec) {
-    case ADVOPT_PREC_FP32:
-      return pbf ? ADVOPT_DISPATCH(occupancy_one, ADVOPT_PREC_FP32, true, algo, smem_floats, ctas)
-                 : ADVOPT_DISPATCH(occupancy_one, ADVOPT_PREC_FP32, false, algo, smem_floats, ctas);
-    case ADVOPT_PREC_BF16_SR:
-      return pbf ? ADVOPT_DISPATCH(occupancy_one, ADVOPT_PREC_BF16_SR, true, algo, smem_floats, ctas)
-                 : ADVOPT_DISPATCH(occupancy_one, ADVOPT_PREC_BF16_SR, false, algo, smem_floats, ctas);
-    case ADVOPT_PREC_INT8_SR:
-      return pbf ? ADVOPT_DISPATCH(occupancy_one, ADVOPT_PREC_INT8_SR, true, algo, smem_floats, ctas)
-                 : ADVOPT_DISPATCH(occupancy_one, ADVOPT_PREC_INT8_SR, false, algo, smem_floats, ctas);
+  switch (algo) {
+    case ADVOPT_ALGO_ADAMW:
+      return pbf ? occupancy_adam_algo<PREC, true, ADVOPT_ALGO_ADAMW>(smem_floats, ctas) : occupancy_adam_algo<PREC, false, ADVOPT_ALGO_ADAMW>(smem_floats, ctas);
+    case ADVOPT_ALGO_AUXADAM:
+      return pbf ? occupancy_adam_algo<PREC, true, ADVOPT_ALGO_AUXADAM>(smem_floats, ctas) : occupancy_adam_algo<PREC, false, ADVOPT_ALGO_AUXADAM>(smem_floats, ctas);
     default:
-      return pbf ? ADVOPT_DISPATCH(occupancy_one, ADVOPT_PREC_AUTO, true, algo, smem_floats, ctas)
-                 : ADVOPT_DISPATCH(occupancy_one, ADVOPT_PREC_FP32, false, algo, smem_floats, ctas);
+      return pbf ? occupancy_adam_algo<PREC, true, ADVOPT_ALGO_PRODIGY>(smem_floats, ctas) : occupancy_adam_algo<PREC, false, ADVOPT_ALGO_PRODIGY>(smem_floats, ctas);
   }
 }
+
+// declared here, defined (instantiated) in adam_fp32.cu, adam_bf16sr.cu, adam_int8.cu, adam_auto.cu
+cudaError_t launch_adam_fp32(const advopt_adam_launch& L, cudaStream_t s);
+cudaError_t launch_adam_bf16sr(const advopt_adam_launch& L, cudaStream_t s);
+cudaError_t launch_adam_int8(const advopt_adam_launch& L, cudaStream_t s);
+cudaError_t launch_adam_auto(const advopt_adam_launch& L, cudaStream_t s);
+cudaError_t occupancy_adam_fp32(int pdt, int algo, int smem_floats, int* ctas);
+cudaError_t occupancy_adam_bf16sr(int pdt, int algo, int smem_floats, int* ctas);
+cudaError_t occupancy_adam_int8(int pdt, int algo, int smem_floats, int* ctas);
+cudaError_t occupancy_adam_auto(int pdt, int algo, int smem_floats, int* ctas);
 
 }  // namespace advopt
-
-using namespace advopt;
-
-extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
-  if (!L || !L->tensors || !L->pieces || !L->cta_offsets || L->grid <= 0)
-    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: null table or empty grid");
-  if (L->precision < 0 || L->precision > 3 || L->algo < 0 || L->algo > 2 || L->param_dtype < 0 || L->param_dtype > 1)
-    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: bad precision/algo/dtype code");
-  if ((L->flags & (ADVOPT_F_PRODIGY_STATS | ADVOPT_F_FISHER_STATS)) && !L->piece_stats)
-    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: statistics requested without piece_stats");
-  if (L->smem_floats < 0 || L->smem_floats > 49152)
-    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: factored d2 above 49152 columns is not supported");
-  return check_cuda(run_adam(*L, static_cast<cudaStream_t>(stream)), "advopt_adam_step");
-}
-
-extern "C" int advopt_factored_finish(const advopt_adam_launch* L, const int32_t* index, int32_t n_factored,
-                                      int32_t max_d2, void* stream) {
-  if (!L || (n_factored > 0 && !index)) return set_error(ADVOPT_E_INVALID, "advopt_factored_finish: null argument");
-  if (n_factored <= 0) return ADVOPT_OK;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  dim3 ga((unsigned)((max_d2 + 255) / 256), (unsigned)n_factored);
-  factored_cols_kernel<<<ga, 256, 0, s>>>(L->tensors, index);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return check_cuda(e, "advopt_factored_finish");
-  factored_norm_kernel<<<n_factored, 1024, 0, s>>>(L->tensors, index);
-  return check_cuda(cudaGetLastError(), "advopt_factored_finish");
-}
-
-extern "C" int advopt_prodigy_finish(const advopt_adam_launch* L, float* sums, float coef, int32_t s_is_bf16,
-                                     void* stream) {
-  if (!L || !sums || !L->piece_stats) return set_error(ADVOPT_E_INVALID, "advopt_prodigy_finish: null argument");
-  prodigy_finish_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(*L, sums, coef, s_is_bf16);
-  return check_cuda(cudaGetLastError(), "advopt_prodigy_finish");
-}
-
-extern "C" int advopt_fisher_finish(const advopt_adam_launch* L, advopt_adam_tensor* tensors_rw, void* stream) {
-  if (!L || !tensors_rw || !L->piece_stats) return set_error(ADVOPT_E_INVALID, "advopt_fisher_finish: null argument");
-  fisher_finish_kernel<<<L->n_tensors, 256, 0, static_cast<cudaStream_t>(stream)>>>(*L, tensors_rw);
-  return check_cuda(cudaGetLastError(), "advopt_fisher_finish");
-}
-
-extern "C" int advopt_adam_occupancy(int32_t precision, int32_t param_dtype, int32_t algo, int32_t smem_floats,
-                                     int32_t* sm_count, int32_t* ctas_per_sm) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return check_cuda(e, "advopt_adam_occupancy");
-  int sms = 0;
-  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) return check_cuda(e, "advopt_adam_occupancy");
-  int ctas = 0;
-  e = run_occupancy(precision, param_dtype, algo, smem_floats, &ctas);
-  if (e != cudaSuccess) return check_cuda(e, "advopt_adam_occupancy");
-  if (sm_count) *sm_count = sms;
-  if (ctas_per_sm) *ctas_per_sm = ctas;
-  return ADVOPT_OK;
-}

@@ -57,9 +57,10 @@ struct U4 {
 __device__ __forceinline__ U4 philox4x32_10(U4 c, uint32_t k0, uint32_t k1) {
 #pragma unroll
   for (int i = 0; i < 10; ++i) {
-    const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
-    const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
-    c = U4{hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0};
+    // one 32x32->64 multiply per lane word (hi and lo from a single wide product)
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c.x;
+    const uint64_t p1 = (uint64_t)0xCD9E8D57u * c.z;
+    c = U4{(uint32_t)(p1 >> 32) ^ c.y ^ k0, (uint32_t)p1, (uint32_t)(p0 >> 32) ^ c.w ^ k1, (uint32_t)p0};
     k0 += 0x9E3779B9u;
     k1 += 0xBB67AE85u;
   }
@@ -221,6 +222,57 @@ __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+}  // namespace advopt
+
+namespace advopt {
+
+// RN(x / d) from r = RN(1/d): q0 = x*r, then two residual corrections
+// q <- q + r*(x - q*d) (Markstein, "Computation of elementary functions on
+// the IBM RISC System/6000 processor", IBM J. Res. Dev. 34, 1990).  After
+// the first correction q is faithful; the second then yields the correctly
+// rounded quotient, provided the residuals stay normal.  Callers use it only
+// for |x| >= 2^-100 with a normal divisor and fall back to __fdiv_rn below.
+__device__ __forceinline__ float div_rcp(float x, float d, float r) {
+  float q = __fmul_rn(x, r);
+  float e = __fmaf_rn(-q, d, x);
+  q = __fmaf_rn(e, r, q);
+  e = __fmaf_rn(-q, d, x);
+  return __fmaf_rn(e, r, q);
+}
+__device__ __forceinline__ float div_const(float x, float d, float r) {
+  return fabsf(x) >= 0x1p-100f ? div_rcp(x, d, r) : __fdiv_rn(x, d);
+}
+
+// r16 * 2^-16 exactly, without the conversion pipe: 1 + r*2^-16 built from
+// bits, minus 1 (exact by Sterbenz).
+__device__ __forceinline__ float noise_unit(uint32_t r16) {
+  return __fsub_rn(__uint_as_float(0x3F800000u | (r16 << 7)), 1.0f);
+}
+
+// floor(y) as an int for |y| < 2^22: y + 1.5*2^23 rounded toward -inf lands on
+// the integer grid of that binade, so its low bits are 2^22 + floor(y).
+__device__ __forceinline__ int floor_int(float y) {
+  return (int)(__float_as_uint(__fadd_rd(y, 12582912.0f)) - 0x4B400000u);
+}
+
+// Four int8 (SIGNED) or uint8 codes of w as exact floats, via 2^23 + byte.
+template <bool SIGNED>
+__device__ __forceinline__ void codes4_to_f(uint32_t w, float* out) {
+  const uint32_t x = SIGNED ? (w ^ 0x80808080u) : w;
+  const float bias = SIGNED ? 8388736.0f : 8388608.0f;  // 2^23 + 128 | 2^23
+  out[0] = __fsub_rn(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7440)), bias);
+  out[1] = __fsub_rn(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7441)), bias);
+  out[2] = __fsub_rn(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7442)), bias);
+  out[3] = __fsub_rn(__uint_as_float(__byte_perm(x, 0x4B000000u, 0x7443)), bias);
+}
+
+// Pack the low bytes of four ints.
+__device__ __forceinline__ uint32_t pack4_bytes(int c0, int c1, int c2, int c3) {
+  const uint32_t lo = __byte_perm((uint32_t)c0, (uint32_t)c1, 0x0040);
+  const uint32_t hi = __byte_perm((uint32_t)c2, (uint32_t)c3, 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
 }
 
 }  // namespace advopt
