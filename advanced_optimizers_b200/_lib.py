@@ -60,14 +60,14 @@ LION_TENSOR_DT = np.dtype([
 class AdamLaunch(ctypes.Structure):
     _fields_ = [
         ("tensors", ctypes.c_uint64), ("pieces", ctypes.c_uint64), ("cta_offsets", ctypes.c_uint64),
-        ("piece_stats", ctypes.c_uint64),
+        ("piece_stats", ctypes.c_uint64), ("err", ctypes.c_uint64),
         ("n_tensors", ctypes.c_int32), ("n_pieces", ctypes.c_int32), ("grid", ctypes.c_int32),
         ("smem_floats", ctypes.c_int32), ("gen_offset", ctypes.c_int32), ("algo", ctypes.c_int32),
         ("precision", ctypes.c_int32), ("param_dtype", ctypes.c_int32), ("flags", ctypes.c_uint32),
         ("beta1", ctypes.c_float), ("beta2", ctypes.c_float), ("w_m", ctypes.c_float),
         ("w_nest", ctypes.c_float), ("c_v", ctypes.c_float), ("c_m", ctypes.c_float),
         ("d_eps", ctypes.c_float), ("beta3", ctypes.c_float), ("s_alpha", ctypes.c_float),
-        ("d", ctypes.c_float), ("pad0", ctypes.c_float), ("seed", ctypes.c_uint64),
+        ("d", ctypes.c_float), ("stages", ctypes.c_int32), ("seed", ctypes.c_uint64),
     ]
 
 
@@ -101,7 +101,8 @@ def lib():
             "advopt_sizeof": ([ctypes.c_int], ctypes.c_size_t),
             "advopt_abi_version": ([], ctypes.c_int),
             "advopt_last_error": ([], ctypes.c_char_p),
-            "advopt_adam_occupancy": ([I32, I32, I32, I32, ctypes.POINTER(I32), ctypes.POINTER(I32)], ctypes.c_int),
+            "advopt_adam_occupancy": ([I32, I32, I32, I32, I32, ctypes.POINTER(I32), ctypes.POINTER(I32)],
+                                      ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -134,11 +135,11 @@ def exported_symbols():
 _OCC_CACHE = {}
 
 
-def adam_occupancy(precision: int, param_dtype: int, algo: int, smem_floats: int):
-    key = (precision, param_dtype, algo, smem_floats)
+def adam_occupancy(precision: int, param_dtype: int, algo: int, smem_floats: int, fast: bool = False):
+    key = (precision, param_dtype, algo, smem_floats, bool(fast))
     if key not in _OCC_CACHE:
         sms, ctas = ctypes.c_int32(0), ctypes.c_int32(0)
-        check(lib().advopt_adam_occupancy(precision, param_dtype, algo, smem_floats,
+        check(lib().advopt_adam_occupancy(precision, param_dtype, algo, smem_floats, 1 if fast else 0,
                                           ctypes.byref(sms), ctypes.byref(ctas)), "advopt_adam_occupancy")
         _OCC_CACHE[key] = (sms.value, max(1, ctas.value))
     return _OCC_CACHE[key]

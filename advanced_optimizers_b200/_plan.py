@@ -44,51 +44,68 @@ def unit_of(numel: int, d2: int) -> int:
 def plan(numels, d2s, grid: int):
     """numels[i], d2s[i] (0 = not factored) -> (pieces, cta_offsets, n_slots).
 
-    The last CTA takes whatever remains, so len(cta_offsets) == grid + 1 and
-    every CTA index in [0, grid) is valid (some may own no piece)."""
-    total = int(sum(int(n) for n in numels))
+    All tensors are laid end to end; CTA c owns the elements between global
+    cut points c and c+1, where cut point c is c*total/grid rounded to the
+    nearest position a piece may start at (a multiple of the tensor's unit, or
+    a tensor boundary).  Rounding errors therefore never accumulate: every CTA
+    holds its share to within one unit.  len(cta_offsets) == grid + 1."""
     grid = max(1, int(grid))
-    target = max(CHUNK, -(-total // grid))
+    starts = []
+    total = 0
+    for n in numels:
+        starts.append(total)
+        total += max(0, int(n))
+    units = [unit_of(int(n), int(d2)) for n, d2 in zip(numels, d2s)]
+
+    def snap(x):
+        """nearest allowed cut position to global element x"""
+        if x <= 0:
+            return 0
+        if x >= total:
+            return total
+        # tensor containing x
+        lo, hi = 0, len(starts) - 1
+        while lo < hi:
+            mid = (lo + hi + 1) // 2
+            if starts[mid] <= x:
+                lo = mid
+            else:
+                hi = mid - 1
+        t = lo
+        while t < len(numels) and int(numels[t]) <= 0:
+            t += 1
+        s0, n, u = starts[t], int(numels[t]), units[t]
+        off = x - s0
+        down = (off // u) * u
+        up = min(n, down + u)
+        return s0 + (down if off - down <= up - off else up)
+
+    cuts = [0]
+    for c in range(1, grid):
+        cuts.append(max(cuts[-1], snap((c * total) // grid)))
+    cuts.append(total)
+
     pieces = []
     offsets = [0]
     n_slots = [0] * len(numels)
-    budget = target
-    cta = 0
-
-    def close():
-        nonlocal budget, cta
+    t = 0
+    for c in range(grid):
+        a, b = cuts[c], cuts[c + 1]
+        while a < b:
+            while t < len(numels) and starts[t] + int(numels[t]) <= a:
+                t += 1
+            s0, n, d2, u = starts[t], int(numels[t]), int(d2s[t]), units[t]
+            end = min(b, s0 + n)
+            pos = a - s0
+            stop = end - s0
+            cap = max(u, (MAX_ROWS * d2 // u) * u) if d2 > 0 else stop - pos
+            while pos < stop:
+                take = min(stop - pos, cap)
+                pieces.append((pos, pos + take, t, n_slots[t]))
+                n_slots[t] += 1
+                pos += take
+            a = end
         offsets.append(len(pieces))
-        cta += 1
-        budget = target
-
-    for t, (n, d2) in enumerate(zip(numels, d2s)):
-        n, d2 = int(n), int(d2)
-        if n <= 0:
-            continue
-        unit = unit_of(n, d2)
-        cap = max(unit, (MAX_ROWS * d2 // unit) * unit) if d2 > 0 else 1 << 62
-        pos = 0
-        while pos < n:
-            take = min(n - pos, cap)
-            last_cta = cta >= grid - 1
-            if not last_cta and take > budget:
-                fit = (budget // unit) * unit
-                if fit == 0:
-                    if offsets[-1] != len(pieces):       # CTA already has work: next CTA
-                        close()
-                        continue
-                    fit = unit
-                take = min(take, fit)
-            pieces.append((pos, pos + take, t, n_slots[t]))
-            n_slots[t] += 1
-            pos += take
-            budget -= take
-            if not last_cta and budget < CHUNK:
-                close()
-    while len(offsets) < grid + 1:
-        offsets.append(len(pieces))
-    offsets = offsets[: grid + 1]
-    offsets[-1] = len(pieces)
     arr = np.zeros(len(pieces), PIECE_DT)
     if pieces:
         p = np.array(pieces, dtype=np.int64)

@@ -114,13 +114,13 @@ static cudaError_t run_adam(const advopt_adam_launch& L, cudaStream_t s) {
   }
 }
 
-static cudaError_t run_occupancy(int prec, int pdt, int algo, int smem_floats, int* ctas) {
+static cudaError_t run_occupancy(int prec, int pdt, int algo, int smem_floats, int* ctas, int fast) {
   switch (prec) {
-    case ADVOPT_PREC_FP32: return occupancy_adam_fp32(pdt, algo, smem_floats, ctas);
-    case ADVOPT_PREC_BF16_SR: return occupancy_adam_bf16sr(pdt, algo, smem_floats, ctas);
-    case ADVOPT_PREC_INT8_SR: return occupancy_adam_int8(pdt, algo, smem_floats, ctas);
-    default: return pdt == ADVOPT_DT_BF16 ? occupancy_adam_auto(pdt, algo, smem_floats, ctas)
-                                          : occupancy_adam_fp32(pdt, algo, smem_floats, ctas);
+    case ADVOPT_PREC_FP32: return occupancy_adam_fp32(pdt, algo, smem_floats, ctas, fast);
+    case ADVOPT_PREC_BF16_SR: return occupancy_adam_bf16sr(pdt, algo, smem_floats, ctas, fast);
+    case ADVOPT_PREC_INT8_SR: return occupancy_adam_int8(pdt, algo, smem_floats, ctas, fast);
+    default: return pdt == ADVOPT_DT_BF16 ? occupancy_adam_auto(pdt, algo, smem_floats, ctas, fast)
+                                          : occupancy_adam_fp32(pdt, algo, smem_floats, ctas, fast);
   }
 }
 
@@ -135,8 +135,9 @@ extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: bad precision/algo/dtype code");
   if ((L->flags & (ADVOPT_F_PRODIGY_STATS | ADVOPT_F_FISHER_STATS)) && !L->piece_stats)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: statistics requested without piece_stats");
-  if (L->smem_floats < 0 || L->smem_floats > 49152)
-    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: factored d2 above 49152 columns is not supported");
+  if (L->smem_floats < 0 || L->smem_floats > 56832)
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: shared memory request above 227 KB (factored d2 too large)");
+  if (L->stages < 0 || L->stages > 4) return set_error(ADVOPT_E_INVALID, "advopt_adam_step: stages must be 0..4");
   return check_cuda(run_adam(*L, static_cast<cudaStream_t>(stream)), "advopt_adam_step");
 }
 
@@ -167,7 +168,7 @@ extern "C" int advopt_fisher_finish(const advopt_adam_launch* L, advopt_adam_ten
 }
 
 extern "C" int advopt_adam_occupancy(int32_t precision, int32_t param_dtype, int32_t algo, int32_t smem_floats,
-                                     int32_t* sm_count, int32_t* ctas_per_sm) {
+                                     int32_t fast, int32_t* sm_count, int32_t* ctas_per_sm) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return check_cuda(e, "advopt_adam_occupancy");
@@ -175,7 +176,7 @@ extern "C" int advopt_adam_occupancy(int32_t precision, int32_t param_dtype, int
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return check_cuda(e, "advopt_adam_occupancy");
   int ctas = 0;
-  e = run_occupancy(precision, param_dtype, algo, smem_floats, &ctas);
+  e = run_occupancy(precision, param_dtype, algo, smem_floats, &ctas, fast);
   if (e != cudaSuccess) return check_cuda(e, "advopt_adam_occupancy");
   if (sm_count) *sm_count = sms;
   if (ctas_per_sm) *ctas_per_sm = ctas;

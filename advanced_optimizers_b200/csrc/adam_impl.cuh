@@ -742,15 +742,30 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
   }
 }
 
-// Host launchers, instantiated per precision in adam_<precision>.cu.
+}  // namespace advopt
+
+#include "adam_fast.cuh"
+
+namespace advopt {
+
+// Host launchers, instantiated per precision in adam_<precision>.cu.  A
+// launch with L.stages > 0 (and none of the extended options) runs the fast
+// kernel; everything else runs the general one.
 template <int PREC, bool PBF, int ALGO>
 cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
   const bool ext = L.flags & (ADVOPT_F_ATAN2 | ADVOPT_F_NORMED | ADVOPT_F_FISHER | ADVOPT_F_FISHER_STATS |
                               ADVOPT_F_ANCHORS);
   const bool nin = L.flags & ADVOPT_F_NOISE_IN;
+  const size_t smem = (size_t)L.smem_floats * sizeof(float);
+  if (!ext && L.stages > 0) {
+    auto kf = nin ? adam_fast_kernel<PREC, PBF, ALGO, true> : adam_fast_kernel<PREC, PBF, ALGO, false>;
+    cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kf<<<L.grid, kThreads, smem, s>>>(L);
+    return cudaGetLastError();
+  }
   auto k = ext ? (nin ? adam_kernel<PREC, PBF, ALGO, true, true> : adam_kernel<PREC, PBF, ALGO, true, false>)
                : (nin ? adam_kernel<PREC, PBF, ALGO, false, true> : adam_kernel<PREC, PBF, ALGO, false, false>);
-  const size_t smem = (size_t)L.smem_floats * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   k<<<L.grid, kThreads, smem, s>>>(L);
@@ -758,8 +773,8 @@ cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
 }
 
 template <int PREC, bool PBF, int ALGO>
-cudaError_t occupancy_adam_algo(int smem_floats, int* ctas) {
-  auto k = adam_kernel<PREC, PBF, ALGO, false, false>;
+cudaError_t occupancy_adam_algo(int smem_floats, int* ctas, int fast) {
+  auto k = fast ? adam_fast_kernel<PREC, PBF, ALGO, false> : adam_kernel<PREC, PBF, ALGO, false, false>;
   const size_t smem = (size_t)smem_floats * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -780,15 +795,15 @@ cudaError_t launch_adam_prec(const advopt_adam_launch& L, cudaStream_t s) {
 }
 
 template <int PREC>
-cudaError_t occupancy_adam_prec(int pdt, int algo, int smem_floats, int* ctas) {
+cudaError_t occupancy_adam_prec(int pdt, int algo, int smem_floats, int* ctas, int fast) {
   const bool pbf = pdt == ADVOPT_DT_BF16;
   switch (algo) {
     case ADVOPT_ALGO_ADAMW:
-      return pbf ? occupancy_adam_algo<PREC, true, ADVOPT_ALGO_ADAMW>(smem_floats, ctas) : occupancy_adam_algo<PREC, false, ADVOPT_ALGO_ADAMW>(smem_floats, ctas);
+      return pbf ? occupancy_adam_algo<PREC, true, ADVOPT_ALGO_ADAMW>(smem_floats, ctas, fast) : occupancy_adam_algo<PREC, false, ADVOPT_ALGO_ADAMW>(smem_floats, ctas, fast);
     case ADVOPT_ALGO_AUXADAM:
-      return pbf ? occupancy_adam_algo<PREC, true, ADVOPT_ALGO_AUXADAM>(smem_floats, ctas) : occupancy_adam_algo<PREC, false, ADVOPT_ALGO_AUXADAM>(smem_floats, ctas);
+      return pbf ? occupancy_adam_algo<PREC, true, ADVOPT_ALGO_AUXADAM>(smem_floats, ctas, fast) : occupancy_adam_algo<PREC, false, ADVOPT_ALGO_AUXADAM>(smem_floats, ctas, fast);
     default:
-      return pbf ? occupancy_adam_algo<PREC, true, ADVOPT_ALGO_PRODIGY>(smem_floats, ctas) : occupancy_adam_algo<PREC, false, ADVOPT_ALGO_PRODIGY>(smem_floats, ctas);
+      return pbf ? occupancy_adam_algo<PREC, true, ADVOPT_ALGO_PRODIGY>(smem_floats, ctas, fast) : occupancy_adam_algo<PREC, false, ADVOPT_ALGO_PRODIGY>(smem_floats, ctas, fast);
   }
 }
 
@@ -797,9 +812,9 @@ cudaError_t launch_adam_fp32(const advopt_adam_launch& L, cudaStream_t s);
 cudaError_t launch_adam_bf16sr(const advopt_adam_launch& L, cudaStream_t s);
 cudaError_t launch_adam_int8(const advopt_adam_launch& L, cudaStream_t s);
 cudaError_t launch_adam_auto(const advopt_adam_launch& L, cudaStream_t s);
-cudaError_t occupancy_adam_fp32(int pdt, int algo, int smem_floats, int* ctas);
-cudaError_t occupancy_adam_bf16sr(int pdt, int algo, int smem_floats, int* ctas);
-cudaError_t occupancy_adam_int8(int pdt, int algo, int smem_floats, int* ctas);
-cudaError_t occupancy_adam_auto(int pdt, int algo, int smem_floats, int* ctas);
+cudaError_t occupancy_adam_fp32(int pdt, int algo, int smem_floats, int* ctas, int fast);
+cudaError_t occupancy_adam_bf16sr(int pdt, int algo, int smem_floats, int* ctas, int fast);
+cudaError_t occupancy_adam_int8(int pdt, int algo, int smem_floats, int* ctas, int fast);
+cudaError_t occupancy_adam_auto(int pdt, int algo, int smem_floats, int* ctas, int fast);
 
 }  // namespace advopt

@@ -3,7 +3,7 @@
 
 namespace advopt {
 cudaError_t launch_adam_int8(const advopt_adam_launch& L, cudaStream_t s) { return launch_adam_prec<ADVOPT_PREC_INT8_SR>(L, s); }
-cudaError_t occupancy_adam_int8(int pdt, int algo, int smem_floats, int* ctas) {
-  return occupancy_adam_prec<ADVOPT_PREC_INT8_SR>(pdt, algo, smem_floats, ctas);
+cudaError_t occupancy_adam_int8(int pdt, int algo, int smem_floats, int* ctas, int fast) {
+  return occupancy_adam_prec<ADVOPT_PREC_INT8_SR>(pdt, algo, smem_floats, ctas, fast);
 }
 }  // namespace advopt

@@ -276,3 +276,71 @@ __device__ __forceinline__ uint32_t pack4_bytes(int c0, int c1, int c2, int c3) 
 }
 
 }  // namespace advopt
+
+namespace advopt {
+
+// ---------------------------------------------------------------------------
+// Packed fp32x2 arithmetic (sm_100): one instruction, two IEEE-rounded lanes.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 splat2(float a) { return make_float2(a, a); }
+// end - self, exactly as one fused op: fma(self, -1, end)
+__device__ __forceinline__ float2 sub2(float2 end, float2 self) { return __ffma2_rn(self, splat2(-1.0f), end); }
+
+// torch.lerp, two lanes (weight uniform): fmadd(coeff, end-self, base).
+__device__ __forceinline__ float2 lerp2(float2 self, float2 end, float w, float wm1, bool small) {
+  const float2 d = sub2(end, self);
+  return small ? fma2(splat2(w), d, self) : fma2(splat2(wm1), d, end);
+}
+
+// Two-lane div_rcp (same Markstein sequence as div_rcp).
+__device__ __forceinline__ float2 div_rcp2(float2 x, float d, float r) {
+  const float2 D = splat2(-d), Rr = splat2(r);
+  float2 q = mul2(x, Rr);
+  float2 e = fma2(q, D, x);
+  q = fma2(e, Rr, q);
+  e = fma2(q, D, x);
+  return fma2(e, Rr, q);
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk asynchronous copy (global -> shared, no multicast).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after `limit` polls (each try_wait itself suspends
+// for a hardware-defined interval) and reports it instead of hanging.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 24)) {
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+}  // namespace advopt

@@ -188,6 +188,11 @@ class AdamW_adv(torch.optim.Optimizer):
         self._runner.test_noise = None
         return loss
 
+    def check_errors(self):
+        """Synchronise and raise if a kernel of this optimizer reported a
+        bounded wait that gave up (never expected; a guard against hangs)."""
+        self._runner.check_errors()
+
     # ---- test hook: the reference's own random integers ----
     def set_test_noise(self, noise):
         """Use the given int32 noise for the next step only:

@@ -241,8 +241,22 @@ class GroupPlan:
         self.vec_ok = vec_ok
         self.max_d2 = max_d2
         self.gen_offset = ((max_d2 + 3) // 4) * 4
-        self.smem_floats = self.gen_offset + (2 * 2048 + 4 if any_generic else 0)
-        sms, ctas = L.adam_occupancy(self.precision, self.pdt, cfg.algo, self.smem_floats)
+        # fast path: no extended options and only wide factored tensors
+        ext = cfg.use_atan2 or cfg.normed or cfg.fisher or self.has_anchor
+        factors_aligned = all(aligned16(st["mu_v_nmf"], st["mv_v_nmf"]) for st in self.states
+                              if st.get("factored_2nd", False))
+        self.fast = (not ext) and (not any_generic) and factors_aligned
+        if self.fast:
+            bpp = 2 if self.pdt == L.DT_BF16 else 4
+            bps = {0: 4, 1: 2, 2: 1, 3: 2 if self.pdt == L.DT_BF16 else 4}[self.precision]
+            stage = 2048 * (2 * bpp + 2 * bps)
+            budget = 112 * 1024 - self.gen_offset * 4   # two CTAs per SM
+            self.stages = int(max(2, min(4, budget // stage)))
+            self.smem_floats = self.gen_offset + self.stages * stage // 4
+        else:
+            self.stages = 0
+            self.smem_floats = self.gen_offset + (2 * 2048 + 4 if any_generic else 0)
+        sms, ctas = L.adam_occupancy(self.precision, self.pdt, cfg.algo, self.smem_floats, self.fast)
         total_chunks = sum((x + 2047) // 2048 for x in numels)
         self.grid = max(1, min(sms * ctas, total_chunks))
         pieces, offsets, n_slots = plan_pieces(numels, d2s, self.grid)
@@ -266,6 +280,7 @@ class GroupPlan:
         self.stats = torch.zeros(max(1, 2 * self.n_pieces), dtype=torch.float64, device=self.device) \
             if need_stats else None
         self.table = DeviceTable(self.descs.nbytes, self.device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.eps_cache = [None] * n
 
     def launch_struct(self, cfg: AdamCfg, flags: int, seed: int) -> L.AdamLaunch:
@@ -284,6 +299,8 @@ class GroupPlan:
         s.param_dtype = self.pdt
         s.flags = flags
         s.seed = seed
+        s.stages = self.stages
+        s.err = int(self.err.data_ptr())
         return s
 
 
@@ -303,6 +320,13 @@ class AdamFamilyRunner:
 
     def invalidate(self):
         self.plans.clear()
+
+    def check_errors(self):
+        """Raise if a kernel reported a bounded wait that gave up (synchronises)."""
+        for pl in self.plans.values():
+            if int(pl.err.item()) != 0:
+                raise L.AdvOptError("an optimizer kernel gave up waiting for its shared-memory copies; "
+                                    "the step's results are invalid")
 
     def get_plan(self, key, params, states, ids, cfg):
         pl = self.plans.get(key)

@@ -130,6 +130,7 @@ typedef struct advopt_adam_launch {
   const advopt_piece* pieces;         /* [n_pieces], grouped by CTA           */
   const int32_t* cta_offsets;         /* [grid + 1]: CTA c runs pieces [off[c], off[c+1]) */
   double* piece_stats;                /* [n_pieces * 2] Prodigy / Fisher partials */
+  int32_t* err;                       /* set to 1 if a bounded wait gave up (may be NULL) */
   int32_t n_tensors;
   int32_t n_pieces;
   int32_t grid;                       /* CTAs (= length of cta_offsets - 1)   */
@@ -149,7 +150,7 @@ typedef struct advopt_adam_launch {
   float beta3;                        /* Prodigy s decay                      */
   float s_alpha;                      /* Prodigy s add alpha                  */
   float d;                            /* Prodigy d (grad.mul(d) without momentum) */
-  float pad0;
+  int32_t stages;                     /* fast path: shared-memory ring depth (2..4); 0 = general kernel */
   uint64_t seed;                      /* Philox key                           */
 } advopt_adam_launch;
 
@@ -203,9 +204,10 @@ int advopt_abi_version(void);
 /* Last error message of the calling thread ("" if none). */
 const char* advopt_last_error(void);
 /* Number of SMs and the Adam kernel's resident CTAs per SM for a given
- * dynamic shared-memory size (floats); used by the host planner. */
+ * dynamic shared-memory size (floats), for the general (fast = 0) or the
+ * fast-path (fast = 1) kernel; used by the host planner. */
 int advopt_adam_occupancy(int32_t precision, int32_t param_dtype, int32_t algo, int32_t smem_floats,
-                          int32_t* sm_count, int32_t* ctas_per_sm);
+                          int32_t fast, int32_t* sm_count, int32_t* ctas_per_sm);
 
 #ifdef __cplusplus
 }

@@ -70,8 +70,13 @@ def _oracle_state_from_torch(st):
 
 @pytest.mark.parametrize("case", [
     # (shapes, dtype, kwargs) — effective shapes hit d2 = 2048, 4096, 7168 (fast path) and small d2
-    ([(4096, 1024), (2048, 2048), (4096,), (777, 3)], "bf16",
+    ([(4096, 1024), (2048, 2048), (4096,), (1024, 4096)], "bf16",
      dict(state_precision="int8_sr", factored_2nd=True, nesterov=True)),
+    # a factored tensor with d2 < 2048 sends the launch through the general kernel
+    ([(4096, 1024), (777, 3), (300, 70)], "bf16", dict(state_precision="int8_sr", factored_2nd=True, nesterov=True)),
+    ([(2048, 2048), (96,)], "bf16", dict(state_precision="bf16_sr", factored_2nd=True, weight_decay=0.1,
+                                         cautious_wd=True)),
+    ([(2048, 2048), (96,)], "bf16", dict(state_precision="auto", nesterov=True, weight_decay=0.01)),
     ([(14336, 4096)], "bf16", dict(state_precision="int8_sr", factored_2nd=True, nesterov=True)),
     ([(1024, 4096), (4096,), (33, 65)], "bf16", dict(state_precision="int8_sr", weight_decay=0.1, lr=1e-2)),
     ([(768, 2304), (2304,), (50257, 64)], "f32",
