@@ -117,7 +117,10 @@ def test_adamw_matches_oracle_large(case):
         for i, (p, sh) in enumerate(zip(params, shapes)):
             gnp = to_numpy(grads[i])
             gv = O.from_bf16_bits(gnp).reshape(sh) if dt == "bf16" else gnp
-            nz = {k: v.numpy() for k, v in noise[p].items()}
+            n = math.prod(sh)
+            # int8_sr draws over the padded numel, bf16_sr over the numel (param_update.py:181-264)
+            nz = {k: (v.numpy() if (k != "param" and hp["precision"] == "int8_sr") else v.numpy()[:n])
+                  for k, v in noise[p].items()}
             prev = p_o[i].copy()
             p_o[i] = O.adam_family_step(p_o[i], dt, gv, ostate[i], hp, nz, algo="adamw")
             what = f"{shapes[i]} step {s}"
