@@ -104,7 +104,7 @@ __global__ void fisher_finish_kernel(const advopt_adam_launch L, advopt_adam_ten
 }
 
 
-static cudaError_t run_adam(const advopt_adam_launch& L, cudaStream_t s) {
+cudaError_t run_adam(const advopt_adam_launch& L, cudaStream_t s) {
   switch (L.precision) {
     case ADVOPT_PREC_FP32: return launch_adam_fp32(L, s);
     case ADVOPT_PREC_BF16_SR: return launch_adam_bf16sr(L, s);
@@ -114,7 +114,7 @@ static cudaError_t run_adam(const advopt_adam_launch& L, cudaStream_t s) {
   }
 }
 
-static cudaError_t run_occupancy(int prec, int pdt, int algo, int smem_floats, int* ctas, int fast) {
+cudaError_t run_occupancy(int prec, int pdt, int algo, int smem_floats, int* ctas, int fast) {
   switch (prec) {
     case ADVOPT_PREC_FP32: return occupancy_adam_fp32(pdt, algo, smem_floats, ctas, fast);
     case ADVOPT_PREC_BF16_SR: return occupancy_adam_bf16sr(pdt, algo, smem_floats, ctas, fast);
@@ -141,17 +141,24 @@ extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
   return check_cuda(run_adam(*L, static_cast<cudaStream_t>(stream)), "advopt_adam_step");
 }
 
+namespace advopt {
+cudaError_t run_factored_finish(const advopt_adam_tensor* tensors, const int32_t* index, int n_factored, int max_d2,
+                                cudaStream_t s) {
+  dim3 ga((unsigned)((max_d2 + 255) / 256), (unsigned)n_factored);
+  factored_cols_kernel<<<ga, 256, 0, s>>>(tensors, index);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  factored_norm_kernel<<<n_factored, 1024, 0, s>>>(tensors, index);
+  return cudaGetLastError();
+}
+}  // namespace advopt
+
 extern "C" int advopt_factored_finish(const advopt_adam_launch* L, const int32_t* index, int32_t n_factored,
                                       int32_t max_d2, void* stream) {
   if (!L || (n_factored > 0 && !index)) return set_error(ADVOPT_E_INVALID, "advopt_factored_finish: null argument");
   if (n_factored <= 0) return ADVOPT_OK;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  dim3 ga((unsigned)((max_d2 + 255) / 256), (unsigned)n_factored);
-  factored_cols_kernel<<<ga, 256, 0, s>>>(L->tensors, index);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return check_cuda(e, "advopt_factored_finish");
-  factored_norm_kernel<<<n_factored, 1024, 0, s>>>(L->tensors, index);
-  return check_cuda(cudaGetLastError(), "advopt_factored_finish");
+  return check_cuda(run_factored_finish(L->tensors, index, n_factored, max_d2, static_cast<cudaStream_t>(stream)),
+                    "advopt_factored_finish");
 }
 
 extern "C" int advopt_prodigy_finish(const advopt_adam_launch* L, float* sums, float coef, int32_t s_is_bf16,

@@ -79,15 +79,24 @@ __device__ __forceinline__ void issue_chunk(const Cursor& c, unsigned char* stag
   if (!fact) bulk_g2s(stage + LY::V, static_cast<const unsigned char*>(c.v) + c.cs * LY::BPS, bs, bar);
 }
 
+// Move the cursor to the first chunk of the first non-empty piece at or after
+// c.pi (empty pieces have no chunks on the consumer side either).
+template <int PREC, bool PBF>
+__device__ __forceinline__ bool cursor_seek(const advopt_adam_launch& L, Cursor& c, int pend_piece) {
+  for (; c.pi < pend_piece; ++c.pi) {
+    cursor_load_piece<PREC, PBF>(L, c);
+    if (c.cs < c.pend) return true;
+  }
+  return false;
+}
+
 // Advance the cursor by one chunk; false when the CTA has no more chunks.
 template <int PREC, bool PBF>
 __device__ __forceinline__ bool cursor_next(const advopt_adam_launch& L, Cursor& c, int pend_piece) {
   c.cs += kChunk;
   if (c.cs < c.pend) return true;
   ++c.pi;
-  if (c.pi >= pend_piece) return false;
-  cursor_load_piece<PREC, PBF>(L, c);
-  return true;
+  return cursor_seek<PREC, PBF>(L, c, pend_piece);
 }
 
 template <int BPE>
@@ -194,8 +203,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_fast_kernel(const advopt_ada
     mbar_fence_init();
     cur.pi = pbeg;
     cur.tensor = -1;
-    cursor_load_piece<PREC, PBF>(L, cur);
-    cur_valid = true;
+    cur_valid = cursor_seek<PREC, PBF>(L, cur, pend);
     for (int s = 0; s < S && cur_valid; ++s) {
       issue_chunk<PREC, PBF>(cur, stages + (size_t)s * LY::BYTES, &bars[s], &direct[s], has_m);
       cur_valid = cursor_next<PREC, PBF>(L, cur, pend);
