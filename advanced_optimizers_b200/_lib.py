@@ -103,6 +103,7 @@ def lib():
             "advopt_last_error": ([], ctypes.c_char_p),
             "advopt_adam_occupancy": ([I32, I32, I32, I32, I32, ctypes.POINTER(I32), ctypes.POINTER(I32)],
                                       ctypes.c_int),
+            "advopt_adam_step_noalloc": ([P, ctypes.POINTER(AdamLaunch), P], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -129,7 +130,7 @@ def exported_symbols():
     """Names the header declares (used by the load test)."""
     return ["advopt_adam_step", "advopt_factored_finish", "advopt_prodigy_finish", "advopt_fisher_finish",
             "advopt_lion_step", "advopt_sizeof", "advopt_abi_version", "advopt_last_error",
-            "advopt_adam_occupancy"]
+            "advopt_adam_occupancy", "advopt_adam_step_noalloc"]
 
 
 _OCC_CACHE = {}

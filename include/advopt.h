@@ -198,6 +198,27 @@ int advopt_lion_step(const advopt_lion_tensor* tensors, int32_t n_tensors, const
                      int32_t n_pieces, int32_t param_dtype, float w1, float w2, uint32_t flags,
                      uint64_t seed, void* stream);
 
+/* Adam-family step of ONE tensor that allocates nothing.  No counterpart in
+ * the reference (whose step is eager PyTorch): it exists for callers that
+ * cannot allocate device memory during a step — a runtime with its own
+ * fixed device arena and no allocator hook, or code that must not call
+ * cudaMalloc or a caching allocator mid-step.  The scratch that
+ * advopt_adam_step takes from the caller (descriptor table, CTA plan,
+ * factored column partials) lives instead in a file-scope __device__ array of
+ * ADVOPT_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * exit.  `tensor` and `launch` are HOST structs: the caller's device buffers
+ * and the hyperparameters/flags (their table, plan, grid, shared-memory and
+ * stage fields are ignored; launch->err, if set, receives a bounded-wait
+ * give-up).  AdamW and the auxiliary Adam only (no Prodigy, no Fisher).
+ * Factored tensors whose d2 column partials would not fit the array are
+ * rejected with ADVOPT_E_INVALID.  The first call on a device looks up the
+ * array's address (cudaGetSymbolAddress, that device current): make it before
+ * any stream capture.  Calls share the array and it keeps the last call's
+ * contents; calls whose kernels overlap on the GPU race and must be
+ * serialised by the caller. */
+#define ADVOPT_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+int advopt_adam_step_noalloc(const advopt_adam_tensor* tensor, const advopt_adam_launch* launch, void* stream);
+
 /* Layout checks for bindings: sizeof of each struct. */
 size_t advopt_sizeof(int which); /* 0 adam_tensor, 1 piece, 2 adam_launch, 3 lion_tensor */
 int advopt_abi_version(void);
