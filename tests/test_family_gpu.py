@@ -1,0 +1,77 @@
+"""Prodigy_adv and Lion_adv on the GPU against the reference's own outputs
+(golden fixtures, the reference's random integers injected).  Every step
+starts from the reference's params, states and (Prodigy) group scalars.
+
+Tolerances: bf16 params within 1 bf16 ulp; fp32 params 1e-6 relative to the
+larger of the old and new value; bf16-SR'd states within 1 ulp; fp32 states
+2e-6; Prodigy's d within 1e-4 relative (it is d_coef * sum<g, p0 - p> /
+sum|s|, a cancelling float32 reduction whose order differs)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from _compare import check_bf16_param, check_fp32, check_state
+from _gpu import load_state, to_numpy, to_torch
+from _replay import list_cases, load
+
+pytestmark = pytest.mark.gpu
+
+CASES = [c for c in list_cases() if c.startswith(("prodigy_", "lion_"))]
+
+
+def _draws(z, s, i):
+    pre = f"r_{s}_{i}_"
+    return {k[len(pre):]: torch.from_numpy(z[k].astype(np.int32)).cuda() for k in z.files if k.startswith(pre)}
+
+
+@pytest.mark.parametrize("name", CASES)
+def test_matches_reference_golden(name):
+    import advanced_optimizers_b200 as A
+    meta, z = load(name)
+    dt = meta["dtype"]
+    shapes = [tuple(s) for s in meta["shapes"]]
+    params = [torch.nn.Parameter(to_torch(z[f"p0_{i}"], dt).reshape(sh)) for i, sh in enumerate(shapes)]
+    cls = getattr(A, meta["cls"])
+    opt = cls(params, **meta["kw"])
+    prodigy = meta["cls"] == "Prodigy_adv"
+    for s in range(meta["steps"]):
+        for i, p in enumerate(params):
+            if s > 0:
+                p.data.copy_(to_torch(z[f"p_{s - 1}_{i}"], dt).reshape(p.shape))
+            if s == 0 and prodigy:
+                # Prodigy creates its states at the first step: step once the
+                # init path only when states exist
+                pass
+            if opt.state.get(p):
+                load_state(opt, p, z, s - 1 if s > 0 else -1, i)
+            p.grad = to_torch(z[f"g_{s}_{i}"], dt).reshape(p.shape)
+        if prodigy and s > 0:
+            ref = z[f"d_{s - 1}"]
+            for g in opt.param_groups:
+                g["d"], g["d_max"], g["d_numerator"] = float(ref[0]), float(ref[1]), float(ref[2])
+            opt._d_num_carry = float(np.float32(float(ref[2]) * opt.beta3))
+        opt.set_test_noise({p: _draws(z, s, i) for i, p in enumerate(params)})
+        opt.step()
+        torch.cuda.synchronize()
+        for i, p in enumerate(params):
+            what = f"{name} step {s} param {i}"
+            ref_p = z[f"p_{s}_{i}"]
+            if dt == "bf16":
+                check_bf16_param(to_numpy(p), ref_p, what)
+            else:
+                prev = z[f"p_{s - 1}_{i}"] if s > 0 else z[f"p0_{i}"]
+                check_fp32(to_numpy(p), ref_p, 1e-6, what, prev)
+            for key, val in opt.state[p].items():
+                rk = f"st_{s}_{i}_{key}"
+                if torch.is_tensor(val) and rk in z.files:
+                    pk = f"st_{s - 1}_{i}_{key}" if s > 0 else f"st0_{i}_{key}"
+                    prev = z[pk] if pk in z.files and z[pk].shape == z[rk].shape else None
+                    check_state(key, to_numpy(val), z[rk], f"{what} {key}", prev)
+        if prodigy:
+            ref = z[f"d_{s}"]
+            g0 = opt.param_groups[0]
+            assert g0["k"] == int(ref[3])
+            for j, key in enumerate(("d", "d_max", "d_numerator")):
+                np.testing.assert_allclose(g0[key], ref[j], rtol=1e-4, err_msg=f"{name} step {s} {key}")
