@@ -104,6 +104,7 @@ def lib():
             "advopt_adam_occupancy": ([I32, I32, I32, I32, I32, ctypes.POINTER(I32), ctypes.POINTER(I32)],
                                       ctypes.c_int),
             "advopt_adam_step_noalloc": ([P, ctypes.POINTER(AdamLaunch), P], ctypes.c_int),
+            "advopt_ns_gemm": ([P, I32, P, I32, P, I32, I32, P, I32, I32, I32, I32, F, F, P, P], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -130,7 +131,7 @@ def exported_symbols():
     """Names the header declares (used by the load test)."""
     return ["advopt_adam_step", "advopt_factored_finish", "advopt_prodigy_finish", "advopt_fisher_finish",
             "advopt_lion_step", "advopt_sizeof", "advopt_abi_version", "advopt_last_error",
-            "advopt_adam_occupancy", "advopt_adam_step_noalloc"]
+            "advopt_adam_occupancy", "advopt_adam_step_noalloc", "advopt_ns_gemm"]
 
 
 _OCC_CACHE = {}

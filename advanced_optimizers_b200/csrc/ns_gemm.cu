@@ -1,0 +1,325 @@
+// Newton–Schulz GEMM for sm_100a: D = bf16(alpha * (A @ B) + beta * C)
+//
+// One CTA computes one 128 x 256 output tile with 5th-generation tensor cores:
+//   * warp 0 (one elected lane) streams 128x64 A and 256x64 B tiles into a
+//     4-stage shared-memory ring with TMA (cp.async.bulk.tensor, 128-byte
+//     swizzle, no multicast), completing on "full" mbarriers;
+//   * warp 1 owns the tensor memory (256 fp32 columns x 128 lanes), and one
+//     elected lane issues tcgen05.mma (kind::f16, bf16 in, fp32 accumulate),
+//     four K=16 steps per stage, committing each stage to its "empty"
+//     mbarrier so the producer may refill it;
+//   * warps 2..5 read the accumulator back with tcgen05.ld (each warp its
+//     32-lane quarter of the tile's rows) and write bf16(alpha*acc + beta*C).
+// A is K-major ([M][K], K contiguous).  B is K-major ([N][K]) or N-major
+// ([K][N], N contiguous) — the latter is how X enters X' = a X + B X.
+// Every wait is bounded; a wait that gives up sets *err, the CTA drains its
+// tensor-core work (bounded), frees its tensor memory and returns.
+//
+// Newton–Schulz itself (Muon_util.py:7-121): per iteration
+//   quintic: A = X X^T;  B = b A + c A A;  X = a X + B X
+//   CANS:    A = X X^T;  X = c1 X + c3 A X
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "advopt.h"
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace advopt {
+namespace ns {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;            // 16 KB
+constexpr int B_BYTES = BN * BK * 2;            // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // 48 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 256;
+
+// ---- descriptors ----
+// Shared-memory matrix descriptor (tcgen05): start address, leading / stride
+// byte offsets (>> 4), version 1, 128-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;          // version = 1 (sm_100)
+  d |= (uint64_t)2 << 61;          // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: bf16 A/B, fp32 D, M=128, N=256.
+__host__ __device__ constexpr uint32_t instr_desc(bool b_mn_major) {
+  return (1u << 4)                 // D format f32
+         | (1u << 7)               // A bf16
+         | (1u << 10)              // B bf16
+         | (0u << 15)              // A K-major
+         | ((b_mn_major ? 1u : 0u) << 16)
+         | ((uint32_t)(BN >> 3) << 17)
+         | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+struct GemmArgs {
+  uint16_t* D;
+  const uint16_t* C;
+  int ldd, ldc;
+  int M, N, K;
+  float alpha, beta;
+  int32_t* err;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+    ns_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmArgs g,
+                   int b_mn_major) {
+  extern __shared__ unsigned char smem_raw[];
+  // 1024-byte alignment for the 128-byte swizzle atoms
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], tmem_full, drain;
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int ktiles = g.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&tmem_full, 1);
+    mbar_init(&drain, 1);
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    // ---- TMA producer ----
+    if (lane == 0) {
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int s = kt % STAGES;
+        if (kt >= STAGES) {
+          if (!mbar_wait(&empty_bar[s], ((kt / STAGES) - 1) & 1)) {
+            abort_flag = 1;
+            break;
+          }
+        }
+        if (abort_flag) break;
+        unsigned char* sa = smem + s * STAGE_BYTES;
+        unsigned char* sb = sa + A_BYTES;
+        mbar_arrive_tx(&full_bar[s], STAGE_BYTES);
+        tma_load_2d(sa, &mapA, kt * BK, m0, &full_bar[s]);
+        if (b_mn_major) {
+          // B tile = 4 boxes of [64 k-rows][64 n-cols], each 8 KB
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &mapB, n0 + 64 * j, kt * BK, &full_bar[s]);
+        } else {
+          tma_load_2d(sb, &mapB, kt * BK, n0, &full_bar[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      const uint32_t idesc = instr_desc(b_mn_major != 0);
+      for (int kt = 0; kt < ktiles; ++kt) {
+        const int s = kt % STAGES;
+        if (!mbar_wait(&full_bar[s], (kt / STAGES) & 1)) {
+          abort_flag = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+        const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          // A K-major: 16 elements = 32 bytes along the swizzled row
+          const uint64_t ad = smem_desc(sa + k * 32, 16, 1024);
+          const uint64_t bd = b_mn_major ? smem_desc(sb + k * 2048, 8192, 1024)   // 2 groups of 8 k-rows per step
+                                         : smem_desc(sb + k * 32, 16, 1024);
+          mma_bf16(tmem, ad, bd, idesc, (kt > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty_bar[s]);
+      }
+      mma_commit(&tmem_full);
+    }
+  } else {
+    // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----
+    const int quarter = warp & 3;
+    const int row = m0 + quarter * 32 + lane;
+    const bool ok = mbar_wait(&tmem_full, 0);
+    if (!ok) abort_flag = 1;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(taddr + c, r);
+        if (row < g.M) {
+          const int col = n0 + c;
+          float cv[16];
+          if (g.beta != 0.0f && g.C) {
+            const uint4* cp = reinterpret_cast<const uint4*>(g.C + (size_t)row * g.ldc + col);
+            const uint4 c0 = __ldg(cp), c1 = __ldg(cp + 1);
+            const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              cv[2 * i] = __uint_as_float(w[i] << 16);
+              cv[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) cv[i] = 0.0f;
+          }
+          uint32_t o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float v0 = __fmaf_rn(g.alpha, __uint_as_float(r[2 * i]), __fmul_rn(g.beta, cv[2 * i]));
+            const float v1 = __fmaf_rn(g.alpha, __uint_as_float(r[2 * i + 1]), __fmul_rn(g.beta, cv[2 * i + 1]));
+            o[i] = f_to_bf16_rne(v0) | (f_to_bf16_rne(v1) << 16);
+          }
+          uint4* dp = reinterpret_cast<uint4*>(g.D + (size_t)row * g.ldd + col);
+          dp[0] = make_uint4(o[0], o[1], o[2], o[3]);
+          dp[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (abort_flag) {
+    // drain: wait (bounded) for every tensor-core op issued so far before the
+    // tensor memory is released
+    if (threadIdx.x == 32) {
+      mma_commit(&drain);
+      mbar_wait(&drain, 0);
+    }
+    if (threadIdx.x == 0 && g.err) atomicExch(g.err, 1);
+    __syncthreads();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ---- host: tensor maps ----
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encode() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode ? ADVOPT_OK : set_error(ADVOPT_E_CUDA, "cuTensorMapEncodeTiled is unavailable");
+}
+
+// 2-D bf16 tensor map: rows x cols row-major with leading dimension ld
+// (elements); box = box_cols x box_rows, 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
+             uint32_t box_rows) {
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(ADVOPT_E_INVALID, "cuTensorMapEncodeTiled rejected a Newton-Schulz operand");
+  return ADVOPT_OK;
+}
+
+}  // namespace ns
+}  // namespace advopt
+
+using namespace advopt;
+
+extern "C" int advopt_ns_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B, int32_t ldb,
+                              int32_t b_mn_major, const void* C, int32_t ldc, int32_t M, int32_t N, int32_t K,
+                              float alpha, float beta, int32_t* err, void* stream) {
+  using namespace advopt::ns;
+  if (!D || !A || !B || M <= 0 || N <= 0 || K <= 0)
+    return set_error(ADVOPT_E_INVALID, "advopt_ns_gemm: null operand or empty shape");
+  if (M % BM || N % BN || K % BK)
+    return set_error(ADVOPT_E_INVALID, "advopt_ns_gemm: M must be a multiple of 128, N of 256, K of 64");
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(D)) & 15 ||
+      (C && (reinterpret_cast<uintptr_t>(C) & 15)) || lda % 8 || ldb % 8 || ldd % 8 || (C && ldc % 8))
+    return set_error(ADVOPT_E_INVALID, "advopt_ns_gemm: operands must be 16-byte aligned with ld % 8 == 0");
+  if (beta != 0.0f && !C) return set_error(ADVOPT_E_INVALID, "advopt_ns_gemm: beta != 0 needs C");
+  int rc = get_encode();
+  if (rc != ADVOPT_OK) return rc;
+  CUtensorMap ma, mb;
+  rc = make_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BK, BM);
+  if (rc != ADVOPT_OK) return rc;
+  if (b_mn_major) rc = make_map(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, BK);
+  else rc = make_map(&mb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, BK, BN);
+  if (rc != ADVOPT_OK) return rc;
+  GemmArgs g;
+  g.D = static_cast<uint16_t*>(D);
+  g.C = static_cast<const uint16_t*>(C);
+  g.ldd = ldd;
+  g.ldc = ldc;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.alpha = alpha;
+  g.beta = beta;
+  g.err = err;
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(ns_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return check_cuda(attr_err, "advopt_ns_gemm: smem attribute");
+  dim3 grid(N / BN, M / BM);
+  ns_gemm_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, g, b_mn_major);
+  return check_cuda(cudaGetLastError(), "advopt_ns_gemm");
+}

@@ -219,6 +219,18 @@ int advopt_lion_step(const advopt_lion_tensor* tensors, int32_t n_tensors, const
 #define ADVOPT_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 int advopt_adam_step_noalloc(const advopt_adam_tensor* tensor, const advopt_adam_launch* launch, void* stream);
 
+/* Newton–Schulz GEMM on the 5th-generation tensor cores (tcgen05 + TMEM,
+ * TMA operand loads): D = bf16(alpha * A @ B + beta * C), bf16 in, fp32
+ * accumulate.  A is [M][K] (K contiguous, leading dimension lda); B is [N][K]
+ * (b_mn_major = 0) or [K][N] (b_mn_major = 1); C and D are [M][N].  M must be
+ * a multiple of 128, N of 256, K of 64; pointers 16-byte aligned, leading
+ * dimensions multiples of 8.  Replaces the torch.addmm calls of
+ * Muon_util._newton_schulz_iteration (Muon_util.py:98-114).  `err`, if set,
+ * receives 1 when a bounded wait gave up. */
+int advopt_ns_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B, int32_t ldb, int32_t b_mn_major,
+                   const void* C, int32_t ldc, int32_t M, int32_t N, int32_t K, float alpha, float beta,
+                   int32_t* err, void* stream);
+
 /* Layout checks for bindings: sizeof of each struct. */
 size_t advopt_sizeof(int which); /* 0 adam_tensor, 1 piece, 2 adam_launch, 3 lion_tensor */
 int advopt_abi_version(void);
