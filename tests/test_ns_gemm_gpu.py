@@ -1,8 +1,9 @@
 """The tcgen05 Newton–Schulz GEMM against an fp32 reference of the same op:
 D = bf16(alpha * A @ B + beta * C) with bf16 inputs.  The tensor cores
-accumulate in fp32 in their own order, so D may differ from the reference by
-one bf16 rounding step: at most 1 bf16 ulp per element, and the relative
-Frobenius error stays below 4e-3 (bf16's half-ulp is 2^-9)."""
+accumulate in fp32 in their own order, so D may land on the other side of a
+bf16 rounding boundary: per element |D - ref| <= 2^-8 |ref| + 1e-3 rms(ref)
+(one bf16 ulp, plus the fp32 accumulation-order error that dominates for
+outputs near zero), and the relative Frobenius error stays below 4e-3."""
 import ctypes
 
 import numpy as np
@@ -45,8 +46,9 @@ def test_ns_gemm_matches_fp32_reference(M, N, K, bmn, alpha, beta):
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     ref32 = alpha * (A.float() @ Bt.float()) + (beta * C.float() if beta != 0 else 0.0)
-    ref = ref32.bfloat16()
-    u = _ulps(D, ref)
-    assert int(u.max()) <= 1, f"max {int(u.max())} bf16 ulps"
+    diff = (D.float() - ref32).abs()
+    rms = float(ref32.pow(2).mean().sqrt())
+    bad = int((diff > 2.0 ** -8 * ref32.abs() + 1e-3 * rms).sum())
+    assert bad == 0, f"{bad} elements beyond 1 bf16 ulp + 1e-3 rms; max diff {float(diff.max()):.3g}, rms {rms:.3g}"
     rel = float((D.float() - ref32).norm() / ref32.norm())
     assert rel < 4e-3, rel
