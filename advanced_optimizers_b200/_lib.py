@@ -71,6 +71,32 @@ class AdamLaunch(ctypes.Structure):
     ]
 
 
+MU_NESTEROV = 1 << 0
+MU_SIGN = 1 << 1
+MU_SR = 1 << 2
+MU_CAUTIOUS = 1 << 3
+MU_NOISE_IN = 1 << 4
+MU_RMS = 1 << 5
+MU_TRANSPOSED = 1 << 6
+MU_ATAN2 = 1 << 7
+ST_F32, ST_BF16, ST_BF16_SR, ST_Q8 = 0, 1, 2, 3
+
+
+class MuonArgs(ctypes.Structure):
+    """advopt_muon_args."""
+    _fields_ = [(n, ctypes.c_uint64) for n in (
+        "param", "grad", "m", "m_scale", "v", "v_scale", "x0", "ns", "ns_result", "u", "partial", "scalars",
+        "noise_m", "noise_v", "noise_p")] + [
+        ("numel", ctypes.c_int64), ("rows", ctypes.c_int64), ("cols", ctypes.c_int64), ("ld_ns", ctypes.c_int64),
+        ("m_pad", ctypes.c_int64), ("n_pad", ctypes.c_int64), ("seed", ctypes.c_uint64),
+        ("w_m", ctypes.c_float), ("w_nest", ctypes.c_float), ("beta2", ctypes.c_float), ("c_v", ctypes.c_float),
+        ("eps", ctypes.c_float), ("ns_eps", ctypes.c_float), ("wd", ctypes.c_float), ("scale_const", ctypes.c_float),
+        ("tensor_id", ctypes.c_uint32), ("step", ctypes.c_uint32), ("flags", ctypes.c_uint32),
+        ("m_storage", ctypes.c_int32), ("v_storage", ctypes.c_int32), ("param_bf16", ctypes.c_int32),
+        ("math_bf16", ctypes.c_int32), ("update_bf16", ctypes.c_int32),
+    ]
+
+
 _LIB = None
 _LOCK = threading.Lock()
 
@@ -105,6 +131,7 @@ def lib():
                                       ctypes.c_int),
             "advopt_adam_step_noalloc": ([P, ctypes.POINTER(AdamLaunch), P], ctypes.c_int),
             "advopt_ns_gemm": ([P, I32, P, I32, P, I32, I32, P, I32, I32, I32, I32, F, F, P, P], ctypes.c_int),
+            "advopt_muon_stage": ([ctypes.POINTER(MuonArgs), I32, P], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -113,7 +140,8 @@ def lib():
         if L.advopt_abi_version() != ABI_VERSION:
             raise AdvOptError("libadvopt.so ABI version mismatch; rebuild the library")
         for which, size in ((0, ADAM_TENSOR_DT.itemsize), (1, PIECE_DT.itemsize),
-                            (2, ctypes.sizeof(AdamLaunch)), (3, LION_TENSOR_DT.itemsize)):
+                            (2, ctypes.sizeof(AdamLaunch)), (3, LION_TENSOR_DT.itemsize),
+                            (4, ctypes.sizeof(MuonArgs))):
             got = L.advopt_sizeof(which)
             if got != size:
                 raise AdvOptError(f"struct layout mismatch (#{which}: C {got} bytes, Python {size})")
@@ -131,7 +159,7 @@ def exported_symbols():
     """Names the header declares (used by the load test)."""
     return ["advopt_adam_step", "advopt_factored_finish", "advopt_prodigy_finish", "advopt_fisher_finish",
             "advopt_lion_step", "advopt_sizeof", "advopt_abi_version", "advopt_last_error",
-            "advopt_adam_occupancy", "advopt_adam_step_noalloc", "advopt_ns_gemm"]
+            "advopt_adam_occupancy", "advopt_adam_step_noalloc", "advopt_ns_gemm", "advopt_muon_stage"]
 
 
 _OCC_CACHE = {}

@@ -30,6 +30,7 @@ extern "C" size_t advopt_sizeof(int which) {
     case 1: return sizeof(advopt_piece);
     case 2: return sizeof(advopt_adam_launch);
     case 3: return sizeof(advopt_lion_tensor);
+    case 4: return sizeof(advopt_muon_args);
     default: return 0;
   }
 }

@@ -1,0 +1,162 @@
+"""Shared host logic of Muon_adv and AdaMuon_adv: routing of each parameter
+to the Muon path or the auxiliary Adam (Muon_adv.py:283-357,
+AdaMuon_adv.py:293-395), state creation, and the per-step dispatch."""
+from __future__ import annotations
+
+import torch
+
+from .. import _lib as L
+from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, init_adam_state
+from ._common import post_process_loaded_state, reject
+from ._muon_family import MuonMatrixRunner, init_muon_state, is_suitable_for_muon
+
+
+class MuonFamilyBase(torch.optim.Optimizer):
+    _adamuon = False
+
+    def _setup(self):
+        self.device = self.param_groups[0]["params"][0].device if self.param_groups[0]["params"] else None
+        self._adam_runner = AdamFamilyRunner(seed=42)
+        self._muon_runner = MuonMatrixRunner(seed=42)
+        self._ids = {}
+        self._mstep = {}
+        self._test_noise = None
+        self.init_step()
+
+    def load_state_dict(self, state_dict: dict) -> None:
+        super().load_state_dict(state_dict)
+        post_process_loaded_state(self)
+        self._adam_runner.invalidate()
+
+    @property
+    def supports_fused_back_pass(self):
+        return True
+
+    @property
+    def supports_memory_efficient_fp16(self):
+        return True
+
+    @property
+    def supports_flat_params(self):
+        return False
+
+    def compile(self, *args, **kwargs):
+        """The step is already fused into native kernels: nothing to compile."""
+        return None
+
+    def init_step(self):
+        for group in self.param_groups:
+            for p in group["params"]:
+                self._init_state(p, group)
+
+    def _tid(self, p):
+        t = self._ids.get(id(p))
+        if t is None:
+            t = len(self._ids)
+            self._ids[id(p)] = t
+        return t
+
+    @torch.no_grad()
+    def _init_state(self, p, group):
+        state = self.state[p]
+        if "is_muon" in state:
+            return
+        if group.get("use_muon") is not None:
+            is_muon = bool(group["use_muon"])
+        elif group.get("optim_type") is not None:
+            is_muon = group["optim_type"] == "muon"
+        else:
+            is_muon = is_suitable_for_muon(p)
+        if is_muon:
+            req = group["state_precision"]
+            reject(req not in SUPPORTED_PRECISIONS, f"state_precision='{req}' on the Muon path")
+            group["actual_state_precision"] = req
+            init_muon_state(p, state, req, self._adamuon)
+            group["adam_kourkoutas_beta"] = False
+            state["is_muon"] = True
+        else:
+            req = group.get("adam_state_precision", "auto")
+            reject(req not in SUPPORTED_PRECISIONS, f"adam_state_precision='{req}'")
+            group["adam_actual_state_precision"] = req
+            init_adam_state(p, state, precision=req, factored_2nd=group.get("adam_factored_2nd", False),
+                            beta1=group["adam_betas"][0], vector_reshape=group.get("vector_reshape", False),
+                            centered_wd=group.get("centered_wd", 0.0),
+                            centered_wd_mode=group.get("centered_wd_mode", "float8"),
+                            fisher_wd=group.get("adam_fisher_wd", False))
+            state["is_muon"] = False
+
+    def _adam_cfg(self, group):
+        """Muon_AuxAdam._adam_step_parameter's hyperparameters (Muon_AuxAdam.py:70-192)."""
+        return AdamCfg(algo=L.ALGO_AUXADAM, lr=group["lr"], betas=group["adam_betas"], eps=group["adam_eps"],
+                       weight_decay=group["adam_weight_decay"],
+                       precision=group.get("adam_actual_state_precision", group.get("adam_state_precision", "auto")),
+                       nesterov=group.get("adam_nesterov", False), nesterov_coef=group.get("adam_nesterov_coef"),
+                       use_bias_correction=group.get("adam_use_bias_correction", True),
+                       use_atan2=group.get("adam_use_atan2", False), cautious_wd=group.get("cautious_wd", False),
+                       fisher_wd=group.get("adam_fisher_wd", False), centered_wd=group.get("centered_wd", 0.0),
+                       centered_wd_mode=group.get("centered_wd_mode", "float8"),
+                       stochastic_rounding=self.stochastic_rounding)
+
+    def _muon_hp(self, group, p):
+        raise NotImplementedError
+
+    def _step_params(self, gi, group, params):
+        for p in params:
+            self._init_state(p, group)
+        adam = [p for p in params if not self.state[p]["is_muon"]]
+        muon = [p for p in params if self.state[p]["is_muon"]]
+        if adam:
+            by_dtype = {}
+            for p in adam:
+                by_dtype.setdefault((p.dtype, p.device), []).append(p)
+            cfg = self._adam_cfg(group)
+            if self._test_noise is not None:
+                self._adam_runner.test_noise = {k: v for k, v in self._test_noise.items()
+                                                if any(id(p) == k for p in adam)}
+            for (dt, dev), ps in by_dtype.items():
+                key = (gi, dt, dev, tuple(id(p) for p in ps))
+                self._adam_runner.run(key, ps, [self.state[p] for p in ps], [self._tid(p) for p in ps], cfg)
+            self._adam_runner.test_noise = None
+        for p in muon:
+            hp = self._muon_hp(group, p)
+            t = self._mstep.get(id(p), 0)
+            self._mstep[id(p)] = t + 1
+            nz = None if self._test_noise is None else self._test_noise.get(id(p), {})
+            self._muon_runner.step_matrix(p, self.state[p], adamuon=self._adamuon, tensor_id=self._tid(p), step=t,
+                                          noise=nz, sr=self.stochastic_rounding,
+                                          precision=group["actual_state_precision"], **hp)
+
+    @torch.no_grad()
+    def step_parameter(self, p: torch.Tensor, group: dict, i: int | None = None):
+        if p.grad is None:
+            return
+        gi = next(k for k, g in enumerate(self.param_groups) if g is group)
+        self._step_params(gi, group, [p])
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for gi, group in enumerate(self.param_groups):
+            params = [p for p in group["params"] if p.grad is not None]
+            if params:
+                self._step_params(gi, group, params)
+        self._test_noise = None
+        return loss
+
+    def check_errors(self):
+        """Synchronise and raise if a kernel of this optimizer reported a bounded wait that gave up."""
+        self._adam_runner.check_errors()
+        self._muon_runner.check_errors()
+
+    def set_test_noise(self, noise):
+        """Use the reference's random integers for the next step only:
+        {param: {'momentum_buffer' | 'second_momentum_buffer' | 'exp_avg' |
+        'exp_avg_sq' | 'param': int tensor}}.  None restores Philox."""
+        self._test_noise = None if noise is None else {id(p): v for p, v in noise.items()}
+
+    @property
+    def launch_count(self):
+        return self._adam_runner.launch_count + self._muon_runner.launch_count

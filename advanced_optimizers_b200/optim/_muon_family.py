@@ -1,0 +1,358 @@
+"""Host side of Muon_adv / AdaMuon_adv: state creation with the reference's
+keys, the Newton–Schulz GEMM chain on a per-device workspace, and the
+elementwise stages of csrc/muon.cu.
+
+Per matrix the device runs: stage 0 (momentum, X0, ||X0||, normalised and
+possibly transposed X in the padded workspace), then ns_steps iterations of
+bf16 tcgen05 GEMMs (quintic: A = X X^T, B = bA + cAA, X = aX + BX; CANS:
+A = X X^T, X = c1 X + c3 AX; Muon_util.py:7-121), then the RMS rescale and
+parameter update (Muon) or the second moment, RMS rescale and update
+(AdaMuon).  The auxiliary Adam groups run through the Adam-family runner
+with algo AUXADAM (Muon_AuxAdam.py:70-192).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from .. import _lib as L
+from .._device import dtype_code, ptr, require_cuda_tensor, stream_handle
+from ._adam_family import adjust_wds, f32, init_state_tensor
+
+NS_ALIGN = 256   # the GEMM's N tile; also a multiple of its M (128) and K (64) tiles
+
+
+def round_up(x: int, a: int) -> int:
+    return (x + a - 1) // a * a
+
+
+def cans_coeffs(steps: int, a_bound: float):
+    """(c1, c3) of each CANS iteration from the singular-value bounds,
+    Muon_util.py:69-105, in Python double as the reference computes them."""
+    lb, ub = a_bound, 1.0
+    out = []
+    for _ in range(steps):
+        lb_ub = lb * ub
+        e_sq = (lb * lb + lb_ub + ub * ub) / 3.0
+        k = 2.0 * e_sq ** 1.5
+        l_ = lb_ub * (lb + ub)
+        den = k + l_
+        alpha = 6.0 / den
+        out.append((alpha * e_sq, -alpha / 3.0))
+        eps_val = (k - l_) / den
+        lb, ub = 1.0 - eps_val, 1.0 + eps_val
+    return out
+
+
+def default_cns_bound(rows: int, cols: int) -> float:
+    """Muon_util.py:229-237."""
+    return max(1.0 / math.sqrt(rows * cols), abs(1.0 / math.sqrt(cols) - 1.0 / math.sqrt(rows)))
+
+
+def is_suitable_for_muon(p: torch.Tensor, min_dim_size: int = 4, max_aspect_ratio: float = 128.0) -> bool:
+    """_is_suitable_for_muon (Muon_util.py:285-331)."""
+    s = p.shape
+    if p.ndim < 2 or sum(1 for d in s if d > 1) < 2:
+        return False
+    if s[0] == 1 or s[1] == 1:
+        return False
+    if p.ndim >= 3:
+        inner = 1
+        for d in s[1:]:
+            inner *= d
+        dims = (s[0], inner)
+    else:
+        dims = tuple(s)
+    lo = min(dims)
+    if lo < min_dim_size:
+        return False
+    return max(dims) / lo <= max_aspect_ratio
+
+
+def storage_code(precision: str, p: torch.Tensor) -> int:
+    if precision == "fp32":
+        return L.ST_F32
+    if precision == "bf16_sr":
+        return L.ST_BF16_SR
+    if precision == "int8_sr":
+        return L.ST_Q8
+    if precision == "auto":
+        return L.ST_BF16 if p.dtype == torch.bfloat16 else L.ST_F32
+    raise NotImplementedError(f"state_precision '{precision}' is not supported by the B200 kernels")
+
+
+class NSWorkspace:
+    """Per-device scratch of the Muon path, grown on demand and then reused:
+    the Newton–Schulz buffers X, C ([m_pad][n_pad]) and A, B ([m_pad][m_pad])
+    in bf16, X0 and U (bf16, one matrix), partial sums, scalars and the
+    bounded-wait error word."""
+
+    def __init__(self, device):
+        self.device = device
+        self.ns = None
+        self.ns_cap = 0
+        self.vec = None
+        self.vec_cap = 0
+        self.partial = None
+        self.part_cap = 0
+        self.scalars = torch.zeros(4, dtype=torch.float32, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def ensure(self, numel: int, m_pad: int, n_pad: int):
+        need_ns = 2 * m_pad * n_pad + 2 * m_pad * m_pad
+        if need_ns > self.ns_cap:
+            self.ns = torch.empty(need_ns, dtype=torch.bfloat16, device=self.device)
+            self.ns_cap = need_ns
+        need_vec = 2 * round_up(numel, 128)
+        if need_vec > self.vec_cap:
+            self.vec = torch.empty(need_vec, dtype=torch.bfloat16, device=self.device)
+            self.vec_cap = need_vec
+        need_part = max((numel + 2047) // 2048, ((m_pad + 31) // 32) * ((n_pad + 31) // 32)) + 1
+        if need_part > self.part_cap:
+            self.partial = torch.empty(need_part, dtype=torch.float64, device=self.device)
+            self.part_cap = need_part
+
+    def pointers(self, numel: int, m_pad: int, n_pad: int):
+        base = int(self.ns.data_ptr())
+        xy = m_pad * n_pad * 2
+        aa = m_pad * m_pad * 2
+        x, c = base, base + xy
+        a, b = base + 2 * xy, base + 2 * xy + aa
+        v = int(self.vec.data_ptr())
+        return dict(x=x, c=c, a=a, b=b, x0=v, u=v + 2 * round_up(numel, 128))
+
+
+def run_ns_chain(ws: NSWorkspace, ptrs, m_pad: int, n_pad: int, steps: int, coeffs, cns: bool, cns_bound: float,
+                 stream: int) -> int:
+    """The Newton–Schulz iterations on the workspace (X already loaded);
+    returns the device address of the final X.  Every GEMM is
+    advopt_ns_gemm (tcgen05, fp32 accumulate, one bf16 rounding of
+    alpha*acc + beta*C), matching torch.addmm's bf16 semantics."""
+    lib = L.lib()
+    err = int(ws.err.data_ptr())
+    x, c, a, b = ptrs["x"], ptrs["c"], ptrs["a"], ptrs["b"]
+
+    def gemm(d, ldd, a_, lda, b_, ldb, b_mn, c_, ldc, M, N, K, alpha, beta):
+        L.check(lib.advopt_ns_gemm(d, ldd, a_, lda, b_, ldb, b_mn, c_, ldc, M, N, K, f32(alpha), f32(beta), err,
+                                   stream), "advopt_ns_gemm")
+
+    if cns:
+        for c1, c3 in cans_coeffs(steps, cns_bound):
+            gemm(a, m_pad, x, n_pad, x, n_pad, 0, 0, 0, m_pad, m_pad, n_pad, 1.0, 0.0)          # A = X X^T
+            gemm(c, n_pad, a, m_pad, x, n_pad, 1, x, n_pad, m_pad, n_pad, m_pad, c3, c1)      # X' = c1 X + c3 A X
+            x, c = c, x
+    else:
+        qa, qb, qc = coeffs
+        for _ in range(steps):
+            gemm(a, m_pad, x, n_pad, x, n_pad, 0, 0, 0, m_pad, m_pad, n_pad, 1.0, 0.0)          # A = X X^T
+            gemm(b, m_pad, a, m_pad, a, m_pad, 1, a, m_pad, m_pad, m_pad, m_pad, qc, qb)      # B = b A + c A A
+            gemm(c, n_pad, b, m_pad, x, n_pad, 1, x, n_pad, m_pad, n_pad, m_pad, 1.0, qa)     # X' = a X + B X
+            x, c = c, x
+    return x
+
+
+def ns_launches(steps: int, cns: bool) -> int:
+    return steps * (2 if cns else 3)
+
+
+def ns_flops(m: int, n: int, steps: int, cns: bool) -> int:
+    """Algorithmic FLOPs of the chain on an m x n matrix (m <= n):
+    quintic 4m^2n + 2m^3 per iteration, CANS 4m^2n."""
+    return steps * (4 * m * m * n + (0 if cns else 2 * m ** 3))
+
+
+class MuonMatrixRunner:
+    """Runs the Muon / AdaMuon step of one matrix at a time on its device."""
+
+    def __init__(self, seed: int = 42):
+        self.seed = int(seed)
+        self.ws = {}
+        self.launch_count = 0
+        self.gemm_events = None   # list collecting (start, end, flops) around each NS chain
+
+    def workspace(self, device) -> NSWorkspace:
+        ws = self.ws.get(device)
+        if ws is None:
+            ws = NSWorkspace(device)
+            self.ws[device] = ws
+        return ws
+
+    def check_errors(self):
+        for ws in self.ws.values():
+            if int(ws.err.item()) != 0:
+                raise L.AdvOptError("a Newton-Schulz GEMM gave up waiting for its shared-memory copies; "
+                                    "the step's results are invalid")
+
+    @torch.no_grad()
+    def step_matrix(self, p, state, *, adamuon: bool, lr: float, beta1: float, beta2: float, eps, nesterov: bool,
+                    nesterov_coef, ns_steps: int, ns_eps, ns_coeffs, cns: bool, cns_a_bound, rms_rescaling: bool,
+                    use_atan2: bool, sign_projection: bool, weight_decay: float, cautious_wd: bool, sr: bool,
+                    precision: str, tensor_id: int, step: int, noise=None):
+        require_cuda_tensor(p, "param")
+        require_cuda_tensor(p.grad, "grad")
+        if p.ndim < 2:
+            raise NotImplementedError("the Muon path needs a parameter with at least 2 dimensions")
+        numel = p.numel()
+        if numel == 0:
+            return
+        pbf = dtype_code(p.dtype) == L.DT_BF16
+        rows = p.shape[0]
+        cols = numel // rows
+        m, n = min(rows, cols), max(rows, cols)
+        m_pad, n_pad = round_up(m, NS_ALIGN), round_up(n, NS_ALIGN)
+        ws = self.workspace(p.device)
+        ws.ensure(numel, m_pad, n_pad)
+        ptrs = ws.pointers(numel, m_pad, n_pad)
+        stream = stream_handle(p.device)
+
+        a = L.MuonArgs()
+        a.param, a.grad = ptr(p), ptr(p.grad)
+        mb = state["momentum_buffer"]
+        a.m = ptr(mb)
+        a.m_scale = ptr(state.get("momentum_buffer_scale"))
+        if adamuon:
+            vb = state["second_momentum_buffer"]
+            a.v = ptr(vb)
+            a.v_scale = ptr(state.get("second_momentum_buffer_scale"))
+        a.x0, a.ns, a.u = ptrs["x0"], ptrs["x"], ptrs["u"]
+        a.partial, a.scalars = ptr(ws.partial), ptr(ws.scalars)
+        a.numel, a.rows, a.cols = numel, rows, cols
+        a.ld_ns, a.m_pad, a.n_pad = n_pad, m_pad, n_pad
+        a.seed = self.seed
+        a.w_m = f32(1.0 - beta1)
+        nv = beta1 if nesterov_coef is None else nesterov_coef
+        a.w_nest = f32(nv)
+        a.beta2 = f32(beta2)
+        a.c_v = f32(1.0 - beta2)
+        a.eps = f32(eps if eps is not None else 1.0 / math.sqrt(numel))
+        a.ns_eps = f32(ns_eps if ns_eps is not None else 1.0 / math.sqrt(numel))
+        wd, _ = adjust_wds(weight_decay, 0.0, p)
+        a.wd = f32(wd * lr) if wd != 0 else 0.0
+        step_scale = lr * (4 / math.pi) if (adamuon and use_atan2) else lr
+        if rms_rescaling:
+            a.scale_const = f32(step_scale * 0.2 * math.sqrt(numel))
+        else:
+            # AdaMuon rescales in the param's shape, Muon in the flattened one
+            r, c = (p.shape[-2], p.shape[-1]) if adamuon else (rows, cols)
+            a.scale_const = f32(step_scale * math.sqrt(max(1, r / c)))
+        a.tensor_id = tensor_id & 0xFFFFFFFF
+        a.step = step & 0xFFFFFFFF
+        flags = 0
+        if nesterov:
+            flags |= L.MU_NESTEROV
+        if sign_projection:
+            flags |= L.MU_SIGN
+        if sr and pbf:
+            flags |= L.MU_SR
+        if cautious_wd:
+            flags |= L.MU_CAUTIOUS
+        if rms_rescaling:
+            flags |= L.MU_RMS
+        if rows > cols:
+            flags |= L.MU_TRANSPOSED
+        if adamuon and use_atan2:
+            flags |= L.MU_ATAN2
+        keep = []
+        if noise is not None:
+            flags |= L.MU_NOISE_IN
+            for label, field in (("momentum_buffer", "noise_m"), ("second_momentum_buffer", "noise_v"),
+                                 ("param", "noise_p")):
+                t = noise.get(label)
+                if t is not None:
+                    t = t.to(device=p.device, dtype=torch.int32).contiguous()
+                    if t.numel() < numel:
+                        raise ValueError(f"injected noise '{label}' has {t.numel()} entries, {numel} needed")
+                    keep.append(t)
+                    setattr(a, field, ptr(t))
+        a.flags = flags
+        a.m_storage = storage_code(precision, p)
+        a.v_storage = storage_code(precision, p) if adamuon else 0
+        auto_bf16 = precision == "auto" and pbf
+        a.param_bf16 = 1 if pbf else 0
+        a.math_bf16 = 1 if auto_bf16 else 0
+        a.update_bf16 = 1 if auto_bf16 else 0
+
+        lib = L.lib()
+        L.check(lib.advopt_muon_stage(ctypes.byref(a), 0, stream), "advopt_muon_stage (prep)")
+        bound = cns_a_bound if cns_a_bound is not None else default_cns_bound(rows, cols)
+        if self.gemm_events is not None:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(torch.cuda.current_stream(p.device))
+        final = run_ns_chain(ws, ptrs, m_pad, n_pad, ns_steps, ns_coeffs, cns, bound, stream)
+        if self.gemm_events is not None:
+            ev1.record(torch.cuda.current_stream(p.device))
+            self.gemm_events.append((ev0, ev1, ns_flops(m, n, ns_steps, cns)))
+        a.ns_result = final
+        if adamuon:
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 4, stream), "advopt_muon_stage (AdaMuon statistics)")
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 5, stream), "advopt_muon_stage (AdaMuon update)")
+            self.launch_count += 3 + 1 + 2 + 1
+        else:
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 1, stream), "advopt_muon_stage (U, scale)")
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 2, stream), "advopt_muon_stage (update)")
+            self.launch_count += 3 + 2 + 1
+        self.launch_count += ns_launches(ns_steps, cns)
+        if keep:
+            torch.cuda.current_stream(p.device).synchronize()
+
+
+_NS_RUNNER = None
+
+
+@torch.no_grad()
+def newton_schulz(G: torch.Tensor, steps: int = 5, eps: float | None = 1e-7,
+                  coeffs: tuple[float, float, float] = (3.4445, -4.7750, 2.0315), cns: bool = False,
+                  cns_a_bound: float | None = None, low_rank_ortho: bool = False, ortho_rank: int = 128,
+                  G_sketch=None, compiled: bool = False) -> torch.Tensor:
+    """Muon_util.newton_schulz (Muon_util.py:193-283), standard path, on the
+    tcgen05 GEMM chain: X = bf16(G) (transposed if rows > cols), divided by
+    max(||X||_F, eps), then `steps` quintic or CANS iterations in bf16 with
+    fp32 accumulation; returns a new tensor in G's dtype."""
+    global _NS_RUNNER
+    if low_rank_ortho:
+        raise NotImplementedError("low_rank_ortho is not supported by the B200 optimizer kernels")
+    if G.ndim != 2:
+        raise NotImplementedError("newton_schulz takes one 2-D matrix")
+    require_cuda_tensor(G, "G")
+    dtype_code(G.dtype)
+    rows, cols = G.shape
+    numel = G.numel()
+    out = torch.empty((rows, cols), dtype=torch.bfloat16, device=G.device)
+    if numel == 0:
+        return out.to(G.dtype)
+    if _NS_RUNNER is None:
+        _NS_RUNNER = MuonMatrixRunner()
+    ws = _NS_RUNNER.workspace(G.device)
+    m, n = min(rows, cols), max(rows, cols)
+    m_pad, n_pad = round_up(m, NS_ALIGN), round_up(n, NS_ALIGN)
+    ws.ensure(numel, m_pad, n_pad)
+    ptrs = ws.pointers(numel, m_pad, n_pad)
+    stream = stream_handle(G.device)
+    a = L.MuonArgs()
+    a.grad = ptr(G)
+    a.x0, a.ns, a.u = ptrs["x0"], ptrs["x"], ptr(out)
+    a.partial, a.scalars = ptr(ws.partial), ptr(ws.scalars)
+    a.numel, a.rows, a.cols = numel, rows, cols
+    a.ld_ns, a.m_pad, a.n_pad = n_pad, m_pad, n_pad
+    a.ns_eps = f32(eps if eps is not None else 1.0 / math.sqrt(numel))
+    a.flags = L.MU_TRANSPOSED if rows > cols else 0
+    a.param_bf16 = 1 if G.dtype == torch.bfloat16 else 0
+    lib = L.lib()
+    L.check(lib.advopt_muon_stage(ctypes.byref(a), 6, stream), "advopt_muon_stage (load)")
+    bound = cns_a_bound if cns_a_bound is not None else default_cns_bound(rows, cols)
+    a.ns_result = run_ns_chain(ws, ptrs, m_pad, n_pad, steps, coeffs, cns, bound, stream)
+    L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (store)")
+    return out if G.dtype == torch.bfloat16 else out.to(G.dtype)
+
+
+def init_muon_state(p, state, precision: str, adamuon: bool):
+    """Muon_adv.__init_state / AdaMuon_adv.__init_state, non-factored
+    (Muon_adv.py:304-330, AdaMuon_adv.py:334-359)."""
+    state["factored"] = False
+    init_state_tensor(state, "momentum_buffer", p, precision)
+    if adamuon:
+        state["factored_2nd"] = False
+        init_state_tensor(state, "second_momentum_buffer", p, precision, non_neg=True)

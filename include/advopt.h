@@ -231,8 +231,83 @@ int advopt_ns_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void*
                    const void* C, int32_t ldc, int32_t M, int32_t N, int32_t K, float alpha, float beta,
                    int32_t* err, void* stream);
 
+/*
+ * Muon_adv / AdaMuon_adv: the elementwise work around the Newton–Schulz
+ * GEMMs for ONE 2-D (or flattened) matrix.  The host runs, in order:
+ *   stage 0  momentum (+ Nesterov, + AdaMuon's sign projection), the
+ *            momentum_buffer store, X0 = bf16(update), ||X0|| (bf16) and
+ *            X = bf16(X0 / max(||X0||, ns_eps)) into the zero-padded
+ *            workspace `ns` ([m_pad][n_pad], transposed when rows > cols);
+ *   the Newton–Schulz chain with advopt_ns_gemm on the workspace;
+ *   Muon:    stage 1 (U = result in the param's layout, RMS scale), stage 2
+ *            (param update);
+ *   AdaMuon: stage 3 (U), stage 4 (second moment statistics + RMS scale),
+ *            stage 5 (second_momentum_buffer store + param update).
+ * Replaces Muon_adv._muon_step_parameter (Muon_adv.py:443-555) and
+ * AdaMuon_adv._muon_step_parameter (AdaMuon_adv.py:492-659) for non-factored
+ * matrices, with Muon_util.rms_adjustment (Muon_util.py:362-372) and
+ * param_update.apply_parameter_update (param_update.py:77-156).
+ */
+#define ADVOPT_MU_NESTEROV (1u << 0)
+#define ADVOPT_MU_SIGN (1u << 1)      /* AdaMuon kappa_p = 1: sign(update) before NS */
+#define ADVOPT_MU_SR (1u << 2)        /* stochastic rounding of bf16 params */
+#define ADVOPT_MU_CAUTIOUS (1u << 3)
+#define ADVOPT_MU_NOISE_IN (1u << 4)  /* read SR noise from noise_* */
+#define ADVOPT_MU_RMS (1u << 5)       /* rms_rescaling */
+#define ADVOPT_MU_TRANSPOSED (1u << 6)/* rows > cols: the workspace holds X^T */
+#define ADVOPT_MU_ATAN2 (1u << 7)     /* AdaMuon use_atan2 */
+
+/* storage codes of momentum_buffer / second_momentum_buffer */
+#define ADVOPT_ST_F32 0
+#define ADVOPT_ST_BF16 1      /* bf16, round to nearest ('auto' with bf16 params) */
+#define ADVOPT_ST_BF16_SR 2   /* bf16, stochastic rounding ('bf16_sr')           */
+#define ADVOPT_ST_Q8 3        /* int8 / uint8 codes + 2048-element block scales   */
+
+typedef struct advopt_muon_args {
+  void* param;               /* p (f32 or bf16), [rows][cols] flattened          */
+  const void* grad;
+  void* m;                   /* momentum_buffer                                  */
+  float* m_scale;            /* momentum_buffer_scale (ADVOPT_ST_Q8)             */
+  void* v;                   /* AdaMuon second_momentum_buffer                   */
+  float* v_scale;
+  uint16_t* x0;              /* scratch bf16 [numel]                             */
+  uint16_t* ns;              /* workspace X, bf16 [m_pad][ld_ns]                 */
+  const uint16_t* ns_result; /* the chain's final X (stages 1 and 3)             */
+  uint16_t* u;               /* scratch bf16 [numel]: U in the param's layout    */
+  double* partial;           /* scratch [max(ceil(numel/2048), tiles32)]         */
+  float* scalars;            /* scratch [4]: ||X0|| (bf16 value), update scale   */
+  const int32_t* noise_m;
+  const int32_t* noise_v;
+  const int32_t* noise_p;
+  int64_t numel;
+  int64_t rows;              /* p.shape[0]                                       */
+  int64_t cols;              /* numel / rows                                     */
+  int64_t ld_ns;             /* workspace leading dimension (= n_pad)            */
+  int64_t m_pad;             /* workspace rows: min(rows, cols) rounded up to 256 */
+  int64_t n_pad;             /* workspace cols: max(rows, cols) rounded up to 256 */
+  uint64_t seed;             /* Philox key                                       */
+  float w_m;                 /* 1 - beta1                                        */
+  float w_nest;              /* Nesterov coefficient (grad.lerp(m, coef))        */
+  float beta2;               /* AdaMuon                                          */
+  float c_v;                 /* AdaMuon 1 - beta2                                */
+  float eps;                 /* AdaMuon eps (or 1/sqrt(numel))                   */
+  float ns_eps;              /* Newton–Schulz norm clamp                         */
+  float wd;                  /* weight_decay * lr (0: none)                      */
+  float scale_const;         /* rms: step_scale*0.2*sqrt(numel); else lr*sqrt(max(1, r/c)) */
+  uint32_t tensor_id;
+  uint32_t step;
+  uint32_t flags;            /* ADVOPT_MU_*                                      */
+  int32_t m_storage;         /* ADVOPT_ST_*                                      */
+  int32_t v_storage;
+  int32_t param_bf16;        /* 1: bf16 params, 0: f32                           */
+  int32_t math_bf16;         /* 1: momentum and AdaMuon math in bf16 ('auto', bf16 params) */
+  int32_t update_bf16;       /* 1: the orthogonalised update is bf16 (else f32)  */
+} advopt_muon_args;
+
+int advopt_muon_stage(const advopt_muon_args* args, int32_t stage, void* stream);
+
 /* Layout checks for bindings: sizeof of each struct. */
-size_t advopt_sizeof(int which); /* 0 adam_tensor, 1 piece, 2 adam_launch, 3 lion_tensor */
+size_t advopt_sizeof(int which); /* 0 adam_tensor, 1 piece, 2 adam_launch, 3 lion_tensor, 4 muon_args */
 int advopt_abi_version(void);
 /* Last error message of the calling thread ("" if none). */
 const char* advopt_last_error(void);
