@@ -29,6 +29,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 WORKLOAD = "adamw_adv int8_sr+factored_2nd+nesterov, llama-3-8b shapes, bf16"
+# DRAM bytes (read + write) of adam_fast_kernel per algorithmic byte, from one ncu
+# capture of the 2-layer subset (profiles/adam_fast_kernel_int8sr_factored_llama8b.md):
+# 3.476 GB measured / 3.493 GB algorithmic.  Traffic grows with the elements processed,
+# so the full launch's traffic is reported as this ratio times its algorithmic bytes.
+TRAFFIC_PER_ALG_BYTE = 3.476247e9 / 3.492700320e9
 
 
 def llama3_8b_shapes(layers=32, embed=True):
@@ -278,11 +283,105 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, owned, step, world, dev)
+    ns = None
+    if not args.no_ns:
+        del opt, owned, params, step
+        torch.cuda.empty_cache()
+        ns = run_ns_leg(args, world, rank, dev)
     if rank == 0:
-        emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, launches, clocks, e2e)
+        emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, launches, clocks, e2e, ns)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def muon_shapes(layers=32):
+    """Every 2-D hidden weight of Llama-3-8B (the Muon matrices)."""
+    d, kv, ffn = 4096, 1024, 14336
+    return [(d, d), (kv, d), (kv, d), (d, d), (ffn, d), (ffn, d), (d, ffn)] * layers
+
+
+def run_ns_leg(args, world, rank, dev):
+    """Muon_adv (momentum 0.95, 5 quintic Newton-Schulz iterations, bf16
+    'auto' states) over every hidden matrix; matrices are split across ranks
+    by FLOPs (LPT) and the updated params broadcast from their owners."""
+    import torch.distributed as dist
+    import advanced_optimizers_b200 as A
+    from advanced_optimizers_b200.optim._muon_family import ns_flops
+    shapes = muon_shapes(args.layers)
+    flops = [ns_flops(min(s), max(s), 5, False) for s in shapes]
+    order = sorted(range(len(shapes)), key=lambda i: -flops[i])
+    load = [0] * world
+    owner = [0] * len(shapes)
+    for i in order:
+        r = min(range(world), key=lambda k: load[k])
+        owner[i] = r
+        load[r] += flops[i]
+    gen = torch.Generator(device=dev).manual_seed(4321 + rank)
+    params = []
+    for i, sh in enumerate(shapes):
+        t = torch.empty(sh, dtype=torch.bfloat16, device=dev)
+        if owner[i] == rank:
+            t.normal_(0, 0.02, generator=gen)
+        params.append(torch.nn.Parameter(t))
+    owned = [params[i] for i in range(len(shapes)) if owner[i] == rank]
+    for p in owned:
+        p.grad = torch.empty_like(p).normal_(0, 1e-3, generator=gen)
+    opt = A.Muon_adv([dict(params=owned, optim_type="muon")], lr=1e-3, beta1=0.95)
+
+    def step():
+        opt.step()
+        if world > 1:
+            with torch.no_grad():
+                for i, p in enumerate(params):
+                    dist.broadcast(p.data, src=owner[i])
+
+    warm = 1
+    steps = 2
+    for _ in range(warm):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    runner = opt._muon_runner
+    runner.gemm_events = []
+    l0 = opt.launch_count
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in runner.gemm_events) / steps
+    fl = sum(f for _, _, f in runner.gemm_events) / steps
+    runner.gemm_events = None
+    launches = opt.launch_count - l0
+    if world > 1:
+        t = torch.tensor([ms, gemm_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, gemm_ms = (float(x) for x in t.tolist())
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, kind = float(json.load(f)["bf16_tflops_sustained"]), "measured sustained"
+    except Exception:
+        peak, kind = 1400.0, "fallback sustained"
+    total_flops = sum(flops)
+    del opt, owned, params
+    torch.cuda.empty_cache()
+    return {"workload": f"Muon_adv over {len(shapes)} Llama-3-8B hidden matrices (q/o 4096x4096, k/v 1024x4096, "
+                        "gate/up 14336x4096, down 4096x14336), momentum 0.95, 5 quintic Newton-Schulz "
+                        "iterations, bf16 'auto' states", "steps": steps, "warmup": warm,
+            "ms_per_step": ms, "value": 1000.0 / ms, "unit": "optimizer steps/s",
+            "ns_ms_per_step": gemm_ms,
+            "roofline": {"bound": "tensor", "achieved": (fl / (gemm_ms * 1e-3)) / 1e12 if gemm_ms > 0 else 0.0,
+                         "peak": peak, "unit": "TFLOP/s",
+                         "frac": ((fl / (gemm_ms * 1e-3)) / 1e12) / peak if gemm_ms > 0 else 0.0,
+                         "peak_kind": kind, "kernel": "ns_gemm_kernel (tcgen05, 128x256 tiles)",
+                         "algorithmic_flops_per_step": total_flops,
+                         "note": "achieved = this rank's algorithmic Newton-Schulz FLOPs / its chain time "
+                                 "(the chains include the tiny normalise/transpose kernels)"},
+            "gpu_launches": launches}
 
 
 def run_e2e(args, owned, step, world, dev):
@@ -317,7 +416,7 @@ def run_e2e(args, owned, step, world, dev):
             "d2h_bytes_per_step": readback.numel() * 2}
 
 
-def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, launches, clocks, e2e):
+def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, launches, clocks, e2e, ns=None):
     if True:
         alg = algorithmic_bytes([shapes[i] for i in mine])
         peak, peak_kind = measured_peaks()
@@ -333,13 +432,17 @@ def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, la
                        "parallelism": f"per-tensor sharding x{world}" + (" + bf16 param all-gather" if world > 1 else ""),
                        "l2": "inputs larger than L2 (about 40 GB resident per step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_kind": peak_kind,
+                         "frac": achieved / peak, "traffic": TRAFFIC_PER_ALG_BYTE * alg,
+                         "traffic_note": "dram bytes per launch scaled from the 2-layer ncu capture",
+                         "peak_kind": peak_kind,
                          "kernel": "adam_kernel<INT8_SR, bf16, AdamW>", "kernel_ms": kernel_avg_ms,
                          "algorithmic_bytes": alg},
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,
         }
+        if ns is not None:
+            out["muon_ns"] = ns
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline(total)
         print(json.dumps(out), flush=True)
@@ -355,6 +458,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--layers", type=int, default=32, help="decoder layers (32 = the full model; fewer for profiling)")
     ap.add_argument("--no-embed", action="store_true", help="leave out embed/lm_head (profiling only)")
+    ap.add_argument("--no-ns", action="store_true", help="skip the Muon Newton-Schulz leg")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
