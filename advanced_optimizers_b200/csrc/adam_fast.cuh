@@ -1,18 +1,81 @@
 // Fast path of the Adam-family step (included by adam_impl.cuh users).
 //
-// Same arithmetic as adam_kernel (op for op), restricted to the common
-// configurations: no atan2 / normed momentum / Fisher / centered anchors, and
-// factored tensors only with d2 >= 2048, d2 % 8 == 0 (every Llama-shaped
-// effective shape).  Differences in structure:
+// Same arithmetic as adam_kernel (op for op, same roundings), restricted to
+// the common configurations: no atan2 / normed momentum / Fisher / centered
+// anchors, and factored tensors only with d2 >= 2048, d2 % 8 == 0 (every
+// Llama-shaped effective shape).  Differences in structure:
 //   * each chunk's inputs (grad, param, m codes, v codes) stream into a ring
 //     of shared-memory stages with cp.async.bulk (TMA bulk copies, no
-//     multicast) completed on mbarriers, `stages` chunks ahead, so memory
-//     latency is hidden without holding prefetched data in registers;
+//     multicast) completed on mbarriers, `stages` chunks ahead;
 //   * element arithmetic runs on fp32x2 lanes (sm_100 packed FFMA2/FADD2/FMUL2);
+//   * the per-element square root and division use Newton–Markstein
+//     sequences (below) that are correctly rounded on the value ranges a
+//     thread checks for; a warp with any element outside them recomputes its
+//     chunk with the IEEE intrinsics;
+//   * block maxima use warp max-reductions of the float bit patterns
+//     (redux.sync), factored row sums are reduced across the CTA once per row;
 //   * waits are bounded: a wait that gives up sets *L.err and the CTA stops.
 #pragma once
 
+#include <type_traits>
+
 namespace advopt {
+
+// ---------------------------------------------------------------------------
+// Correctly rounded sqrt and division by Newton–Markstein iteration
+// (P. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Dev. 34(1), 1990; J.-M. Muller et al.,
+// Handbook of Floating-Point Arithmetic, ch. 5):
+//   sqrt(v): y ~ 1/sqrt(v) (hardware estimate), s = v*y, r = v - s*s (exact
+//            by FMA), s' = s + r*(y/2);
+//   u / d:   y ~ 1/d (hardware estimate), y1 = y + y*(1 - d*y), q = u*y1,
+//            r = u - q*d (exact by FMA), q' = q + r*y1.
+// Checked on B200 against __fsqrt_rn / __fdiv_rn: the square root matches for
+// every float in [2^-102, FLT_MAX]; the quotient matches (every divisor
+// mantissa x 64 dividend mantissas per exponent pair, dividends down to the
+// subnormals) whenever |u| >= 2^-102 or u = 0, and the quotient is normal.
+// The fast path therefore requires v >= 2^-100 (so d >= 2^-50), d <= 2^24 and
+// |u| >= 2^-100 (so 2^-124 <= |q| <= |u| * 2^50; |u| large enough to overflow
+// comes only with an infinite v, which fails d <= 2^24); a warp with any
+// element outside takes the IEEE path.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float rsqrt_est(float x) {
+  float y;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_est(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float2 neg2(float2 a) { return make_float2(-a.x, -a.y); }
+
+__device__ __forceinline__ float2 sqrt_nm2(float2 v) {
+  const float2 y = make_float2(rsqrt_est(v.x), rsqrt_est(v.y));
+  const float2 s = mul2(v, y);
+  const float2 h = mul2(y, splat2(0.5f));
+  const float2 r = fma2(neg2(s), s, v);
+  return fma2(r, h, s);
+}
+__device__ __forceinline__ float2 div_nm2(float2 u, float2 d) {
+  const float2 y = make_float2(rcp_est(d.x), rcp_est(d.y));
+  const float2 e = fma2(neg2(d), y, splat2(1.0f));
+  const float2 y1 = fma2(e, y, y);
+  const float2 q = mul2(u, y1);
+  const float2 r = fma2(neg2(q), d, u);
+  return fma2(r, y1, q);
+}
 
 template <int PREC, bool PBF>
 struct FastLayout {
@@ -115,57 +178,243 @@ __device__ __forceinline__ void lds_words(const unsigned char* s, Words<BPE>& ou
   }
 }
 
+// Eight values as four fp32 pairs: BPE 4 = f32, 2 = bf16, 1 = int8 (SIGNED) /
+// uint8 codes (exact via 2^23 + byte, minus the bias on packed lanes).
 template <int BPE, bool SIGNED>
 __device__ __forceinline__ void unpack8x2(const Words<BPE>& in, float2 (&x)[4]) {
-  float t[8];
-  unpack8<BPE, SIGNED>(in, t);
+  if (BPE == 4) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i) x[i] = make_float2(t[2 * i], t[2 * i + 1]);
+    for (int i = 0; i < 4; ++i) x[i] = make_float2(__uint_as_float(in.w[2 * i]), __uint_as_float(in.w[2 * i + 1]));
+  } else if (BPE == 2) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = make_float2(__uint_as_float(in.w[i] << 16), __uint_as_float(in.w[i] & 0xFFFF0000u));
+  } else {
+    const float bias = SIGNED ? -8388736.0f : -8388608.0f;  // -(2^23 + 128) | -2^23
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t w = SIGNED ? (in.w[h] ^ 0x80808080u) : in.w[h];
+      const float2 a = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440)),
+                                   __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441)));
+      const float2 b = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7442)),
+                                   __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7443)));
+      x[2 * h] = add2(a, splat2(bias));
+      x[2 * h + 1] = add2(b, splat2(bias));
+    }
+  }
 }
 
-// Two-lane stochastic quantisation with a per-block divisor; returns the
-// packed codes of 8 values.
+// Stochastic quantisation of 8 values with the block divisor (set_state,
+// state_util.py:124-157): code = clamp(floor(x/safe + r/65536)) with
+// scale = bmax/127 (int8) or bmax/255 (uint8) and safe = max(scale, 1e-12).
+// scale is the Markstein quotient with the correctly rounded reciprocal of
+// the constant (exact for bmax >= 2^-90; below that every code is 0 or -1
+// by the sign, and the block scale is written by the IEEE division).  x/safe
+// is the Newton–Markstein quotient (exact for |x| >= 2^-102 with |x/safe| <=
+// 127; for smaller |x| only the quotient's sign reaches the floor).  floor(y)
+// comes from y + 1.5*2^23 rounded down, whose low byte is the
+// two's-complement code.
 template <bool SIGNED>
-__device__ __forceinline__ uint2 quantize8x2(const float2 (&x)[4], float bmax, const U4& nz) {
-  const float scale = __fdiv_rn(bmax, SIGNED ? 127.0f : 255.0f);
+__device__ __forceinline__ float block_scale(float bmax) {
+  // RN(1/127), RN(1/255) as exact float literals
+  return bmax >= 0x1p-90f ? div_rcp(bmax, SIGNED ? 127.0f : 255.0f, SIGNED ? 0x1.020408p-7f : 0x1.010102p-8f)
+                           : __fdiv_rn(bmax, SIGNED ? 127.0f : 255.0f);
+}
+
+template <bool SIGNED>
+__device__ __forceinline__ uint2 quantize8x2(const float2 (&x)[4], float scale, const U4& nz) {
   const float safe = scale < 1e-12f ? 1e-12f : scale;
-  const float rs = __frcp_rn(safe);
-  bool tiny = false;
-#pragma unroll
-  // zeros are exact through div_rcp2 (and the noise add absorbs a -0); only
-  // nonzero magnitudes below 2^-100 need the IEEE division
-  for (int i = 0; i < 4; ++i)
-    tiny |= (fabsf(x[i].x) < 0x1p-100f && x[i].x != 0.0f) | (fabsf(x[i].y) < 0x1p-100f && x[i].y != 0.0f);
-  const bool any_tiny = __any_sync(0xffffffffu, tiny);
+  const float y0 = rcp_est(safe);
+  const float y1 = __fmaf_rn(__fmaf_rn(-safe, y0, 1.0f), y0, y0);
   const uint32_t nw[4] = {nz.x, nz.y, nz.z, nz.w};
-  int c[8];
+  uint32_t f[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float2 q = div_rcp2(x[i], safe, rs);
-    if (any_tiny) {
-      if (fabsf(x[i].x) < 0x1p-100f && x[i].x != 0.0f) q.x = __fdiv_rn(x[i].x, safe);
-      if (fabsf(x[i].y) < 0x1p-100f && x[i].y != 0.0f) q.y = __fdiv_rn(x[i].y, safe);
-    }
+    const float2 q0 = mul2(x[i], splat2(y1));
+    const float2 q = fma2(fma2(neg2(q0), splat2(safe), x[i]), splat2(y1), q0);
     // noise r * 2^-16 from bits: (1 + r*2^-16) - 1
     const float2 n1 = make_float2(__uint_as_float(0x3F800000u | ((nw[i] & 0xFFFFu) << 7)),
                                   __uint_as_float(0x3F800000u | ((nw[i] >> 16) << 7)));
-    const float2 noise = add2(n1, splat2(-1.0f));
-    const float2 y = add2(q, noise);
-    const float2 f = __fadd2_rd(y, splat2(12582912.0f));   // 1.5*2^23 + floor(y)
-    const int f0 = (int)(__float_as_uint(f.x) - 0x4B400000u), f1 = (int)(__float_as_uint(f.y) - 0x4B400000u);
-    c[2 * i] = SIGNED ? min(max(f0, -127), 127) : min(max(f0, 0), 255);
-    c[2 * i + 1] = SIGNED ? min(max(f1, -127), 127) : min(max(f1, 0), 255);
+    float2 y = add2(q, add2(n1, splat2(-1.0f)));
+    // int8: floor(y) >= -128 needs the lower clamp only (y < 128 when
+    // |x| <= bmax); uint8: y can reach 256.0 exactly, so clamp above too
+    if (SIGNED) y = make_float2(fmaxf(y.x, -127.0f), fmaxf(y.y, -127.0f));
+    else y = make_float2(fminf(fmaxf(y.x, 0.0f), 255.5f), fminf(fmaxf(y.y, 0.0f), 255.5f));
+    const float2 F = __fadd2_rd(y, splat2(12582912.0f));   // 1.5*2^23 + floor(y)
+    f[2 * i] = __float_as_uint(F.x);
+    f[2 * i + 1] = __float_as_uint(F.y);
   }
-  return make_uint2(pack4_bytes(c[0], c[1], c[2], c[3]), pack4_bytes(c[4], c[5], c[6], c[7]));
+  const uint32_t a0 = __byte_perm(f[0], f[1], 0x0040), a1 = __byte_perm(f[2], f[3], 0x0040);
+  const uint32_t b0 = __byte_perm(f[4], f[5], 0x0040), b1 = __byte_perm(f[6], f[7], 0x0040);
+  return make_uint2(__byte_perm(a0, a1, 0x5410), __byte_perm(b0, b1, 0x5410));
 }
 
+// One thread's inputs of one chunk as loaded (packed words: bf16 pairs,
+// int8 quads, ...); the element math unpacks one pair at a time, which keeps
+// the live register set small.
+template <int PREC, bool PBF>
+struct FastIn {
+  using LY = FastLayout<PREC, PBF>;
+  Words<LY::BPP> g, p;
+  Words<LY::BPS> m, v;
+  float ms, vs, mu;
+  float4 mva, mvb;
+};
+
+template <int PREC, bool PBF>
+__device__ __forceinline__ void fast_load(const TensorRegs& T, const unsigned char* st, bool dir, int64_t k0, int nv,
+                                          bool v8, bool has_m, bool fact, FastIn<PREC, PBF>& in) {
+  using LY = FastLayout<PREC, PBF>;
+  constexpr int SB = LY::BPS;
+  const int tid = threadIdx.x;
+  if (dir) {
+    ld_words<LY::BPP>(T.grad, k0, nv, v8, in.g);
+    ld_words<LY::BPP>(T.param, k0, nv, v8, in.p);
+    if (has_m) ld_words<SB>(T.m, k0, nv, v8, in.m);
+    if (!fact) ld_words<SB>(T.v, k0, nv, v8, in.v);
+  } else {
+    lds_words<LY::BPP>(st + LY::G + tid * kVec * LY::BPP, in.g);
+    lds_words<LY::BPP>(st + LY::P + tid * kVec * LY::BPP, in.p);
+    if (has_m) lds_words<SB>(st + LY::M + tid * kVec * SB, in.m);
+    if (!fact) lds_words<SB>(st + LY::V + tid * kVec * SB, in.v);
+  }
+}
+
+// Pair i (elements 2i, 2i+1) of 8 packed values: BPE 4 = f32, 2 = bf16,
+// 1 = int8 (SIGNED) / uint8 codes (exact via 2^23 + byte, minus the bias).
+template <int BPE, bool SIGNED>
+__device__ __forceinline__ float2 pair_of(const Words<BPE>& in, int i) {
+  if (BPE == 4) return make_float2(__uint_as_float(in.w[2 * i]), __uint_as_float(in.w[2 * i + 1]));
+  if (BPE == 2) return make_float2(__uint_as_float(in.w[i] << 16), __uint_as_float(in.w[i] & 0xFFFF0000u));
+  const uint32_t w0 = in.w[i >> 1];
+  const uint32_t w = SIGNED ? (w0 ^ 0x80808080u) : w0;
+  const uint32_t sel = (i & 1) ? 0x7442u : 0x7440u;
+  const float2 a = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, sel)),
+                               __uint_as_float(__byte_perm(w, 0x4B000000u, sel + 1)));
+  return add2(a, splat2(SIGNED ? -8388736.0f : -8388608.0f));   // -(2^23 + 128) | -2^23
+}
+
+// Uniform scalars of the element math.
+struct FastScalars {
+  float beta1, beta2, c_v, c_m, w_m, w_m1, w_n, w_n1, d;
+  float sbc2, rcp_sbc2, eps, step_size, wd;
+  bool w_m_small, w_n_small, has_m, nest, cautious, sr, fact;
+};
+
+// Element math of one thread's 8 values (AdamW_adv.py:401-465,
+// Muon_AuxAdam.py:148-192, Prodigy_adv.py:430-519, param_update.py:77-156).
+// FAST: Newton–Markstein sqrt / division; `hard` reports elements outside
+// their exact range.  Outputs the new m, the new v (factored: before the
+// factor rebuild) and the packed param words (bf16 pairs after stochastic
+// rounding or RNE; f32 values).
+template <int PREC, bool PBF, int ALGO, bool FAST>
+__device__ __forceinline__ void fast_math(const FastIn<PREC, PBF>& in, const FastScalars& S, int nv,
+                                          const uint32_t (&npw)[4], float2 (&m_new)[4], float2 (&v)[4],
+                                          uint32_t (&pw)[PBF ? 4 : 8], bool& hard) {
+  using TR = StateTraits<PREC, PBF>;
+  using LY = FastLayout<PREC, PBF>;
+  constexpr bool kMBF = TR::kMathBF;
+  constexpr int kStore = TR::kStore;
+  auto Rm2 = [](float2 x) { return kMBF ? make_float2(round_bf16(x.x), round_bf16(x.y)) : x; };
+  const bool vbf = kMBF && !S.fact;
+  float lo = 0x1p100f, hi = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 gi = pair_of<LY::BPP, true>(in.g, i);
+    float2 vh;
+    if (S.fact) {
+      const float2 mv = (i == 0) ? make_float2(in.mva.x, in.mva.y) : (i == 1) ? make_float2(in.mva.z, in.mva.w)
+                      : (i == 2) ? make_float2(in.mvb.x, in.mvb.y) : make_float2(in.mvb.z, in.mvb.w);
+      vh = mul2(splat2(in.mu), mv);
+    } else {
+      vh = pair_of<LY::BPS, false>(in.v, i);
+      if (kStore == 2) vh = mul2(vh, splat2(in.vs));
+    }
+    // v = v*beta2 + c_v*g*g  (factored v is >= 0, so its abs() is the identity)
+    float2 vi = mul2(vh, splat2(S.beta2));
+    if (vbf) vi = make_float2(round_bf16(vi.x), round_bf16(vi.y));
+    vi = fma2(mul2(splat2(S.c_v), gi), gi, vi);
+    if (vbf) vi = make_float2(round_bf16(vi.x), round_bf16(vi.y));
+    v[i] = vi;
+    float2 ui;
+    if (S.has_m) {
+      float2 m0 = pair_of<LY::BPS, true>(in.m, i);
+      if (kStore == 2) m0 = mul2(m0, splat2(in.ms));
+      float2 mi;
+      if (ALGO == ADVOPT_ALGO_PRODIGY) mi = Rm2(fma2(gi, splat2(S.c_m), Rm2(mul2(m0, splat2(S.beta1)))));
+      else mi = Rm2(lerp2(m0, gi, S.w_m, S.w_m1, S.w_m_small));
+      m_new[i] = mi;
+      ui = S.nest ? Rm2(lerp2(mi, gi, S.w_n, S.w_n1, S.w_n_small)) : mi;
+    } else {
+      m_new[i] = splat2(0.0f);
+      ui = (ALGO == ADVOPT_ALGO_PRODIGY) ? Rm2(mul2(gi, splat2(S.d))) : gi;
+    }
+    // denominator
+    float2 den;
+    if (FAST) {
+      lo = min3f(lo, vi.x, vi.y);
+      lo = min3f(lo, fabsf(ui.x), fabsf(ui.y));
+      den = sqrt_nm2(vi);
+    } else {
+      den = make_float2(__fsqrt_rn(vi.x), __fsqrt_rn(vi.y));
+    }
+    if (vbf) den = make_float2(round_bf16(den.x), round_bf16(den.y));
+    if (ALGO != ADVOPT_ALGO_PRODIGY) {
+      den = div_rcp2(den, S.sbc2, S.rcp_sbc2);
+      if (vbf) den = make_float2(round_bf16(den.x), round_bf16(den.y));
+    }
+    den = add2(den, splat2(S.eps));
+    if (vbf) den = make_float2(round_bf16(den.x), round_bf16(den.y));
+    const float2 du = kMBF ? make_float2(round_bf16(den.x), round_bf16(den.y)) : den;
+    if (FAST) hi = max3f(hi, du.x, du.y);
+    ui = FAST ? div_nm2(ui, du) : make_float2(__fdiv_rn(ui.x, du.x), __fdiv_rn(ui.y, du.y));
+    ui = Rm2(ui);
+    ui = Rm2(mul2(ui, splat2(S.step_size)));
+    if (!(2 * i < nv)) { m_new[i].x = 0.0f; v[i].x = 0.0f; }
+    if (!(2 * i + 1 < nv)) { m_new[i].y = 0.0f; v[i].y = 0.0f; }
+    // parameter update (param_update.py:77-156)
+    float2 pc2 = pair_of<LY::BPP, true>(in.p, i);
+    if (S.wd != 0.0f) {
+      if (S.cautious) {
+        float2 prod = mul2(ui, pc2);
+        if (PBF && !S.sr) prod = make_float2(round_bf16(prod.x), round_bf16(prod.y));
+        const float2 mask = make_float2(prod.x >= 0.0f ? 1.0f : 0.0f, prod.y >= 0.0f ? 1.0f : 0.0f);
+        pc2 = fma2(mul2(splat2(-S.wd), pc2), mask, pc2);
+      } else {
+        pc2 = fma2(pc2, splat2(-S.wd), pc2);
+      }
+      if (PBF && !S.sr) pc2 = make_float2(round_bf16(pc2.x), round_bf16(pc2.y));
+    }
+    const float2 pn = add2(pc2, neg2(ui));
+    if (PBF) {
+      if (S.sr)
+        pw[i] = __byte_perm(__float_as_uint(pn.x) + (npw[i] & 0xFFFFu), __float_as_uint(pn.y) + (npw[i] >> 16), 0x7632);
+      else
+        pw[i] = f_to_bf16_rne(pn.x) | (f_to_bf16_rne(pn.y) << 16);
+    } else {
+      pw[2 * i] = __float_as_uint(pn.x);
+      pw[2 * i + 1] = __float_as_uint(pn.y);
+    }
+  }
+  // NaN inputs fail both comparisons and take the IEEE path as well
+  hard = FAST && !(lo >= 0x1p-100f && hi <= 0x1p24f);
+}
+
+__device__ __forceinline__ uint32_t fbits_max_warp(float a) {
+  return __reduce_max_sync(0xffffffffu, __float_as_uint(a));
+}
+
+// Resident CTAs per SM the register budget is sized for: three for the
+// int8_sr / bf16 Adam step (the Llama configuration), two elsewhere.
+template <int PREC, bool PBF, int ALGO>
+struct FastOcc {
+  static constexpr int v = (PREC == ADVOPT_PREC_INT8_SR && PBF && ALGO != ADVOPT_ALGO_PRODIGY) ? 3 : 2;
+};
+
 template <int PREC, bool PBF, int ALGO, bool NOISE_IN>
-__global__ void __launch_bounds__(kThreads, 2) adam_fast_kernel(const advopt_adam_launch L) {
+__global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v)) adam_fast_kernel(const advopt_adam_launch L) {
   using TR = StateTraits<PREC, PBF>;
   using LY = FastLayout<PREC, PBF>;
   constexpr int kStore = TR::kStore;
-  constexpr bool kMBF = TR::kMathBF;
-  constexpr int SB = LY::BPS;
   constexpr int kMaxStages = 4;
   extern __shared__ float4 dsm4[];
   float* colacc = reinterpret_cast<float*>(dsm4);
@@ -173,30 +422,39 @@ __global__ void __launch_bounds__(kThreads, 2) adam_fast_kernel(const advopt_ada
   __shared__ uint64_t bars[kMaxStages];
   __shared__ int direct[kMaxStages];
   __shared__ int abort_flag;
-  __shared__ float red[2][kWarps][4];
+  __shared__ uint32_t redm[2][kWarps], redv[2][kWarps];
+  __shared__ float redr[2][kWarps];
   __shared__ double dred[kWarps][2];
   __shared__ TensorRegs Ts;
+  __shared__ Cursor cur;          // producer state (thread 0 only)
+  __shared__ int cur_valid;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int S = L.stages;
   const uint32_t F = L.flags;
   const bool has_m = F & ADVOPT_F_HAS_M;
-  const bool nest = F & ADVOPT_F_NESTEROV;
-  const bool cautious = F & ADVOPT_F_CAUTIOUS;
-  const bool sr = PBF && (F & ADVOPT_F_SR);
   const bool pstats = (ALGO == ADVOPT_ALGO_PRODIGY) && (F & ADVOPT_F_PRODIGY_STATS);
-  const float beta1 = L.beta1, beta2 = L.beta2, c_v = L.c_v, c_m = L.c_m;
-  const float w_m = L.w_m, w_m1 = __fsub_rn(L.w_m, 1.0f), w_n = L.w_nest, w_n1 = __fsub_rn(L.w_nest, 1.0f);
-  const bool w_m_small = fabsf(w_m) < 0.5f, w_n_small = fabsf(w_n) < 0.5f;
-  auto Rm = [](float x) { return kMBF ? round_bf16(x) : x; };
-  auto Rm2 = [](float2 x) { return kMBF ? make_float2(round_bf16(x.x), round_bf16(x.y)) : x; };
+  FastScalars SC;
+  SC.beta1 = L.beta1;
+  SC.beta2 = L.beta2;
+  SC.c_v = L.c_v;
+  SC.c_m = L.c_m;
+  SC.w_m = L.w_m;
+  SC.w_m1 = __fsub_rn(L.w_m, 1.0f);
+  SC.w_n = L.w_nest;
+  SC.w_n1 = __fsub_rn(L.w_nest, 1.0f);
+  SC.d = L.d;
+  SC.w_m_small = fabsf(L.w_m) < 0.5f;
+  SC.w_n_small = fabsf(L.w_nest) < 0.5f;
+  SC.has_m = has_m;
+  SC.nest = F & ADVOPT_F_NESTEROV;
+  SC.cautious = F & ADVOPT_F_CAUTIOUS;
+  SC.sr = PBF && (F & ADVOPT_F_SR);
 
   const int pbeg = L.cta_offsets[blockIdx.x], pend = L.cta_offsets[blockIdx.x + 1];
   if (pbeg >= pend) return;
 
   // ---- producer prologue: fill the ring ----
-  Cursor cur{};
-  bool cur_valid = false;
   if (tid == 0) {
     abort_flag = 0;
     for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
@@ -222,41 +480,63 @@ __global__ void __launch_bounds__(kThreads, 2) adam_fast_kernel(const advopt_ada
     const bool fact = T.flags & ADVOPT_T_FACTORED;
     const bool vec = T.flags & ADVOPT_T_VEC;
     const int64_t d2 = fact ? T.d2 : 1;
-    const bool vbf = kMBF && !fact;
-    const float sbc2 = T.sqrt_bc2, rcp_sbc2 = __frcp_rn(T.sqrt_bc2), eps = T.eps, step_size = T.step_size, wd = T.wd;
+    // factored tensors wider than the shared-memory accumulator keep their
+    // column partials in their own global slot row (read-modify-write)
+    const bool col_global = fact && d2 > (int64_t)L.gen_offset;
+    float* colrow = fact ? (col_global ? T.colpart + (int64_t)pc.slot * d2 : colacc) : nullptr;
+    SC.fact = fact;
+    SC.sbc2 = T.sqrt_bc2;
+    SC.rcp_sbc2 = __frcp_rn(T.sqrt_bc2);
+    SC.eps = T.eps;
+    SC.step_size = T.step_size;
+    SC.wd = T.wd;
     if (fact) {
       for (int j2 = tid * 4; j2 < (int)d2; j2 += kThreads * 4)
-        *reinterpret_cast<float4*>(colacc + j2) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(colrow + j2) = make_float4(0.f, 0.f, 0.f, 0.f);
       __syncthreads();
     }
     int64_t r0 = fact ? pc.begin / d2 : 0;
     int64_t c0 = fact ? pc.begin - r0 * d2 : 0;
-    double row_carry = 0.0, st0 = 0.0, st1 = 0.0;
+    float racc0 = 0.0f, racc1 = 0.0f;   // this thread's part of rows r0 and r0 + 1
+    double st0 = 0.0, st1 = 0.0;
     const uint32_t slice_p = T.slice_p ? T.slice_p : 1u;
 
-    for (int64_t cs = pc.begin; cs < pc.end; cs += kChunk, ++j) {
+    // One chunk; FULL: all 2048 elements present and 16-byte aligned (the
+    // common case, with the tail predicates compiled out).  Returns false
+    // when a bounded wait gave up.
+    auto chunk = [&](int64_t cs, auto full_tag, auto fact_tag) -> bool {
+      constexpr bool kFull = decltype(full_tag)::value;
+      constexpr bool fact = decltype(fact_tag)::value;   // shadows the piece's flag
       const int slot = (int)(j % (uint32_t)S);
       const uint32_t par = (j / (uint32_t)S) & 1u;
-      const int clen = (int)min((int64_t)kChunk, pc.end - cs);
+      const int clen = kFull ? kChunk : (int)min((int64_t)kChunk, pc.end - cs);
       const int64_t k0 = cs + tid * kVec;
-      const int nv = max(0, min(kVec, clen - tid * kVec));
-      const bool v8 = vec && nv == kVec;
+      const int nv = kFull ? kVec : max(0, min(kVec, clen - tid * kVec));
+      const bool v8 = kFull ? true : (vec && nv == kVec);
       const int64_t blk = cs >> 11;
-      // factored column factors of this chunk (L2-resident; issued before the wait)
-      float mu = 0.0f;
-      float4 mva = make_float4(0.f, 0.f, 0.f, 0.f), mvb = mva;
       int64_t col = 0;
       bool second = false;
       if (fact) {
         const int64_t cc = c0 + tid * kVec;
         second = cc >= d2;
         col = second ? cc - d2 : cc;
-        mu = nv > 0 ? T.row[r0 + (second ? 1 : 0)] : 0.0f;
-        mva = *reinterpret_cast<const float4*>(T.col + col);
-        mvb = *(reinterpret_cast<const float4*>(T.col + col) + 1);
       }
-      const float ms = (has_m && kStore == 2) ? T.m_scale[blk] : 0.0f;
-      const float vs = (!fact && kStore == 2) ? T.v_scale[blk] : 0.0f;
+      // per-chunk scalars and factored column factors (L2-resident; issued
+      // before the wait, and again by the IEEE path)
+      auto load_scalars = [&](FastIn<PREC, PBF>& in) {
+        in.mu = 0.0f;
+        in.mva = make_float4(0.f, 0.f, 0.f, 0.f);
+        in.mvb = in.mva;
+        if (fact) {
+          in.mu = nv > 0 ? T.row[r0 + (second ? 1 : 0)] : 0.0f;
+          in.mva = *reinterpret_cast<const float4*>(T.col + col);
+          in.mvb = *(reinterpret_cast<const float4*>(T.col + col) + 1);
+        }
+        in.ms = (has_m && kStore == 2) ? T.m_scale[blk] : 0.0f;
+        in.vs = (!fact && kStore == 2) ? T.v_scale[blk] : 0.0f;
+      };
+      FastIn<PREC, PBF> in;
+      load_scalars(in);
       if (!mbar_wait(&bars[slot], par)) {
         // the copies never arrived: report, finish this chunk on whatever is
         // in the stage, and leave uniformly after the next barrier
@@ -264,233 +544,141 @@ __global__ void __launch_bounds__(kThreads, 2) adam_fast_kernel(const advopt_ada
         if (L.err) atomicExch(L.err, 1);
       }
       const unsigned char* st = stages + (size_t)slot * LY::BYTES;
-      const bool dir = direct[slot] != 0;
-      Words<LY::BPP> wg, wp;
-      Words<SB> wm, wv;
-      if (dir) {
-        ld_words<LY::BPP>(T.grad, k0, nv, v8, wg);
-        ld_words<LY::BPP>(T.param, k0, nv, v8, wp);
-        if (has_m) ld_words<SB>(T.m, k0, nv, v8, wm);
-        if (!fact) ld_words<SB>(T.v, k0, nv, v8, wv);
-      } else {
-        lds_words<LY::BPP>(st + LY::G + tid * kVec * LY::BPP, wg);
-        lds_words<LY::BPP>(st + LY::P + tid * kVec * LY::BPP, wp);
-        if (has_m) lds_words<SB>(st + LY::M + tid * kVec * SB, wm);
-        if (!fact) lds_words<SB>(st + LY::V + tid * kVec * SB, wv);
-      }
-      float2 g[4], p[4], m[4], vh[4];
-      unpack8x2<LY::BPP, true>(wg, g);
-      unpack8x2<LY::BPP, true>(wp, p);
-      if (has_m) {
-        unpack8x2<SB, true>(wm, m);
-        if (kStore == 2) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) m[i] = mul2(m[i], splat2(ms));
-        }
-      }
-      if (fact) {
-        const float2 mu2 = splat2(mu);
-        vh[0] = mul2(mu2, make_float2(mva.x, mva.y));
-        vh[1] = mul2(mu2, make_float2(mva.z, mva.w));
-        vh[2] = mul2(mu2, make_float2(mvb.x, mvb.y));
-        vh[3] = mul2(mu2, make_float2(mvb.z, mvb.w));
-      } else {
-        unpack8x2<SB, false>(wv, vh);
-        if (kStore == 2) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) vh[i] = mul2(vh[i], splat2(vs));
-        }
-      }
+      const bool dir = kFull ? false : (direct[slot] != 0);
+      fast_load<PREC, PBF>(T, st, dir, k0, nv, v8, has_m, fact, in);
       U4 nzp{0u, 0u, 0u, 0u};
-      if (sr) nzp = noise_words<NOISE_IN>(L, T, T.nz_p, kNoiseP, k0, nv);
+      if (SC.sr) nzp = noise_words<NOISE_IN>(L, T, T.nz_p, kNoiseP, k0, nv);
       const uint32_t npw[4] = {nzp.x, nzp.y, nzp.z, nzp.w};
-      int slice_off = 0;
-      if (pstats) slice_off = (int)((slice_p - (uint32_t)(k0 % slice_p)) % slice_p);
-
       float2 m_new[4], v[4];
-      float amax_m = 0.0f, vmax = 0.0f;
-      uint32_t pout[8];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 gi = g[i];
-        // v = v*beta2 + c_v*g*g
-        float2 vi = mul2(vh[i], splat2(beta2));
-        if (vbf) vi = make_float2(round_bf16(vi.x), round_bf16(vi.y));
-        vi = fma2(mul2(splat2(c_v), gi), gi, vi);
-        if (vbf) vi = make_float2(round_bf16(vi.x), round_bf16(vi.y));
-        if (fact) vi = make_float2(fabsf(vi.x), fabsf(vi.y));
-        v[i] = vi;
-        // denominator
-        float2 den = make_float2(__fsqrt_rn(vi.x), __fsqrt_rn(vi.y));
-        if (vbf) den = make_float2(round_bf16(den.x), round_bf16(den.y));
-        if (ALGO != ADVOPT_ALGO_PRODIGY) {
-          den = div_rcp2(den, sbc2, rcp_sbc2);
-          if (vbf) den = make_float2(round_bf16(den.x), round_bf16(den.y));
-        }
-        den = add2(den, splat2(eps));
-        if (vbf) den = make_float2(round_bf16(den.x), round_bf16(den.y));
-        const float2 du = kMBF ? make_float2(round_bf16(den.x), round_bf16(den.y)) : den;
-        float2 ui;
-        if (has_m) {
-          float2 mi;
-          if (ALGO == ADVOPT_ALGO_PRODIGY) mi = Rm2(fma2(gi, splat2(c_m), Rm2(mul2(m[i], splat2(beta1)))));
-          else mi = Rm2(lerp2(m[i], gi, w_m, w_m1, w_m_small));
-          m_new[i] = mi;
-          ui = nest ? Rm2(lerp2(mi, gi, w_n, w_n1, w_n_small)) : mi;
-        } else {
-          m_new[i] = splat2(0.0f);
-          ui = (ALGO == ADVOPT_ALGO_PRODIGY) ? Rm2(mul2(gi, splat2(L.d))) : gi;
-        }
-        ui = make_float2(Rm(__fdiv_rn(ui.x, du.x)), Rm(__fdiv_rn(ui.y, du.y)));
-        ui = Rm2(mul2(ui, splat2(step_size)));
-        const bool ok0 = 2 * i < nv, ok1 = 2 * i + 1 < nv;
-        if (!ok0) { m_new[i].x = 0.0f; v[i].x = 0.0f; }
-        if (!ok1) { m_new[i].y = 0.0f; v[i].y = 0.0f; }
-        amax_m = fmaxf(amax_m, fmaxf(fabsf(m_new[i].x), fabsf(m_new[i].y)));
-        vmax = fmaxf(vmax, fmaxf(v[i].x, v[i].y));
+      uint32_t pw[PBF ? 4 : 8];
+      bool hard = false;
+      fast_math<PREC, PBF, ALGO, true>(in, SC, nv, npw, m_new, v, pw, hard);
+      if (__any_sync(0xffffffffu, hard)) {
+        // some lane of the warp is outside the Newton–Markstein ranges:
+        // recompute the warp's elements with the IEEE operations
+        bool h2;
+        fast_math<PREC, PBF, ALGO, false>(in, SC, nv, npw, m_new, v, pw, h2);
+      }
 
-        if (pstats) {
+      if (pstats) {
+        // Prodigy slice statistics on p before the update (Prodigy_adv.py:494-509)
+        const int slice_off = (int)((slice_p - (uint32_t)(k0 % slice_p)) % slice_p);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int e = 2 * i + h;
-            if (e < nv && e >= slice_off && ((e - slice_off) % (int)slice_p) == 0) {
-              const float gv = h ? gi.y : gi.x, pv = h ? p[i].y : p[i].x;
-              const int64_t si = (k0 + e) / slice_p;
-              float p0v = 0.0f;
-              if (!(T.flags & ADVOPT_T_P0_SCALAR))
-                p0v = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux1)[si]) : static_cast<const float*>(T.aux1)[si];
-              st0 += (double)gv * (double)__fsub_rn(p0v, pv);
-              const float s_old = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux0)[si])
-                                      : static_cast<const float*>(T.aux0)[si];
-              float s1 = __fmul_rn(s_old, L.beta3);
-              if (PBF) s1 = round_bf16(s1);
-              float s2 = __fmaf_rn(gv, L.s_alpha, s1);
-              if (PBF) {
-                const uint32_t b = f_to_bf16_rne(s2);
-                static_cast<uint16_t*>(T.aux0)[si] = (uint16_t)b;
-                s2 = bf16_to_f(b);
-              } else {
-                static_cast<float*>(T.aux0)[si] = s2;
-              }
-              st1 += (double)fabsf(s2);
+        for (int e = 0; e < 8; ++e) {
+          if (e < nv && e >= slice_off && ((e - slice_off) % (int)slice_p) == 0) {
+            const float2 gp = pair_of<LY::BPP, true>(in.g, e >> 1), pp = pair_of<LY::BPP, true>(in.p, e >> 1);
+            const float gv = (e & 1) ? gp.y : gp.x;
+            const float pv = (e & 1) ? pp.y : pp.x;
+            const int64_t si = (k0 + e) / slice_p;
+            float p0v = 0.0f;
+            if (!(T.flags & ADVOPT_T_P0_SCALAR))
+              p0v = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux1)[si]) : static_cast<const float*>(T.aux1)[si];
+            st0 += (double)gv * (double)__fsub_rn(p0v, pv);
+            const float s_old = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux0)[si])
+                                    : static_cast<const float*>(T.aux0)[si];
+            float s1 = __fmul_rn(s_old, L.beta3);
+            if (PBF) s1 = round_bf16(s1);
+            float s2 = __fmaf_rn(gv, L.s_alpha, s1);
+            if (PBF) {
+              const uint32_t b = f_to_bf16_rne(s2);
+              static_cast<uint16_t*>(T.aux0)[si] = (uint16_t)b;
+              s2 = bf16_to_f(b);
+            } else {
+              static_cast<float*>(T.aux0)[si] = s2;
             }
+            st1 += (double)fabsf(s2);
           }
-        }
-        // parameter update (param_update.py:77-156)
-        float2 pc2 = p[i];
-        if (wd != 0.0f) {
-          if (cautious) {
-            float2 prod = mul2(ui, pc2);
-            if (PBF && !sr) prod = make_float2(round_bf16(prod.x), round_bf16(prod.y));
-            const float2 mask = make_float2(prod.x >= 0.0f ? 1.0f : 0.0f, prod.y >= 0.0f ? 1.0f : 0.0f);
-            pc2 = fma2(mul2(splat2(-wd), pc2), mask, pc2);
-          } else {
-            pc2 = fma2(pc2, splat2(-wd), pc2);
-          }
-          if (PBF && !sr) pc2 = make_float2(round_bf16(pc2.x), round_bf16(pc2.y));
-        }
-        const float2 pn = add2(pc2, make_float2(-ui.x, -ui.y));
-        if (PBF) {
-          if (sr) {
-            pout[2 * i] = __float_as_uint(pn.x) + (npw[i] & 0xFFFFu);
-            pout[2 * i + 1] = __float_as_uint(pn.y) + (npw[i] >> 16);
-          } else {
-            pout[2 * i] = f_to_bf16_rne(pn.x);
-            pout[2 * i + 1] = f_to_bf16_rne(pn.y);
-          }
-        } else {
-          pout[2 * i] = __float_as_uint(pn.x);
-          pout[2 * i + 1] = __float_as_uint(pn.y);
         }
       }
+
       // param store
       if (PBF) {
-        uint32_t o[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o[i] = sr ? __byte_perm(pout[2 * i], pout[2 * i + 1], 0x7632) : (pout[2 * i] | (pout[2 * i + 1] << 16));
         uint16_t* dst = static_cast<uint16_t*>(T.param) + k0;
         if (v8) {
-          *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
         } else {
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            if (e < nv) dst[e] = (uint16_t)(o[e >> 1] >> (16 * (e & 1)));
+            if (e < nv) dst[e] = (uint16_t)(pw[e >> 1] >> (16 * (e & 1)));
         }
       } else {
         float* dst = static_cast<float*>(T.param) + k0;
         if (v8) {
-          reinterpret_cast<uint4*>(dst)[0] = make_uint4(pout[0], pout[1], pout[2], pout[3]);
-          reinterpret_cast<uint4*>(dst)[1] = make_uint4(pout[4], pout[5], pout[6], pout[7]);
+          reinterpret_cast<uint4*>(dst)[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+          reinterpret_cast<uint4*>(dst)[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);
         } else {
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            if (e < nv) dst[e] = __uint_as_float(pout[e]);
+            if (e < nv) dst[e] = __uint_as_float(pw[e]);
         }
       }
 
-      // factored: column partials (vector smem) and this thread's row part
-      float rsum0 = 0.0f, rsum1 = 0.0f;
+      // block maxima of the quantised states (bit patterns of non-negative
+      // floats order like the values)
+      if (has_m && kStore == 2) {
+        float a = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a = max3f(a, fabsf(m_new[i].x), fabsf(m_new[i].y));
+        const uint32_t wm = fbits_max_warp(a);
+        if (lane == 0) redm[parity][warp] = wm;
+      }
+      if (!fact && kStore == 2) {
+        float b = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) b = max3f(b, v[i].x, v[i].y);
+        const uint32_t wv = fbits_max_warp(b);
+        if (lane == 0) redv[parity][warp] = wv;
+      }
+      // factored: column partials and this thread's row parts
+      bool row_done = false;
       if (fact) {
         if (nv > 0) {
-          float4* ca = reinterpret_cast<float4*>(colacc + col);
+          float4* ca = reinterpret_cast<float4*>(colrow + col);
           float4 a = ca[0], b = ca[1];
           const float2 a01 = add2(make_float2(a.x, a.y), v[0]), a23 = add2(make_float2(a.z, a.w), v[1]);
           const float2 b01 = add2(make_float2(b.x, b.y), v[2]), b23 = add2(make_float2(b.z, b.w), v[3]);
           ca[0] = make_float4(a01.x, a01.y, a23.x, a23.y);
           ca[1] = make_float4(b01.x, b01.y, b23.x, b23.y);
         }
-        // same association as the general kernel: ((v0+v1)+(v2+v3)) + ((v4+v5)+(v6+v7))
-        const float2 pairs = add2(make_float2(v[0].x, v[2].x), make_float2(v[0].y, v[2].y));   // v0+v1, v4+v5
-        const float2 pairs2 = add2(make_float2(v[1].x, v[3].x), make_float2(v[1].y, v[3].y));  // v2+v3, v6+v7
-        const float2 halves = add2(pairs, pairs2);
-        const float sum = __fadd_rn(halves.x, halves.y);
-        if (second) rsum1 = sum; else rsum0 = sum;
-      }
-      // noise of the quantised states, drawn before the barrier
-      U4 nzm{0u, 0u, 0u, 0u}, nzv{0u, 0u, 0u, 0u};
-      if (kStore == 2 || TR::kSRStates) {
-        if (has_m) nzm = noise_words<NOISE_IN>(L, T, T.nz_m, kNoiseM, k0, nv);
-        if (!fact) nzv = noise_words<NOISE_IN>(L, T, T.nz_v, kNoiseV, k0, nv);
-      }
-      {
-        const float a = (has_m && kStore == 2) ? warp_max(amax_m) : 0.0f;
-        const float b = (!fact && kStore == 2) ? warp_max(vmax) : 0.0f;
-        const float c = fact ? warp_sum(rsum0) : 0.0f;
-        const float d = fact ? warp_sum(rsum1) : 0.0f;
-        if (lane == 0) {
-          red[parity][warp][0] = a;
-          red[parity][warp][1] = b;
-          red[parity][warp][2] = c;
-          red[parity][warp][3] = d;
+        const float2 s01 = add2(v[0], v[1]), s23 = add2(v[2], v[3]);
+        const float2 s = add2(s01, s23);
+        const float sum = __fadd_rn(s.x, s.y);
+        if (second) racc1 = __fadd_rn(racc1, sum);
+        else racc0 = __fadd_rn(racc0, sum);
+        row_done = clen >= d2 - c0;   // row r0 ends inside this chunk (uniform)
+        if (row_done) {
+          const float w = warp_sum(racc0);
+          if (lane == 0) redr[parity][warp] = w;
         }
       }
       __syncthreads();
-      if (abort_flag) return;   // every thread reads the same flag after the barrier
+      if (abort_flag) return false;   // every thread reads the same flag after the barrier
       // every thread is done with this stage: refill it with the chunk S ahead
       if (tid == 0 && cur_valid) {
         issue_chunk<PREC, PBF>(cur, stages + (size_t)slot * LY::BYTES, &bars[slot], &direct[slot], has_m);
         cur_valid = cursor_next<PREC, PBF>(L, cur, pend);
       }
-      if (fact && tid == 0) {
-        float s0 = 0.0f, s1 = 0.0f;
+      // noise of the quantised states
+      U4 nzm{0u, 0u, 0u, 0u}, nzv{0u, 0u, 0u, 0u};
+      if (kStore == 2 || TR::kSRStates) {
+        if (has_m) nzm = noise_words<NOISE_IN>(L, T, T.nz_m, kNoiseM, k0, nv);
+        if (!fact) nzv = noise_words<NOISE_IN>(L, T, T.nz_v, kNoiseV, k0, nv);
+      }
+      if (row_done) {
+        if (tid == 0) {
+          double t = 0.0;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) {
-          s0 = __fadd_rn(s0, red[parity][w][2]);
-          s1 = __fadd_rn(s1, red[parity][w][3]);
+          for (int w = 0; w < kWarps; ++w) t += (double)redr[parity][w];
+          T.row[r0] = (float)t;
         }
-        row_carry += (double)s0;
-        if (clen >= d2 - c0) {
-          T.row[r0] = (float)row_carry;
-          row_carry = (double)s1;
-        }
+        racc0 = racc1;
+        racc1 = 0.0f;
       }
       if (has_m) {
         if (kStore == 2) {
-          float bmax = 0.0f;
-#pragma unroll
-          for (int w = 0; w < kWarps; ++w) bmax = fmaxf(bmax, red[parity][w][0]);
-          const uint2 q = quantize8x2<true>(m_new, bmax, nzm);
+          const float bmax = __uint_as_float(__reduce_max_sync(0xffffffffu, redm[parity][lane & (kWarps - 1)]));
+          const float scale = block_scale<true>(bmax);
+          const uint2 q = quantize8x2<true>(m_new, scale, nzm);
           uint8_t* dst = static_cast<uint8_t*>(T.m) + k0;
           if (v8) {
             *reinterpret_cast<uint2*>(dst) = q;
@@ -499,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_fast_kernel(const advopt_ada
             for (int e = 0; e < 8; ++e)
               if (e < nv) dst[e] = (uint8_t)((e < 4 ? q.x : q.y) >> (8 * (e & 3)));
           }
-          if (tid == 0) T.m_scale[blk] = __fdiv_rn(bmax, 127.0f);
+          if (tid == 0) T.m_scale[blk] = scale;
         } else if (kStore == 1) {
           uint32_t b[8];
           const uint32_t nmw[4] = {nzm.x, nzm.y, nzm.z, nzm.w};
@@ -517,10 +705,9 @@ __global__ void __launch_bounds__(kThreads, 2) adam_fast_kernel(const advopt_ada
       }
       if (!fact) {
         if (kStore == 2) {
-          float bmax = 0.0f;
-#pragma unroll
-          for (int w = 0; w < kWarps; ++w) bmax = fmaxf(bmax, red[parity][w][1]);
-          const uint2 q = quantize8x2<false>(v, bmax, nzv);
+          const float bmax = __uint_as_float(__reduce_max_sync(0xffffffffu, redv[parity][lane & (kWarps - 1)]));
+          const float scale = block_scale<false>(bmax);
+          const uint2 q = quantize8x2<false>(v, scale, nzv);
           uint8_t* dst = static_cast<uint8_t*>(T.v) + k0;
           if (v8) {
             *reinterpret_cast<uint2*>(dst) = q;
@@ -529,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_fast_kernel(const advopt_ada
             for (int e = 0; e < 8; ++e)
               if (e < nv) dst[e] = (uint8_t)((e < 4 ? q.x : q.y) >> (8 * (e & 3)));
           }
-          if (tid == 0) T.v_scale[blk] = __fdiv_rn(bmax, 255.0f);
+          if (tid == 0) T.v_scale[blk] = scale;
         } else if (kStore == 1) {
           uint32_t b[8];
           const uint32_t nvw[4] = {nzv.x, nzv.y, nzv.z, nzv.w};
@@ -552,13 +739,24 @@ __global__ void __launch_bounds__(kThreads, 2) adam_fast_kernel(const advopt_ada
         }
       }
       parity ^= 1;
+      return true;
+    };
+    for (int64_t cs = pc.begin; cs < pc.end; cs += kChunk, ++j) {
+      const bool full = vec && (pc.end - cs >= kChunk);
+      const bool ok = full ? (fact ? chunk(cs, std::true_type{}, std::true_type{})
+                                   : chunk(cs, std::true_type{}, std::false_type{}))
+                           : (fact ? chunk(cs, std::false_type{}, std::true_type{})
+                                   : chunk(cs, std::false_type{}, std::false_type{}));
+      if (!ok) return;
     }
 
     if (fact) {
       __syncthreads();
-      float* dstp = T.colpart + (int64_t)pc.slot * d2;
-      for (int j2 = tid * 4; j2 < (int)d2; j2 += kThreads * 4)
-        *reinterpret_cast<float4*>(dstp + j2) = *reinterpret_cast<const float4*>(colacc + j2);
+      if (!col_global) {
+        float* dstp = T.colpart + (int64_t)pc.slot * d2;
+        for (int j2 = tid * 4; j2 < (int)d2; j2 += kThreads * 4)
+          *reinterpret_cast<float4*>(dstp + j2) = *reinterpret_cast<const float4*>(colacc + j2);
+      }
       __syncthreads();
     }
     if (pstats) {

@@ -57,9 +57,11 @@ struct U4 {
 __device__ __forceinline__ U4 philox4x32_10(U4 c, uint32_t k0, uint32_t k1) {
 #pragma unroll
   for (int i = 0; i < 10; ++i) {
-    // one 32x32->64 multiply per lane word (hi and lo from a single wide product)
-    const uint64_t p0 = (uint64_t)0xD2511F53u * c.x;
-    const uint64_t p1 = (uint64_t)0xCD9E8D57u * c.z;
+    // one 32x32->64 multiply per lane word (hi and lo from a single wide
+    // product; written as mul.wide so it stays one instruction)
+    uint64_t p0, p1;
+    asm("mul.wide.u32 %0, %1, %2;" : "=l"(p0) : "r"(c.x), "r"(0xD2511F53u));
+    asm("mul.wide.u32 %0, %1, %2;" : "=l"(p1) : "r"(c.z), "r"(0xCD9E8D57u));
     c = U4{(uint32_t)(p1 >> 32) ^ c.y ^ k0, (uint32_t)p1, (uint32_t)(p0 >> 32) ^ c.w ^ k1, (uint32_t)p0};
     k0 += 0x9E3779B9u;
     k1 += 0xBB67AE85u;

@@ -22,6 +22,7 @@ A_ATAN2 = 4 / math.pi
 SHIFTER = [1, 2, 4, 8, 16, 32, 64, 128]
 BLOCK = 2048
 SUPPORTED_PRECISIONS = ("auto", "fp32", "bf16_sr", "int8_sr")
+FAST_COLS = 8192   # shared-memory column accumulator of the fast kernel (floats)
 
 
 def f32(x) -> float:
@@ -250,7 +251,12 @@ class GroupPlan:
             bpp = 2 if self.pdt == L.DT_BF16 else 4
             bps = {0: 4, 1: 2, 2: 1, 3: 2 if self.pdt == L.DT_BF16 else 4}[self.precision]
             stage = 2048 * (2 * bpp + 2 * bps)
-            budget = 112 * 1024 - self.gen_offset * 4   # two CTAs per SM
+            # factored tensors wider than FAST_COLS keep their column partials
+            # in global memory, so one wide tensor does not cut occupancy
+            self.gen_offset = min(self.gen_offset, FAST_COLS)
+            three = self.precision == L.PREC["int8_sr"] and self.pdt == L.DT_BF16 and cfg.algo != L.ALGO_PRODIGY
+            per_cta = (227 * 1024) // (3 if three else 2) - 2048
+            budget = per_cta - self.gen_offset * 4
             self.stages = int(max(2, min(4, budget // stage)))
             self.smem_floats = self.gen_offset + self.stages * stage // 4
         else:
