@@ -470,7 +470,8 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v)) adam_
   __syncthreads();
 
   int parity = 0;
-  uint32_t j = 0;   // chunk counter (consumer)
+  int slot = 0;         // consumer position in the ring
+  uint32_t par = 0u;    // its mbarrier phase
   for (int pi = pbeg; pi < pend; ++pi) {
     const advopt_piece pc = L.pieces[pi];
     __syncthreads();
@@ -507,8 +508,6 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v)) adam_
     auto chunk = [&](int64_t cs, auto full_tag, auto fact_tag) -> bool {
       constexpr bool kFull = decltype(full_tag)::value;
       constexpr bool fact = decltype(fact_tag)::value;   // shadows the piece's flag
-      const int slot = (int)(j % (uint32_t)S);
-      const uint32_t par = (j / (uint32_t)S) & 1u;
       const int clen = kFull ? kChunk : (int)min((int64_t)kChunk, pc.end - cs);
       const int64_t k0 = cs + tid * kVec;
       const int nv = kFull ? kVec : max(0, min(kVec, clen - tid * kVec));
@@ -739,9 +738,13 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v)) adam_
         }
       }
       parity ^= 1;
+      if (++slot == S) {
+        slot = 0;
+        par ^= 1u;
+      }
       return true;
     };
-    for (int64_t cs = pc.begin; cs < pc.end; cs += kChunk, ++j) {
+    for (int64_t cs = pc.begin; cs < pc.end; cs += kChunk) {
       const bool full = vec && (pc.end - cs >= kChunk);
       const bool ok = full ? (fact ? chunk(cs, std::true_type{}, std::true_type{})
                                    : chunk(cs, std::true_type{}, std::false_type{}))
