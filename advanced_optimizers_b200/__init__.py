@@ -6,7 +6,8 @@ the C ABI in include/advopt.h (libadvopt.so, built in-tree).
 """
 from .optim import *  # noqa: F401,F403
 from .optim import __all__ as _optim_all
+from .distributed import ShardedOptimizer
 
 __version__ = "0.1.0"
 reference_version = "2.5.4"
-__all__ = list(_optim_all)
+__all__ = list(_optim_all) + ["ShardedOptimizer"]

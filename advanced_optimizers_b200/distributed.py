@@ -1,0 +1,216 @@
+"""Per-tensor sharding of the optimizer step across the ranks of one node
+(one process per GPU, torch.distributed over NCCL).
+
+Every parameter tensor is owned by exactly one rank, chosen by
+longest-processing-time assignment of a per-tensor cost (bytes for the
+elementwise optimizers, Newton–Schulz FLOPs for Muon/AdaMuon matrices).  A
+rank keeps optimizer state only for the tensors it owns and steps only
+those; afterwards the updated parameters are all-gathered so that every rank
+holds the full model again.  Prodigy's global d estimate needs the two sums
+of every rank: they are all-reduced (one 2-float NCCL all-reduce per step),
+with the previous step's numerator carried by rank 0 only, so the sharded
+run reproduces the single-GPU d.
+
+With `flat=True` (default) the parameters become views into one rank-ordered
+buffer per dtype — [rank 0's tensors | rank 1's | ...], every segment padded to
+the largest — so the all-gather is a single in-place
+`all_gather_into_tensor` per dtype with no packing copies.  With
+`flat=False` each tensor is broadcast from its owner.
+
+This module is plumbing around the single-GPU classes (it adds no kernel);
+the reference's own distributed hook is Prodigy's `fsdp_in_use`
+all-reduce (Prodigy_adv.py:550-554), which the Prodigy class keeps.
+"""
+from __future__ import annotations
+
+import math
+from typing import Callable, Iterable, Optional
+
+import torch
+import torch.distributed as dist
+
+from .optim._muon_family import is_suitable_for_muon, ns_flops
+
+ALIGN_ELEMS = 64   # every parameter view starts on a 128-byte boundary (bf16)
+
+
+def lpt_partition(costs, world: int):
+    """Owner rank of each item: items in decreasing cost (ties by index) go
+    to the currently least-loaded rank (ties to the lower rank)."""
+    order = sorted(range(len(costs)), key=lambda i: (-costs[i], i))
+    load = [0] * world
+    owner = [0] * len(costs)
+    for i in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        owner[i] = r
+        load[r] += costs[i]
+    return owner
+
+
+def default_cost(optimizer_cls, group: dict, p: torch.Tensor) -> float:
+    """Bytes touched per step for the elementwise optimizers; for the Muon
+    family, the Newton–Schulz FLOPs of matrices routed to the Muon path."""
+    name = getattr(optimizer_cls, "__name__", "")
+    if name in ("Muon_adv", "AdaMuon_adv") and p.ndim >= 2:
+        if group.get("use_muon") is not None:
+            muon = bool(group["use_muon"])
+        elif group.get("optim_type") is not None:
+            muon = group["optim_type"] == "muon"
+        else:
+            muon = is_suitable_for_muon(p)
+        if muon:
+            rows = p.shape[0]
+            cols = p.numel() // max(1, rows)
+            return float(ns_flops(min(rows, cols), max(rows, cols), group.get("ns_steps", 5),
+                                  group.get("accelerated_ns", False)))
+    return float(p.numel() * p.element_size())
+
+
+class FlatParams:
+    """Rank-ordered flat storage of the parameters (one buffer per dtype and
+    device); `all_gather()` refreshes every parameter in place."""
+
+    def __init__(self, params, owner, world: int, rank: int, group=None):
+        self.world, self.rank, self.group = world, rank, group
+        self.buffers = []   # (flat, seg)
+        by_key = {}
+        for p, r in zip(params, owner):
+            by_key.setdefault((p.dtype, p.device), []).append((p, r))
+        for (dt, dev), items in by_key.items():
+            offsets = {}
+            seg_used = [0] * world
+            for p, r in items:
+                off = seg_used[r]
+                offsets[id(p)] = (r, off)
+                seg_used[r] = off + math.ceil(p.numel() / ALIGN_ELEMS) * ALIGN_ELEMS
+            seg = max(max(seg_used), ALIGN_ELEMS)
+            flat = torch.zeros(world * seg, dtype=dt, device=dev)
+            with torch.no_grad():
+                for p, _ in items:
+                    r, off = offsets[id(p)]
+                    view = flat[r * seg + off: r * seg + off + p.numel()].view(p.shape)
+                    view.copy_(p.data)
+                    p.data = view
+            self.buffers.append((flat, seg))
+
+    @torch.no_grad()
+    def all_gather(self):
+        for flat, seg in self.buffers:
+            mine = flat[self.rank * seg:(self.rank + 1) * seg]
+            if dist.get_backend(self.group) == "nccl":
+                dist.all_gather_into_tensor(flat, mine, group=self.group)
+            else:
+                chunks = list(flat.split(seg))
+                dist.all_gather(chunks, mine.clone(), group=self.group)
+
+
+class ShardedOptimizer:
+    """Wraps one of the five optimizer classes for per-tensor sharding.
+
+        opt = ShardedOptimizer(AdamW_adv, model.parameters(), lr=1e-3,
+                               state_precision="int8_sr", factored_2nd=True)
+        loss.backward(); opt.step(); opt.zero_grad()
+
+    `params` may be an iterable of tensors or of param-group dicts (the
+    group options are kept for the owned tensors).  `cost(group, p)` overrides
+    the partition cost.  Every rank must call step() (it ends in
+    collectives)."""
+
+    def __init__(self, optimizer_cls, params, *, process_group=None,
+                 cost: Optional[Callable[[dict, torch.Tensor], float]] = None, flat: bool = True, **kwargs):
+        if not (dist.is_available() and dist.is_initialized()):
+            raise RuntimeError("ShardedOptimizer needs an initialised torch.distributed process group")
+        self.group = process_group
+        self.world = dist.get_world_size(process_group)
+        self.rank = dist.get_rank(process_group)
+        groups = list(params)
+        if groups and not isinstance(groups[0], dict):
+            groups = [{"params": groups}]
+        self.all_params = []
+        costs = []
+        for g in groups:
+            g["params"] = list(g["params"])
+            for p in g["params"]:
+                self.all_params.append(p)
+                merged = dict(kwargs)
+                merged.update({k: v for k, v in g.items() if k != "params"})
+                costs.append(cost(g, p) if cost is not None else default_cost(optimizer_cls, merged, p))
+        self.owner = lpt_partition(costs, self.world)
+        own = {id(p) for p, r in zip(self.all_params, self.owner) if r == self.rank}
+        self.flat = FlatParams(self.all_params, self.owner, self.world, self.rank, process_group) if flat else None
+        owned_groups = []
+        for g in groups:
+            ps = [p for p in g["params"] if id(p) in own]
+            if ps:
+                owned_groups.append(dict(g, params=ps))
+        self.is_prodigy = getattr(optimizer_cls, "__name__", "") == "Prodigy_adv"
+        if self.is_prodigy:
+            kwargs = dict(kwargs, fsdp_in_use=self.world > 1)
+        self.optimizer = optimizer_cls(owned_groups, **kwargs) if owned_groups else None
+        if self.optimizer is not None and hasattr(self.optimizer, "_ids"):
+            # Philox streams keyed by the tensor's global index: the sharded
+            # step draws the same noise as a single-process step
+            for i, (p, r) in enumerate(zip(self.all_params, self.owner)):
+                if r == self.rank:
+                    self.optimizer._ids[id(p)] = i
+        if self.is_prodigy and self.optimizer is not None:
+            # the carried numerator is already global: count it on one rank
+            self.optimizer._carry_scale = 1.0 if self.rank == 0 else 0.0
+            self.optimizer._process_group = process_group
+
+    @property
+    def param_groups(self):
+        return self.optimizer.param_groups if self.optimizer is not None else []
+
+    @property
+    def state(self):
+        return self.optimizer.state if self.optimizer is not None else {}
+
+    def owned(self, p) -> bool:
+        return self.owner[self._index(p)] == self.rank
+
+    def _index(self, p):
+        for i, q in enumerate(self.all_params):
+            if q is p:
+                return i
+        raise KeyError("not a parameter of this optimizer")
+
+    @torch.no_grad()
+    def gather(self):
+        """Bring every rank's updated tensors to all ranks."""
+        if self.world == 1:
+            return
+        if self.flat is not None:
+            self.flat.all_gather()
+        else:
+            for p, r in zip(self.all_params, self.owner):
+                dist.broadcast(p.data, src=r, group=self.group)
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        if self.optimizer is not None:
+            self.optimizer.step()
+        elif self.is_prodigy and self.world > 1:
+            # a rank without tensors still takes part in the d all-reduce
+            dist.all_reduce(torch.zeros(2, dtype=torch.float32, device=self.all_params[0].device),
+                            op=dist.ReduceOp.SUM, group=self.group)
+        self.gather()
+        return loss
+
+    def zero_grad(self, set_to_none: bool = True):
+        for p in self.all_params:
+            if set_to_none:
+                p.grad = None
+            elif p.grad is not None:
+                p.grad.zero_()
+
+    def state_dict(self):
+        return self.optimizer.state_dict() if self.optimizer is not None else {}
+
+    def load_state_dict(self, sd):
+        if self.optimizer is not None:
+            self.optimizer.load_state_dict(sd)

@@ -109,6 +109,8 @@ class Prodigy_adv(torch.optim.Optimizer):
         self._runner = AdamFamilyRunner(seed=42)
         self._ids = {}
         self._first = True
+        self._carry_scale = 1.0      # 0 on the ranks of a sharded run that do not carry the numerator
+        self._process_group = None   # group of the d all-reduce (default group when None)
         self.init_step()
 
     def load_state_dict(self, state_dict: dict) -> None:
@@ -139,7 +141,7 @@ class Prodigy_adv(torch.optim.Optimizer):
         if self.beta3 is None:
             self.beta3 = math.sqrt(self.beta2_default)
         if not self._first:
-            self._d_num_carry = float(np.float32(g.get("d_numerator", 0.0) * self.beta3))
+            self._d_num_carry = float(np.float32(g.get("d_numerator", 0.0) * self.beta3)) * self._carry_scale
 
     def _tid(self, p):
         t = self._ids.get(id(p))
@@ -182,7 +184,7 @@ class Prodigy_adv(torch.optim.Optimizer):
     def _ensure_sums(self):
         if not hasattr(self, "_sums"):
             self._sums = torch.zeros(2, dtype=torch.float32, device=self.device)
-            self._d_num_carry = float(np.float32(self.param_groups[0].get("d_numerator", 0.0)))
+            self._d_num_carry = float(np.float32(self.param_groups[0].get("d_numerator", 0.0))) * self._carry_scale
             self._first = False
 
     def _step_params(self, gi, group, params):
@@ -237,7 +239,7 @@ class Prodigy_adv(torch.optim.Optimizer):
         if active:
             d_max, d_coef, growth_rate = g_group["d_max"], g_group["d_coef"], g_group["growth_rate"]
             if self.fsdp_in_use and dist.is_available() and dist.is_initialized():
-                dist.all_reduce(self._sums, op=dist.ReduceOp.SUM)
+                dist.all_reduce(self._sums, op=dist.ReduceOp.SUM, group=self._process_group)
             gn, gd = self._sums.tolist()
             d_hat = g_group["d"]
             if gd > 0:

@@ -63,18 +63,6 @@ def algorithmic_bytes(shapes):
     return tot
 
 
-def lpt_shard(shapes, world):
-    """Longest-processing-time assignment of tensors to ranks by bytes."""
-    order = sorted(range(len(shapes)), key=lambda i: -math.prod(shapes[i]))
-    load = [0] * world
-    owner = [0] * len(shapes)
-    for i in order:
-        r = min(range(world), key=lambda k: load[k])
-        owner[i] = r
-        load[r] += math.prod(shapes[i])
-    return owner
-
-
 def sample_clocks_start(path):
     try:
         f = open(path, "w")
@@ -210,18 +198,24 @@ def run_ours(args):
 
     shapes = llama3_8b_shapes(args.layers, not args.no_embed)
     total = sum(math.prod(s) for s in shapes)
-    owner = lpt_shard(shapes, world)
-    mine = [i for i in range(len(shapes)) if owner[i] == rank]
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     # every rank holds all bf16 params (they are all-gathered each step), but
     # grads and optimizer states only for the tensors it owns
-    params = []
-    for i, sh in enumerate(shapes):
-        t = torch.empty(sh, dtype=torch.bfloat16, device=dev)
-        if owner[i] == rank:
-            t.copy_(torch.randn(sh, generator=gen, device=dev) * 0.02)
-        params.append(torch.nn.Parameter(t))
+    params = [torch.nn.Parameter(torch.empty(sh, dtype=torch.bfloat16, device=dev)) for sh in shapes]
+    kw = dict(state_precision="int8_sr", factored_2nd=True, nesterov=True)
+    if world > 1:
+        # per-tensor sharding: parameters become views of one rank-ordered
+        # flat buffer, refreshed by a single all_gather_into_tensor per step
+        sharded = A.ShardedOptimizer(A.AdamW_adv, params, **kw)
+        owner = sharded.owner
+    else:
+        sharded = None
+        owner = [0] * len(shapes)
+    mine = [i for i in range(len(shapes)) if owner[i] == rank]
     owned = [params[i] for i in mine]
+    with torch.no_grad():
+        for p in owned:
+            p.copy_(torch.randn(p.shape, generator=gen, device=dev) * 0.02)
     for p in owned:
         g = torch.randn(p.shape, generator=gen, device=dev, dtype=torch.float32).mul_(1e-3)
         mask = torch.rand(p.shape, generator=gen, device=dev) < 0.01
@@ -229,19 +223,13 @@ def run_ours(args):
         p.grad = g.to(torch.bfloat16)
         del g, mask
     torch.cuda.empty_cache()
-    opt = A.AdamW_adv(owned, state_precision="int8_sr", factored_2nd=True, nesterov=True)
-
-    # all-gather layout: rank r broadcasts each tensor it owns
-    def gather_params():
-        if world == 1:
-            return
-        with torch.no_grad():
-            for i, p in enumerate(params):
-                dist.broadcast(p.data, src=owner[i])
+    opt = sharded.optimizer if sharded is not None else A.AdamW_adv(owned, **kw)
 
     def step():
-        opt.step()
-        gather_params()
+        if sharded is not None:
+            sharded.step()
+        else:
+            opt.step()
 
     for _ in range(args.warmup):
         step()
@@ -285,7 +273,7 @@ def run_ours(args):
         e2e = run_e2e(args, owned, step, world, dev)
     ns = None
     if not args.no_ns:
-        del opt, owned, params, step
+        del opt, owned, params, step, sharded
         torch.cuda.empty_cache()
         ns = run_ns_leg(args, world, rank, dev)
     if rank == 0:
@@ -303,38 +291,37 @@ def muon_shapes(layers=32):
 
 def run_ns_leg(args, world, rank, dev):
     """Muon_adv (momentum 0.95, 5 quintic Newton-Schulz iterations, bf16
-    'auto' states) over every hidden matrix; matrices are split across ranks
-    by FLOPs (LPT) and the updated params broadcast from their owners."""
+    'auto' states) over every hidden matrix; with N ranks the matrices are
+    split by Newton-Schulz FLOPs (ShardedOptimizer) and the updated params
+    all-gathered."""
     import torch.distributed as dist
     import advanced_optimizers_b200 as A
     from advanced_optimizers_b200.optim._muon_family import ns_flops
     shapes = muon_shapes(args.layers)
     flops = [ns_flops(min(s), max(s), 5, False) for s in shapes]
-    order = sorted(range(len(shapes)), key=lambda i: -flops[i])
-    load = [0] * world
-    owner = [0] * len(shapes)
-    for i in order:
-        r = min(range(world), key=lambda k: load[k])
-        owner[i] = r
-        load[r] += flops[i]
     gen = torch.Generator(device=dev).manual_seed(4321 + rank)
-    params = []
-    for i, sh in enumerate(shapes):
-        t = torch.empty(sh, dtype=torch.bfloat16, device=dev)
-        if owner[i] == rank:
-            t.normal_(0, 0.02, generator=gen)
-        params.append(torch.nn.Parameter(t))
+    params = [torch.nn.Parameter(torch.empty(sh, dtype=torch.bfloat16, device=dev)) for sh in shapes]
+    groups = [dict(params=params, optim_type="muon")]
+    if world > 1:
+        sharded = A.ShardedOptimizer(A.Muon_adv, groups, lr=1e-3, beta1=0.95)
+        owner = sharded.owner
+    else:
+        sharded = None
+        owner = [0] * len(shapes)
     owned = [params[i] for i in range(len(shapes)) if owner[i] == rank]
+    with torch.no_grad():
+        for p in owned:
+            p.normal_(0, 0.02, generator=gen)
     for p in owned:
         p.grad = torch.empty_like(p).normal_(0, 1e-3, generator=gen)
-    opt = A.Muon_adv([dict(params=owned, optim_type="muon")], lr=1e-3, beta1=0.95)
+    opt = sharded.optimizer if sharded is not None else A.Muon_adv([dict(params=owned, optim_type="muon")],
+                                                                   lr=1e-3, beta1=0.95)
 
     def step():
-        opt.step()
-        if world > 1:
-            with torch.no_grad():
-                for i, p in enumerate(params):
-                    dist.broadcast(p.data, src=owner[i])
+        if sharded is not None:
+            sharded.step()
+        else:
+            opt.step()
 
     warm = 1
     steps = 2
@@ -367,7 +354,7 @@ def run_ns_leg(args, world, rank, dev):
     except Exception:
         peak, kind = 1400.0, "fallback sustained"
     total_flops = sum(flops)
-    del opt, owned, params
+    del opt, owned, params, sharded
     torch.cuda.empty_cache()
     return {"workload": f"Muon_adv over {len(shapes)} Llama-3-8B hidden matrices (q/o 4096x4096, k/v 1024x4096, "
                         "gate/up 14336x4096, down 4096x14336), momentum 0.95, 5 quintic Newton-Schulz "
@@ -429,7 +416,8 @@ def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, la
             "config": {"workload": WORKLOAD if (args.layers == 32 and not args.no_embed) else
                        f"profiling subset: {args.layers} layers" + ("" if not args.no_embed else ", no embeddings"),
                        "params": total, "tensors": len(shapes),
-                       "parallelism": f"per-tensor sharding x{world}" + (" + bf16 param all-gather" if world > 1 else ""),
+                       "parallelism": f"per-tensor sharding x{world}" + (" + one bf16 all_gather_into_tensor of the flat params"
+                                                                 if world > 1 else ""),
                        "l2": "inputs larger than L2 (about 40 GB resident per step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": TRAFFIC_PER_ALG_BYTE * alg,

@@ -1,0 +1,92 @@
+"""Per-tensor sharding host logic on CPU: two gloo ranks (world_size 2).
+
+The optimizer here is a stand-in (plain SGD on CPU tensors) because the B200
+classes run only on CUDA; what is tested is the partition, the rank-ordered
+flat parameter storage and the all-gather: after a sharded step every rank
+holds exactly the parameters a single process would have."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from advanced_optimizers_b200.distributed import ShardedOptimizer, lpt_partition
+
+
+class PlainSGD(torch.optim.Optimizer):
+    def __init__(self, params, lr=0.1):
+        super().__init__(params, dict(lr=lr))
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        for g in self.param_groups:
+            for p in g["params"]:
+                if p.grad is not None:
+                    p.add_(p.grad, alpha=-g["lr"])
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+SHAPES = [(64, 48), (10,), (33, 7), (128,), (5, 5, 3), (1,), (300,)]
+
+
+def _make(seed=0):
+    g = torch.Generator().manual_seed(seed)
+    ps = [torch.nn.Parameter(torch.randn(s, generator=g)) for s in SHAPES]
+    grads = [torch.randn(s, generator=g) for s in SHAPES]
+    return ps, grads
+
+
+def _worker(rank, world, port, flat, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ps, grads = _make()
+        opt = ShardedOptimizer(PlainSGD, ps, lr=0.5, flat=flat)
+        for step in range(3):
+            for p, g in zip(ps, grads):
+                p.grad = g * (step + 1)
+            opt.step()
+            opt.zero_grad()
+        out[rank] = [p.detach().clone() for p in ps]
+        out[f"owner{rank}"] = list(opt.owner)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("flat", [True, False])
+def test_sharded_step_matches_single_process(flat):
+    world = 2
+    port = _free_port()
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_worker, args=(world, port, flat, out), nprocs=world, join=True)
+    ref, grads = _make()
+    opt = PlainSGD(ref, lr=0.5)
+    for step in range(3):
+        for p, g in zip(ref, grads):
+            p.grad = g * (step + 1)
+        opt.step()
+    for r in range(world):
+        for a, b in zip(out[r], ref):
+            assert torch.equal(a, b.detach())
+    assert out["owner0"] == out["owner1"]
+    assert set(out["owner0"]) == {0, 1}
+
+
+def test_lpt_partition_is_balanced_and_deterministic():
+    costs = [100, 90, 80, 10, 10, 10, 5, 1]
+    own = lpt_partition(costs, 3)
+    assert own == lpt_partition(costs, 3)
+    loads = [sum(c for c, r in zip(costs, own) if r == k) for k in range(3)]
+    assert max(loads) - min(loads) <= max(costs)
+    assert lpt_partition([5], 4) == [0]
