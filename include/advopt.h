@@ -135,7 +135,7 @@ typedef struct advopt_adam_launch {
   int32_t n_pieces;
   int32_t grid;                       /* CTAs (= length of cta_offsets - 1)   */
   int32_t smem_floats;                /* dynamic shared memory, floats        */
-  int32_t gen_offset;                 /* float offset of the generic-path buffers (>= max d2) */
+  int32_t gen_offset;                 /* floats before the stage ring: column accumulator (fast path: factored tensors with larger d2 accumulate in col_partial) */
   int32_t algo;                       /* ADVOPT_ALGO_*                        */
   int32_t precision;                  /* ADVOPT_PREC_*                        */
   int32_t param_dtype;                /* ADVOPT_DT_*                          */
@@ -305,6 +305,21 @@ typedef struct advopt_muon_args {
 } advopt_muon_args;
 
 int advopt_muon_stage(const advopt_muon_args* args, int32_t stage, void* stream);
+
+/* The stochastic-rounding noise generator.  No reference counterpart: the
+ * reference draws torch.randint from a generator seeded 42
+ * (param_update.py:159-204); the kernels draw counter-based Philox4x32-10
+ * instead (or the reference's own integers in the test mode).
+ *   advopt_philox4x32_10: n raw evaluations; counters_keys holds n records
+ *     {c0, c1, c2, c3, k0, k1}, out receives n x 4 words (device pointers).
+ *   advopt_noise_fill: the n 16-bit values a kernel draws for elements
+ *     0 .. n-1 of tensor `tensor_id` at `step` from noise stream `stream_id`
+ *     (0 = v, 1 = m, 2 = param); counter = (k >> 3, stream_id << 24,
+ *     tensor_id, step), key = seed, element k takes half (k & 1) of word
+ *     (k & 7) >> 1. */
+int advopt_philox4x32_10(const uint32_t* counters_keys, uint32_t* out, int64_t n, void* stream);
+int advopt_noise_fill(uint16_t* out, int64_t n, uint64_t seed, uint32_t tensor_id, uint32_t step,
+                      uint32_t stream_id, void* stream);
 
 /* Layout checks for bindings: sizeof of each struct. */
 size_t advopt_sizeof(int which); /* 0 adam_tensor, 1 piece, 2 adam_launch, 3 lion_tensor, 4 muon_args */
