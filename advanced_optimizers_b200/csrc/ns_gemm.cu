@@ -1,19 +1,24 @@
 // Newton–Schulz GEMM for sm_100a: D = bf16(alpha * (A @ B) + beta * C)
 //
-// One CTA computes one 128 x 256 output tile with 5th-generation tensor cores:
+// A persistent kernel: each CTA (one per SM) walks the 128 x 256 output
+// tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... with 5th-generation
+// tensor cores and two accumulators in tensor memory, so the epilogue of one
+// tile overlaps the main loop of the next:
 //   * warp 0 (one elected lane) streams 128x64 A and 256x64 B tiles into a
 //     4-stage shared-memory ring with TMA (cp.async.bulk.tensor, 128-byte
 //     swizzle, no multicast), completing on "full" mbarriers;
-//   * warp 1 owns the tensor memory (256 fp32 columns x 128 lanes), and one
+//   * warp 1 owns the tensor memory (2 x 256 fp32 columns x 128 lanes); one
 //     elected lane issues tcgen05.mma (kind::f16, bf16 in, fp32 accumulate),
-//     four K=16 steps per stage, committing each stage to its "empty"
-//     mbarrier so the producer may refill it;
-//   * warps 2..5 read the accumulator back with tcgen05.ld (each warp its
-//     32-lane quarter of the tile's rows) and write bf16(alpha*acc + beta*C).
+//     four K=16 steps per stage, commits each stage to its "empty" mbarrier
+//     and each finished tile to its accumulator's "full" mbarrier;
+//   * warps 2..5 wait for an accumulator, read it with tcgen05.ld (each warp
+//     its 32-lane quarter of the tile's rows), write bf16(alpha*acc + beta*C)
+//     and release the accumulator on its "empty" mbarrier.
 // A is K-major ([M][K], K contiguous).  B is K-major ([N][K]) or N-major
 // ([K][N], N contiguous) — the latter is how X enters X' = a X + B X.
-// Every wait is bounded; a wait that gives up sets *err, the CTA drains its
-// tensor-core work (bounded), frees its tensor memory and returns.
+// Every wait is bounded and also gives up when another role has; the CTA
+// then drains its tensor-core work (bounded), frees its tensor memory,
+// reports through *err and returns.
 //
 // Newton–Schulz itself (Muon_util.py:7-121): per iteration
 //   quintic: A = X X^T;  B = b A + c A A;  X = a X + B X
@@ -102,33 +107,53 @@ struct GemmArgs {
   int32_t* err;
 };
 
+constexpr uint32_t TMEM_ALLOC = 2 * TMEM_COLS;   // two accumulators
+
+// Bounded wait that also gives up once another role of the CTA has.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && *abort_flag) return false;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     ns_gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, GemmArgs g,
                    int b_mn_major) {
   extern __shared__ unsigned char smem_raw[];
   // 1024-byte alignment for the 128-byte swizzle atoms
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], tmem_full, drain;
+  __shared__ uint64_t full_bar[STAGES], empty_bar[STAGES], acc_full[2], acc_empty[2], drain;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
+  volatile int* abort_v = &abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int ktiles = g.K / BK;
+  const int n_nb = g.N / BN;
+  const int ntiles = (g.M / BM) * n_nb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&tmem_full, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
     mbar_init(&drain, 1);
     abort_flag = 0;
     mbar_fence_init();
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                 "r"(TMEM_COLS)
+                 "r"(TMEM_ALLOC)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -140,25 +165,27 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     // ---- TMA producer ----
     if (lane == 0) {
-      for (int kt = 0; kt < ktiles; ++kt) {
-        const int s = kt % STAGES;
-        if (kt >= STAGES) {
-          if (!mbar_wait(&empty_bar[s], ((kt / STAGES) - 1) & 1)) {
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort_v; t += gridDim.x) {
+        const int m0 = (t / n_nb) * BM, n0 = (t % n_nb) * BN;
+        for (int kt = 0; kt < ktiles; ++kt, ++it) {
+          const int s = (int)(it % STAGES);
+          const uint32_t use = it / STAGES;
+          if (use > 0 && !wait_or_abort(&empty_bar[s], (use - 1) & 1u, abort_v)) {
             abort_flag = 1;
             break;
           }
-        }
-        if (abort_flag) break;
-        unsigned char* sa = smem + s * STAGE_BYTES;
-        unsigned char* sb = sa + A_BYTES;
-        mbar_arrive_tx(&full_bar[s], STAGE_BYTES);
-        tma_load_2d(sa, &mapA, kt * BK, m0, &full_bar[s]);
-        if (b_mn_major) {
-          // B tile = 4 boxes of [64 k-rows][64 n-cols], each 8 KB
+          unsigned char* sa = smem + s * STAGE_BYTES;
+          unsigned char* sb = sa + A_BYTES;
+          mbar_arrive_tx(&full_bar[s], STAGE_BYTES);
+          tma_load_2d(sa, &mapA, kt * BK, m0, &full_bar[s]);
+          if (b_mn_major) {
+            // B tile = 4 boxes of [64 k-rows][64 n-cols], each 8 KB
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &mapB, n0 + 64 * j, kt * BK, &full_bar[s]);
-        } else {
-          tma_load_2d(sb, &mapB, kt * BK, n0, &full_bar[s]);
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &mapB, n0 + 64 * j, kt * BK, &full_bar[s]);
+          } else {
+            tma_load_2d(sb, &mapB, kt * BK, n0, &full_bar[s]);
+          }
         }
       }
     }
@@ -166,67 +193,91 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---- MMA issuer ----
     if (lane == 0) {
       const uint32_t idesc = instr_desc(b_mn_major != 0);
-      for (int kt = 0; kt < ktiles; ++kt) {
-        const int s = kt % STAGES;
-        if (!mbar_wait(&full_bar[s], (kt / STAGES) & 1)) {
+      uint32_t it = 0;
+      int i = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort_v; t += gridDim.x, ++i) {
+        const int acc = i & 1;
+        const uint32_t use = (uint32_t)i >> 1;
+        if (use > 0 && !wait_or_abort(&acc_empty[acc], (use - 1) & 1u, abort_v)) {
           abort_flag = 1;
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
-        const uint32_t sb = sa + A_BYTES;
+        const uint32_t d_tmem = tmem + (uint32_t)acc * TMEM_COLS;
+        bool ok = true;
+        for (int kt = 0; kt < ktiles; ++kt, ++it) {
+          const int s = (int)(it % STAGES);
+          if (!wait_or_abort(&full_bar[s], (it / STAGES) & 1u, abort_v)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
-          // A K-major: 16 elements = 32 bytes along the swizzled row
-          const uint64_t ad = smem_desc(sa + k * 32, 16, 1024);
-          const uint64_t bd = b_mn_major ? smem_desc(sb + k * 2048, 8192, 1024)   // 2 groups of 8 k-rows per step
-                                         : smem_desc(sb + k * 32, 16, 1024);
-          mma_bf16(tmem, ad, bd, idesc, (kt > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BK / 16; ++k) {
+            // A K-major: 16 elements = 32 bytes along the swizzled row
+            const uint64_t ad = smem_desc(sa + k * 32, 16, 1024);
+            const uint64_t bd = b_mn_major ? smem_desc(sb + k * 2048, 8192, 1024)   // 2 groups of 8 k-rows per step
+                                           : smem_desc(sb + k * 32, 16, 1024);
+            mma_bf16(d_tmem, ad, bd, idesc, (kt > 0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty_bar[s]);
         }
-        mma_commit(&empty_bar[s]);
+        if (!ok) {
+          abort_flag = 1;
+          break;
+        }
+        mma_commit(&acc_full[acc]);
       }
-      mma_commit(&tmem_full);
     }
   } else {
     // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----
     const int quarter = warp & 3;
-    const int row = m0 + quarter * 32 + lane;
-    const bool ok = mbar_wait(&tmem_full, 0);
-    if (!ok) abort_flag = 1;
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (ok) {
-      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+    int i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      const int acc = i & 1;
+      const uint32_t use = (uint32_t)i >> 1;
+      if (!wait_or_abort(&acc_full[acc], use & 1u, abort_v)) {
+        abort_flag = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int m0 = (t / n_nb) * BM, n0 = (t % n_nb) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * TMEM_COLS;
       for (int c = 0; c < BN; c += 16) {
         uint32_t r[16];
         tmem_ld16(taddr + c, r);
-        if (row < g.M) {
-          const int col = n0 + c;
-          float cv[16];
-          if (g.beta != 0.0f && g.C) {
-            const uint4* cp = reinterpret_cast<const uint4*>(g.C + (size_t)row * g.ldc + col);
-            const uint4 c0 = __ldg(cp), c1 = __ldg(cp + 1);
-            const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        const int col = n0 + c;
+        float cv[16];
+        if (g.beta != 0.0f && g.C) {
+          const uint4* cp = reinterpret_cast<const uint4*>(g.C + (size_t)row * g.ldc + col);
+          const uint4 c0 = __ldg(cp), c1 = __ldg(cp + 1);
+          const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              cv[2 * i] = __uint_as_float(w[i] << 16);
-              cv[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) cv[i] = 0.0f;
+          for (int q = 0; q < 8; ++q) {
+            cv[2 * q] = __uint_as_float(w[q] << 16);
+            cv[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
           }
-          uint32_t o[8];
+        } else {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float v0 = __fmaf_rn(g.alpha, __uint_as_float(r[2 * i]), __fmul_rn(g.beta, cv[2 * i]));
-            const float v1 = __fmaf_rn(g.alpha, __uint_as_float(r[2 * i + 1]), __fmul_rn(g.beta, cv[2 * i + 1]));
-            o[i] = f_to_bf16_rne(v0) | (f_to_bf16_rne(v1) << 16);
-          }
-          uint4* dp = reinterpret_cast<uint4*>(g.D + (size_t)row * g.ldd + col);
-          dp[0] = make_uint4(o[0], o[1], o[2], o[3]);
-          dp[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          for (int q = 0; q < 16; ++q) cv[q] = 0.0f;
         }
+        uint32_t o[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float v0 = __fmaf_rn(g.alpha, __uint_as_float(r[2 * q]), __fmul_rn(g.beta, cv[2 * q]));
+          const float v1 = __fmaf_rn(g.alpha, __uint_as_float(r[2 * q + 1]), __fmul_rn(g.beta, cv[2 * q + 1]));
+          o[q] = f_to_bf16_rne(v0) | (f_to_bf16_rne(v1) << 16);
+        }
+        uint4* dp = reinterpret_cast<uint4*>(g.D + (size_t)row * g.ldd + col);
+        dp[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        dp[1] = make_uint4(o[4], o[5], o[6], o[7]);
       }
+      // the accumulator has been read: the MMA warp may overwrite it
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(&acc_empty[acc]);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -243,7 +294,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_ALLOC) : "memory");
   }
 }
 
@@ -319,7 +370,14 @@ extern "C" int advopt_ns_gemm(void* D, int32_t ldd, const void* A, int32_t lda, 
     attr_err = cudaFuncSetAttribute(ns_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return check_cuda(attr_err, "advopt_ns_gemm: smem attribute");
-  dim3 grid(N / BN, M / BM);
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms = 148;
+  }
+  const int ntiles = (M / BM) * (N / BN);
+  const int grid = ntiles < sms ? ntiles : sms;
   ns_gemm_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, g, b_mn_major);
   return check_cuda(cudaGetLastError(), "advopt_ns_gemm");
 }
