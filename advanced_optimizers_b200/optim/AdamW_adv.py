@@ -14,7 +14,7 @@ import torch
 
 from .. import _lib as L
 from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, init_adam_state
-from ._common import post_process_loaded_state, reject
+from ._common import load_state_dict_exact, reject
 
 
 class AdamW_adv(torch.optim.Optimizer):
@@ -102,8 +102,7 @@ class AdamW_adv(torch.optim.Optimizer):
 
     # ---- reference API surface ----
     def load_state_dict(self, state_dict: dict) -> None:
-        super().load_state_dict(state_dict)
-        post_process_loaded_state(self)
+        load_state_dict_exact(self, state_dict)
         self._runner.invalidate()
 
     @property

@@ -18,7 +18,7 @@ from .. import _lib as L
 from .._device import DeviceTable, aligned16, dtype_code, ptr, require_cuda_tensor, stream_handle, upload_static
 from .._plan import plan as plan_pieces
 from ._adam_family import adjust_wds, f32
-from ._common import post_process_loaded_state, reject
+from ._common import load_state_dict_exact, reject
 
 
 class _LionPlan:
@@ -95,8 +95,7 @@ class Lion_adv(torch.optim.Optimizer):
         self.init_step()
 
     def load_state_dict(self, state_dict: dict) -> None:
-        super().load_state_dict(state_dict)
-        post_process_loaded_state(self)
+        load_state_dict_exact(self, state_dict)
         self._plans.clear()
 
     @property

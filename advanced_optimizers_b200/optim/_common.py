@@ -14,7 +14,11 @@ def fix_loaded_state_dtype(state: dict, p: torch.Tensor, group: dict) -> None:
     """state_util.fix_loaded_state_dtype (state_util.py:181-263): undo
     torch's load_state_dict casting of quantised / factored states."""
     mode = group.get("centered_wd_mode", "full")
-    actual = group.get("actual_state_precision", group.get("state_precision", "auto"))
+    if state.get("is_muon") is False:
+        # auxiliary Adam state of Muon_adv / AdaMuon_adv: its own precision key
+        actual = group.get("adam_actual_state_precision", group.get("adam_state_precision", "auto"))
+    else:
+        actual = group.get("actual_state_precision", group.get("state_precision", "auto"))
     is_factored = state.get("factored", False) or actual == "factored"
     if actual == "fp32":
         base = torch.float32
@@ -62,6 +66,31 @@ def fix_loaded_state_dtype(state: dict, p: torch.Tensor, group: dict) -> None:
             state[key] = state[key].to(p.device)
         if not state[key].is_contiguous():
             state[key] = state[key].contiguous()
+
+
+def load_state_dict_exact(optimizer, state_dict: dict) -> None:
+    """torch.optim.Optimizer.load_state_dict followed by the reference's dtype
+    repair (param_update.post_process_loaded_state).  torch casts every state
+    tensor of a floating-point parameter to the parameter's dtype on load, so
+    a bf16 model's float32 block scales and factors would come back rounded
+    to bf16 (and int8 codes through bf16) before the repair widens them
+    again; here every loaded state tensor keeps the exact value and dtype it
+    was saved with, and the repair then only fixes states saved in another
+    dtype (checkpoints written by other code)."""
+    saved = state_dict.get("state", {})
+    torch.optim.Optimizer.load_state_dict(optimizer, state_dict)
+    params = [p for g in optimizer.param_groups for p in g["params"]]
+    for idx, st in saved.items():
+        if not isinstance(idx, int) or idx >= len(params):
+            continue
+        p = params[idx]
+        live = optimizer.state.get(p)
+        if live is None:
+            continue
+        for key, val in st.items():
+            if torch.is_tensor(val) and key in live and key != "step":
+                live[key] = val.detach().to(device=p.device, copy=True)
+    post_process_loaded_state(optimizer)
 
 
 def post_process_loaded_state(optimizer) -> None:

@@ -7,7 +7,7 @@ import torch
 
 from .. import _lib as L
 from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, init_adam_state
-from ._common import post_process_loaded_state, reject
+from ._common import load_state_dict_exact, reject
 from ._muon_family import MuonMatrixRunner, init_muon_state, is_suitable_for_muon
 
 
@@ -24,8 +24,7 @@ class MuonFamilyBase(torch.optim.Optimizer):
         self.init_step()
 
     def load_state_dict(self, state_dict: dict) -> None:
-        super().load_state_dict(state_dict)
-        post_process_loaded_state(self)
+        load_state_dict_exact(self, state_dict)
         self._adam_runner.invalidate()
 
     @property

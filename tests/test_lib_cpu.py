@@ -67,3 +67,38 @@ def test_planner_covers_every_element_once(shapes, grid):
         covered[t] = pos
         assert sorted(ps["slot"].tolist()) == list(range(n_slots[t]))
     assert covered == numels
+
+
+def test_state_dict_round_trip_keeps_exact_states_cpu():
+    """load_state_dict keeps every saved state's dtype and value (torch alone
+    would round float32 scales and factors of bf16 params to bf16), and the
+    auxiliary Adam states of Muon keep their own precision."""
+    import torch
+    import advanced_optimizers_b200 as A
+    g = torch.Generator().manual_seed(0)
+    p = [torch.nn.Parameter(torch.randn(256, 64, generator=g).bfloat16()), torch.nn.Parameter(torch.randn(64).bfloat16())]
+    o = A.AdamW_adv(p, state_precision="int8_sr", factored_2nd=True)
+    for st in o.state.values():
+        for k, v in st.items():
+            if torch.is_tensor(v) and v.is_floating_point():
+                v.copy_(torch.rand(v.shape, generator=g) + 0.1234567)
+    sd = o.state_dict()
+    q = [torch.nn.Parameter(t.detach().clone()) for t in p]
+    o2 = A.AdamW_adv(q, state_precision="int8_sr", factored_2nd=True)
+    o2.load_state_dict(sd)
+    for a, b in zip(p, q):
+        for k, v in o.state[a].items():
+            if torch.is_tensor(v):
+                w = o2.state[b][k]
+                assert w.dtype == v.dtype, k
+                assert torch.equal(w, v), k
+    m = [torch.nn.Parameter(torch.randn(64, 48, generator=g).bfloat16()), torch.nn.Parameter(torch.randn(48).bfloat16())]
+    mo = A.Muon_adv([dict(params=[m[0]], optim_type="muon"), dict(params=[m[1]], optim_type="adam")],
+                    state_precision="int8_sr")
+    sd = mo.state_dict()
+    m2 = [torch.nn.Parameter(t.detach().clone()) for t in m]
+    mo2 = A.Muon_adv([dict(params=[m2[0]], optim_type="muon"), dict(params=[m2[1]], optim_type="adam")],
+                     state_precision="int8_sr")
+    mo2.load_state_dict(sd)
+    assert mo2.state[m2[1]]["exp_avg"].dtype == torch.bfloat16       # adam_state_precision 'auto'
+    assert mo2.state[m2[0]]["momentum_buffer"].dtype == torch.int8
