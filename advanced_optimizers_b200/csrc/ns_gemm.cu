@@ -136,7 +136,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ktiles = g.K / BK;
   const int n_nb = g.N / BN;
-  const int ntiles = (g.M / BM) * n_nb;
+  const int n_mb = g.M / BM;
+  const int ntiles = n_mb * n_nb;   // walked m-fastest: concurrent tiles share B column blocks
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -167,7 +168,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int t = blockIdx.x; t < ntiles && !*abort_v; t += gridDim.x) {
-        const int m0 = (t / n_nb) * BM, n0 = (t % n_nb) * BN;
+        const int m0 = (t % n_mb) * BM, n0 = (t / n_mb) * BN;
         for (int kt = 0; kt < ktiles; ++kt, ++it) {
           const int s = (int)(it % STAGES);
           const uint32_t use = it / STAGES;
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int m0 = (t / n_nb) * BM, n0 = (t % n_nb) * BN;
+      const int m0 = (t % n_mb) * BM, n0 = (t / n_mb) * BN;
       const int row = m0 + quarter * 32 + lane;
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * TMEM_COLS;
       for (int c = 0; c < BN; c += 16) {
@@ -375,7 +376,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const uint32_t rank = cluster_rank();
   const int ktiles = g.K / BK;
   const int n_nb = g.N / BN;
-  const int ntiles = (g.M / PM) * n_nb;
+  const int n_mb = g.M / PM;
+  const int ntiles = n_mb * n_nb;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
@@ -408,7 +410,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int t = pair; t < ntiles && !*abort_v; t += npairs) {
-        const int m0 = (t / n_nb) * PM + (int)rank * 128, n0 = (t % n_nb) * BN + (int)rank * 128;
+        const int m0 = (t % n_mb) * PM + (int)rank * 128, n0 = (t / n_mb) * BN + (int)rank * 128;
         for (int kt = 0; kt < ktiles; ++kt, ++it) {
           const int s = (int)(it % PSTAGES);
           const uint32_t use = it / PSTAGES;
@@ -484,7 +486,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int m0 = (t / n_nb) * PM + (int)rank * 128, n0 = (t % n_nb) * BN;
+      const int m0 = (t % n_mb) * PM + (int)rank * 128, n0 = (t / n_mb) * BN;
       const int row = m0 + quarter * 32 + lane;
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * TMEM_COLS;
       for (int c = 0; c < BN; c += 16) {
