@@ -26,8 +26,10 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cmath>
 #include <cstdio>
 #include <mutex>
+#include <utility>
 
 #include "advopt.h"
 #include "capi_internal.h"
@@ -576,10 +578,11 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, u
 
 using namespace advopt;
 
-extern "C" int advopt_ns_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B, int32_t ldb,
-                              int32_t b_mn_major, const void* C, int32_t ldc, int32_t M, int32_t N, int32_t K,
-                              float alpha, float beta, int32_t* err, void* stream) {
-  using namespace advopt::ns;
+namespace advopt {
+namespace ns {
+int launch_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B, int32_t ldb, int32_t b_mn_major,
+                const void* C, int32_t ldc, int32_t M, int32_t N, int32_t K, float alpha, float beta, int32_t* err,
+                void* stream) {
   if (!D || !A || !B || M <= 0 || N <= 0 || K <= 0)
     return set_error(ADVOPT_E_INVALID, "advopt_ns_gemm: null operand or empty shape");
   if (M % BM || N % BN || K % BK)
@@ -643,3 +646,58 @@ extern "C" int advopt_ns_gemm(void* D, int32_t ldd, const void* A, int32_t lda, 
   }
   return check_cuda(cudaGetLastError(), "advopt_ns_gemm");
 }
+}  // namespace ns
+}  // namespace advopt
+
+extern "C" int advopt_ns_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B, int32_t ldb,
+                              int32_t b_mn_major, const void* C, int32_t ldc, int32_t M, int32_t N, int32_t K,
+                              float alpha, float beta, int32_t* err, void* stream) {
+  return advopt::ns::launch_gemm(D, ldd, A, lda, B, ldb, b_mn_major, C, ldc, M, N, K, alpha, beta, err, stream);
+}
+
+// The whole Newton–Schulz chain on a loaded workspace (Muon_util.py:7-121):
+// quintic (a, b, c) or CANS with coefficients from the singular-value bounds
+// starting at [cns_lower_bound, 1] (Muon_util.py:69-105), computed here in
+// double precision exactly as the reference's Python does.
+extern "C" int advopt_ns_chain(void* x, void* c, void* a, void* b, int32_t m_pad, int32_t n_pad, int32_t steps,
+                               int32_t cns, double coef_a, double coef_b, double coef_c, double cns_lower_bound,
+                               void** final_x, int32_t* err, void* stream) {
+  using advopt::ns::launch_gemm;
+  if (!x || !c || !a || (!cns && !b) || !final_x || steps < 0 || m_pad <= 0 || n_pad <= 0)
+    return advopt::set_error(ADVOPT_E_INVALID, "advopt_ns_chain: bad arguments");
+  int rc = ADVOPT_OK;
+  if (cns) {
+    double lb = cns_lower_bound, ub = 1.0;
+    for (int i = 0; i < steps && rc == ADVOPT_OK; ++i) {
+      const double lb_ub = lb * ub;
+      const double e_sq = (lb * lb + lb_ub + ub * ub) / 3.0;
+      const double kk = 2.0 * std::pow(e_sq, 1.5);
+      const double ll = lb_ub * (lb + ub);
+      const double den = kk + ll;
+      const double alpha = 6.0 / den;
+      const double c1 = alpha * e_sq, c3 = -alpha / 3.0;
+      rc = launch_gemm(a, m_pad, x, n_pad, x, n_pad, 0, nullptr, 0, m_pad, m_pad, n_pad, 1.0f, 0.0f, err, stream);
+      if (rc == ADVOPT_OK)
+        rc = launch_gemm(c, n_pad, a, m_pad, x, n_pad, 1, x, n_pad, m_pad, n_pad, m_pad, (float)c3, (float)c1, err,
+                         stream);
+      std::swap(x, c);
+      const double e = (kk - ll) / den;
+      lb = 1.0 - e;
+      ub = 1.0 + e;
+    }
+  } else {
+    for (int i = 0; i < steps && rc == ADVOPT_OK; ++i) {
+      rc = launch_gemm(a, m_pad, x, n_pad, x, n_pad, 0, nullptr, 0, m_pad, m_pad, n_pad, 1.0f, 0.0f, err, stream);
+      if (rc == ADVOPT_OK)
+        rc = launch_gemm(b, m_pad, a, m_pad, a, m_pad, 1, a, m_pad, m_pad, m_pad, m_pad, (float)coef_c, (float)coef_b,
+                         err, stream);
+      if (rc == ADVOPT_OK)
+        rc = launch_gemm(c, n_pad, b, m_pad, x, n_pad, 1, x, n_pad, m_pad, n_pad, m_pad, 1.0f, (float)coef_a, err,
+                         stream);
+      std::swap(x, c);
+    }
+  }
+  *final_x = x;
+  return rc;
+}
+

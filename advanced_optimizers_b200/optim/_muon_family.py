@@ -126,31 +126,17 @@ class NSWorkspace:
 
 def run_ns_chain(ws: NSWorkspace, ptrs, m_pad: int, n_pad: int, steps: int, coeffs, cns: bool, cns_bound: float,
                  stream: int) -> int:
-    """The Newton–Schulz iterations on the workspace (X already loaded);
-    returns the device address of the final X.  Every GEMM is
-    advopt_ns_gemm (tcgen05, fp32 accumulate, one bf16 rounding of
-    alpha*acc + beta*C), matching torch.addmm's bf16 semantics."""
-    lib = L.lib()
-    err = int(ws.err.data_ptr())
-    x, c, a, b = ptrs["x"], ptrs["c"], ptrs["a"], ptrs["b"]
-
-    def gemm(d, ldd, a_, lda, b_, ldb, b_mn, c_, ldc, M, N, K, alpha, beta):
-        L.check(lib.advopt_ns_gemm(d, ldd, a_, lda, b_, ldb, b_mn, c_, ldc, M, N, K, f32(alpha), f32(beta), err,
-                                   stream), "advopt_ns_gemm")
-
-    if cns:
-        for c1, c3 in cans_coeffs(steps, cns_bound):
-            gemm(a, m_pad, x, n_pad, x, n_pad, 0, 0, 0, m_pad, m_pad, n_pad, 1.0, 0.0)          # A = X X^T
-            gemm(c, n_pad, a, m_pad, x, n_pad, 1, x, n_pad, m_pad, n_pad, m_pad, c3, c1)      # X' = c1 X + c3 A X
-            x, c = c, x
-    else:
-        qa, qb, qc = coeffs
-        for _ in range(steps):
-            gemm(a, m_pad, x, n_pad, x, n_pad, 0, 0, 0, m_pad, m_pad, n_pad, 1.0, 0.0)          # A = X X^T
-            gemm(b, m_pad, a, m_pad, a, m_pad, 1, a, m_pad, m_pad, m_pad, m_pad, qc, qb)      # B = b A + c A A
-            gemm(c, n_pad, b, m_pad, x, n_pad, 1, x, n_pad, m_pad, n_pad, m_pad, 1.0, qa)     # X' = a X + B X
-            x, c = c, x
-    return x
+    """The Newton–Schulz iterations on the workspace (X already loaded), in
+    one native call (advopt_ns_chain: 3 GEMMs per quintic iteration, 2 per
+    CANS iteration, each a tcgen05 GEMM with fp32 accumulation and one bf16
+    rounding of alpha*acc + beta*C, matching torch.addmm's bf16 semantics);
+    returns the device address of the final X."""
+    out = ctypes.c_void_p(0)
+    qa, qb, qc = (float(v) for v in coeffs)
+    L.check(L.lib().advopt_ns_chain(ptrs["x"], ptrs["c"], ptrs["a"], ptrs["b"], m_pad, n_pad, int(steps),
+                                    1 if cns else 0, qa, qb, qc, float(cns_bound), ctypes.byref(out),
+                                    int(ws.err.data_ptr()), stream), "advopt_ns_chain")
+    return int(out.value)
 
 
 def ns_launches(steps: int, cns: bool) -> int:

@@ -321,6 +321,18 @@ int advopt_philox4x32_10(const uint32_t* counters_keys, uint32_t* out, int64_t n
 int advopt_noise_fill(uint16_t* out, int64_t n, uint64_t seed, uint32_t tensor_id, uint32_t step,
                       uint32_t stream_id, void* stream);
 
+/* The whole Newton–Schulz chain on a loaded workspace with advopt_ns_gemm:
+ * x, c are [m_pad][n_pad] bf16 (x holds the normalised input), a, b are
+ * [m_pad][m_pad] (b unused for CANS).  Quintic: `steps` iterations of
+ * A = X X^T, B = coef_b A + coef_c A A, X = coef_a X + B X.  CANS (cns != 0):
+ * A = X X^T, X = c1 X + c3 A X with (c1, c3) from the bounds starting at
+ * [cns_lower_bound, 1], computed in double as Muon_util.py:69-105 does.
+ * *final_x receives the buffer holding the result (x or c).  Replaces the
+ * loops of Muon_util._newton_schulz_iteration (Muon_util.py:78-114). */
+int advopt_ns_chain(void* x, void* c, void* a, void* b, int32_t m_pad, int32_t n_pad, int32_t steps, int32_t cns,
+                    double coef_a, double coef_b, double coef_c, double cns_lower_bound, void** final_x,
+                    int32_t* err, void* stream);
+
 /* Layout checks for bindings: sizeof of each struct. */
 size_t advopt_sizeof(int which); /* 0 adam_tensor, 1 piece, 2 adam_launch, 3 lion_tensor, 4 muon_args */
 int advopt_abi_version(void);
