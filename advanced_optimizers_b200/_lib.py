@@ -32,6 +32,7 @@ F_PRODIGY_STATS = 1 << 7
 F_FISHER = 1 << 8
 F_FISHER_STATS = 1 << 9
 F_ANCHORS = 1 << 10
+F_NO_WD = 1 << 11
 T_FACTORED = 1 << 0
 T_VEC = 1 << 1
 T_P0_SCALAR = 1 << 2

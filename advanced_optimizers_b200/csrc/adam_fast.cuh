@@ -297,31 +297,41 @@ __device__ __forceinline__ float2 pair_of(const Words<BPE>& in, int i) {
 struct FastScalars {
   float beta1, beta2, c_v, c_m, w_m, w_m1, w_n, w_n1, d;
   float sbc2, rcp_sbc2, eps, step_size, wd;
-  bool w_m_small, w_n_small, has_m, nest, cautious, sr, fact;
+  bool w_m_small, w_n_small, has_m, nest, cautious, sr;
 };
 
-// Element math of one thread's 8 values (AdamW_adv.py:401-465,
-// Muon_AuxAdam.py:148-192, Prodigy_adv.py:430-519, param_update.py:77-156).
-// FAST: Newton–Markstein sqrt / division; `hard` reports elements outside
-// their exact range.  Outputs the new m, the new v (factored: before the
-// factor rebuild) and the packed param words (bf16 pairs after stochastic
-// rounding or RNE; f32 values).
-template <int PREC, bool PBF, int ALGO, bool FAST>
-__device__ __forceinline__ void fast_math(const FastIn<PREC, PBF>& in, const FastScalars& S, int nv,
-                                          const uint32_t (&npw)[4], float2 (&m_new)[4], float2 (&v)[4],
-                                          uint32_t (&pw)[PBF ? 4 : 8], bool& hard) {
+// Option flags of the element math.  A kernel instantiated with CF = kCfDyn
+// reads them from the launch; the others have them compiled in (the host
+// picks such a kernel only when the launch matches it exactly).  Compiled-in
+// flags remove a uniform branch per element pair and let the scheduler
+// interleave the pairs.
+enum : int { kCfDyn = -1, kCfHasM = 1, kCfNest = 2, kCfWd = 4, kCfSR = 8, kCfMSmall = 16, kCfNSmall = 32 };
+template <int CF> __device__ __forceinline__ bool cf_has_m(const FastScalars& S) { return CF < 0 ? S.has_m : (CF & kCfHasM) != 0; }
+template <int CF> __device__ __forceinline__ bool cf_nest(const FastScalars& S) { return CF < 0 ? S.nest : (CF & kCfNest) != 0; }
+template <int CF> __device__ __forceinline__ bool cf_wd(const FastScalars& S) { return CF < 0 ? S.wd != 0.0f : (CF & kCfWd) != 0 && S.wd != 0.0f; }
+template <int CF> __device__ __forceinline__ bool cf_cautious(const FastScalars& S) { return CF < 0 ? S.cautious : false; }
+template <int CF> __device__ __forceinline__ bool cf_sr(const FastScalars& S) { return CF < 0 ? S.sr : (CF & kCfSR) != 0; }
+template <int CF> __device__ __forceinline__ bool cf_msmall(const FastScalars& S) { return CF < 0 ? S.w_m_small : (CF & kCfMSmall) != 0; }
+template <int CF> __device__ __forceinline__ bool cf_nsmall(const FastScalars& S) { return CF < 0 ? S.w_n_small : (CF & kCfNSmall) != 0; }
+
+// Moments of one thread's 8 values (AdamW_adv.py:401-440,
+// Muon_AuxAdam.py:148-175, Prodigy_adv.py:430-470): the new m and the new v
+// (factored: before the factor rebuild).  No square root or division is
+// involved, so these are exact whichever update path follows.
+template <int PREC, bool PBF, int ALGO, int CF, bool FACT>
+__device__ __forceinline__ void fast_moments(const FastIn<PREC, PBF>& in, const FastScalars& S, float2 (&m_new)[4],
+                                             float2 (&v)[4]) {
   using TR = StateTraits<PREC, PBF>;
   using LY = FastLayout<PREC, PBF>;
   constexpr bool kMBF = TR::kMathBF;
   constexpr int kStore = TR::kStore;
   auto Rm2 = [](float2 x) { return kMBF ? make_float2(round_bf16(x.x), round_bf16(x.y)) : x; };
-  const bool vbf = kMBF && !S.fact;
-  float lo = 0x1p100f, hi = 0.0f;
+  constexpr bool vbf = kMBF && !FACT;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const float2 gi = pair_of<LY::BPP, true>(in.g, i);
     float2 vh;
-    if (S.fact) {
+    if (FACT) {
       const float2 mv = (i == 0) ? make_float2(in.mva.x, in.mva.y) : (i == 1) ? make_float2(in.mva.z, in.mva.w)
                       : (i == 2) ? make_float2(in.mvb.x, in.mvb.y) : make_float2(in.mvb.z, in.mvb.w);
       vh = mul2(splat2(in.mu), mv);
@@ -335,17 +345,43 @@ __device__ __forceinline__ void fast_math(const FastIn<PREC, PBF>& in, const Fas
     vi = fma2(mul2(splat2(S.c_v), gi), gi, vi);
     if (vbf) vi = make_float2(round_bf16(vi.x), round_bf16(vi.y));
     v[i] = vi;
-    float2 ui;
-    if (S.has_m) {
+    if (cf_has_m<CF>(S)) {
       float2 m0 = pair_of<LY::BPS, true>(in.m, i);
       if (kStore == 2) m0 = mul2(m0, splat2(in.ms));
-      float2 mi;
-      if (ALGO == ADVOPT_ALGO_PRODIGY) mi = Rm2(fma2(gi, splat2(S.c_m), Rm2(mul2(m0, splat2(S.beta1)))));
-      else mi = Rm2(lerp2(m0, gi, S.w_m, S.w_m1, S.w_m_small));
-      m_new[i] = mi;
-      ui = S.nest ? Rm2(lerp2(mi, gi, S.w_n, S.w_n1, S.w_n_small)) : mi;
+      if (ALGO == ADVOPT_ALGO_PRODIGY) m_new[i] = Rm2(fma2(gi, splat2(S.c_m), Rm2(mul2(m0, splat2(S.beta1)))));
+      else m_new[i] = Rm2(lerp2(m0, gi, S.w_m, S.w_m1, cf_msmall<CF>(S)));
     } else {
       m_new[i] = splat2(0.0f);
+    }
+  }
+}
+
+// Parameter update from the moments (AdamW_adv.py:441-465,
+// Muon_AuxAdam.py:176-192, Prodigy_adv.py:471-519, param_update.py:77-156):
+// packed param words (bf16 pairs after stochastic rounding or RNE; f32
+// values).  FAST: Newton–Markstein sqrt / division; `hard` reports elements
+// outside their exact range, for which the caller reruns this function with
+// the IEEE operations.
+template <int PREC, bool PBF, int ALGO, int CF, bool FACT, bool FAST>
+__device__ __forceinline__ void fast_update(const Words<FastLayout<PREC, PBF>::BPP>& g,
+                                            const Words<FastLayout<PREC, PBF>::BPP>& p, const float2 (&m_new)[4],
+                                            const float2 (&v)[4], const FastScalars& S, const uint32_t (&npw)[4],
+                                            uint32_t (&pw)[PBF ? 4 : 8], bool& hard) {
+  using TR = StateTraits<PREC, PBF>;
+  using LY = FastLayout<PREC, PBF>;
+  constexpr bool kMBF = TR::kMathBF;
+  auto Rm2 = [](float2 x) { return kMBF ? make_float2(round_bf16(x.x), round_bf16(x.y)) : x; };
+  constexpr bool vbf = kMBF && !FACT;
+  float lo = 0x1p100f, hi = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 gi = pair_of<LY::BPP, true>(g, i);
+    const float2 vi = v[i];
+    float2 ui;
+    if (cf_has_m<CF>(S)) {
+      const float2 mi = m_new[i];
+      ui = cf_nest<CF>(S) ? Rm2(lerp2(mi, gi, S.w_n, S.w_n1, cf_nsmall<CF>(S))) : mi;
+    } else {
       ui = (ALGO == ADVOPT_ALGO_PRODIGY) ? Rm2(mul2(gi, splat2(S.d))) : gi;
     }
     // denominator
@@ -369,24 +405,22 @@ __device__ __forceinline__ void fast_math(const FastIn<PREC, PBF>& in, const Fas
     ui = FAST ? div_nm2(ui, du) : make_float2(__fdiv_rn(ui.x, du.x), __fdiv_rn(ui.y, du.y));
     ui = Rm2(ui);
     ui = Rm2(mul2(ui, splat2(S.step_size)));
-    if (!(2 * i < nv)) { m_new[i].x = 0.0f; v[i].x = 0.0f; }
-    if (!(2 * i + 1 < nv)) { m_new[i].y = 0.0f; v[i].y = 0.0f; }
     // parameter update (param_update.py:77-156)
-    float2 pc2 = pair_of<LY::BPP, true>(in.p, i);
-    if (S.wd != 0.0f) {
-      if (S.cautious) {
+    float2 pc2 = pair_of<LY::BPP, true>(p, i);
+    if (cf_wd<CF>(S)) {
+      if (cf_cautious<CF>(S)) {
         float2 prod = mul2(ui, pc2);
-        if (PBF && !S.sr) prod = make_float2(round_bf16(prod.x), round_bf16(prod.y));
+        if (PBF && !cf_sr<CF>(S)) prod = make_float2(round_bf16(prod.x), round_bf16(prod.y));
         const float2 mask = make_float2(prod.x >= 0.0f ? 1.0f : 0.0f, prod.y >= 0.0f ? 1.0f : 0.0f);
         pc2 = fma2(mul2(splat2(-S.wd), pc2), mask, pc2);
       } else {
         pc2 = fma2(pc2, splat2(-S.wd), pc2);
       }
-      if (PBF && !S.sr) pc2 = make_float2(round_bf16(pc2.x), round_bf16(pc2.y));
+      if (PBF && !cf_sr<CF>(S)) pc2 = make_float2(round_bf16(pc2.x), round_bf16(pc2.y));
     }
     const float2 pn = add2(pc2, neg2(ui));
     if (PBF) {
-      if (S.sr)
+      if (cf_sr<CF>(S))
         pw[i] = __byte_perm(__float_as_uint(pn.x) + (npw[i] & 0xFFFFu), __float_as_uint(pn.y) + (npw[i] >> 16), 0x7632);
       else
         pw[i] = f_to_bf16_rne(pn.x) | (f_to_bf16_rne(pn.y) << 16);
@@ -410,8 +444,9 @@ struct FastOcc {
   static constexpr int v = (PREC == ADVOPT_PREC_INT8_SR && PBF && ALGO != ADVOPT_ALGO_PRODIGY) ? 3 : 2;
 };
 
-template <int PREC, bool PBF, int ALGO, bool NOISE_IN>
-__global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v)) adam_fast_kernel(const advopt_adam_launch L) {
+template <int PREC, bool PBF, int ALGO, bool NOISE_IN, int CF>
+__global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
+    adam_fast_kernel(const advopt_adam_launch L, const PhiloxKeys K) {
   using TR = StateTraits<PREC, PBF>;
   using LY = FastLayout<PREC, PBF>;
   constexpr int kStore = TR::kStore;
@@ -432,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v)) adam_
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int S = L.stages;
   const uint32_t F = L.flags;
-  const bool has_m = F & ADVOPT_F_HAS_M;
+  const bool has_m = CF < 0 ? (F & ADVOPT_F_HAS_M) != 0 : (CF & kCfHasM) != 0;
   const bool pstats = (ALGO == ADVOPT_ALGO_PRODIGY) && (F & ADVOPT_F_PRODIGY_STATS);
   FastScalars SC;
   SC.beta1 = L.beta1;
@@ -485,7 +520,6 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v)) adam_
     // column partials in their own global slot row (read-modify-write)
     const bool col_global = fact && d2 > (int64_t)L.gen_offset;
     float* colrow = fact ? (col_global ? T.colpart + (int64_t)pc.slot * d2 : colacc) : nullptr;
-    SC.fact = fact;
     SC.sbc2 = T.sqrt_bc2;
     SC.rcp_sbc2 = __frcp_rn(T.sqrt_bc2);
     SC.eps = T.eps;
@@ -546,17 +580,35 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v)) adam_
       const bool dir = kFull ? false : (direct[slot] != 0);
       fast_load<PREC, PBF>(T, st, dir, k0, nv, v8, has_m, fact, in);
       U4 nzp{0u, 0u, 0u, 0u};
-      if (SC.sr) nzp = noise_words<NOISE_IN>(L, T, T.nz_p, kNoiseP, k0, nv);
-      const uint32_t npw[4] = {nzp.x, nzp.y, nzp.z, nzp.w};
+      if (cf_sr<CF>(SC)) nzp = noise_words_k<NOISE_IN>(K, T, T.nz_p, kNoiseP, k0, nv);
       float2 m_new[4], v[4];
       uint32_t pw[PBF ? 4 : 8];
-      bool hard = false;
-      fast_math<PREC, PBF, ALGO, true>(in, SC, nv, npw, m_new, v, pw, hard);
-      if (__any_sync(0xffffffffu, hard)) {
-        // some lane of the warp is outside the Newton–Markstein ranges:
-        // recompute the warp's elements with the IEEE operations
-        bool h2;
-        fast_math<PREC, PBF, ALGO, false>(in, SC, nv, npw, m_new, v, pw, h2);
+      fast_moments<PREC, PBF, ALGO, CF, fact>(in, SC, m_new, v);
+      {
+        const uint32_t npw[4] = {nzp.x, nzp.y, nzp.z, nzp.w};
+        bool hard = false;
+        fast_update<PREC, PBF, ALGO, CF, fact, true>(in.g, in.p, m_new, v, SC, npw, pw, hard);
+        if (__any_sync(0xffffffffu, hard)) {
+          // some lane of the warp is outside the Newton–Markstein ranges:
+          // redo the warp's parameter update with the IEEE operations (the
+          // moments are exact either way); its grad / param words and noise
+          // are fetched again rather than kept live through the fast path
+          FastIn<PREC, PBF> in2;
+          fast_load<PREC, PBF>(T, st, dir, k0, nv, v8, false, true, in2);
+          U4 nz2{0u, 0u, 0u, 0u};
+          if (cf_sr<CF>(SC)) nz2 = noise_words_k<NOISE_IN>(K, T, T.nz_p, kNoiseP, k0, nv);
+          const uint32_t npw2[4] = {nz2.x, nz2.y, nz2.z, nz2.w};
+          bool h2;
+          fast_update<PREC, PBF, ALGO, CF, fact, false>(in2.g, in2.p, m_new, v, SC, npw2, pw, h2);
+        }
+      }
+      if (!kFull) {
+        // elements past the tensor's end stay out of the block maxima and sums
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (!(2 * i < nv)) { m_new[i].x = 0.0f; v[i].x = 0.0f; }
+          if (!(2 * i + 1 < nv)) { m_new[i].y = 0.0f; v[i].y = 0.0f; }
+        }
       }
 
       if (pstats) {
@@ -660,8 +712,8 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v)) adam_
       // noise of the quantised states
       U4 nzm{0u, 0u, 0u, 0u}, nzv{0u, 0u, 0u, 0u};
       if (kStore == 2 || TR::kSRStates) {
-        if (has_m) nzm = noise_words<NOISE_IN>(L, T, T.nz_m, kNoiseM, k0, nv);
-        if (!fact) nzv = noise_words<NOISE_IN>(L, T, T.nz_v, kNoiseV, k0, nv);
+        if (has_m) nzm = noise_words_k<NOISE_IN>(K, T, T.nz_m, kNoiseM, k0, nv);
+        if (!fact) nzv = noise_words_k<NOISE_IN>(K, T, T.nz_v, kNoiseV, k0, nv);
       }
       if (row_done) {
         if (tid == 0) {

@@ -284,6 +284,20 @@ __device__ __forceinline__ U4 noise_words(const advopt_adam_launch& L, const Ten
   U4 c{(uint32_t)grp, (uint32_t)(grp >> 32) | (stream << 24), T.tensor_id, T.step};
   return philox4x32_10(c, (uint32_t)L.seed, (uint32_t)(L.seed >> 32));
 }
+// noise_words with the Philox round keys from a kernel-parameter table.
+template <bool NOISE_IN>
+__device__ __forceinline__ U4 noise_words_k(const PhiloxKeys& K, const TensorRegs& T, const int32_t* arr,
+                                            uint32_t stream, int64_t k0, int nv) {
+  if (NOISE_IN) {
+    uint32_t r[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) r[e] = e < nv ? ((uint32_t)arr[k0 + e] & 0xFFFFu) : 0u;
+    return U4{r[0] | (r[1] << 16), r[2] | (r[3] << 16), r[4] | (r[5] << 16), r[6] | (r[7] << 16)};
+  }
+  const uint64_t grp = (uint64_t)k0 >> 3;
+  U4 c{(uint32_t)grp, (uint32_t)(grp >> 32) | (stream << 24), T.tensor_id, T.step};
+  return philox4x32_10_k(c, K);
+}
 __device__ __forceinline__ uint32_t noise_at(const U4& n, int e) {
   const uint32_t w = (e >> 1) == 0 ? n.x : (e >> 1) == 1 ? n.y : (e >> 1) == 2 ? n.z : n.w;
   return (e & 1) ? (w >> 16) : (w & 0xFFFFu);
@@ -751,6 +765,37 @@ namespace advopt {
 // Host launchers, instantiated per precision in adam_<precision>.cu.  A
 // launch with L.stages > 0 (and none of the extended options) runs the fast
 // kernel; everything else runs the general one.
+// Option flags compiled into a specialised fast kernel for this launch, or
+// kCfDyn.  Specialisations exist for the int8_sr / bf16 AdamW step (every
+// tensor with momentum and stochastic rounding, lerp weights below 1/2, no
+// cautious decay): with and without Nesterov, with and without decay.
+template <int PREC, bool PBF, int ALGO>
+int fast_config(const advopt_adam_launch& L) {
+  if (!(PREC == ADVOPT_PREC_INT8_SR && PBF && ALGO == ADVOPT_ALGO_ADAMW)) return kCfDyn;
+  const uint32_t F = L.flags;
+  if (!(F & ADVOPT_F_HAS_M) || !(F & ADVOPT_F_SR) || (F & (ADVOPT_F_CAUTIOUS | ADVOPT_F_NOISE_IN))) return kCfDyn;
+  if (!(fabsf(L.w_m) < 0.5f)) return kCfDyn;
+  int cf = kCfHasM | kCfSR | kCfMSmall;
+  if (F & ADVOPT_F_NESTEROV) {
+    if (!(fabsf(L.w_nest) < 0.5f)) return kCfDyn;
+    cf |= kCfNest | kCfNSmall;
+  }
+  if (!(F & ADVOPT_F_NO_WD)) cf |= kCfWd;
+  return cf;
+}
+
+template <int PREC, bool PBF, int ALGO, int CF>
+cudaError_t launch_fast(const advopt_adam_launch& L, size_t smem, cudaStream_t s) {
+  auto kf = adam_fast_kernel<PREC, PBF, ALGO, false, CF>;
+  cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  kf<<<L.grid, kThreads, smem, s>>>(L, philox_keys(L.seed));
+  return cudaGetLastError();
+}
+
+// Host launchers, instantiated per precision in adam_<precision>.cu.  A
+// launch with L.stages > 0 (and none of the extended options) runs the fast
+// kernel; everything else runs the general one.
 template <int PREC, bool PBF, int ALGO>
 cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
   const bool ext = L.flags & (ADVOPT_F_ATAN2 | ADVOPT_F_NORMED | ADVOPT_F_FISHER | ADVOPT_F_FISHER_STATS |
@@ -758,11 +803,24 @@ cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
   const bool nin = L.flags & ADVOPT_F_NOISE_IN;
   const size_t smem = (size_t)L.smem_floats * sizeof(float);
   if (!ext && L.stages > 0) {
-    auto kf = nin ? adam_fast_kernel<PREC, PBF, ALGO, true> : adam_fast_kernel<PREC, PBF, ALGO, false>;
-    cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    kf<<<L.grid, kThreads, smem, s>>>(L);
-    return cudaGetLastError();
+    if (nin) {
+      auto kf = adam_fast_kernel<PREC, PBF, ALGO, true, kCfDyn>;
+      cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      kf<<<L.grid, kThreads, smem, s>>>(L, philox_keys(L.seed));
+      return cudaGetLastError();
+    }
+    if constexpr (PREC == ADVOPT_PREC_INT8_SR && PBF && ALGO == ADVOPT_ALGO_ADAMW) {
+      constexpr int B = kCfHasM | kCfSR | kCfMSmall, N = kCfNest | kCfNSmall;
+      switch (fast_config<PREC, PBF, ALGO>(L)) {
+        case B: return launch_fast<PREC, PBF, ALGO, B>(L, smem, s);
+        case B | kCfWd: return launch_fast<PREC, PBF, ALGO, B | kCfWd>(L, smem, s);
+        case B | N: return launch_fast<PREC, PBF, ALGO, B | N>(L, smem, s);
+        case B | N | kCfWd: return launch_fast<PREC, PBF, ALGO, B | N | kCfWd>(L, smem, s);
+        default: break;
+      }
+    }
+    return launch_fast<PREC, PBF, ALGO, kCfDyn>(L, smem, s);
   }
   auto k = ext ? (nin ? adam_kernel<PREC, PBF, ALGO, true, true> : adam_kernel<PREC, PBF, ALGO, true, false>)
                : (nin ? adam_kernel<PREC, PBF, ALGO, false, true> : adam_kernel<PREC, PBF, ALGO, false, false>);
@@ -774,8 +832,14 @@ cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
 
 template <int PREC, bool PBF, int ALGO>
 cudaError_t occupancy_adam_algo(int smem_floats, int* ctas, int fast) {
-  auto k = fast ? adam_fast_kernel<PREC, PBF, ALGO, false> : adam_kernel<PREC, PBF, ALGO, false, false>;
   const size_t smem = (size_t)smem_floats * sizeof(float);
+  if (fast) {
+    auto k = adam_fast_kernel<PREC, PBF, ALGO, false, kCfDyn>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas, k, kThreads, smem);
+  }
+  auto k = adam_kernel<PREC, PBF, ALGO, false, false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas, k, kThreads, smem);

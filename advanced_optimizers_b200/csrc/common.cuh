@@ -69,6 +69,38 @@ __device__ __forceinline__ U4 philox4x32_10(U4 c, uint32_t k0, uint32_t k1) {
   return c;
 }
 
+// The ten round keys of a Philox4x32-10 key, computed once on the host and
+// passed as a kernel parameter: the rounds then read them from the constant
+// bank instead of re-deriving the Weyl sequence per call.
+struct PhiloxKeys {
+  uint32_t k[20];   // round i uses k[2i], k[2i+1]
+};
+
+inline PhiloxKeys philox_keys(uint64_t seed) {
+  PhiloxKeys K;
+  uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+  for (int i = 0; i < 10; ++i) {
+    K.k[2 * i] = k0;
+    K.k[2 * i + 1] = k1;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return K;
+}
+
+// Same rounds as philox4x32_10 with the keys from the table.
+__device__ __forceinline__ U4 philox4x32_10_k(U4 c, const PhiloxKeys& K) {
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    uint64_t p0, p1;
+    asm("mul.wide.u32 %0, %1, %2;" : "=l"(p0) : "r"(c.x), "r"(0xD2511F53u));
+    asm("mul.wide.u32 %0, %1, %2;" : "=l"(p1) : "r"(c.z), "r"(0xCD9E8D57u));
+    c = U4{(uint32_t)(p1 >> 32) ^ c.y ^ K.k[2 * i], (uint32_t)p1, (uint32_t)(p0 >> 32) ^ c.w ^ K.k[2 * i + 1],
+           (uint32_t)p0};
+  }
+  return c;
+}
+
 // Noise streams (counter word y carries the stream id in its top byte).
 enum NoiseStream : uint32_t { kNoiseV = 0, kNoiseM = 1, kNoiseP = 2, kNoiseAux = 3 };
 

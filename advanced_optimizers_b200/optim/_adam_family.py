@@ -406,6 +406,8 @@ class AdamFamilyRunner:
             flags |= L.F_SR
         if pl.has_anchor:
             flags |= L.F_ANCHORS
+        if not d["wd"].any():
+            flags |= L.F_NO_WD
         noise_keep = []
         if self.test_noise is not None:
             flags |= L.F_NOISE_IN

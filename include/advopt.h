@@ -62,6 +62,7 @@ extern "C" {
 #define ADVOPT_F_FISHER (1u << 8)      /* Fisher weight decay (needs a stats pass) */
 #define ADVOPT_F_FISHER_STATS (1u << 9)/* this launch only accumulates sum((p*ws)^2) */
 #define ADVOPT_F_ANCHORS (1u << 10)    /* some tensor carries a centered-WD anchor */
+#define ADVOPT_F_NO_WD (1u << 11)      /* no tensor of the launch has weight decay (optional hint) */
 
 /* per-tensor flags */
 #define ADVOPT_T_FACTORED (1u << 0)    /* second moment as rank-1 factors (factored_2nd) */
