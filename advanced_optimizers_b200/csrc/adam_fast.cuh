@@ -89,6 +89,34 @@ struct FastLayout {
   static constexpr int BYTES = V + kChunk * BPS;                  // one stage
 };
 
+// Descriptor fields of the current piece with its first element folded in
+// (written by thread 0 at the start of each piece; the chunks index them with
+// 32-bit offsets).
+struct PieceRegs {
+  unsigned char* p;     // param bytes of the piece
+  unsigned char* m;     // first-moment storage of the piece
+  float* ms;            // block scales of m from the piece's first block
+  float* vs;            // block scales of v
+  float* row;           // factored row factor
+  const float* col;     // factored column factor
+  uint32_t gbase;       // Philox element group of the piece's first element
+  uint32_t tensor_id, step;
+};
+
+template <int PREC, bool PBF>
+__device__ __forceinline__ void piece_regs(const TensorRegs& T, int64_t pb, PieceRegs& P) {
+  using LY = FastLayout<PREC, PBF>;
+  P.p = static_cast<unsigned char*>(T.param) + pb * LY::BPP;
+  P.m = T.m ? static_cast<unsigned char*>(T.m) + pb * LY::BPS : nullptr;
+  P.ms = T.m_scale ? T.m_scale + (pb >> 11) : nullptr;
+  P.vs = T.v_scale ? T.v_scale + (pb >> 11) : nullptr;
+  P.row = T.row;
+  P.col = T.col;
+  P.gbase = (uint32_t)((uint64_t)pb >> 3);
+  P.tensor_id = T.tensor_id;
+  P.step = T.step;
+}
+
 struct Cursor {      // producer position (thread 0)
   int pi;            // piece index
   int64_t cs;        // chunk start
@@ -461,6 +489,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
   __shared__ float redr[2][kWarps];
   __shared__ double dred[kWarps][2];
   __shared__ TensorRegs Ts;
+  __shared__ PieceRegs Ps;
   __shared__ Cursor cur;          // producer state (thread 0 only)
   __shared__ int cur_valid;
 
@@ -510,7 +539,10 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
   for (int pi = pbeg; pi < pend; ++pi) {
     const advopt_piece pc = L.pieces[pi];
     __syncthreads();
-    if (tid == 0) load_tensor(L.tensors + pc.tensor, Ts);
+    if (tid == 0) {
+      load_tensor(L.tensors + pc.tensor, Ts);
+      piece_regs<PREC, PBF>(Ts, pc.begin, Ps);
+    }
     __syncthreads();
     const TensorRegs& T = Ts;
     const bool fact = T.flags & ADVOPT_T_FACTORED;
@@ -530,46 +562,70 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
         *reinterpret_cast<float4*>(colrow + j2) = make_float4(0.f, 0.f, 0.f, 0.f);
       __syncthreads();
     }
-    int64_t r0 = fact ? pc.begin / d2 : 0;
-    int64_t c0 = fact ? pc.begin - r0 * d2 : 0;
+    // Per-piece constants: the descriptor fields the chunks use, read once
+    // from shared memory, with the piece's first element folded in.  Offsets
+    // inside a piece fit 32 bits (the host sends tensors of 2^34 or more
+    // elements to the general kernel), as do the Philox element groups.
+    const int64_t pb = pc.begin;          // a multiple of the 2048-element block
+    const int plen = (int)(pc.end - pc.begin);
+    const PieceRegs& P = Ps;
+    const int d2i = (int)d2;
+    int r0 = fact ? (int)(pb / d2) : 0;
+    int c0 = fact ? (int)(pb - (int64_t)r0 * d2) : 0;
     float racc0 = 0.0f, racc1 = 0.0f;   // this thread's part of rows r0 and r0 + 1
     double st0 = 0.0, st1 = 0.0;
     const uint32_t slice_p = T.slice_p ? T.slice_p : 1u;
 
-    // One chunk; FULL: all 2048 elements present and 16-byte aligned (the
-    // common case, with the tail predicates compiled out).  Returns false
-    // when a bounded wait gave up.
-    auto chunk = [&](int64_t cs, auto full_tag, auto fact_tag) -> bool {
+    // Scalars of a chunk (factored row / column factors, block scales),
+    // loaded one chunk ahead so their L2 latency overlaps the current chunk.
+    float pre_mu = 0.0f, pre_ms = 0.0f, pre_vs = 0.0f;
+    float4 pre_a = make_float4(0.f, 0.f, 0.f, 0.f), pre_b = pre_a;
+    auto prefetch = [&](int off, int c0n, int r0n, auto fact_tag) {
+      constexpr bool fct = decltype(fact_tag)::value;
+      if (fct) {
+        const int nvn = min(kVec, plen - off - tid * kVec);
+        const int cc = c0n + tid * kVec;
+        const bool sec = cc >= d2i;
+        const int col = sec ? cc - d2i : cc;
+        pre_mu = nvn > 0 ? P.row[r0n + (sec ? 1 : 0)] : 0.0f;
+        pre_a = *reinterpret_cast<const float4*>(P.col + col);
+        pre_b = *(reinterpret_cast<const float4*>(P.col + col) + 1);
+      }
+      if (kStore == 2 && has_m) pre_ms = P.ms[off >> 11];
+      if (kStore == 2 && !fct) pre_vs = P.vs[off >> 11];
+    };
+    if (fact) prefetch(0, c0, r0, std::true_type{});
+    else prefetch(0, c0, r0, std::false_type{});
+
+    // One chunk at piece offset `off`; FULL: all 2048 elements present and
+    // 16-byte aligned (the common case, with the tail predicates compiled
+    // out).  Returns false when a bounded wait gave up.
+    auto chunk = [&](int off, auto full_tag, auto fact_tag) -> bool {
       constexpr bool kFull = decltype(full_tag)::value;
       constexpr bool fact = decltype(fact_tag)::value;   // shadows the piece's flag
-      const int clen = kFull ? kChunk : (int)min((int64_t)kChunk, pc.end - cs);
-      const int64_t k0 = cs + tid * kVec;
+      const int clen = kFull ? kChunk : min(kChunk, plen - off);
+      const int toff = off + tid * kVec;                 // this thread's first element in the piece
+      const int64_t k0 = pb + toff;
       const int nv = kFull ? kVec : max(0, min(kVec, clen - tid * kVec));
       const bool v8 = kFull ? true : (vec && nv == kVec);
-      const int64_t blk = cs >> 11;
-      int64_t col = 0;
+      int col = 0;
       bool second = false;
       if (fact) {
-        const int64_t cc = c0 + tid * kVec;
-        second = cc >= d2;
-        col = second ? cc - d2 : cc;
+        const int cc = c0 + tid * kVec;
+        second = cc >= d2i;
+        col = second ? cc - d2i : cc;
       }
-      // per-chunk scalars and factored column factors (L2-resident; issued
-      // before the wait, and again by the IEEE path)
-      auto load_scalars = [&](FastIn<PREC, PBF>& in) {
-        in.mu = 0.0f;
-        in.mva = make_float4(0.f, 0.f, 0.f, 0.f);
-        in.mvb = in.mva;
-        if (fact) {
-          in.mu = nv > 0 ? T.row[r0 + (second ? 1 : 0)] : 0.0f;
-          in.mva = *reinterpret_cast<const float4*>(T.col + col);
-          in.mvb = *(reinterpret_cast<const float4*>(T.col + col) + 1);
-        }
-        in.ms = (has_m && kStore == 2) ? T.m_scale[blk] : 0.0f;
-        in.vs = (!fact && kStore == 2) ? T.v_scale[blk] : 0.0f;
+      // Philox words of one noise stream for this thread's 8 elements
+      auto noise = [&](const int32_t* arr, uint32_t stream) -> U4 {
+        if (NOISE_IN) return noise_words_k<true>(K, T, arr, stream, k0, nv);
+        return philox4x32_10_k(U4{P.gbase + ((uint32_t)toff >> 3), stream << 24, P.tensor_id, P.step}, K);
       };
       FastIn<PREC, PBF> in;
-      load_scalars(in);
+      in.mu = pre_mu;
+      in.mva = pre_a;
+      in.mvb = pre_b;
+      in.ms = pre_ms;
+      in.vs = pre_vs;
       if (!mbar_wait(&bars[slot], par)) {
         // the copies never arrived: report, finish this chunk on whatever is
         // in the stage, and leave uniformly after the next barrier
@@ -580,7 +636,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
       const bool dir = kFull ? false : (direct[slot] != 0);
       fast_load<PREC, PBF>(T, st, dir, k0, nv, v8, has_m, fact, in);
       U4 nzp{0u, 0u, 0u, 0u};
-      if (cf_sr<CF>(SC)) nzp = noise_words_k<NOISE_IN>(K, T, T.nz_p, kNoiseP, k0, nv);
+      if (cf_sr<CF>(SC)) nzp = noise(T.nz_p, kNoiseP);
       float2 m_new[4], v[4];
       uint32_t pw[PBF ? 4 : 8];
       fast_moments<PREC, PBF, ALGO, CF, fact>(in, SC, m_new, v);
@@ -596,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
           FastIn<PREC, PBF> in2;
           fast_load<PREC, PBF>(T, st, dir, k0, nv, v8, false, true, in2);
           U4 nz2{0u, 0u, 0u, 0u};
-          if (cf_sr<CF>(SC)) nz2 = noise_words_k<NOISE_IN>(K, T, T.nz_p, kNoiseP, k0, nv);
+          if (cf_sr<CF>(SC)) nz2 = noise(T.nz_p, kNoiseP);
           const uint32_t npw2[4] = {nz2.x, nz2.y, nz2.z, nz2.w};
           bool h2;
           fast_update<PREC, PBF, ALGO, CF, fact, false>(in2.g, in2.p, m_new, v, SC, npw2, pw, h2);
@@ -644,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
 
       // param store
       if (PBF) {
-        uint16_t* dst = static_cast<uint16_t*>(T.param) + k0;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(P.p) + toff;
         if (v8) {
           *reinterpret_cast<uint4*>(dst) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
         } else {
@@ -653,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
             if (e < nv) dst[e] = (uint16_t)(pw[e >> 1] >> (16 * (e & 1)));
         }
       } else {
-        float* dst = static_cast<float*>(T.param) + k0;
+        float* dst = reinterpret_cast<float*>(P.p) + toff;
         if (v8) {
           reinterpret_cast<uint4*>(dst)[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
           reinterpret_cast<uint4*>(dst)[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);
@@ -696,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
         const float sum = __fadd_rn(s.x, s.y);
         if (second) racc1 = __fadd_rn(racc1, sum);
         else racc0 = __fadd_rn(racc0, sum);
-        row_done = clen >= d2 - c0;   // row r0 ends inside this chunk (uniform)
+        row_done = clen >= d2i - c0;   // row r0 ends inside this chunk (uniform)
         if (row_done) {
           const float w = warp_sum(racc0);
           if (lane == 0) redr[parity][warp] = w;
@@ -712,15 +768,15 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
       // noise of the quantised states
       U4 nzm{0u, 0u, 0u, 0u}, nzv{0u, 0u, 0u, 0u};
       if (kStore == 2 || TR::kSRStates) {
-        if (has_m) nzm = noise_words_k<NOISE_IN>(K, T, T.nz_m, kNoiseM, k0, nv);
-        if (!fact) nzv = noise_words_k<NOISE_IN>(K, T, T.nz_v, kNoiseV, k0, nv);
+        if (has_m) nzm = noise(T.nz_m, kNoiseM);
+        if (!fact) nzv = noise(T.nz_v, kNoiseV);
       }
       if (row_done) {
         if (tid == 0) {
           double t = 0.0;
 #pragma unroll
           for (int w = 0; w < kWarps; ++w) t += (double)redr[parity][w];
-          T.row[r0] = (float)t;
+          P.row[r0] = (float)t;
         }
         racc0 = racc1;
         racc1 = 0.0f;
@@ -730,7 +786,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
           const float bmax = __uint_as_float(__reduce_max_sync(0xffffffffu, redm[parity][lane & (kWarps - 1)]));
           const float scale = block_scale<true>(bmax);
           const uint2 q = quantize8x2<true>(m_new, scale, nzm);
-          uint8_t* dst = static_cast<uint8_t*>(T.m) + k0;
+          uint8_t* dst = P.m + toff;
           if (v8) {
             *reinterpret_cast<uint2*>(dst) = q;
           } else {
@@ -738,7 +794,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
             for (int e = 0; e < 8; ++e)
               if (e < nv) dst[e] = (uint8_t)((e < 4 ? q.x : q.y) >> (8 * (e & 3)));
           }
-          if (tid == 0) T.m_scale[blk] = scale;
+          if (tid == 0) P.ms[off >> 11] = scale;
         } else if (kStore == 1) {
           uint32_t b[8];
           const uint32_t nmw[4] = {nzm.x, nzm.y, nzm.z, nzm.w};
@@ -767,7 +823,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
             for (int e = 0; e < 8; ++e)
               if (e < nv) dst[e] = (uint8_t)((e < 4 ? q.x : q.y) >> (8 * (e & 3)));
           }
-          if (tid == 0) T.v_scale[blk] = scale;
+          if (tid == 0) P.vs[off >> 11] = scale;
         } else if (kStore == 1) {
           uint32_t b[8];
           const uint32_t nvw[4] = {nzv.x, nzv.y, nzv.z, nzv.w};
@@ -784,11 +840,12 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
       }
       if (fact) {
         c0 += clen;
-        if (c0 >= d2) {
-          c0 -= d2;
+        if (c0 >= d2i) {
+          c0 -= d2i;
           r0 += 1;
         }
       }
+      if (off + kChunk < plen) prefetch(off + kChunk, c0, r0, fact_tag);
       parity ^= 1;
       if (++slot == S) {
         slot = 0;
@@ -796,12 +853,12 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
       }
       return true;
     };
-    for (int64_t cs = pc.begin; cs < pc.end; cs += kChunk) {
-      const bool full = vec && (pc.end - cs >= kChunk);
-      const bool ok = full ? (fact ? chunk(cs, std::true_type{}, std::true_type{})
-                                   : chunk(cs, std::true_type{}, std::false_type{}))
-                           : (fact ? chunk(cs, std::false_type{}, std::true_type{})
-                                   : chunk(cs, std::false_type{}, std::false_type{}));
+    for (int off = 0; off < plen; off += kChunk) {
+      const bool full = vec && (plen - off >= kChunk);
+      const bool ok = full ? (fact ? chunk(off, std::true_type{}, std::true_type{})
+                                   : chunk(off, std::true_type{}, std::false_type{}))
+                           : (fact ? chunk(off, std::false_type{}, std::true_type{})
+                                   : chunk(off, std::false_type{}, std::false_type{}));
       if (!ok) return;
     }
 

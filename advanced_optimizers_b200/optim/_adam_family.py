@@ -246,7 +246,8 @@ class GroupPlan:
         ext = cfg.use_atan2 or cfg.normed or cfg.fisher or self.has_anchor
         factors_aligned = all(aligned16(st["mu_v_nmf"], st["mv_v_nmf"]) for st in self.states
                               if st.get("factored_2nd", False))
-        self.fast = (not ext) and (not any_generic) and factors_aligned
+        # the fast kernel keeps element offsets in 32 bits (tensors below 2^34 elements)
+        self.fast = (not ext) and (not any_generic) and factors_aligned and max(numels, default=0) < (1 << 34)
         if self.fast:
             bpp = 2 if self.pdt == L.DT_BF16 else 4
             bps = {0: 4, 1: 2, 2: 1, 3: 2 if self.pdt == L.DT_BF16 else 4}[self.precision]
