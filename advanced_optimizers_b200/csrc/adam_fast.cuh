@@ -259,10 +259,12 @@ __device__ __forceinline__ uint2 quantize8x2(const float2 (&x)[4], float scale, 
   for (int i = 0; i < 4; ++i) {
     const float2 q0 = mul2(x[i], splat2(y1));
     const float2 q = fma2(fma2(neg2(q0), splat2(safe), x[i]), splat2(y1), q0);
-    // noise r * 2^-16 from bits: (1 + r*2^-16) - 1
-    const float2 n1 = make_float2(__uint_as_float(0x3F800000u | ((nw[i] & 0xFFFFu) << 7)),
-                                  __uint_as_float(0x3F800000u | ((nw[i] >> 16) << 7)));
-    float2 y = add2(q, add2(n1, splat2(-1.0f)));
+    // noise r * 2^-16 from bits: the 16 bits placed under the exponent of 1
+    // give 1 + r*2^-23 (one byte permute), minus 1 exactly, then r*2^-23 * 128
+    // = r*2^-16 enters a single rounding: y = RN(q + r*2^-16)
+    const float2 n1 = make_float2(__uint_as_float(__byte_perm(nw[i], 0x3F80u, 0x5410)),
+                                  __uint_as_float(__byte_perm(nw[i], 0x3F80u, 0x5432)));
+    float2 y = fma2(add2(n1, splat2(-1.0f)), splat2(128.0f), q);
     // int8: floor(y) >= -128 needs the lower clamp only (y < 128 when
     // |x| <= bmax); uint8: y can reach 256.0 exactly, so clamp above too
     if (SIGNED) y = make_float2(fmaxf(y.x, -127.0f), fmaxf(y.y, -127.0f));
@@ -312,7 +314,9 @@ __device__ __forceinline__ void fast_load(const TensorRegs& T, const unsigned ch
 template <int BPE, bool SIGNED>
 __device__ __forceinline__ float2 pair_of(const Words<BPE>& in, int i) {
   if (BPE == 4) return make_float2(__uint_as_float(in.w[2 * i]), __uint_as_float(in.w[2 * i + 1]));
-  if (BPE == 2) return make_float2(__uint_as_float(in.w[i] << 16), __uint_as_float(in.w[i] & 0xFFFF0000u));
+  // bf16 pair: low half moved up by a byte permute (ALU pipe rather than a
+  // shift on the FMA pipe), high half masked
+  if (BPE == 2) return make_float2(__uint_as_float(__byte_perm(in.w[i], 0u, 0x1044)), __uint_as_float(in.w[i] & 0xFFFF0000u));
   const uint32_t w0 = in.w[i >> 1];
   const uint32_t w = SIGNED ? (w0 ^ 0x80808080u) : w0;
   const uint32_t sel = (i & 1) ? 0x7442u : 0x7440u;
