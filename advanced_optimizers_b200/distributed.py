@@ -11,11 +11,14 @@ of every rank: they are all-reduced (one 2-float NCCL all-reduce per step),
 with the previous step's numerator carried by rank 0 only, so the sharded
 run reproduces the single-GPU d.
 
-With `flat=True` (default) the parameters become views into one rank-ordered
-buffer per dtype — [rank 0's tensors | rank 1's | ...], every segment padded to
-the largest — so the all-gather is a single in-place
-`all_gather_into_tensor` per dtype with no packing copies.  With
-`flat=False` each tensor is broadcast from its owner.
+With `flat=True` (default) the parameters become views into rank-ordered
+flat buffers — [rank 0's tensors | rank 1's | ...], every segment padded to
+the largest — so each all-gather is one in-place `all_gather_into_tensor`
+with no packing copies.  Each rank's owned tensors are split, in step order,
+into the same number of gather buckets of about `bucket_bytes` (one flat
+buffer per bucket and dtype): bucket k is stepped, its all-gather is issued
+asynchronously on NCCL's stream, and bucket k+1 is stepped while it runs.
+With `flat=False` each tensor is broadcast from its owner.
 
 This module is plumbing around the single-GPU classes (it adds no kernel);
 the reference's own distributed hook is Prodigy's `fsdp_in_use`
@@ -94,14 +97,42 @@ class FlatParams:
             self.buffers.append((flat, seg))
 
     @torch.no_grad()
-    def all_gather(self):
+    def all_gather(self, async_op: bool = False):
+        """Refresh every parameter from its owner; with async_op the work
+        handles are returned (NCCL: waiting on them orders the caller's
+        stream after the gather)."""
+        works = []
         for flat, seg in self.buffers:
             mine = flat[self.rank * seg:(self.rank + 1) * seg]
             if dist.get_backend(self.group) == "nccl":
-                dist.all_gather_into_tensor(flat, mine, group=self.group)
+                w = dist.all_gather_into_tensor(flat, mine, group=self.group, async_op=async_op)
             else:
                 chunks = list(flat.split(seg))
-                dist.all_gather(chunks, mine.clone(), group=self.group)
+                w = dist.all_gather(chunks, mine.clone(), group=self.group, async_op=async_op)
+            if async_op:
+                works.append(w)
+        return works
+
+
+def gather_buckets(sizes, owner, world: int, bucket_bytes: Optional[int]):
+    """Split every rank's owned tensors (in parameter order) into the same
+    number of consecutive buckets of about `bucket_bytes` each, by byte
+    fraction, so that bucket k holds a similar byte count on every rank.
+    Returns the bucket index of each tensor."""
+    per_rank = [[i for i in range(len(sizes)) if owner[i] == r] for r in range(world)]
+    totals = [sum(sizes[i] for i in idx) for idx in per_rank]
+    if not bucket_bytes or bucket_bytes <= 0:
+        return [0] * len(sizes)
+    k = max(1, math.ceil(max(totals, default=0) / bucket_bytes))
+    bucket = [0] * len(sizes)
+    for r, idx in enumerate(per_rank):
+        run = 0
+        for i in idx:
+            # bucket of the tensor's midpoint within the rank's byte range
+            mid = run + sizes[i] / 2
+            bucket[i] = min(k - 1, int(mid * k / totals[r])) if totals[r] > 0 else 0
+            run += sizes[i]
+    return bucket
 
 
 class ShardedOptimizer:
@@ -117,7 +148,8 @@ class ShardedOptimizer:
     collectives)."""
 
     def __init__(self, optimizer_cls, params, *, process_group=None,
-                 cost: Optional[Callable[[dict, torch.Tensor], float]] = None, flat: bool = True, **kwargs):
+                 cost: Optional[Callable[[dict, torch.Tensor], float]] = None, flat: bool = True,
+                 bucket_bytes: Optional[int] = 1 << 30, **kwargs):
         if not (dist.is_available() and dist.is_initialized()):
             raise RuntimeError("ShardedOptimizer needs an initialised torch.distributed process group")
         self.group = process_group
@@ -136,35 +168,60 @@ class ShardedOptimizer:
                 merged.update({k: v for k, v in g.items() if k != "params"})
                 costs.append(cost(g, p) if cost is not None else default_cost(optimizer_cls, merged, p))
         self.owner = lpt_partition(costs, self.world)
-        own = {id(p) for p, r in zip(self.all_params, self.owner) if r == self.rank}
-        self.flat = FlatParams(self.all_params, self.owner, self.world, self.rank, process_group) if flat else None
-        owned_groups = []
-        for g in groups:
-            ps = [p for p in g["params"] if id(p) in own]
-            if ps:
-                owned_groups.append(dict(g, params=ps))
         self.is_prodigy = getattr(optimizer_cls, "__name__", "") == "Prodigy_adv"
+        # Gather buckets: each is stepped, then its all-gather is issued
+        # asynchronously while the next bucket is stepped.  Prodigy keeps one
+        # bucket (its d estimate couples every tensor of the step).
+        sizes = [p.numel() * p.element_size() for p in self.all_params]
+        overlap = flat and self.world > 1 and not self.is_prodigy
+        self.bucket = gather_buckets(sizes, self.owner, self.world, bucket_bytes if overlap else None)
+        n_buckets = max(self.bucket, default=0) + 1
+        self.flats = []
+        if flat:
+            for k in range(n_buckets):
+                idx = [i for i in range(len(self.all_params)) if self.bucket[i] == k]
+                self.flats.append(FlatParams([self.all_params[i] for i in idx], [self.owner[i] for i in idx],
+                                             self.world, self.rank, process_group))
         if self.is_prodigy:
             kwargs = dict(kwargs, fsdp_in_use=self.world > 1)
-        self.optimizer = optimizer_cls(owned_groups, **kwargs) if owned_groups else None
-        if self.optimizer is not None and hasattr(self.optimizer, "_ids"):
-            # Philox streams keyed by the tensor's global index: the sharded
-            # step draws the same noise as a single-process step
-            for i, (p, r) in enumerate(zip(self.all_params, self.owner)):
-                if r == self.rank:
-                    self.optimizer._ids[id(p)] = i
-        if self.is_prodigy and self.optimizer is not None:
-            # the carried numerator is already global: count it on one rank
-            self.optimizer._carry_scale = 1.0 if self.rank == 0 else 0.0
-            self.optimizer._process_group = process_group
+        self.optimizers = []
+        for k in range(n_buckets):
+            own = {id(p) for i, p in enumerate(self.all_params) if self.owner[i] == self.rank and self.bucket[i] == k}
+            owned_groups = []
+            for g in groups:
+                ps = [p for p in g["params"] if id(p) in own]
+                if ps:
+                    owned_groups.append(dict(g, params=ps))
+            opt = optimizer_cls(owned_groups, **kwargs) if owned_groups else None
+            if opt is not None and hasattr(opt, "_ids"):
+                # Philox streams keyed by the tensor's global index: the sharded
+                # step draws the same noise as a single-process step
+                for i, p in enumerate(self.all_params):
+                    if id(p) in own:
+                        opt._ids[id(p)] = i
+            if self.is_prodigy and opt is not None:
+                # the carried numerator is already global: count it on one rank
+                opt._carry_scale = 1.0 if self.rank == 0 else 0.0
+                opt._process_group = process_group
+            self.optimizers.append(opt)
+
+    @property
+    def optimizer(self):
+        """The inner optimizer of this rank when there is one bucket (the
+        first non-empty one otherwise)."""
+        return next((o for o in self.optimizers if o is not None), None)
 
     @property
     def param_groups(self):
-        return self.optimizer.param_groups if self.optimizer is not None else []
+        return [g for o in self.optimizers if o is not None for g in o.param_groups]
 
     @property
     def state(self):
-        return self.optimizer.state if self.optimizer is not None else {}
+        out = {}
+        for o in self.optimizers:
+            if o is not None:
+                out.update(o.state)
+        return out
 
     def owned(self, p) -> bool:
         return self.owner[self._index(p)] == self.rank
@@ -180,8 +237,9 @@ class ShardedOptimizer:
         """Bring every rank's updated tensors to all ranks."""
         if self.world == 1:
             return
-        if self.flat is not None:
-            self.flat.all_gather()
+        if self.flats:
+            for f in self.flats:
+                f.all_gather()
         else:
             for p, r in zip(self.all_params, self.owner):
                 dist.broadcast(p.data, src=r, group=self.group)
@@ -192,13 +250,20 @@ class ShardedOptimizer:
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        if self.optimizer is not None:
-            self.optimizer.step()
-        elif self.is_prodigy and self.world > 1:
-            # a rank without tensors still takes part in the d all-reduce
-            dist.all_reduce(torch.zeros(2, dtype=torch.float32, device=self.all_params[0].device),
-                            op=dist.ReduceOp.SUM, group=self.group)
-        self.gather()
+        works = []
+        for k, opt in enumerate(self.optimizers):
+            if opt is not None:
+                opt.step()
+            elif self.is_prodigy and self.world > 1:
+                # a rank without tensors still takes part in the d all-reduce
+                dist.all_reduce(torch.zeros(2, dtype=torch.float32, device=self.all_params[0].device),
+                                op=dist.ReduceOp.SUM, group=self.group)
+            if self.world > 1 and self.flats:
+                works += self.flats[k].all_gather(async_op=True)
+        for w in works:
+            w.wait()
+        if self.world > 1 and not self.flats:
+            self.gather()
         return loss
 
     def zero_grad(self, set_to_none: bool = True):
@@ -209,8 +274,15 @@ class ShardedOptimizer:
                 p.grad.zero_()
 
     def state_dict(self):
-        return self.optimizer.state_dict() if self.optimizer is not None else {}
+        if len(self.optimizers) == 1:
+            return self.optimizers[0].state_dict() if self.optimizers[0] is not None else {}
+        return {"buckets": [o.state_dict() if o is not None else {} for o in self.optimizers]}
 
     def load_state_dict(self, sd):
-        if self.optimizer is not None:
-            self.optimizer.load_state_dict(sd)
+        if len(self.optimizers) == 1:
+            if self.optimizers[0] is not None:
+                self.optimizers[0].load_state_dict(sd)
+            return
+        for o, s in zip(self.optimizers, sd["buckets"]):
+            if o is not None:
+                o.load_state_dict(s)

@@ -149,6 +149,9 @@ def ns_flops(m: int, n: int, steps: int, cns: bool) -> int:
     return steps * (4 * m * m * n + (0 if cns else 2 * m ** 3))
 
 
+_DEVICE_WS = {}
+
+
 class MuonMatrixRunner:
     """Runs the Muon / AdaMuon step of one matrix at a time on its device."""
 
@@ -159,10 +162,13 @@ class MuonMatrixRunner:
         self.gemm_events = None   # list collecting (start, end, flops) around each NS chain
 
     def workspace(self, device) -> NSWorkspace:
-        ws = self.ws.get(device)
+        # one workspace per device, shared by every runner: the chains of all
+        # optimizers on a device run in stream order, one matrix at a time
+        ws = _DEVICE_WS.get(device)
         if ws is None:
             ws = NSWorkspace(device)
-            self.ws[device] = ws
+            _DEVICE_WS[device] = ws
+        self.ws[device] = ws
         return ws
 
     def check_errors(self):

@@ -204,8 +204,9 @@ def run_ours(args):
     params = [torch.nn.Parameter(torch.empty(sh, dtype=torch.bfloat16, device=dev)) for sh in shapes]
     kw = dict(state_precision="int8_sr", factored_2nd=True, nesterov=True)
     if world > 1:
-        # per-tensor sharding: parameters become views of one rank-ordered
-        # flat buffer, refreshed by a single all_gather_into_tensor per step
+        # per-tensor sharding: parameters become views of rank-ordered flat
+        # buffers (gather buckets), each refreshed by one asynchronous
+        # all_gather_into_tensor while the next bucket is stepped
         sharded = A.ShardedOptimizer(A.AdamW_adv, params, **kw)
         owner = sharded.owner
     else:
@@ -223,7 +224,8 @@ def run_ours(args):
         p.grad = g.to(torch.bfloat16)
         del g, mask
     torch.cuda.empty_cache()
-    opt = sharded.optimizer if sharded is not None else A.AdamW_adv(owned, **kw)
+    opts = [o for o in sharded.optimizers if o is not None] if sharded is not None else [A.AdamW_adv(owned, **kw)]
+    opt = opts[0]
 
     def step():
         if sharded is not None:
@@ -239,8 +241,9 @@ def run_ours(args):
 
     clock_path = os.path.join(tempfile.gettempdir(), f"advopt_clocks_{rank}.csv")
     proc, fh = sample_clocks_start(clock_path)
-    opt._runner.kernel_events = []
-    launches0 = opt._runner.launch_count
+    for o in opts:
+        o._runner.kernel_events = []
+    launches0 = sum(o._runner.launch_count for o in opts)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -255,9 +258,10 @@ def run_ours(args):
     clocks = sample_clocks_stop(proc, fh, clock_path, torch.cuda.get_device_properties(dev).index
                                 if hasattr(torch.cuda.get_device_properties(dev), "index") else local)
     elapsed_ms = e0.elapsed_time(e1)
-    kev = opt._runner.kernel_events
-    opt._runner.kernel_events = None
-    launches = opt._runner.launch_count - launches0
+    kev = [e for o in opts for e in o._runner.kernel_events]
+    for o in opts:
+        o._runner.kernel_events = None
+    launches = sum(o._runner.launch_count for o in opts) - launches0
     kernel_ms = [a.elapsed_time(b) for a, b, _ in kev]
     kernel_avg_ms = float(np.sum(kernel_ms) / max(1, args.steps))
     if world > 1:
@@ -273,7 +277,7 @@ def run_ours(args):
         e2e = run_e2e(args, owned, step, world, dev)
     ns = None
     if not args.no_ns:
-        del opt, owned, params, step, sharded
+        del opt, opts, owned, params, step, sharded
         torch.cuda.empty_cache()
         ns = run_ns_leg(args, world, rank, dev)
     if rank == 0:
@@ -314,8 +318,9 @@ def run_ns_leg(args, world, rank, dev):
             p.normal_(0, 0.02, generator=gen)
     for p in owned:
         p.grad = torch.empty_like(p).normal_(0, 1e-3, generator=gen)
-    opt = sharded.optimizer if sharded is not None else A.Muon_adv([dict(params=owned, optim_type="muon")],
-                                                                   lr=1e-3, beta1=0.95)
+    opts = ([o for o in sharded.optimizers if o is not None] if sharded is not None else
+            [A.Muon_adv([dict(params=owned, optim_type="muon")], lr=1e-3, beta1=0.95)])
+    opt = opts[0]
 
     def step():
         if sharded is not None:
@@ -330,9 +335,9 @@ def run_ns_leg(args, world, rank, dev):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    runner = opt._muon_runner
-    runner.gemm_events = []
-    l0 = opt.launch_count
+    for o in opts:
+        o._muon_runner.gemm_events = []
+    l0 = sum(o.launch_count for o in opts)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
@@ -340,10 +345,12 @@ def run_ns_leg(args, world, rank, dev):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in runner.gemm_events) / steps
-    fl = sum(f for _, _, f in runner.gemm_events) / steps
-    runner.gemm_events = None
-    launches = opt.launch_count - l0
+    gev = [e for o in opts for e in o._muon_runner.gemm_events]
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in gev) / steps
+    fl = sum(f for _, _, f in gev) / steps
+    for o in opts:
+        o._muon_runner.gemm_events = None
+    launches = sum(o.launch_count for o in opts) - l0
     if world > 1:
         t = torch.tensor([ms, gemm_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -354,7 +361,7 @@ def run_ns_leg(args, world, rank, dev):
     except Exception:
         peak, kind = 1400.0, "fallback sustained"
     total_flops = sum(flops)
-    del opt, owned, params, sharded
+    del opt, opts, owned, params, sharded
     torch.cuda.empty_cache()
     return {"workload": f"Muon_adv over {len(shapes)} Llama-3-8B hidden matrices (q/o 4096x4096, k/v 1024x4096, "
                         "gate/up 14336x4096, down 4096x14336), momentum 0.95, 5 quintic Newton-Schulz "

@@ -45,13 +45,14 @@ def _make(seed=0):
     return ps, grads
 
 
-def _worker(rank, world, port, flat, out):
+def _worker(rank, world, port, flat, out, bucket_bytes=1 << 30):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         ps, grads = _make()
-        opt = ShardedOptimizer(PlainSGD, ps, lr=0.5, flat=flat)
+        opt = ShardedOptimizer(PlainSGD, ps, lr=0.5, flat=flat, bucket_bytes=bucket_bytes)
+        out[f"buckets{rank}"] = len(opt.optimizers)
         for step in range(3):
             for p, g in zip(ps, grads):
                 p.grad = g * (step + 1)
@@ -63,13 +64,16 @@ def _worker(rank, world, port, flat, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("flat", [True, False])
-def test_sharded_step_matches_single_process(flat):
+@pytest.mark.parametrize("flat,bucket_bytes", [(True, 1 << 30), (False, 1 << 30), (True, 512)])
+def test_sharded_step_matches_single_process(flat, bucket_bytes):
     world = 2
     port = _free_port()
     mgr = mp.Manager()
     out = mgr.dict()
-    mp.spawn(_worker, args=(world, port, flat, out), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, port, flat, out, bucket_bytes), nprocs=world, join=True)
+    if bucket_bytes == 512:
+        # small buckets: several gather buckets, each all-gathered asynchronously
+        assert out["buckets0"] == out["buckets1"] > 1
     ref, grads = _make()
     opt = PlainSGD(ref, lr=0.5)
     for step in range(3):
