@@ -149,6 +149,81 @@ __global__ void __launch_bounds__(256) prep_kernel(const Args a) {
   }
 }
 
+// ---- vectorised stage 0 for the common layout: bf16 grads, f32 / bf16 /
+// bf16-SR momentum, numel a multiple of 8, 16-byte aligned buffers.  Same
+// element arithmetic, noise and summation order as prep_kernel (each thread
+// sums its 8 squares in float64 in element order, then the CTA sum).
+__device__ __forceinline__ void unpack_bf16x8(const uint4 w, float (&x)[8]) {
+  const uint32_t q[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = bf16_to_f(q[i] & 0xFFFFu);
+    x[2 * i + 1] = bf16_to_f(q[i] >> 16);
+  }
+}
+__device__ __forceinline__ uint4 pack_bf16x8(const uint32_t (&b)[8]) {
+  return make_uint4(b[0] | (b[1] << 16), b[2] | (b[3] << 16), b[4] | (b[5] << 16), b[6] | (b[7] << 16));
+}
+
+template <bool MBF, bool RAW, int ST>
+__global__ void __launch_bounds__(256) prep_vec_kernel(const Args a) {
+  __shared__ double redd[kWarps];
+  const int64_t nchunks = (a.numel + kChunk - 1) / kChunk;
+  for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const int64_t k0 = c * kChunk + threadIdx.x * 8;
+    double ss = 0.0;
+    if (k0 < a.numel) {
+      float g[8], m0[8];
+      unpack_bf16x8(__ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.grad) + k0)), g);
+      if (!RAW) {
+        if (ST == ADVOPT_ST_F32) {
+          const float4 lo = *reinterpret_cast<const float4*>(static_cast<const float*>(a.m) + k0);
+          const float4 hi = *(reinterpret_cast<const float4*>(static_cast<const float*>(a.m) + k0) + 1);
+          m0[0] = lo.x; m0[1] = lo.y; m0[2] = lo.z; m0[3] = lo.w;
+          m0[4] = hi.x; m0[5] = hi.y; m0[6] = hi.z; m0[7] = hi.w;
+        } else {
+          unpack_bf16x8(*reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(a.m) + k0), m0);
+        }
+      }
+      uint32_t r[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (!RAW && ST == ADVOPT_ST_BF16_SR) noise8(a, a.noise_m, kNoiseM, k0, a.numel, r);
+      uint32_t xb[8], mb[8];
+      float mf[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float u = g[e];
+        if (!RAW) {
+          float m1 = lerp_t(m0[e], g[e], a.w_m);
+          if (MBF) m1 = round_bf16(m1);
+          mf[e] = m1;
+          u = m1;
+          if (a.flags & ADVOPT_MU_NESTEROV) {
+            u = lerp_t(g[e], m1, a.w_nest);
+            if (MBF) u = round_bf16(u);
+          }
+          if (a.flags & ADVOPT_MU_SIGN) u = u > 0.0f ? 1.0f : (u < 0.0f ? -1.0f : u);
+          mb[e] = ST == ADVOPT_ST_BF16_SR ? f_to_bf16_sr(m1, r[e]) : f_to_bf16_rne(m1);
+        }
+        xb[e] = f_to_bf16_rne(u);
+        const float xf = bf16_to_f(xb[e]);
+        ss += (double)xf * (double)xf;
+      }
+      *reinterpret_cast<uint4*>(a.x0 + k0) = pack_bf16x8(xb);
+      if (!RAW) {
+        if (ST == ADVOPT_ST_F32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.m) + k0);
+          dst[0] = make_float4(mf[0], mf[1], mf[2], mf[3]);
+          dst[1] = make_float4(mf[4], mf[5], mf[6], mf[7]);
+        } else {
+          *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.m) + k0) = pack_bf16x8(mb);
+        }
+      }
+    }
+    const double s = block_sum_d(ss, redd, 256);
+    if (threadIdx.x == 0) a.partial[c] = s;
+  }
+}
+
 // ||X0||_F -> bf16, clamped at bf16(ns_eps): scalars[0].  One CTA of 1024.
 __global__ void __launch_bounds__(1024) norm_kernel(const Args a, int64_t nparts) {
   __shared__ double red[32];
@@ -193,6 +268,62 @@ __global__ void __launch_bounds__(256) load_kernel(const Args a) {
   for (int ii = threadIdx.y; ii < 32; ii += 8) a.ns[(i0 + ii) * a.ld_ns + j0 + tx] = tile[tx][ii];
 }
 
+// Vectorised load for cols a multiple of 8.  Not transposed: one thread per
+// 8 consecutive workspace columns.  Transposed: 64 x 64 tiles through shared
+// memory (row stride 66 elements keeps 32-bit stores aligned and limits bank
+// conflicts of the column reads to two ways).
+constexpr int kTile = 64, kTileLd = 66;
+
+__global__ void __launch_bounds__(256) load_vec_kernel(const Args a) {
+  const float nrm = a.scalars[0];
+  const float rn = __frcp_rn(nrm);
+  const int64_t gpr = a.n_pad / 8;
+  const int64_t groups = a.m_pad * gpr;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < groups; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = t / gpr, j = (t - i * gpr) * 8;
+    uint4 out = make_uint4(0u, 0u, 0u, 0u);
+    if (i < a.rows && j < a.cols) {   // cols % 8 == 0: the group is all inside
+      float x[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(a.x0 + i * a.cols + j), x);
+      uint32_t b[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) b[e] = f_to_bf16_rne(div_const(x[e], nrm, rn));
+      out = pack_bf16x8(b);
+    }
+    *reinterpret_cast<uint4*>(a.ns + i * a.ld_ns + j) = out;
+  }
+}
+
+__global__ void __launch_bounds__(256) load_vec_t_kernel(const Args a) {
+  __shared__ __align__(16) uint16_t tile[kTile * kTileLd];
+  const float nrm = a.scalars[0];
+  const float rn = __frcp_rn(nrm);
+  // workspace tile rows i0.. (= source columns), columns j0.. (= source rows)
+  const int64_t i0 = (int64_t)blockIdx.y * kTile, j0 = (int64_t)blockIdx.x * kTile;
+  for (int t = threadIdx.x; t < kTile * 8; t += blockDim.x) {
+    const int jj = t >> 3, ig = (t & 7) * 8;
+    const int64_t r = j0 + jj, c = i0 + ig;
+    uint32_t b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (r < a.rows && c < a.cols) {
+      float x[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(a.x0 + r * a.cols + c), x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) b[e] = f_to_bf16_rne(div_const(x[e], nrm, rn));
+    }
+    uint32_t* row = reinterpret_cast<uint32_t*>(tile + jj * kTileLd + ig);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) row[e] = b[2 * e] | (b[2 * e + 1] << 16);
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < kTile * 8; t += blockDim.x) {
+    const int ii = t >> 3, jg = (t & 7) * 8;
+    uint32_t b[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) b[e] = tile[(jg + e) * kTileLd + ii];
+    *reinterpret_cast<uint4*>(a.ns + (i0 + ii) * a.ld_ns + j0 + jg) = pack_bf16x8(b);
+  }
+}
+
 // ---- stage 1/3: U in the param's layout, per-tile sum(U^2) ----
 __global__ void __launch_bounds__(256) store_kernel(const Args a) {
   __shared__ uint16_t tile[32][33];
@@ -221,6 +352,59 @@ __global__ void __launch_bounds__(256) store_kernel(const Args a) {
   }
   const double s = block_sum_d(ss, red, 256);
   if (tx == 0 && threadIdx.y == 0) a.partial[(int64_t)blockIdx.y * gridDim.x + blockIdx.x] = s;
+}
+
+// Vectorised stage 1/3 for cols a multiple of 8: U in the param's layout and
+// per-CTA sum(U^2) (each thread in element order, float64).  Not transposed:
+// a grid-stride loop over 8-element groups; transposed: 64 x 64 tiles.
+__global__ void __launch_bounds__(256) store_vec_kernel(const Args a) {
+  __shared__ double red[8];
+  const int64_t gpr = a.cols / 8, groups = a.rows * gpr;
+  double ss = 0.0;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < groups; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = t / gpr, c = (t - r * gpr) * 8;
+    const uint4 w = *reinterpret_cast<const uint4*>(a.ns_result + r * a.ld_ns + c);
+    *reinterpret_cast<uint4*>(a.u + r * a.cols + c) = w;
+    float x[8];
+    unpack_bf16x8(w, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += (double)x[e] * (double)x[e];
+  }
+  const double s = block_sum_d(ss, red, 256);
+  if (threadIdx.x == 0) a.partial[blockIdx.x] = s;
+}
+
+__global__ void __launch_bounds__(256) store_vec_t_kernel(const Args a) {
+  __shared__ __align__(16) uint16_t tile[kTile * kTileLd];
+  __shared__ double red[8];
+  // param tile rows r0.. (= workspace columns), columns c0.. (= workspace rows)
+  const int64_t r0 = (int64_t)blockIdx.y * kTile, c0 = (int64_t)blockIdx.x * kTile;
+  for (int t = threadIdx.x; t < kTile * 8; t += blockDim.x) {
+    const int cc = t >> 3, rg = (t & 7) * 8;
+    // the workspace is [m_pad][n_pad] with zero padding: always readable
+    const uint4 w = *reinterpret_cast<const uint4*>(a.ns_result + (c0 + cc) * a.ld_ns + r0 + rg);
+    uint32_t* row = reinterpret_cast<uint32_t*>(tile + cc * kTileLd + rg);
+    row[0] = w.x; row[1] = w.y; row[2] = w.z; row[3] = w.w;
+  }
+  __syncthreads();
+  double ss = 0.0;
+  for (int t = threadIdx.x; t < kTile * 8; t += blockDim.x) {
+    const int rr = t >> 3, cg = (t & 7) * 8;
+    const int64_t r = r0 + rr, c = c0 + cg;
+    if (r < a.rows && c < a.cols) {
+      uint32_t b[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) b[e] = tile[(cg + e) * kTileLd + rr];
+      *reinterpret_cast<uint4*>(a.u + r * a.cols + c) = pack_bf16x8(b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float f = bf16_to_f(b[e]);
+        ss += (double)f * (double)f;
+      }
+    }
+  }
+  const double s = block_sum_d(ss, red, 256);
+  if (threadIdx.x == 0) a.partial[(int64_t)blockIdx.y * gridDim.x + blockIdx.x] = s;
 }
 
 // rms_adjustment (Muon_util.py:362-372) in the update's dtype:
@@ -290,6 +474,42 @@ __global__ void __launch_bounds__(256) apply_kernel(const Args a) {
         apply_one(a, k, u, r[e]);
       }
     }
+  }
+}
+
+// Vectorised stage 2 for bf16 params, numel a multiple of 8 (same arithmetic as apply_kernel).
+__global__ void __launch_bounds__(256) apply_vec_kernel(const Args a) {
+  const float sc = a.scalars[1];
+  const bool ubf = a.update_bf16 != 0;
+  const bool sr = a.flags & ADVOPT_MU_SR;
+  const int64_t groups = a.numel / 8;
+  for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k0 = gi * 8;
+    uint32_t r[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (sr) noise8(a, a.noise_p, kNoiseP, k0, a.numel, r);
+    float u[8], p[8];
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(a.u + k0), u);
+    uint16_t* pp = static_cast<uint16_t*>(a.param) + k0;
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(pp), p);
+    uint32_t b[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float ue = __fmul_rn(u[e], sc);
+      if (ubf) ue = round_bf16(ue);
+      float pe = p[e];
+      if (a.wd != 0.0f) {
+        if (a.flags & ADVOPT_MU_CAUTIOUS) {
+          const float mask = __fmul_rn(ue, pe) >= 0.0f ? 1.0f : 0.0f;
+          pe = __fmaf_rn(__fmul_rn(-a.wd, pe), mask, pe);
+        } else {
+          pe = __fmaf_rn(pe, -a.wd, pe);
+        }
+        if (!sr) pe = round_bf16(pe);
+      }
+      const float pn = __fadd_rn(pe, -ue);
+      b[e] = sr ? f_to_bf16_sr(pn, r[e]) : f_to_bf16_rne(pn);
+    }
+    *reinterpret_cast<uint4*>(pp) = pack_bf16x8(b);
   }
 }
 
@@ -420,27 +640,68 @@ extern "C" int advopt_muon_stage(const advopt_muon_args* ap, int32_t stage, void
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t nchunks = (a.numel + kChunk - 1) / kChunk;
   const dim3 tb(32, 8);
+  // the vectorised kernels read and write 8 elements (16 bytes of bf16) at a time
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  const bool vec = a.numel % 8 == 0 && al16(a.grad) && al16(a.x0) && al16(a.u) && (!a.ns || al16(a.ns)) &&
+                   (!a.param || al16(a.param)) && (!a.m || al16(a.m)) && (!a.ns_result || al16(a.ns_result)) &&
+                   a.ld_ns % 8 == 0;
   switch (stage) {
     case 0:
     case 6: {
       if (!a.ns) return set_error(ADVOPT_E_INVALID, "advopt_muon_stage: null workspace");
-      if (stage == 6) prep_kernel<false, true><<<grid_for(nchunks), 256, 0, s>>>(a);
-      else if (a.math_bf16) prep_kernel<true, false><<<grid_for(nchunks), 256, 0, s>>>(a);
-      else prep_kernel<false, false><<<grid_for(nchunks), 256, 0, s>>>(a);
+      const unsigned gp = grid_for(nchunks);
+      if (vec && a.param_bf16 && (stage == 6 || a.m_storage != ADVOPT_ST_Q8)) {
+        if (stage == 6) prep_vec_kernel<false, true, ADVOPT_ST_BF16><<<gp, 256, 0, s>>>(a);
+        else if (a.m_storage == ADVOPT_ST_F32)
+          a.math_bf16 ? prep_vec_kernel<true, false, ADVOPT_ST_F32><<<gp, 256, 0, s>>>(a)
+                      : prep_vec_kernel<false, false, ADVOPT_ST_F32><<<gp, 256, 0, s>>>(a);
+        else if (a.m_storage == ADVOPT_ST_BF16)
+          a.math_bf16 ? prep_vec_kernel<true, false, ADVOPT_ST_BF16><<<gp, 256, 0, s>>>(a)
+                      : prep_vec_kernel<false, false, ADVOPT_ST_BF16><<<gp, 256, 0, s>>>(a);
+        else
+          a.math_bf16 ? prep_vec_kernel<true, false, ADVOPT_ST_BF16_SR><<<gp, 256, 0, s>>>(a)
+                      : prep_vec_kernel<false, false, ADVOPT_ST_BF16_SR><<<gp, 256, 0, s>>>(a);
+      } else if (stage == 6) {
+        prep_kernel<false, true><<<gp, 256, 0, s>>>(a);
+      } else if (a.math_bf16) {
+        prep_kernel<true, false><<<gp, 256, 0, s>>>(a);
+      } else {
+        prep_kernel<false, false><<<gp, 256, 0, s>>>(a);
+      }
       norm_kernel<<<1, 1024, 0, s>>>(a, nchunks);
-      load_kernel<<<dim3((unsigned)(a.n_pad / 32), (unsigned)(a.m_pad / 32)), tb, 0, s>>>(a);
+      if (vec && a.cols % 8 == 0 && tr)
+        load_vec_t_kernel<<<dim3((unsigned)(a.n_pad / kTile), (unsigned)(a.m_pad / kTile)), 256, 0, s>>>(a);
+      else if (vec && a.cols % 8 == 0)
+        load_vec_kernel<<<grid_for(a.m_pad * a.n_pad / 2048), 256, 0, s>>>(a);
+      else
+        load_kernel<<<dim3((unsigned)(a.n_pad / 32), (unsigned)(a.m_pad / 32)), tb, 0, s>>>(a);
       break;
     }
     case 1:
     case 3: {
       if (!a.ns_result) return set_error(ADVOPT_E_INVALID, "advopt_muon_stage: null Newton-Schulz result");
-      const dim3 tg((unsigned)((a.cols + 31) / 32), (unsigned)((a.rows + 31) / 32));
-      store_kernel<<<tg, tb, 0, s>>>(a);
-      if (stage == 1) scale_kernel<<<1, 1024, 0, s>>>(a, (int64_t)tg.x * tg.y);
+      int64_t nparts;
+      if (vec && a.cols % 8 == 0 && tr) {
+        const dim3 tg((unsigned)((a.cols + kTile - 1) / kTile), (unsigned)((a.rows + kTile - 1) / kTile));
+        store_vec_t_kernel<<<tg, 256, 0, s>>>(a);
+        nparts = (int64_t)tg.x * tg.y;
+      } else if (vec && a.cols % 8 == 0) {
+        const unsigned g = grid_for(a.numel / 2048 + 1);
+        store_vec_kernel<<<g, 256, 0, s>>>(a);
+        nparts = g;
+      } else {
+        const dim3 tg((unsigned)((a.cols + 31) / 32), (unsigned)((a.rows + 31) / 32));
+        store_kernel<<<tg, tb, 0, s>>>(a);
+        nparts = (int64_t)tg.x * tg.y;
+      }
+      if (stage == 1) scale_kernel<<<1, 1024, 0, s>>>(a, nparts);
       break;
     }
     case 2:
-      apply_kernel<<<grid_for((a.numel + 8 * 256 - 1) / (8 * 256)), 256, 0, s>>>(a);
+      if (vec && a.param_bf16)
+        apply_vec_kernel<<<grid_for((a.numel + 8 * 256 - 1) / (8 * 256)), 256, 0, s>>>(a);
+      else
+        apply_kernel<<<grid_for((a.numel + 8 * 256 - 1) / (8 * 256)), 256, 0, s>>>(a);
       break;
     case 4:
     case 5: {

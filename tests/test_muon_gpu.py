@@ -198,6 +198,8 @@ def _oracle_hp(adamuon, **kw):
     (False, "bf16", "int8_sr", dict(weight_decay=0.01, cautious_wd=True)),
     (False, "bf16", "auto", dict(nesterov=False, rms_rescaling=False)),
     (False, "f32", "bf16_sr", dict(weight_decay=0.1)),
+    (False, "bf16", "bf16_sr", dict(weight_decay=0.01)),
+    (False, "bf16", "fp32", dict(nesterov=False)),
     (True, "bf16", "int8_sr", dict(accelerated_ns=True)),
     (True, "bf16", "auto", dict(use_atan2=True)),
     (True, "f32", "fp32", dict(weight_decay=0.01, rms_rescaling=False)),
