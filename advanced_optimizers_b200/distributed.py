@@ -144,12 +144,15 @@ class ShardedOptimizer:
 
     `params` may be an iterable of tensors or of param-group dicts (the
     group options are kept for the owned tensors).  `cost(group, p)` overrides
-    the partition cost.  Every rank must call step() (it ends in
-    collectives)."""
+    the partition cost.  `bucket_bytes` sizes the gather buckets (None: one
+    bucket, gathered after the whole step); with more than one bucket the
+    elementwise kernels leave `reserve_sms` SMs free so that the all-gather of
+    the previous bucket runs beside them.  Every rank must call step() (it
+    ends in collectives)."""
 
     def __init__(self, optimizer_cls, params, *, process_group=None,
                  cost: Optional[Callable[[dict, torch.Tensor], float]] = None, flat: bool = True,
-                 bucket_bytes: Optional[int] = 1 << 30, **kwargs):
+                 bucket_bytes: Optional[int] = 1 << 30, reserve_sms: int = 0, **kwargs):
         if not (dist.is_available() and dist.is_initialized()):
             raise RuntimeError("ShardedOptimizer needs an initialised torch.distributed process group")
         self.group = process_group
@@ -199,6 +202,12 @@ class ShardedOptimizer:
                 for i, p in enumerate(self.all_params):
                     if id(p) in own:
                         opt._ids[id(p)] = i
+            if opt is not None and len(self.flats) > 1:
+                # the elementwise kernels leave SMs free for the NCCL all-gather
+                # of the previous bucket, which runs beside them
+                for r in ("_runner", "_adam_runner"):
+                    if hasattr(opt, r):
+                        getattr(opt, r).reserve_sms = reserve_sms
             if self.is_prodigy and opt is not None:
                 # the carried numerator is already global: count it on one rank
                 opt._carry_scale = 1.0 if self.rank == 0 else 0.0

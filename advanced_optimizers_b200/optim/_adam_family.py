@@ -173,7 +173,7 @@ class GroupPlan:
     """Static part of one launch: the tensors (params with grads, one dtype),
     their descriptor table, the pieces and the scratch buffers."""
 
-    def __init__(self, params, states, tensor_ids, cfg: AdamCfg):
+    def __init__(self, params, states, tensor_ids, cfg: AdamCfg, reserve_sms: int = 0):
         self.params = list(params)
         self.states = list(states)
         p0 = self.params[0]
@@ -265,6 +265,9 @@ class GroupPlan:
             self.smem_floats = self.gen_offset + (2 * 2048 + 4 if any_generic else 0)
         sms, ctas = L.adam_occupancy(self.precision, self.pdt, cfg.algo, self.smem_floats, self.fast)
         total_chunks = sum((x + 2047) // 2048 for x in numels)
+        # SMs left free for work running beside the step (a sharded run's
+        # all-gather of the previous bucket)
+        sms = max(1, sms - max(0, int(reserve_sms)))
         self.grid = max(1, min(sms * ctas, total_chunks))
         pieces, offsets, n_slots = plan_pieces(numels, d2s, self.grid)
         self.n_pieces = len(pieces)
@@ -324,6 +327,7 @@ class AdamFamilyRunner:
         self.test_noise = None   # {id(param): {label: int32 CUDA tensor}} for the next step only
         self.kernel_events = None  # list to collect (start, end) CUDA events around the main launch
         self.launch_count = 0      # kernels launched so far (for launch accounting)
+        self.reserve_sms = 0       # SMs the step's grid leaves free (see GroupPlan)
 
     def invalidate(self):
         self.plans.clear()
@@ -338,7 +342,7 @@ class AdamFamilyRunner:
     def get_plan(self, key, params, states, ids, cfg):
         pl = self.plans.get(key)
         if pl is None or any(pl.descs["param"][i] != ptr(p) for i, p in enumerate(params)):
-            pl = GroupPlan(params, states, ids, cfg)
+            pl = GroupPlan(params, states, ids, cfg, self.reserve_sms)
             self.plans[key] = pl
         return pl
 
