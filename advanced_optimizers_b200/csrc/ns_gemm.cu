@@ -107,7 +107,25 @@ struct GemmArgs {
   int M, N, K;
   float alpha, beta;
   int32_t* err;
+  int sym;   // D is symmetric (M == N): compute the blocks on or above the diagonal, mirror the rest
 };
+
+// Origin of tile t of a CTA's walk.  General: m-fastest over the M/BM x N/BN
+// grid.  Symmetric output: only the BN x BN blocks on or above the diagonal,
+// column block nb holding row tiles 0 .. 2nb+1 (still m-fastest, so the
+// concurrent tiles share B column blocks); the epilogue writes each
+// off-diagonal block twice, as itself and transposed.
+__device__ __forceinline__ void tile_origin(int t, int n_mb, int sym, int& m0, int& n0) {
+  if (!sym) {
+    m0 = (t % n_mb) * BM;
+    n0 = (t / n_mb) * BN;
+    return;
+  }
+  int nb = 0;
+  while ((nb + 1) * (nb + 2) <= t) ++nb;
+  m0 = (t - nb * (nb + 1)) * BM;
+  n0 = nb * BN;
+}
 
 constexpr uint32_t TMEM_ALLOC = 2 * TMEM_COLS;   // two accumulators
 
@@ -139,7 +157,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int ktiles = g.K / BK;
   const int n_nb = g.N / BN;
   const int n_mb = g.M / BM;
-  const int ntiles = n_mb * n_nb;   // walked m-fastest: concurrent tiles share B column blocks
+  // walked m-fastest: concurrent tiles share B column blocks
+  const int ntiles = g.sym ? n_nb * (n_nb + 1) : n_mb * n_nb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -170,7 +189,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       for (int t = blockIdx.x; t < ntiles && !*abort_v; t += gridDim.x) {
-        const int m0 = (t % n_mb) * BM, n0 = (t / n_mb) * BN;
+        int m0, n0;
+        tile_origin(t, n_mb, g.sym, m0, n0);
         for (int kt = 0; kt < ktiles; ++kt, ++it) {
           const int s = (int)(it % STAGES);
           const uint32_t use = it / STAGES;
@@ -246,7 +266,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int m0 = (t % n_mb) * BM, n0 = (t / n_mb) * BN;
+      int m0, n0;
+      tile_origin(t, n_mb, g.sym, m0, n0);
+      const bool mirror = g.sym && (m0 / BN) < (n0 / BN);   // off-diagonal block of a symmetric D
       const int row = m0 + quarter * 32 + lane;
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * TMEM_COLS;
       for (int c = 0; c < BN; c += 16) {
@@ -277,6 +299,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint4* dp = reinterpret_cast<uint4*>(g.D + (size_t)row * g.ldd + col);
         dp[0] = make_uint4(o[0], o[1], o[2], o[3]);
         dp[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        if (mirror) {
+          // D[col + j][row]: the 32 lanes hold consecutive rows, so each
+          // column store of the warp is 64 contiguous bytes
+          uint16_t* dt = g.D + (size_t)col * g.ldd + row;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            dt[(size_t)(2 * q) * g.ldd] = (uint16_t)(o[q] & 0xFFFFu);
+            dt[(size_t)(2 * q + 1) * g.ldd] = (uint16_t)(o[q] >> 16);
+          }
+        }
       }
       // the accumulator has been read: the MMA warp may overwrite it
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -580,9 +612,11 @@ using namespace advopt;
 
 namespace advopt {
 namespace ns {
+// sym: the caller guarantees D is symmetric (A @ B symmetric and C symmetric
+// or unused); only the blocks on or above the diagonal are computed.
 int launch_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B, int32_t ldb, int32_t b_mn_major,
                 const void* C, int32_t ldc, int32_t M, int32_t N, int32_t K, float alpha, float beta, int32_t* err,
-                void* stream) {
+                void* stream, int32_t sym = 0) {
   if (!D || !A || !B || M <= 0 || N <= 0 || K <= 0)
     return set_error(ADVOPT_E_INVALID, "advopt_ns_gemm: null operand or empty shape");
   if (M % BM || N % BN || K % BK)
@@ -591,6 +625,7 @@ int launch_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B,
       (C && (reinterpret_cast<uintptr_t>(C) & 15)) || lda % 8 || ldb % 8 || ldd % 8 || (C && ldc % 8))
     return set_error(ADVOPT_E_INVALID, "advopt_ns_gemm: operands must be 16-byte aligned with ld % 8 == 0");
   if (beta != 0.0f && !C) return set_error(ADVOPT_E_INVALID, "advopt_ns_gemm: beta != 0 needs C");
+  if (sym && (M != N || M % BN)) return set_error(ADVOPT_E_INVALID, "advopt_ns_gemm: a symmetric D needs M == N, a multiple of 256");
   int rc = get_encode();
   if (rc != ADVOPT_OK) return rc;
   CUtensorMap ma, mb;
@@ -610,11 +645,12 @@ int launch_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B,
   g.alpha = alpha;
   g.beta = beta;
   g.err = err;
+  g.sym = sym ? 1 : 0;
   // The pair kernel is correct (same parity tests) but measured no faster
   // than the single-CTA kernel on the Newton–Schulz shapes (both about
   // 1.05-1.1 PFLOP/s on 4096 x 14336 chains), so the single-CTA kernel is
   // dispatched; the pair path is kept for tuning its pipeline depth.
-  const bool use_pair = false && (M % PM) == 0;
+  const bool use_pair = false && (M % PM) == 0 && !sym;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
@@ -640,7 +676,7 @@ int launch_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B,
     const int pairs = ntiles < sms / 2 ? ntiles : sms / 2;
     ns_gemm_pair_kernel<<<2 * pairs, THREADS, PSMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, g, b_mn_major);
   } else {
-    const int ntiles = (M / BM) * (N / BN);
+    const int ntiles = sym ? (N / BN) * (N / BN + 1) : (M / BM) * (N / BN);
     const int grid = ntiles < sms ? ntiles : sms;
     ns_gemm_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, g, b_mn_major);
   }
@@ -676,7 +712,7 @@ extern "C" int advopt_ns_chain(void* x, void* c, void* a, void* b, int32_t m_pad
       const double den = kk + ll;
       const double alpha = 6.0 / den;
       const double c1 = alpha * e_sq, c3 = -alpha / 3.0;
-      rc = launch_gemm(a, m_pad, x, n_pad, x, n_pad, 0, nullptr, 0, m_pad, m_pad, n_pad, 1.0f, 0.0f, err, stream);
+      rc = launch_gemm(a, m_pad, x, n_pad, x, n_pad, 0, nullptr, 0, m_pad, m_pad, n_pad, 1.0f, 0.0f, err, stream, 1);
       if (rc == ADVOPT_OK)
         rc = launch_gemm(c, n_pad, a, m_pad, x, n_pad, 1, x, n_pad, m_pad, n_pad, m_pad, (float)c3, (float)c1, err,
                          stream);
@@ -687,10 +723,11 @@ extern "C" int advopt_ns_chain(void* x, void* c, void* a, void* b, int32_t m_pad
     }
   } else {
     for (int i = 0; i < steps && rc == ADVOPT_OK; ++i) {
-      rc = launch_gemm(a, m_pad, x, n_pad, x, n_pad, 0, nullptr, 0, m_pad, m_pad, n_pad, 1.0f, 0.0f, err, stream);
+      // A = X X^T and B = b A + c A A are symmetric: upper blocks only
+      rc = launch_gemm(a, m_pad, x, n_pad, x, n_pad, 0, nullptr, 0, m_pad, m_pad, n_pad, 1.0f, 0.0f, err, stream, 1);
       if (rc == ADVOPT_OK)
         rc = launch_gemm(b, m_pad, a, m_pad, a, m_pad, 1, a, m_pad, m_pad, m_pad, m_pad, (float)coef_c, (float)coef_b,
-                         err, stream);
+                         err, stream, 1);
       if (rc == ADVOPT_OK)
         rc = launch_gemm(c, n_pad, b, m_pad, x, n_pad, 1, x, n_pad, m_pad, n_pad, m_pad, 1.0f, (float)coef_a, err,
                          stream);

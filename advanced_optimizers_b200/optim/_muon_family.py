@@ -149,6 +149,18 @@ def ns_flops(m: int, n: int, steps: int, cns: bool) -> int:
     return steps * (4 * m * m * n + (0 if cns else 2 * m ** 3))
 
 
+def ns_flops_executed(m_pad: int, n_pad: int, steps: int, cns: bool) -> int:
+    """Tensor-core FLOPs the chain issues on the padded workspace: X X^T and
+    (quintic) b A + c A A computed on the 256 x 256 blocks on or above the
+    diagonal only (they are symmetric), the X update in full."""
+    blocks = (m_pad // 256) * (m_pad // 256 + 1) // 2          # upper 256 x 256 blocks
+    sym_gemm = lambda k: 2 * k * 256 * 256 * blocks             # noqa: E731
+    per_iter = sym_gemm(n_pad) + 2 * m_pad * n_pad * m_pad
+    if not cns:
+        per_iter += sym_gemm(m_pad)
+    return steps * per_iter
+
+
 _DEVICE_WS = {}
 
 
@@ -159,7 +171,7 @@ class MuonMatrixRunner:
         self.seed = int(seed)
         self.ws = {}
         self.launch_count = 0
-        self.gemm_events = None   # list collecting (start, end, flops) around each NS chain
+        self.gemm_events = None   # (start, end, algorithmic flops, executed flops) of each NS chain
 
     def workspace(self, device) -> NSWorkspace:
         # one workspace per device, shared by every runner: the chains of all
@@ -275,7 +287,8 @@ class MuonMatrixRunner:
         final = run_ns_chain(ws, ptrs, m_pad, n_pad, ns_steps, ns_coeffs, cns, bound, stream)
         if self.gemm_events is not None:
             ev1.record(torch.cuda.current_stream(p.device))
-            self.gemm_events.append((ev0, ev1, ns_flops(m, n, ns_steps, cns)))
+            self.gemm_events.append((ev0, ev1, ns_flops(m, n, ns_steps, cns),
+                                     ns_flops_executed(m_pad, n_pad, ns_steps, cns)))
         a.ns_result = final
         if adamuon:
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")

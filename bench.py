@@ -274,7 +274,7 @@ def run_ours(args):
     # ---- e2e: grads copied host->device every step, one result read back ----
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, owned, step, world, dev, opt if world == 1 else None)
+        e2e = run_e2e(args, owned, step, world, dev, opt if world == 1 else None, sharded)
     ns = None
     if not args.no_ns:
         del opt, opts, owned, params, step, sharded
@@ -346,8 +346,9 @@ def run_ns_leg(args, world, rank, dev):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     gev = [e for o in opts for e in o._muon_runner.gemm_events]
-    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in gev) / steps
-    fl = sum(f for _, _, f in gev) / steps
+    gemm_ms = sum(e[0].elapsed_time(e[1]) for e in gev) / steps
+    fl = sum(e[2] for e in gev) / steps      # the reference's FLOP count of the chains
+    fx = sum(e[3] for e in gev) / steps      # FLOPs the tensor cores execute (symmetric products halved)
     for o in opts:
         o._muon_runner.gemm_events = None
     launches = sum(o.launch_count for o in opts) - l0
@@ -368,22 +369,27 @@ def run_ns_leg(args, world, rank, dev):
                         "iterations, bf16 'auto' states", "steps": steps, "warmup": warm,
             "ms_per_step": ms, "value": 1000.0 / ms, "unit": "optimizer steps/s",
             "ns_ms_per_step": gemm_ms,
-            "roofline": {"bound": "tensor", "achieved": (fl / (gemm_ms * 1e-3)) / 1e12 if gemm_ms > 0 else 0.0,
+            "roofline": {"bound": "tensor", "achieved": (fx / (gemm_ms * 1e-3)) / 1e12 if gemm_ms > 0 else 0.0,
                          "peak": peak, "unit": "TFLOP/s",
-                         "frac": ((fl / (gemm_ms * 1e-3)) / 1e12) / peak if gemm_ms > 0 else 0.0,
+                         "frac": ((fx / (gemm_ms * 1e-3)) / 1e12) / peak if gemm_ms > 0 else 0.0,
                          "peak_kind": kind, "kernel": "ns_gemm_kernel (tcgen05, 128x256 tiles)",
                          "algorithmic_flops_per_step": total_flops,
-                         "note": "achieved = this rank's algorithmic Newton-Schulz FLOPs / its chain time "
-                                 "(the chains include the tiny normalise/transpose kernels)"},
+                         "executed_flops_per_step": fx,
+                         "algorithmic_tflops": (fl / (gemm_ms * 1e-3)) / 1e12 if gemm_ms > 0 else 0.0,
+                         "note": "achieved = FLOPs this rank's tensor cores execute (padded workspace; X X^T and "
+                                 "b A + c A A on the blocks on or above the diagonal) / its chain time; "
+                                 "algorithmic_tflops = the reference's FLOP count 5(4m^2n+2m^3) / the same time"},
             "gpu_launches": launches}
 
 
-def run_e2e(args, owned, step, world, dev, opt=None):
+def run_e2e(args, owned, step, world, dev, opt=None, sharded=None):
     """Grads copied host->device from pinned memory every step, one result
     read back.  On one GPU the copies run on a side stream and each tensor is
     stepped through `step_parameter` (the per-parameter entry a fused back-pass
     trainer calls) as soon as its grad has landed, so the kernels overlap the
-    copies of the later grads."""
+    copies of the later grads.  Sharded, the copies run bucket by bucket and
+    each gather bucket is stepped (and its all-gather started) once its grads
+    have landed."""
     import torch.distributed as dist
     stage_elems = max(p.numel() for p in owned)
     host = torch.empty(stage_elems, dtype=torch.bfloat16, pin_memory=True)
@@ -395,8 +401,20 @@ def run_e2e(args, owned, step, world, dev, opt=None):
     copy_stream = torch.cuda.Stream(device=dev)
     group = opt.param_groups[0] if per_param else None
 
+    buckets = sharded.owned_buckets() if sharded is not None else None
+
     def e2e_step():
-        if per_param:
+        if buckets is not None:
+            events = []
+            with torch.cuda.stream(copy_stream):
+                for ps in buckets:
+                    for p in ps:
+                        p.grad.view(-1).copy_(host[: p.numel()], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(copy_stream)
+                    events.append(ev)
+            sharded.step(bucket_events=events)
+        elif per_param:
             events = []
             with torch.cuda.stream(copy_stream):
                 for p in owned:
