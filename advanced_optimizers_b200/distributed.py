@@ -254,13 +254,24 @@ class ShardedOptimizer:
                 dist.broadcast(p.data, src=r, group=self.group)
 
     @torch.no_grad()
-    def step(self, closure=None):
+    def owned_buckets(self):
+        """This rank's parameters per gather bucket, in step order."""
+        return [[p for i, p in enumerate(self.all_params) if self.owner[i] == self.rank and self.bucket[i] == k]
+                for k in range(len(self.optimizers))]
+
+    @torch.no_grad()
+    def step(self, closure=None, bucket_events=None):
+        """One sharded step.  `bucket_events` (optional, one CUDA event per
+        bucket): the current stream waits on event k before stepping bucket k,
+        e.g. for grads of that bucket still being copied on another stream."""
         loss = None
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
         works = []
         for k, opt in enumerate(self.optimizers):
+            if bucket_events is not None:
+                torch.cuda.current_stream().wait_event(bucket_events[k])
             if opt is not None:
                 opt.step()
             elif self.is_prodigy and self.world > 1:
