@@ -94,3 +94,25 @@ def test_lpt_partition_is_balanced_and_deterministic():
     loads = [sum(c for c, r in zip(costs, own) if r == k) for k in range(3)]
     assert max(loads) - min(loads) <= max(costs)
     assert lpt_partition([5], 4) == [0]
+
+
+def test_gather_buckets_keep_order_and_balance():
+    """Every rank's tensors go to buckets in step order, all ranks use the
+    same bucket count, and bucket k holds a similar share of every rank's bytes."""
+    from advanced_optimizers_b200.distributed import gather_buckets
+    import random
+    rng = random.Random(3)
+    sizes = [rng.choice([8 << 20, 33 << 20, 117 << 20, 8192]) for _ in range(300)]
+    world = 4
+    owner = lpt_partition(sizes, world)
+    bucket = gather_buckets(sizes, owner, world, 1 << 30)
+    k = max(bucket) + 1
+    assert k > 1
+    totals = [sum(s for s, o in zip(sizes, owner) if o == r) for r in range(world)]
+    for r in range(world):
+        mine = [b for b, o in zip(bucket, owner) if o == r]
+        assert mine == sorted(mine)                      # step order
+        for b in range(k):
+            share = sum(s for s, o, bb in zip(sizes, owner, bucket) if o == r and bb == b) / totals[r]
+            assert abs(share - 1 / k) < 0.5 / k + max(sizes) / totals[r]
+    assert gather_buckets(sizes, owner, world, None) == [0] * len(sizes)
