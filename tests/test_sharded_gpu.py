@@ -34,6 +34,8 @@ def _params(dev):
 
 def _make(name, params, sharded):
     import advanced_optimizers_b200 as A
+    buckets = name.endswith("_buckets")
+    name = name.replace("_buckets", "")
     if name == "adamw":
         cls, args, kw = A.AdamW_adv, params, dict(state_precision="int8_sr", factored_2nd=True, nesterov=True)
     elif name == "prodigy":
@@ -43,7 +45,9 @@ def _make(name, params, sharded):
         vecs = [p for p in params if p.ndim == 1]
         cls, args, kw = A.Muon_adv, [dict(params=mats, optim_type="muon"), dict(params=vecs, optim_type="adam")], {}
     if sharded:
-        return A.ShardedOptimizer(cls, args, **kw)
+        # small gather buckets: several asynchronous all-gathers per step
+        extra = dict(bucket_bytes=256 << 10) if buckets else {}
+        return A.ShardedOptimizer(cls, args, **kw, **extra)
     return cls(args, **kw)
 
 
@@ -51,7 +55,18 @@ def _run(name, params, grads, opt):
     for step in range(3):
         for p, g in zip(params, grads[step]):
             p.grad = g.clone()
-        opt.step()
+        if name.endswith("_buckets"):
+            # each bucket waits on an event, as a trainer copying grads on a side stream would pass
+            n = len(opt.optimizers)
+            assert n > 1, "expected several gather buckets"
+            events = []
+            for _ in range(n):
+                ev = torch.cuda.Event()
+                ev.record()
+                events.append(ev)
+            opt.step(bucket_events=events)
+        else:
+            opt.step()
     torch.cuda.synchronize()
 
 
@@ -77,7 +92,7 @@ def _worker(rank, world, port, name, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("name", ["adamw", "muon", "prodigy"])
+@pytest.mark.parametrize("name", ["adamw", "muon", "prodigy", "adamw_buckets", "muon_buckets"])
 def test_sharded_matches_single_process(name):
     world = 2
     mgr = mp.Manager()
@@ -85,7 +100,7 @@ def test_sharded_matches_single_process(name):
     mp.spawn(_worker, args=(world, _free_port(), name, out), nprocs=world, join=True)
     ps, grads = _params(torch.device("cuda", 0))
     opt = _make(name, ps, False)
-    _run(name, ps, grads, opt)
+    _run(name.replace("_buckets", ""), ps, grads, opt)
     ref = [p.detach().cpu() for p in ps]
     for r in range(world):
         for i, (a, b) in enumerate(zip(out[r], ref)):
