@@ -132,6 +132,7 @@ def lib():
                                       ctypes.c_int),
             "advopt_adam_step_noalloc": ([P, ctypes.POINTER(AdamLaunch), P], ctypes.c_int),
             "advopt_ns_gemm": ([P, I32, P, I32, P, I32, I32, P, I32, I32, I32, I32, F, F, P, P], ctypes.c_int),
+            "advopt_ns_gemm_sym": ([P, I32, P, I32, P, I32, I32, P, I32, I32, I32, F, F, P, P], ctypes.c_int),
             "advopt_muon_stage": ([ctypes.POINTER(MuonArgs), I32, P], ctypes.c_int),
             "advopt_philox4x32_10": ([P, P, ctypes.c_int64, P], ctypes.c_int),
             "advopt_ns_chain": ([P, P, P, P, I32, I32, I32, I32, ctypes.c_double, ctypes.c_double, ctypes.c_double,
@@ -164,7 +165,8 @@ def exported_symbols():
     """Names the header declares (used by the load test)."""
     return ["advopt_adam_step", "advopt_factored_finish", "advopt_prodigy_finish", "advopt_fisher_finish",
             "advopt_lion_step", "advopt_sizeof", "advopt_abi_version", "advopt_last_error",
-            "advopt_adam_occupancy", "advopt_adam_step_noalloc", "advopt_ns_gemm", "advopt_muon_stage", "advopt_philox4x32_10", "advopt_noise_fill", "advopt_ns_chain"]
+            "advopt_adam_occupancy", "advopt_adam_step_noalloc", "advopt_ns_gemm", "advopt_ns_gemm_sym", "advopt_muon_stage", "advopt_philox4x32_10",
+            "advopt_noise_fill", "advopt_ns_chain"]
 
 
 _OCC_CACHE = {}

@@ -68,7 +68,7 @@ __device__ __forceinline__ void load_tensor(const advopt_adam_tensor* t, TensorR
   r.tensor_id = t->tensor_id; r.step = t->step; r.flags = t->flags; r.slice_p = t->slice_p;
 }
 
-// Centered-WD anchor value of element k as float (centered_decay.py:219-261).
+// Centered-WD anchor value of element k as float (centered_decay.py:78-119).
 __device__ __forceinline__ float anchor_value(const TensorRegs& T, int64_t k, bool pbf) {
   const uint32_t mode = (T.flags >> ADVOPT_T_ANCHOR_SHIFT) & 7u;
   if (mode == ADVOPT_ANCHOR_FULL) {

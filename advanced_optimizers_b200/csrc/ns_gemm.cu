@@ -691,6 +691,16 @@ extern "C" int advopt_ns_gemm(void* D, int32_t ldd, const void* A, int32_t lda, 
   return advopt::ns::launch_gemm(D, ldd, A, lda, B, ldb, b_mn_major, C, ldc, M, N, K, alpha, beta, err, stream);
 }
 
+// Same GEMM with a symmetric output: only the 256 x 256 blocks of D on or
+// above the diagonal are computed, and each off-diagonal block is stored a
+// second time, transposed, below the diagonal (the X X^T and b A + c A A
+// products of the quintic iteration, Muon_util.py:108-112).
+extern "C" int advopt_ns_gemm_sym(void* D, int32_t ldd, const void* A, int32_t lda, const void* B, int32_t ldb,
+                                  int32_t b_mn_major, const void* C, int32_t ldc, int32_t M, int32_t K, float alpha,
+                                  float beta, int32_t* err, void* stream) {
+  return advopt::ns::launch_gemm(D, ldd, A, lda, B, ldb, b_mn_major, C, ldc, M, M, K, alpha, beta, err, stream, 1);
+}
+
 // The whole Newton–Schulz chain on a loaded workspace (Muon_util.py:7-121):
 // quintic (a, b, c) or CANS with coefficients from the singular-value bounds
 // starting at [cns_lower_bound, 1] (Muon_util.py:69-105), computed here in

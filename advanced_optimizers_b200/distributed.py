@@ -187,6 +187,12 @@ class ShardedOptimizer:
                                              self.world, self.rank, process_group))
         if self.is_prodigy:
             kwargs = dict(kwargs, fsdp_in_use=self.world > 1)
+            # a rank without tensors follows the owners' d-estimate schedule:
+            # Prodigy_adv.calculate_d all-reduces only while k < prodigy_steps
+            # (or always when prodigy_steps <= 0), then increments k
+            self._empty_k = 0
+            self._empty_prodigy_steps = int(dict(kwargs, **{k: v for k, v in groups[0].items()
+                                                            if k != "params"}).get("prodigy_steps", 0))
         self.optimizers = []
         for k in range(n_buckets):
             own = {id(p) for i, p in enumerate(self.all_params) if self.owner[i] == self.rank and self.bucket[i] == k}
@@ -275,9 +281,13 @@ class ShardedOptimizer:
             if opt is not None:
                 opt.step()
             elif self.is_prodigy and self.world > 1:
-                # a rank without tensors still takes part in the d all-reduce
-                dist.all_reduce(torch.zeros(2, dtype=torch.float32, device=self.all_params[0].device),
-                                op=dist.ReduceOp.SUM, group=self.group)
+                # a rank without tensors still takes part in the d all-reduce,
+                # on the same steps as the owners
+                ps = self._empty_prodigy_steps
+                if not (ps > 0 and self._empty_k >= ps):
+                    dist.all_reduce(torch.zeros(2, dtype=torch.float32, device=self.all_params[0].device),
+                                    op=dist.ReduceOp.SUM, group=self.group)
+                self._empty_k += 1
             if self.world > 1 and self.flats:
                 works += self.flats[k].all_gather(async_op=True)
         for w in works:

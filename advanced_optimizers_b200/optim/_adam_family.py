@@ -69,7 +69,7 @@ def adjust_wds(wd, cwd, p):
 
 @torch.no_grad()
 def init_anchor(p, state, centered_wd, mode):
-    """centered_decay._init_anchor (centered_decay.py:184-217)."""
+    """centered_decay._init_anchor (centered_decay.py:43-76)."""
     if not centered_wd or is_wd_centered(p) or "anchor_data" in state:
         return
     if mode == "float8":
@@ -98,7 +98,7 @@ def init_anchor(p, state, centered_wd, mode):
 
 def anchor_code(state, mode) -> int:
     """Storage of the centered-WD anchor, as dequantize_anchor reads it
-    (centered_decay.py:219-252): by dtype, with the group's mode telling
+    (centered_decay.py:78-119): by dtype, with the group's mode telling
     int8 from int4 codes."""
     if "anchor_data" not in state:
         return 0

@@ -30,7 +30,7 @@ sys.path.insert(0, ROOT)
 
 WORKLOAD = "adamw_adv int8_sr+factored_2nd+nesterov, llama-3-8b shapes, bf16"
 # DRAM bytes (read + write) of adam_fast_kernel per algorithmic byte, from one ncu
-# capture of the 2-layer subset (profiles/adam_fast_kernel_int8sr_factored_llama8b.md):
+# capture of the 2-layer subset:
 # 3.476 GB measured / 3.493 GB algorithmic.  Traffic grows with the elements processed,
 # so the full launch's traffic is reported as this ratio times its algorithmic bytes.
 TRAFFIC_PER_ALG_BYTE = 3.476247e9 / 3.492700320e9

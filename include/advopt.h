@@ -8,7 +8,7 @@
  * which loops `step_parameter(p, group, i)` over the parameters.  Each entry
  * point below replaces one cluster of that loop's tensor ops for a whole
  * parameter group at once; the Python classes in advanced_optimizers_b200/
- * call them through ctypes (the binding INTEGRATION.md shows).
+ * call them through ctypes.
  *
  * Conventions
  *  - All pointers inside the structs are DEVICE pointers unless stated.
@@ -321,6 +321,16 @@ int advopt_muon_stage(const advopt_muon_args* args, int32_t stage, void* stream)
 int advopt_philox4x32_10(const uint32_t* counters_keys, uint32_t* out, int64_t n, void* stream);
 int advopt_noise_fill(uint16_t* out, int64_t n, uint64_t seed, uint32_t tensor_id, uint32_t step,
                       uint32_t stream_id, void* stream);
+
+/* advopt_ns_gemm for a product the caller knows to be symmetric (D = D^T:
+ * A @ B symmetric and C symmetric or unused), M == N a multiple of 256: only
+ * the 256 x 256 blocks on or above the diagonal are computed; every
+ * off-diagonal block is also stored transposed below the diagonal.  Replaces
+ * the two symmetric addmm calls of each quintic iteration, A = X X^T and
+ * B = b A + c A A (Muon_util.py:108-112). */
+int advopt_ns_gemm_sym(void* D, int32_t ldd, const void* A, int32_t lda, const void* B, int32_t ldb,
+                       int32_t b_mn_major, const void* C, int32_t ldc, int32_t M, int32_t K, float alpha, float beta,
+                       int32_t* err, void* stream);
 
 /* The whole Newton–Schulz chain on a loaded workspace with advopt_ns_gemm:
  * x, c are [m_pad][n_pad] bf16 (x holds the normalised input), a, b are

@@ -314,9 +314,49 @@ def nnmf(matrix):
 # weight decay and the final update (param_update.py:15-156)
 # ---------------------------------------------------------------------------
 
+def f32_to_e4m3fn(x):
+    """float32 -> float8_e4m3fn codes (uint8), round to nearest even, as
+    torch's p.to(torch.float8_e4m3fn) (centered_decay.py:55-57): 1 sign, 4
+    exponent (bias 7) and 3 mantissa bits, subnormals down to 2^-9, largest
+    finite 448; no infinity, so magnitudes that round above 448 become the
+    NaN code 0x7F (the conversion does not saturate)."""
+    x = np.asarray(x, np.float32).reshape(-1)
+    sign = np.where(np.signbit(x), 0x80, 0).astype(np.uint8)
+    a = np.abs(x.astype(np.float64))
+    code = np.zeros(a.shape, np.int64)
+    nan = np.isnan(a)
+    a = np.where(nan, 0.0, a)
+    sub = a < 2.0 ** -6
+    q_sub = np.rint(a / 2.0 ** -9).astype(np.int64)            # 0..8 (8 = the smallest normal)
+    _, e = np.frexp(np.where(sub, 1.0, a))                      # a = f * 2^e, f in [0.5, 1)
+    E = e - 1                                                   # a in [2^E, 2^(E+1))
+    q = np.rint(np.where(sub, 8.0, a) / np.ldexp(1.0, E - 3)).astype(np.int64)   # 8..16
+    E = np.where(q == 16, E + 1, E)
+    q = np.where(q == 16, 8, q)
+    normal_code = ((E + 7) << 3) | (q - 8)
+    code = np.where(sub, q_sub, normal_code)
+    big = (~sub) & ((E > 8) | ((E == 8) & (q - 8 > 6)))         # above 448: NaN
+    code = np.where(big | nan, 0x7F, code)
+    return (code.astype(np.uint8) | sign)
+
+
+def e4m3fn_to_f32(b):
+    """float8_e4m3fn codes -> float32 values (exact)."""
+    b = np.asarray(b, np.uint8).astype(np.int64)
+    s = np.where(b & 0x80, -1.0, 1.0)
+    e = (b >> 3) & 0xF
+    m = b & 0x7
+    v = np.where(e == 0, m * 2.0 ** -9, (1.0 + m / 8.0) * np.ldexp(1.0, e - 7))
+    v = np.where((e == 0xF) & (m == 0x7), np.nan, v)
+    return (s * v).astype(np.float32)
+
+
 def dequantize_anchor(state, mode, n):
-    """centered_decay.py:219-261 (float32 result)."""
+    """centered_decay.py:78-119 (float32 result)."""
     data = state["anchor_data"]
+    if data.dtype == np.uint8:
+        # float8_e4m3fn storage: anchor_data.to(dtype) is exact
+        return e4m3fn_to_f32(data).reshape(-1)[:n]
     if mode in ("full", "float8") or data.dtype in (np.float32, np.uint16):
         if data.dtype == np.uint16:
             return from_bf16_bits(data).reshape(-1)[:n]
@@ -411,14 +451,15 @@ def fisher_wd_scaler(p: T, denom: T, atan2: bool):
 
 
 def init_anchor(p_vals, p_dt, mode):
-    """centered_decay.py:184-217 -> dict of anchor state entries."""
+    """centered_decay.py:43-76 -> dict of anchor state entries."""
     st = {}
     flat = _c(p_vals).reshape(-1)
     if mode == "full":
         st["anchor_data"] = bf16_bits(flat).reshape(np.shape(p_vals)) if p_dt == "bf16" else flat.reshape(np.shape(p_vals)).copy()
         return st
     if mode == "float8":
-        raise NotImplementedError("float8 anchors are compared on device only")
+        st["anchor_data"] = f32_to_e4m3fn(flat).reshape(np.shape(p_vals))
+        return st
     blk, bits = (128, 8) if mode == "int8" else (32, 4)
     n = flat.size
     pad = (blk - n % blk) % blk
@@ -729,6 +770,22 @@ def rms_adjustment(u: T, rms_rescaling, lr):
         return T(u.v * scale.v[0], u.dt)
     r, c = u.v.shape[-2], u.v.shape[-1]
     return u.mul_s(lr * math.sqrt(max(1, r / c)))
+
+
+def is_suitable_for_muon(shape, min_dim_size=4, max_aspect_ratio=128.0):
+    """Muon_util._is_suitable_for_muon (Muon_util.py:285-331) on a shape:
+    at least two non-unit dims, no unit dim in the first two positions, the
+    (out, prod(rest)) view no smaller than min_dim_size and no more elongated
+    than max_aspect_ratio."""
+    s = tuple(int(d) for d in shape)
+    if len(s) < 2 or sum(1 for d in s if d > 1) < 2:
+        return False
+    if s[0] == 1 or s[1] == 1:
+        return False
+    dims = (s[0], int(np.prod(s[1:]))) if len(s) >= 3 else s
+    if min(dims) < min_dim_size:
+        return False
+    return max(dims) / min(dims) <= max_aspect_ratio
 
 
 def muon_step(p, p_dt, g, state, hp, noise):

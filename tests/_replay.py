@@ -54,6 +54,22 @@ def values(arr, dt):
     return O.from_bf16_bits(arr) if dt == "bf16" else np.asarray(arr, np.float32)
 
 
+def route_kinds(meta):
+    """'muon' / 'adam' per param of a Muon-family case: the group's optim_type,
+    or the oracle's _is_suitable_for_muon where the group names none; 'main'
+    for the other optimizers."""
+    shapes = [tuple(s) for s in meta["shapes"]]
+    if not meta["groups"]:
+        return ["main"] * len(shapes)
+    kinds, k = [], 0
+    for g in meta["groups"]:
+        for sh in shapes[k:k + g["n"]]:
+            t = g["optim_type"]
+            kinds.append(t if t is not None else ("muon" if O.is_suitable_for_muon(sh) else "adam"))
+        k += g["n"]
+    return kinds
+
+
 def draws(z, step, i):
     out = {}
     pre = f"r_{step}_{i}_"
@@ -91,12 +107,7 @@ def replay(name, steps=None, pin_d=False, teacher=False):
     cls = meta["cls"]
     nsteps = meta["steps"] if steps is None else steps
     ps = [values(z[f"p0_{i}"], dt).reshape(shapes[i]) for i in range(len(shapes))]
-    kinds = []
-    if meta["groups"]:
-        for g in meta["groups"]:
-            kinds += [g["optim_type"]] * g["n"]
-    else:
-        kinds = ["main"] * len(shapes)
+    kinds = route_kinds(meta)
     states = []
     group = None
     if cls == "AdamW_adv":

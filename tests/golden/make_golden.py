@@ -1,7 +1,7 @@
 """Generate the golden fixtures in tests/golden/*.npz from the reference.
 
 Runs adv_optm 2.5.4 (imported from the reference checkout given by
---reference, default /root/reference) on CPU over small seeded parameter
+--reference or the ADV_OPTM_REFERENCE environment variable) on CPU over small seeded parameter
 sets, and records for every case:
 
   * the constructor kwargs, param-group layout, shapes and dtypes,
@@ -35,6 +35,8 @@ def bits(t: torch.Tensor) -> np.ndarray:
     t = t.detach().cpu()
     if t.dtype == torch.bfloat16:
         return t.view(torch.int16).numpy().view(np.uint16).copy()
+    if t.dtype == torch.float8_e4m3fn:
+        return t.view(torch.uint8).numpy().copy()
     return t.numpy().copy()
 
 
@@ -141,6 +143,12 @@ CASES = {
     "adamw_centered_int4": dict(cls="AdamW_adv", dtype="bf16", shapes=[(64, 33), (50,)],
                                 kw=dict(state_precision="fp32", centered_wd=0.1, centered_wd_mode="int4"),
                                 steps=3),
+    # centered weight decay with the reference's default anchor storage (float8_e4m3fn)
+    "adamw_centered_float8": dict(cls="AdamW_adv", dtype="bf16", shapes=[(64, 33), (50,)],
+                                  kw=dict(state_precision="fp32", centered_wd=0.1, weight_decay=0.01), steps=3),
+    "adamw_centered_float8_f32": dict(cls="AdamW_adv", dtype="f32", shapes=[(64, 33), (50,)],
+                                      kw=dict(state_precision="int8_sr", centered_wd=0.05, cautious_wd=True),
+                                      steps=3),
     "adamw_centered_full_f32": dict(cls="AdamW_adv", dtype="f32", shapes=[(64, 33), (50,)],
                                     kw=dict(state_precision="fp32", centered_wd=0.1, centered_wd_mode="full",
                                             cautious_wd=True), steps=3),
@@ -154,6 +162,12 @@ CASES = {
                                  dict(shapes=[(48,)], optim_type="adam")],
                          kw=dict(lr=2e-3, state_precision="int8_sr", weight_decay=0.01,
                                  adam_state_precision="int8_sr", adam_weight_decay=0.01), steps=2),
+    # no optim_type / use_muon: every param is routed by _is_suitable_for_muon
+    # (2-D, 3-D flattened, 1-D, degenerate and extreme-aspect shapes)
+    "muon_auto_route": dict(cls="Muon_adv", dtype="bf16",
+                            groups=[dict(shapes=[(64, 48), (48,), (2, 64), (600, 4), (8, 4, 3), (1, 64), (40, 96)],
+                                         optim_type=None)],
+                            kw=dict(lr=1e-3, adam_state_precision="fp32"), steps=2),
     # config 4 semantics (Prodigy bf16_sr)
     "prodigy_bf16sr": dict(cls="Prodigy_adv", dtype="bf16", shapes=[(120, 40), (40,), (64, 64)],
                            kw=dict(state_precision="bf16_sr", d0=1e-6, slice_p=11), steps=3,
@@ -184,7 +198,10 @@ def run_case(name, spec, adv_optm, pu):
         groups, k = [], 0
         for gspec in spec["groups"]:
             n = len(gspec["shapes"])
-            groups.append({"params": params[k:k + n], "optim_type": gspec["optim_type"]})
+            grp = {"params": params[k:k + n]}
+            if gspec["optim_type"] is not None:
+                grp["optim_type"] = gspec["optim_type"]
+            groups.append(grp)
             k += n
     else:
         groups = params
@@ -204,6 +221,8 @@ def run_case(name, spec, adv_optm, pu):
         for i, p in enumerate(params):
             out[f"p0_{i}"] = bits(p)
             st = opt.state.get(p, {})
+            if "is_muon" in st:
+                out[f"route_{i}"] = np.array(int(bool(st["is_muon"])))
             for key, val in st.items():
                 if torch.is_tensor(val):
                     out[f"st0_{i}_{key}"] = bits(val)
@@ -242,9 +261,12 @@ def run_case(name, spec, adv_optm, pu):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ADV_OPTM_REFERENCE"),
+                    help="checkout of Koratahiu/Advanced_Optimizers (the directory holding adv_optm/)")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set ADV_OPTM_REFERENCE")
     sys.path.insert(0, args.reference)
     import adv_optm  # noqa: E402
     from adv_optm.util import param_update as pu  # noqa: E402

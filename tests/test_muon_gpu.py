@@ -29,7 +29,7 @@ import torch
 
 from _compare import check_bf16_param, check_fp32, check_state
 from _gpu import load_state, to_numpy, to_torch
-from _replay import O, list_cases, load
+from _replay import O, list_cases, load, route_kinds
 
 pytestmark = pytest.mark.gpu
 
@@ -97,12 +97,19 @@ def test_matches_reference_golden(name):
     dt = meta["dtype"]
     shapes = [tuple(s) for s in meta["shapes"]]
     params = [torch.nn.Parameter(to_torch(z[f"p0_{i}"], dt).reshape(sh)) for i, sh in enumerate(shapes)]
-    kinds, groups, k = [], [], 0
+    groups, k = [], 0
     for g in meta["groups"]:
-        groups.append(dict(params=params[k:k + g["n"]], optim_type=g["optim_type"]))
-        kinds += [g["optim_type"]] * g["n"]
+        grp = dict(params=params[k:k + g["n"]])
+        if g["optim_type"] is not None:
+            grp["optim_type"] = g["optim_type"]
+        groups.append(grp)
         k += g["n"]
+    kinds = route_kinds(meta)
     opt = getattr(A, meta["cls"])(groups, **meta["kw"])
+    for i, p in enumerate(params):
+        if f"route_{i}" in z.files:
+            # routing by _is_suitable_for_muon where the group names no optim_type
+            assert bool(opt.state[p]["is_muon"]) == bool(z[f"route_{i}"]), f"{name} param {i}: routing"
     for s in range(meta["steps"]):
         for i, p in enumerate(params):
             if s > 0:
@@ -166,6 +173,28 @@ def test_newton_schulz_matches_oracle(shape, cns, dtype):
     torch.cuda.synchronize()
     assert mine.dtype == G.dtype and mine.shape == G.shape
     ref = O.newton_schulz(O.T(g, dtype), 5, 1e-7, QUINTIC, cns, None).v
+    _check_ns_output(mine.float().cpu().numpy(), ref, f"NS {shape} cns={cns}")
+
+
+@pytest.mark.parametrize("shape,cns", [
+    ((1024, 4096), False), ((1024, 4096), True),      # k/v projections: m = 1024, 4 x 4 blocks of 256
+    ((4096, 4096), False), ((4096, 4096), True),      # q/o projections: m = 4096, 16 x 16 blocks
+    ((14336, 4096), False),                           # gate/up: transposed into the workspace
+    ((4096, 14336), False),                           # down
+])
+def test_newton_schulz_matches_oracle_at_llama_shapes(shape, cns):
+    """The whole chain at the Llama-3-8B matrix shapes, where the symmetric
+    products run on the production tilings (upper blocks computed, lower
+    blocks mirrored), against the oracle's chain (each GEMM in float32,
+    rounded to bf16), with the tolerance of the smaller shapes above."""
+    import advanced_optimizers_b200 as A
+    rng = np.random.default_rng(shape[0] + 3 * shape[1] + int(cns))
+    g = O.round_bf16((rng.standard_normal(shape, dtype=np.float32) * 1e-3).astype(np.float32))
+    G = torch.from_numpy(g).cuda().to(torch.bfloat16)
+    mine = A.newton_schulz(G, steps=5, eps=1e-7, coeffs=QUINTIC, cns=cns)
+    torch.cuda.synchronize()
+    assert mine.dtype == G.dtype and mine.shape == G.shape
+    ref = O.newton_schulz(O.T(g, "bf16"), 5, 1e-7, QUINTIC, cns, None).v
     _check_ns_output(mine.float().cpu().numpy(), ref, f"NS {shape} cns={cns}")
 
 

@@ -52,3 +52,44 @@ def test_ns_gemm_matches_fp32_reference(M, N, K, bmn, alpha, beta):
     assert bad == 0, f"{bad} elements beyond 1 bf16 ulp + 1e-3 rms; max diff {float(diff.max()):.3g}, rms {rms:.3g}"
     rel = float((D.float() - ref32).norm() / ref32.norm())
     assert rel < 4e-3, rel
+
+
+@pytest.mark.parametrize("m,k", [(1024, 4096), (4096, 4096), (4096, 14336)])
+def test_symmetric_products_at_llama_shapes(m, k):
+    """The symmetric-output path at the production tilings (4 x 4 and
+    16 x 16 blocks of 256): A = X X^T from X [m][k] (the k/v, q and gate
+    Newton-Schulz shapes), then B = b A + c A A with the quintic
+    coefficients.  Every element — the computed blocks on or above the
+    diagonal and the mirrored stores below it — is checked against the fp32
+    product with the tolerance of the general GEMM test, and D must be
+    exactly symmetric."""
+    from advanced_optimizers_b200 import _lib as L
+    g = torch.Generator(device="cuda").manual_seed(m + k)
+    X = (torch.randn(m, k, generator=g, device="cuda") / (m * k) ** 0.25).bfloat16()
+    A = torch.empty(m, m, device="cuda", dtype=torch.bfloat16)
+    B = torch.empty_like(A)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    lib = L.lib()
+    # A = X X^T: both operands X, stored [m][k] (K-major)
+    L.check(lib.advopt_ns_gemm_sym(A.data_ptr(), m, X.data_ptr(), k, X.data_ptr(), k, 0, None, m, m, k,
+                                   1.0, 0.0, err.data_ptr(), s), "advopt_ns_gemm_sym")
+    # B = c A A + b A: A is symmetric, so A stored [m][m] serves as [K][N]
+    b, c = -4.7750, 2.0315
+    L.check(lib.advopt_ns_gemm_sym(B.data_ptr(), m, A.data_ptr(), m, A.data_ptr(), m, 1, A.data_ptr(), m, m, m,
+                                   c, b, err.data_ptr(), s), "advopt_ns_gemm_sym")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    for D, ref32, what in ((A, X.float() @ X.float().t(), "X X^T"),
+                           (B, c * (A.float() @ A.float()) + b * A.float(), "b A + c A A")):
+        assert torch.equal(D.view(torch.int16), D.t().contiguous().view(torch.int16)), f"{what}: not symmetric"
+        diff = (D.float() - ref32).abs()
+        rms = float(ref32.pow(2).mean().sqrt())
+        bad = diff > 2.0 ** -8 * ref32.abs() + 1e-3 * rms
+        nb = int(bad.sum())
+        if nb:
+            r, cidx = torch.nonzero(bad)[0].tolist()
+            raise AssertionError(f"{what} m={m}: {nb} elements beyond 1 bf16 ulp + 1e-3 rms, first at ({r}, {cidx}) "
+                                 f"block ({r // 256}, {cidx // 256}); max diff {float(diff.max()):.3g}, rms {rms:.3g}")
+        rel = float((D.float() - ref32).norm() / ref32.norm())
+        assert rel < 4e-3, (what, rel)

@@ -18,7 +18,7 @@ forcing), so each comparison measures one step.
 import numpy as np
 import pytest
 
-from _replay import O, list_cases, load, replay
+from _replay import O, list_cases, load, replay, route_kinds
 
 CASES = list_cases()
 
@@ -51,10 +51,11 @@ def test_oracle_matches_reference(name):
     meta, z = load(name)
     dt = meta["dtype"]
     ns = meta["cls"] in ("Muon_adv", "AdaMuon_adv")
-    kinds = []
-    if meta["groups"]:
-        for g in meta["groups"]:
-            kinds += [g["optim_type"]] * g["n"]
+    kinds = route_kinds(meta)
+    for i in range(len(meta["shapes"])):
+        if f"route_{i}" in z.files:
+            # the reference's own routing decision (state['is_muon'])
+            assert (kinds[i] == "muon") == bool(z[f"route_{i}"]), f"{name} param {i}: routing"
     prev = {i: z[f"p0_{i}"] for i in range(len(meta["shapes"]))}
     for s, i, p, st, group in replay(name, pin_d=True, teacher=True):
         if i < 0:

@@ -116,3 +116,62 @@ def test_gather_buckets_keep_order_and_balance():
             share = sum(s for s, o, bb in zip(sizes, owner, bucket) if o == r and bb == b) / totals[r]
             assert abs(share - 1 / k) < 0.5 / k + max(sizes) / totals[r]
     assert gather_buckets(sizes, owner, world, None) == [0] * len(sizes)
+
+
+class _ProdigyScheduleStandIn(torch.optim.Optimizer):
+    """CPU stand-in with Prodigy_adv's collective schedule only: calculate_d
+    all-reduces the two d sums while k < prodigy_steps (always when
+    prodigy_steps <= 0), then k += 1 (Prodigy_adv.py:540-576)."""
+
+    def __init__(self, params, lr=0.1, prodigy_steps=0, fsdp_in_use=False):
+        super().__init__(params, dict(lr=lr, prodigy_steps=prodigy_steps, k=0))
+        self.fsdp_in_use = fsdp_in_use
+        self._carry_scale = 1.0
+        self._process_group = None
+        self.reduces = 0
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        g0 = self.param_groups[0]
+        if not (g0["prodigy_steps"] > 0 and g0["k"] >= g0["prodigy_steps"]):
+            dist.all_reduce(torch.zeros(2), op=dist.ReduceOp.SUM, group=self._process_group)
+            self.reduces += 1
+        for g in self.param_groups:
+            g["k"] += 1
+
+
+_ProdigyScheduleStandIn.__name__ = "Prodigy_adv"
+
+
+def _prodigy_worker(rank, world, port, prodigy_steps, out):
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        ps = [torch.nn.Parameter(torch.ones(4)), torch.nn.Parameter(torch.ones(3))]
+        opt = ShardedOptimizer(_ProdigyScheduleStandIn, ps, prodigy_steps=prodigy_steps)
+        for _ in range(5):
+            for p in ps:
+                p.grad = torch.ones_like(p)
+            opt.step()
+        out[rank] = "empty" if opt.optimizer is None else opt.optimizer.reduces
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("prodigy_steps", [0, 1, 3])
+def test_prodigy_rank_without_tensors_follows_the_d_schedule(prodigy_steps):
+    """More ranks than tensors: the empty rank must join exactly the d
+    all-reduces the owners make, also after prodigy_steps freezes d (a
+    mismatch would leave the owners' next collective waiting on it)."""
+    world = 3
+    port = _free_port()
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_prodigy_worker, args=(world, port, prodigy_steps, out), nprocs=world, join=True)
+    owners = [v for v in out.values() if v != "empty"]
+    assert list(out.values()).count("empty") == 1
+    expect = 5 if prodigy_steps <= 0 else min(5, prodigy_steps)
+    assert owners == [expect] * 2
