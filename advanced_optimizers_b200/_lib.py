@@ -15,7 +15,7 @@ import numpy as np
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libadvopt.so")
-ABI_VERSION = 1
+ABI_VERSION = 3
 
 # ---- constants mirrored from include/advopt.h ----
 DT_F32, DT_BF16 = 0, 1
@@ -33,6 +33,7 @@ F_FISHER = 1 << 8
 F_FISHER_STATS = 1 << 9
 F_ANCHORS = 1 << 10
 F_NO_WD = 1 << 11
+F_GRAD_SQ = 1 << 12
 T_FACTORED = 1 << 0
 T_VEC = 1 << 1
 T_P0_SCALAR = 1 << 2
@@ -69,6 +70,41 @@ class AdamLaunch(ctypes.Structure):
         ("w_nest", ctypes.c_float), ("c_v", ctypes.c_float), ("c_m", ctypes.c_float),
         ("d_eps", ctypes.c_float), ("beta3", ctypes.c_float), ("s_alpha", ctypes.c_float),
         ("d", ctypes.c_float), ("stages", ctypes.c_int32), ("seed", ctypes.c_uint64),
+        ("layer_beta2", ctypes.c_uint64), ("layer_of_tensor", ctypes.c_uint64), ("piece_gsq", ctypes.c_uint64),
+        ("prodigy", ctypes.c_uint64),
+    ]
+
+
+# advopt_prodigy_dev: byte offsets inside the 64-byte device block
+PRODIGY_DEV_BYTES = 64
+PRODIGY_DEV_SUMS = 32          # float sums[2]
+
+
+class ProdigyScalarArgs(ctypes.Structure):
+    """advopt_prodigy_scalar_args."""
+    _fields_ = [("dev", ctypes.c_uint64), ("tensors", ctypes.c_uint64), ("tensor_consts", ctypes.c_uint64),
+                ("n_tensors", ctypes.c_int32), ("safeguard_warmup", ctypes.c_int32),
+                ("lr", ctypes.c_double), ("beta1", ctypes.c_double), ("beta2", ctypes.c_double),
+                ("step_scale", ctypes.c_double)]
+
+
+class ProdigyDArgs(ctypes.Structure):
+    """advopt_prodigy_d_args."""
+    _fields_ = [("dev", ctypes.c_uint64), ("active", ctypes.c_int32), ("d_limiter", ctypes.c_int32),
+                ("d_coef", ctypes.c_double), ("growth_rate", ctypes.c_double),
+                ("limiter_factor", ctypes.c_double), ("beta3", ctypes.c_double), ("carry_scale", ctypes.c_double)]
+
+
+class KourkoutasArgs(ctypes.Structure):
+    """advopt_kourkoutas_args."""
+    _fields_ = [(n, ctypes.c_uint64) for n in (
+        "acc", "ema", "layer_beta2", "layer_of_tensor", "piece_gsq", "pieces")] + [
+        ("n_layers", ctypes.c_int32), ("n_tensors", ctypes.c_int32), ("n_pieces", ctypes.c_int32),
+        ("gsq_bf16", ctypes.c_int32),
+        ("beta2_max", ctypes.c_float), ("beta2_min_gap", ctypes.c_float), ("ema_alpha", ctypes.c_float),
+        ("one_minus_alpha", ctypes.c_float), ("tiny_spike", ctypes.c_float), ("w", ctypes.c_float),
+        ("one_minus_w_bmax", ctypes.c_float), ("pad", ctypes.c_float), ("cv_scale", ctypes.c_double),
+        ("d_dev", ctypes.c_uint64),
     ]
 
 
@@ -138,6 +174,10 @@ def lib():
             "advopt_ns_chain": ([P, P, P, P, I32, I32, I32, I32, ctypes.c_double, ctypes.c_double, ctypes.c_double,
                                  ctypes.c_double, ctypes.POINTER(ctypes.c_void_p), P, P], ctypes.c_int),
             "advopt_noise_fill": ([P, ctypes.c_int64, U64, U32, U32, U32, P], ctypes.c_int),
+            "advopt_kourkoutas_prepare": ([ctypes.POINTER(KourkoutasArgs), P], ctypes.c_int),
+            "advopt_kourkoutas_accumulate": ([ctypes.POINTER(KourkoutasArgs), P], ctypes.c_int),
+            "advopt_prodigy_scalars": ([ctypes.POINTER(ProdigyScalarArgs), P], ctypes.c_int),
+            "advopt_prodigy_update_d": ([ctypes.POINTER(ProdigyDArgs), P], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -147,7 +187,9 @@ def lib():
             raise AdvOptError("libadvopt.so ABI version mismatch; rebuild the library")
         for which, size in ((0, ADAM_TENSOR_DT.itemsize), (1, PIECE_DT.itemsize),
                             (2, ctypes.sizeof(AdamLaunch)), (3, LION_TENSOR_DT.itemsize),
-                            (4, ctypes.sizeof(MuonArgs))):
+                            (4, ctypes.sizeof(MuonArgs)), (5, ctypes.sizeof(KourkoutasArgs)),
+                            (6, PRODIGY_DEV_BYTES), (7, ctypes.sizeof(ProdigyScalarArgs)),
+                            (8, ctypes.sizeof(ProdigyDArgs))):
             got = L.advopt_sizeof(which)
             if got != size:
                 raise AdvOptError(f"struct layout mismatch (#{which}: C {got} bytes, Python {size})")
@@ -166,7 +208,8 @@ def exported_symbols():
     return ["advopt_adam_step", "advopt_factored_finish", "advopt_prodigy_finish", "advopt_fisher_finish",
             "advopt_lion_step", "advopt_sizeof", "advopt_abi_version", "advopt_last_error",
             "advopt_adam_occupancy", "advopt_adam_step_noalloc", "advopt_ns_gemm", "advopt_ns_gemm_sym", "advopt_muon_stage", "advopt_philox4x32_10",
-            "advopt_noise_fill", "advopt_ns_chain"]
+            "advopt_noise_fill", "advopt_ns_chain", "advopt_kourkoutas_prepare", "advopt_kourkoutas_accumulate",
+            "advopt_prodigy_scalars", "advopt_prodigy_update_d"]
 
 
 _OCC_CACHE = {}

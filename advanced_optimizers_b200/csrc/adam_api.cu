@@ -8,8 +8,11 @@ namespace advopt {
 // factored_2nd finish: column sums from the partials, then normalise one
 // factor (factorization_util.py:60-80).  Kernel A sums partial rows in slot
 // order (float64) into mv; kernel B normalises mu (d1 < d2) or mv by its total.
+// Both leave the factors untouched when the step's error word is set: a CTA
+// whose bounded wait gave up has not written its column partials.
 // ---------------------------------------------------------------------------
-__global__ void factored_cols_kernel(const advopt_adam_tensor* tensors, const int32_t* index) {
+__global__ void factored_cols_kernel(const advopt_adam_tensor* tensors, const int32_t* index, const int32_t* err) {
+  if (err && *err) return;
   const advopt_adam_tensor* t = tensors + index[blockIdx.y];
   const int64_t d2 = t->d2;
   const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -20,7 +23,8 @@ __global__ void factored_cols_kernel(const advopt_adam_tensor* tensors, const in
   t->col_factor[j] = (float)acc;
 }
 
-__global__ void factored_norm_kernel(const advopt_adam_tensor* tensors, const int32_t* index) {
+__global__ void factored_norm_kernel(const advopt_adam_tensor* tensors, const int32_t* index, const int32_t* err) {
+  if (err && *err) return;
   const advopt_adam_tensor* t = tensors + index[blockIdx.x];
   const int64_t d1 = t->d1, d2 = t->d2;
   float* vec = d1 < d2 ? t->row_factor : t->col_factor;
@@ -46,6 +50,7 @@ __global__ void factored_norm_kernel(const advopt_adam_tensor* tensors, const in
 // Prodigy: per-tensor sums of the piece statistics, folded in param order.
 __global__ void prodigy_finish_kernel(const advopt_adam_launch L, float* sums, float coef, int s_is_bf16) {
   __shared__ double dot_s[256], abs_s[256];
+  if (L.prodigy) coef = L.prodigy->coef;
   float num = sums[0], den = sums[1];
   // pieces of tensor t are found by scanning all pieces (launch sizes are small)
   for (int t = 0; t < L.n_tensors; ++t) {
@@ -78,6 +83,92 @@ __global__ void prodigy_finish_kernel(const advopt_adam_launch L, float* sums, f
   if (threadIdx.x == 0) {
     sums[0] = num;
     sums[1] = den;
+  }
+}
+
+// Python's two-argument min / max: the first argument unless the second is
+// strictly smaller / larger.
+__device__ __forceinline__ double py_min(double a, double b) { return b < a ? b : a; }
+__device__ __forceinline__ double py_max(double a, double b) { return b > a ? b : a; }
+
+// Prodigy step scalars from the device d (Prodigy_adv.py:345-346, 404-520).
+__global__ void prodigy_scalars_kernel(const advopt_prodigy_scalar_args a) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  advopt_prodigy_dev* P = a.dev;
+  const double d = P->d, d0 = P->d0;
+  const double dlr = d * a.lr;
+  P->c_v = (float)(d * d * (1.0 - a.beta2));
+  P->c_m = (float)(d * (1.0 - a.beta1));
+  P->d_f = (float)d;
+  P->s_alpha = (float)(a.safeguard_warmup ? (d / d0) * d : (d / d0) * dlr);
+  P->coef = (float)((d / d0) * dlr);
+  const float ss = (float)(a.step_scale == 1.0 ? dlr : dlr * a.step_scale);
+  for (int t = 0; t < a.n_tensors; ++t) {
+    advopt_adam_tensor& T = a.tensors[t];
+    const double* c = a.tensor_consts + 3 * t;
+    T.step_size = ss;
+    T.eps = (float)(d * c[0]);
+    T.wd = c[1] != 0.0 ? (float)(c[1] * dlr) : 0.0f;
+    T.cwd = c[2] != 0.0 ? (float)(c[2] * dlr) : 0.0f;
+  }
+}
+
+// calculate_d + init_step's carry (Prodigy_adv.py:246-257, 540-572).
+__global__ void prodigy_update_d_kernel(const advopt_prodigy_d_args a) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  advopt_prodigy_dev* P = a.dev;
+  if (a.active) {
+    const double gn = (double)P->sums[0], gd = (double)P->sums[1];
+    double d = P->d, d_max = P->d_max;
+    if (gd > 0.0) {
+      double d_hat = a.d_coef * gn / gd;
+      if (a.d_limiter) d_hat = py_min(d * a.limiter_factor, d_hat);
+      if (d == P->d0) d = py_max(d, d_hat);
+      d_max = py_max(d_max, d_hat);
+      d = py_min(d_max, d * a.growth_rate);
+    }
+    P->d = d;
+    P->d_max = d_max;
+    P->d_numerator = gn;
+  }
+  P->sums[0] = (float)(P->d_numerator * a.beta3) * (float)a.carry_scale;
+  P->sums[1] = 0.0f;
+}
+
+// Kourkoutas-beta: per-layer EMA and dynamic beta2 (Kourkoutas.py:131-187).
+__global__ void kourkoutas_prepare_kernel(const advopt_kourkoutas_args a) {
+  const int l = blockIdx.x * blockDim.x + threadIdx.x;
+  if (l >= a.n_layers) return;
+  const float pooled = __fsqrt_rn(a.acc[l]);
+  float e = __fmul_rn(a.ema[l], a.ema_alpha);
+  e = __fmaf_rn(a.one_minus_alpha, pooled, e);           // add_(pooled, alpha=1 - ema_alpha)
+  a.ema[l] = e;
+  const float raw = __fdiv_rn(pooled, __fadd_rn(e, a.tiny_spike));
+  const float sun = __fdiv_rn(raw, __fadd_rn(1.0f, raw));
+  const float target = __fsub_rn(a.beta2_max, __fmul_rn(a.beta2_min_gap, sun));
+  const float b2 = __fadd_rn(a.one_minus_w_bmax, __fmul_rn(a.w, target));
+  a.layer_beta2[2 * l] = b2;
+  // value=1.0 - beta2 (AdamW) or d * d * (1.0 - beta2) (Prodigy) with beta2 a Python float
+  const double cv = a.d_dev ? a.d_dev[0] * a.d_dev[0] : a.cv_scale;
+  a.layer_beta2[2 * l + 1] = (float)(cv * (1.0 - (double)b2));
+  a.acc[l] = 0.0f;
+}
+
+// Kourkoutas-beta: each tensor's sum of g*g (its pieces, in order) into its
+// layer's accumulator, tensors in launch order (Kourkoutas.py:231-247).
+__global__ void kourkoutas_accumulate_kernel(const advopt_kourkoutas_args a) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  // the planner lays the tensors end to end, so one tensor's pieces are
+  // consecutive and the tensors come in launch order
+  int i = 0;
+  while (i < a.n_pieces) {
+    const int t = a.pieces[i].tensor;
+    double s = 0.0;
+    for (; i < a.n_pieces && a.pieces[i].tensor == t; ++i) s += a.piece_gsq[i];
+    float v = (float)s;
+    if (a.gsq_bf16) v = round_bf16(v);
+    const int l = a.layer_of_tensor[t];
+    if (l >= 0) a.acc[l] = __fadd_rn(a.acc[l], v);
   }
 }
 
@@ -135,6 +226,10 @@ extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: bad precision/algo/dtype code");
   if ((L->flags & (ADVOPT_F_PRODIGY_STATS | ADVOPT_F_FISHER_STATS)) && !L->piece_stats)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: statistics requested without piece_stats");
+  if ((L->flags & ADVOPT_F_GRAD_SQ) && !L->piece_gsq)
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: ADVOPT_F_GRAD_SQ without piece_gsq");
+  if ((L->layer_beta2 != nullptr) != (L->layer_of_tensor != nullptr))
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: layer_beta2 and layer_of_tensor go together");
   if (L->smem_floats < 0 || L->smem_floats > 56832)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: shared memory request above 227 KB (factored d2 too large)");
   if (L->stages < 0 || L->stages > 4) return set_error(ADVOPT_E_INVALID, "advopt_adam_step: stages must be 0..4");
@@ -143,12 +238,12 @@ extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
 
 namespace advopt {
 cudaError_t run_factored_finish(const advopt_adam_tensor* tensors, const int32_t* index, int n_factored, int max_d2,
-                                cudaStream_t s) {
+                                const int32_t* err, cudaStream_t s) {
   dim3 ga((unsigned)((max_d2 + 255) / 256), (unsigned)n_factored);
-  factored_cols_kernel<<<ga, 256, 0, s>>>(tensors, index);
+  factored_cols_kernel<<<ga, 256, 0, s>>>(tensors, index, err);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  factored_norm_kernel<<<n_factored, 1024, 0, s>>>(tensors, index);
+  factored_norm_kernel<<<n_factored, 1024, 0, s>>>(tensors, index, err);
   return cudaGetLastError();
 }
 }  // namespace advopt
@@ -157,8 +252,24 @@ extern "C" int advopt_factored_finish(const advopt_adam_launch* L, const int32_t
                                       int32_t max_d2, void* stream) {
   if (!L || (n_factored > 0 && !index)) return set_error(ADVOPT_E_INVALID, "advopt_factored_finish: null argument");
   if (n_factored <= 0) return ADVOPT_OK;
-  return check_cuda(run_factored_finish(L->tensors, index, n_factored, max_d2, static_cast<cudaStream_t>(stream)),
+  return check_cuda(run_factored_finish(L->tensors, index, n_factored, max_d2, L->err,
+                                        static_cast<cudaStream_t>(stream)),
                     "advopt_factored_finish");
+}
+
+extern "C" int advopt_kourkoutas_prepare(const advopt_kourkoutas_args* a, void* stream) {
+  if (!a || !a->acc || !a->ema || !a->layer_beta2 || a->n_layers < 0)
+    return set_error(ADVOPT_E_INVALID, "advopt_kourkoutas_prepare: null argument");
+  if (a->n_layers == 0) return ADVOPT_OK;
+  kourkoutas_prepare_kernel<<<(a->n_layers + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+  return check_cuda(cudaGetLastError(), "advopt_kourkoutas_prepare");
+}
+
+extern "C" int advopt_kourkoutas_accumulate(const advopt_kourkoutas_args* a, void* stream) {
+  if (!a || !a->acc || !a->layer_of_tensor || !a->piece_gsq || !a->pieces || a->n_tensors < 0 || a->n_pieces < 0)
+    return set_error(ADVOPT_E_INVALID, "advopt_kourkoutas_accumulate: null argument");
+  kourkoutas_accumulate_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+  return check_cuda(cudaGetLastError(), "advopt_kourkoutas_accumulate");
 }
 
 extern "C" int advopt_prodigy_finish(const advopt_adam_launch* L, float* sums, float coef, int32_t s_is_bf16,
@@ -166,6 +277,19 @@ extern "C" int advopt_prodigy_finish(const advopt_adam_launch* L, float* sums, f
   if (!L || !sums || !L->piece_stats) return set_error(ADVOPT_E_INVALID, "advopt_prodigy_finish: null argument");
   prodigy_finish_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(*L, sums, coef, s_is_bf16);
   return check_cuda(cudaGetLastError(), "advopt_prodigy_finish");
+}
+
+extern "C" int advopt_prodigy_scalars(const advopt_prodigy_scalar_args* a, void* stream) {
+  if (!a || !a->dev || a->n_tensors < 0 || (a->n_tensors > 0 && (!a->tensors || !a->tensor_consts)))
+    return set_error(ADVOPT_E_INVALID, "advopt_prodigy_scalars: null argument");
+  prodigy_scalars_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+  return check_cuda(cudaGetLastError(), "advopt_prodigy_scalars");
+}
+
+extern "C" int advopt_prodigy_update_d(const advopt_prodigy_d_args* a, void* stream) {
+  if (!a || !a->dev) return set_error(ADVOPT_E_INVALID, "advopt_prodigy_update_d: null argument");
+  prodigy_update_d_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(*a);
+  return check_cuda(cudaGetLastError(), "advopt_prodigy_update_d");
 }
 
 extern "C" int advopt_fisher_finish(const advopt_adam_launch* L, advopt_adam_tensor* tensors_rw, void* stream) {

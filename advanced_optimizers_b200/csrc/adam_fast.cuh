@@ -492,6 +492,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
   __shared__ uint32_t redm[2][kWarps], redv[2][kWarps];
   __shared__ float redr[2][kWarps];
   __shared__ double dred[kWarps][2];
+  __shared__ double gred[kWarps];
   __shared__ TensorRegs Ts;
   __shared__ PieceRegs Ps;
   __shared__ Cursor cur;          // producer state (thread 0 only)
@@ -502,16 +503,21 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
   const uint32_t F = L.flags;
   const bool has_m = CF < 0 ? (F & ADVOPT_F_HAS_M) != 0 : (CF & kCfHasM) != 0;
   const bool pstats = (ALGO == ADVOPT_ALGO_PRODIGY) && (F & ADVOPT_F_PRODIGY_STATS);
+  const bool gsq = F & ADVOPT_F_GRAD_SQ;
   FastScalars SC;
   SC.beta1 = L.beta1;
   SC.beta2 = L.beta2;
-  SC.c_v = L.c_v;
-  SC.c_m = L.c_m;
+  // Prodigy with d on the device reads its launch scalars from there
+  const bool pdev = ALGO == ADVOPT_ALGO_PRODIGY && L.prodigy != nullptr;
+  const float c_v0 = pdev ? L.prodigy->c_v : L.c_v;
+  const float s_alpha = pdev ? L.prodigy->s_alpha : L.s_alpha;
+  SC.c_v = c_v0;
+  SC.c_m = pdev ? L.prodigy->c_m : L.c_m;
   SC.w_m = L.w_m;
   SC.w_m1 = __fsub_rn(L.w_m, 1.0f);
   SC.w_n = L.w_nest;
   SC.w_n1 = __fsub_rn(L.w_nest, 1.0f);
-  SC.d = L.d;
+  SC.d = pdev ? L.prodigy->d_f : L.d;
   SC.w_m_small = fabsf(L.w_m) < 0.5f;
   SC.w_n_small = fabsf(L.w_nest) < 0.5f;
   SC.has_m = has_m;
@@ -556,6 +562,13 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
     // column partials in their own global slot row (read-modify-write)
     const bool col_global = fact && d2 > (int64_t)L.gen_offset;
     float* colrow = fact ? (col_global ? T.colpart + (int64_t)pc.slot * d2 : colacc) : nullptr;
+    if (L.layer_beta2) {
+      // Kourkoutas-beta: the tensor's layer's dynamic beta2 (Kourkoutas.py:249-257)
+      const int l = L.layer_of_tensor[pc.tensor];
+      SC.beta2 = l >= 0 ? L.layer_beta2[2 * l] : L.beta2;
+      SC.c_v = l >= 0 ? L.layer_beta2[2 * l + 1] : c_v0;
+    }
+    double gacc = 0.0;     // Kourkoutas-beta: this thread's sum of g*g over the piece
     SC.sbc2 = T.sqrt_bc2;
     SC.rcp_sbc2 = __frcp_rn(T.sqrt_bc2);
     SC.eps = T.eps;
@@ -579,6 +592,12 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
     float racc0 = 0.0f, racc1 = 0.0f;   // this thread's part of rows r0 and r0 + 1
     double st0 = 0.0, st1 = 0.0;
     const uint32_t slice_p = T.slice_p ? T.slice_p : 1u;
+    // Prodigy: this thread's first element's remainder mod slice_p, advanced
+    // by one chunk's remainder per chunk (one 64-bit division per piece, none
+    // per element); slice indices below 2^32 divide in 32 bits
+    uint32_t srem = pstats ? (uint32_t)((uint64_t)(pb + tid * kVec) % slice_p) : 0u;
+    const uint32_t srem_step = (uint32_t)kChunk % slice_p;
+    const bool si32 = T.numel < (int64_t(1) << 32);
 
     // Scalars of a chunk (factored row / column factors, block scales),
     // loaded one chunk ahead so their L2 latency overlaps the current chunk.
@@ -641,6 +660,20 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
       fast_load<PREC, PBF>(T, st, dir, k0, nv, v8, has_m, fact, in);
       U4 nzp{0u, 0u, 0u, 0u};
       if (cf_sr<CF>(SC)) nzp = noise(T.nz_p, kNoiseP);
+      if (gsq) {
+        // torch.sum(grad.pow(2)) of the grad the step uses: squares in bf16
+        // for a bf16 grad under 'auto' (Kourkoutas.py:241-245)
+        float s8 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 gp = pair_of<LY::BPP, true>(in.g, i);
+          float q0 = __fmul_rn(gp.x, gp.x), q1 = __fmul_rn(gp.y, gp.y);
+          if (TR::kMathBF) { q0 = round_bf16(q0); q1 = round_bf16(q1); }
+          if (2 * i < nv) s8 = __fadd_rn(s8, q0);
+          if (2 * i + 1 < nv) s8 = __fadd_rn(s8, q1);
+        }
+        gacc += (double)s8;
+      }
       float2 m_new[4], v[4];
       uint32_t pw[PBF ? 4 : 8];
       fast_moments<PREC, PBF, ALGO, CF, fact>(in, SC, m_new, v);
@@ -673,14 +706,15 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
 
       if (pstats) {
         // Prodigy slice statistics on p before the update (Prodigy_adv.py:494-509)
-        const int slice_off = (int)((slice_p - (uint32_t)(k0 % slice_p)) % slice_p);
+        int next = srem ? (int)(slice_p - srem) : 0;   // next slice point at or after k0
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          if (e < nv && e >= slice_off && ((e - slice_off) % (int)slice_p) == 0) {
+          if (e < nv && e == next) {
+            next += (int)slice_p;
             const float2 gp = pair_of<LY::BPP, true>(in.g, e >> 1), pp = pair_of<LY::BPP, true>(in.p, e >> 1);
             const float gv = (e & 1) ? gp.y : gp.x;
             const float pv = (e & 1) ? pp.y : pp.x;
-            const int64_t si = (k0 + e) / slice_p;
+            const int64_t si = si32 ? (int64_t)((uint32_t)(k0 + e) / slice_p) : (k0 + e) / (int64_t)slice_p;
             float p0v = 0.0f;
             if (!(T.flags & ADVOPT_T_P0_SCALAR))
               p0v = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux1)[si]) : static_cast<const float*>(T.aux1)[si];
@@ -689,7 +723,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
                                     : static_cast<const float*>(T.aux0)[si];
             float s1 = __fmul_rn(s_old, L.beta3);
             if (PBF) s1 = round_bf16(s1);
-            float s2 = __fmaf_rn(gv, L.s_alpha, s1);
+            float s2 = __fmaf_rn(gv, s_alpha, s1);
             if (PBF) {
               const uint32_t b = f_to_bf16_rne(s2);
               static_cast<uint16_t*>(T.aux0)[si] = (uint16_t)b;
@@ -700,6 +734,8 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
             st1 += (double)fabsf(s2);
           }
         }
+        srem += srem_step;
+        if (srem >= slice_p) srem -= slice_p;
       }
 
       // param store
@@ -872,6 +908,17 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
         float* dstp = T.colpart + (int64_t)pc.slot * d2;
         for (int j2 = tid * 4; j2 < (int)d2; j2 += kThreads * 4)
           *reinterpret_cast<float4*>(dstp + j2) = *reinterpret_cast<const float4*>(colacc + j2);
+      }
+      __syncthreads();
+    }
+    if (gsq) {
+      const double a = warp_sum_d(gacc);
+      if (lane == 0) gred[warp] = a;
+      __syncthreads();
+      if (tid == 0) {
+        double sa = 0.0;
+        for (int w = 0; w < kWarps; ++w) sa += gred[w];
+        L.piece_gsq[pi] = sa;
       }
       __syncthreads();
     }

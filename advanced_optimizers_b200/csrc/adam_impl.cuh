@@ -349,7 +349,15 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
   const bool fstats = EXT && (F & ADVOPT_F_FISHER_STATS);
   // the Fisher statistics pass writes nothing but piece_stats
   const bool pstats = (ALGO == ADVOPT_ALGO_PRODIGY) && (F & ADVOPT_F_PRODIGY_STATS) && !fstats;
-  const float beta1 = L.beta1, beta2 = L.beta2, w_m = L.w_m, w_nest = L.w_nest, c_v = L.c_v, c_m = L.c_m;
+  // Prodigy with d on the device reads its launch scalars from there
+  const bool pdev = ALGO == ADVOPT_ALGO_PRODIGY && L.prodigy != nullptr;
+  const float c_v0 = pdev ? L.prodigy->c_v : L.c_v;
+  const float d_f = pdev ? L.prodigy->d_f : L.d;
+  const float s_alpha = pdev ? L.prodigy->s_alpha : L.s_alpha;
+  const float beta1 = L.beta1, w_m = L.w_m, w_nest = L.w_nest, c_m = pdev ? L.prodigy->c_m : L.c_m;
+  float beta2 = L.beta2, c_v = c_v0;      // per tensor under Kourkoutas-beta
+  const bool gsq = (F & ADVOPT_F_GRAD_SQ) && !fstats;
+  __shared__ double gred[kWarps];
   auto Rm = [](float x) { return kMBF ? round_bf16(x) : x; };  // rounding of m / update / grad ops
   int parity = 0;
 
@@ -360,6 +368,13 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
     if (tid == 0) load_tensor(L.tensors + pc.tensor, Ts);
     __syncthreads();
     const TensorRegs& T = Ts;  // fields are re-read from shared memory where registers are short
+    if (L.layer_beta2) {
+      // Kourkoutas-beta: the tensor's layer's dynamic beta2 (Kourkoutas.py:249-257)
+      const int l = L.layer_of_tensor[pc.tensor];
+      beta2 = l >= 0 ? L.layer_beta2[2 * l] : L.beta2;
+      c_v = l >= 0 ? L.layer_beta2[2 * l + 1] : c_v0;
+    }
+    double gacc = 0.0;     // Kourkoutas-beta: this thread's sum of g*g over the piece
     const bool fact = T.flags & ADVOPT_T_FACTORED;
     const bool vec = T.flags & ADVOPT_T_VEC;
     const bool has_anchor = EXT && (((T.flags >> ADVOPT_T_ANCHOR_SHIFT) & 7u) != 0);
@@ -378,6 +393,11 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
     double row_carry = 0.0;  // thread 0: running sum of the row in progress
     double st0 = 0.0, st1 = 0.0;
     const uint32_t slice_p = T.slice_p ? T.slice_p : 1u;
+    // Prodigy: running remainder of this thread's first element mod slice_p
+    // (one 64-bit division per piece, none per element)
+    uint32_t srem = pstats ? (uint32_t)((uint64_t)(pc.begin + tid * kVec) % slice_p) : 0u;
+    const uint32_t srem_step = (uint32_t)kChunk % slice_p;
+    const bool si32 = T.numel < (int64_t(1) << 32);
 
     ChunkPos cp;
     cp.cs = pc.begin;
@@ -449,14 +469,27 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
       }
       U4 nzp{0u, 0u, 0u, 0u};
       if (sr && !fstats) nzp = noise_words<NOISE_IN>(L, T, T.nz_p, kNoiseP, k0, nv);
-      int slice_off = 0;  // offset of the next Prodigy slice point from k0
-      if (pstats) slice_off = (int)((slice_p - (uint32_t)(k0 % slice_p)) % slice_p);
+      int slice_next = 0;  // offset of the next Prodigy slice point from k0
+      if (pstats) {
+        slice_next = srem ? (int)(slice_p - srem) : 0;
+        srem += srem_step;
+        if (srem >= slice_p) srem -= slice_p;
+      }
 
       // ---- per-element arithmetic in the reference's op order; the param
       // update does not need the block statistics and happens here ----
       float m_new[8], v[8];
       float amax_m = 0.0f, vmax = 0.0f;
       uint32_t pout[8];
+      if (gsq) {
+        // torch.sum(grad.pow(2)) of the grad the step uses: squares in bf16
+        // for a bf16 grad under 'auto' (Kourkoutas.py:241-245)
+        float s8 = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < nv) s8 = __fadd_rn(s8, kMBF ? round_bf16(__fmul_rn(g[e], g[e])) : __fmul_rn(g[e], g[e]));
+        gacc += (double)s8;
+      }
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const bool ok = e < nv;
@@ -494,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
           ui = nest ? Rm(lerp_t(mi, gi, w_nest)) : mi;
         } else {
           m_new[e] = 0.0f;
-          ui = (ALGO == ADVOPT_ALGO_PRODIGY) ? Rm(__fmul_rn(gi, L.d)) : gi;
+          ui = (ALGO == ADVOPT_ALGO_PRODIGY) ? Rm(__fmul_rn(gi, d_f)) : gi;
         }
         if (!normed) ui = atan2m ? Rm(atan2f(ui, du)) : Rm(__fdiv_rn(ui, du));
         ui = Rm(__fmul_rn(ui, step_size));
@@ -502,8 +535,9 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
         vmax = fmaxf(vmax, v[e]);
 
         // Prodigy slice statistics on p before its update (Prodigy_adv.py:501-509)
-        if (pstats && ok && e >= slice_off && ((e - slice_off) % (int)slice_p) == 0) {
-          const int64_t si = (k0 + e) / slice_p;
+        if (pstats && ok && e == slice_next) {
+          slice_next += (int)slice_p;
+          const int64_t si = si32 ? (int64_t)((uint32_t)(k0 + e) / slice_p) : (k0 + e) / (int64_t)slice_p;
           float p0v = 0.0f;
           if (!(T.flags & ADVOPT_T_P0_SCALAR))
             p0v = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux1)[si]) : static_cast<const float*>(T.aux1)[si];
@@ -512,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
                                   : static_cast<const float*>(T.aux0)[si];
           float s1 = __fmul_rn(s_old, L.beta3);
           if (PBF) s1 = round_bf16(s1);
-          float s2 = __fmaf_rn(gi, L.s_alpha, s1);
+          float s2 = __fmaf_rn(gi, s_alpha, s1);
           if (PBF) {
             const uint32_t b = f_to_bf16_rne(s2);
             static_cast<uint16_t*>(T.aux0)[si] = (uint16_t)b;
@@ -750,6 +784,17 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
         }
         L.piece_stats[2 * pi] = sa;
         L.piece_stats[2 * pi + 1] = sb;
+      }
+      __syncthreads();
+    }
+    if (gsq) {
+      const double a = warp_sum_d(gacc);
+      if (lane == 0) gred[warp] = a;
+      __syncthreads();
+      if (tid == 0) {
+        double sa = 0.0;
+        for (int w = 0; w < kWarps; ++w) sa += gred[w];
+        L.piece_gsq[pi] = sa;
       }
       __syncthreads();
     }

@@ -31,6 +31,10 @@ extern "C" size_t advopt_sizeof(int which) {
     case 2: return sizeof(advopt_adam_launch);
     case 3: return sizeof(advopt_lion_tensor);
     case 4: return sizeof(advopt_muon_args);
+    case 5: return sizeof(advopt_kourkoutas_args);
+    case 6: return sizeof(advopt_prodigy_dev);
+    case 7: return sizeof(advopt_prodigy_scalar_args);
+    case 8: return sizeof(advopt_prodigy_d_args);
     default: return 0;
   }
 }

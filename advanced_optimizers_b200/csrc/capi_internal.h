@@ -16,5 +16,5 @@ int check_cuda(cudaError_t e, const char* where);
 cudaError_t run_adam(const advopt_adam_launch& L, cudaStream_t s);
 cudaError_t run_occupancy(int prec, int pdt, int algo, int smem_floats, int* ctas, int fast);
 cudaError_t run_factored_finish(const advopt_adam_tensor* tensors, const int32_t* index, int n_factored, int max_d2,
-                                cudaStream_t s);
+                                const int32_t* err, cudaStream_t s);
 }  // namespace advopt

@@ -16,9 +16,22 @@
 // first call before any stream capture.  All calls share the one array and it
 // keeps the last call's contents: every call rewrites the descriptor, the plan
 // and the error word before its kernels read them, and the kernels overwrite
-// every column partial they later sum, so nothing needs to start at zero.
+// every column partial they later sum, so nothing needs to start at zero.  A
+// CTA whose bounded wait gives up leaves its partials unwritten; the error
+// word then stops the factored finish, which leaves the factors unchanged.
+// Without launch->err that word is the array's own, which no caller reads:
+// callers that need to know pass their own device word in launch->err.
 // Calls whose kernels overlap on the GPU (other streams, or other host threads
 // on the same device) race on the array and must be serialised by the caller.
+//
+// Kernel choice, shared memory and the fast kernel's limits follow the host
+// planner of the optimizer classes (32-bit element offsets below 2^34
+// elements; factored tensors wider than 8192 columns accumulate their column
+// partials in the array instead of shared memory).  One difference: the plan
+// is one piece per CTA, so a factored tensor's float32 column partials sum
+// up to d1 / grid rows before the float64 reduction (the planner cuts pieces
+// at 64 rows); on the Llama embedding's 24576 x 21376 effective shape, where
+// the array caps the grid near 195 CTAs, that is 126 rows.
 #include <cstdio>
 #include <mutex>
 
@@ -36,6 +49,10 @@ constexpr int kMaxDevices = 128;
 void* g_base[kMaxDevices] = {};
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Columns of the fast kernel's shared-memory column accumulator (the host
+// planner's FAST_COLS).
+constexpr int kNoallocFastCols = 8192;
 
 inline int64_t gcd64(int64_t a, int64_t b) {
   while (b) {
@@ -139,6 +156,12 @@ extern "C" int advopt_adam_step_noalloc(const advopt_adam_tensor* tensor, const 
                      "AdamW / auxiliary Adam (Prodigy needs per-launch statistics buffers)");
   if (hp.flags & (ADVOPT_F_FISHER | ADVOPT_F_FISHER_STATS | ADVOPT_F_PRODIGY_STATS))
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step_noalloc: Fisher weight decay is not supported here");
+  // per-piece grad sums would index pieces the caller never sees; a dynamic
+  // beta2 (layer_beta2 / layer_of_tensor[0]) passes through unchanged
+  if (hp.flags & ADVOPT_F_GRAD_SQ)
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step_noalloc: per-piece grad sums are not supported here");
+  if (hp.layer_beta2 && !hp.layer_of_tensor)
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step_noalloc: layer_beta2 without layer_of_tensor");
   const bool fact = t.flags & ADVOPT_T_FACTORED;
   const int64_t d2 = fact ? t.d2 : 0;
   if (fact && (t.d1 <= 0 || d2 <= 0 || t.d1 * d2 != t.numel))
@@ -154,10 +177,14 @@ extern "C" int advopt_adam_step_noalloc(const advopt_adam_tensor* tensor, const 
   const bool ext = hp.flags & (ADVOPT_F_ATAN2 | ADVOPT_F_NORMED | ADVOPT_F_ANCHORS);
   const bool ffast = !fact || (d2 >= 2048 && d2 % 8 == 0 && (reinterpret_cast<uintptr_t>(t.col_factor) % 16) == 0 &&
                                (reinterpret_cast<uintptr_t>(t.row_factor) % 16) == 0);
-  const int gen_offset = fact ? (int)((d2 + 3) / 4 * 4) : 0;
+  int gen_offset = fact ? (int)((d2 + 3) / 4 * 4) : 0;
   int stages = 0, smem_floats = 0;
-  const bool fast = !ext && ffast;
+  // the fast kernel keeps element offsets in 32 bits
+  const bool fast = !ext && ffast && t.numel < (int64_t(1) << 34);
   if (fast) {
+    // factored tensors wider than the shared-memory accumulator keep their
+    // column partials in their slot rows of the array
+    if (gen_offset > kNoallocFastCols) gen_offset = kNoallocFastCols;
     const int bpp = hp.param_dtype == ADVOPT_DT_BF16 ? 2 : 4;
     int bps = 4;
     if (hp.precision == ADVOPT_PREC_INT8_SR) bps = 1;
@@ -213,6 +240,7 @@ extern "C" int advopt_adam_step_noalloc(const advopt_adam_tensor* tensor, const 
   L.pieces = reinterpret_cast<const advopt_piece*>(base + l.pieces);
   L.cta_offsets = reinterpret_cast<const int32_t*>(base + l.offsets);
   L.piece_stats = nullptr;
+  L.piece_gsq = nullptr;
   // a caller-supplied error word (launch->err) is honoured; otherwise the
   // array's own word records a bounded wait that gave up
   L.err = hp.err ? hp.err : reinterpret_cast<int32_t*>(base + l.err);
@@ -225,7 +253,7 @@ extern "C" int advopt_adam_step_noalloc(const advopt_adam_tensor* tensor, const 
   e = run_adam(L, s);
   if (e != cudaSuccess) return check_cuda(e, "advopt_adam_step_noalloc: step");
   if (fact) {
-    e = run_factored_finish(L.tensors, reinterpret_cast<const int32_t*>(base + l.index), 1, (int)d2, s);
+    e = run_factored_finish(L.tensors, reinterpret_cast<const int32_t*>(base + l.index), 1, (int)d2, L.err, s);
     if (e != cudaSuccess) return check_cuda(e, "advopt_adam_step_noalloc: factored finish");
   }
   return ADVOPT_OK;

@@ -333,248 +333,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// Pair kernel: a cluster of two CTAs computes one 256 x 256 tile with
-// tcgen05.mma.cta_group::2 (M = 256 split across the pair, N = 256 taken half
-// from each CTA's shared memory), so each CTA streams 32 KB per k-step
-// instead of 48 KB.  Each CTA's TMA loads complete on the leader's "full"
-// barrier (cp.async.bulk.tensor .cta_group::2, no multicast); the leader's
-// single MMA thread commits every stage and accumulator to the barriers of
-// both CTAs (one commit per CTA address); both CTAs' epilogue threads release
-// an accumulator on the leader's "empty" barrier.  Same roles, bounded waits
-// and drain as the single-CTA kernel above.  Used when M % 256 == 0.
-// ---------------------------------------------------------------------------
-constexpr int PM = 256;                     // rows of a pair tile
-constexpr int HA = 128 * BK * 2;            // this CTA's A half per stage (16 KB)
-constexpr int HB = 128 * BK * 2;            // this CTA's B half per stage (16 KB)
-constexpr int PSTAGE = HA + HB;             // 32 KB
-constexpr int PSTAGES = 6;
-constexpr int PSMEM_BYTES = PSTAGES * PSTAGE + 1024;
-
-__host__ __device__ constexpr uint32_t instr_desc_pair(bool b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
-         ((uint32_t)(PM >> 4) << 24);
-}
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// shared::cluster address of this CTA's variable `p` in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
-  uint32_t a;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
-  return a;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// expect_tx needs no ordering of this thread's earlier memory operations: relaxed
-__device__ __forceinline__ void mbar_arrive_tx_cl(uint32_t bar_cl, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.relaxed.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cl), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_cl(uint32_t bar_cl) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cl) : "memory");
-}
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar_cl) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(bar_cl)
-      : "memory");
-}
-__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cl) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cl) : "memory");
-}
-
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
-    ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-                        GemmArgs g, int b_mn_major) {
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t full_bar[PSTAGES], empty_bar[PSTAGES], acc_full[2], acc_empty[2], drain;
-  __shared__ uint32_t tmem_base;
-  __shared__ int abort_flag;
-  volatile int* abort_v = &abort_flag;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const int ktiles = g.K / BK;
-  const int n_nb = g.N / BN;
-  const int n_mb = g.M / PM;
-  const int ntiles = n_mb * n_nb;
-  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < PSTAGES; ++s) {
-      mbar_init(&full_bar[s], 2);      // one expect_tx arrival from each CTA's producer
-      mbar_init(&empty_bar[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 256);   // both CTAs' epilogue threads
-    }
-    mbar_init(&drain, 1);
-    abort_flag = 0;
-    mbar_fence_init();
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                 "r"(TMEM_ALLOC)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  cluster_sync_all();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem = tmem_base;
-
-  if (warp == 0) {
-    // ---- TMA producer (both CTAs): this CTA's A rows and B columns ----
-    if (lane == 0) {
-      uint32_t it = 0;
-      for (int t = pair; t < ntiles && !*abort_v; t += npairs) {
-        const int m0 = (t % n_mb) * PM + (int)rank * 128, n0 = (t / n_mb) * BN + (int)rank * 128;
-        for (int kt = 0; kt < ktiles; ++kt, ++it) {
-          const int s = (int)(it % PSTAGES);
-          const uint32_t use = it / PSTAGES;
-          if (use > 0 && !wait_or_abort(&empty_bar[s], (use - 1) & 1u, abort_v)) {
-            abort_flag = 1;
-            break;
-          }
-          const uint32_t full_cl = cluster_addr(&full_bar[s], 0);
-          unsigned char* sa = smem + s * PSTAGE;
-          unsigned char* sb = sa + HA;
-          mbar_arrive_tx_cl(full_cl, PSTAGE);
-          tma_load_2d_pair(sa, &mapA, kt * BK, m0, full_cl);
-          if (b_mn_major) {
-            tma_load_2d_pair(sb, &mapB, n0, kt * BK, full_cl);
-            tma_load_2d_pair(sb + 8192, &mapB, n0 + 64, kt * BK, full_cl);
-          } else {
-            tma_load_2d_pair(sb, &mapB, kt * BK, n0, full_cl);
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ---- MMA issuer (leader CTA only) ----
-    if (rank == 0 && lane == 0) {
-      const uint32_t idesc = instr_desc_pair(b_mn_major != 0);
-      uint32_t it = 0;
-      int i = 0;
-      for (int t = pair; t < ntiles && !*abort_v; t += npairs, ++i) {
-        const int acc = i & 1;
-        const uint32_t use = (uint32_t)i >> 1;
-        if (use > 0 && !wait_or_abort(&acc_empty[acc], (use - 1) & 1u, abort_v)) {
-          abort_flag = 1;
-          break;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t d_tmem = tmem + (uint32_t)acc * TMEM_COLS;
-        bool ok = true;
-        for (int kt = 0; kt < ktiles; ++kt, ++it) {
-          const int s = (int)(it % PSTAGES);
-          if (!wait_or_abort(&full_bar[s], (it / PSTAGES) & 1u, abort_v)) {
-            ok = false;
-            break;
-          }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t sa = smem_u32(smem + s * PSTAGE);
-          const uint32_t sb = sa + HA;
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = smem_desc(sa + k * 32, 16, 1024);
-            const uint64_t bd = b_mn_major ? smem_desc(sb + k * 2048, 8192, 1024) : smem_desc(sb + k * 32, 16, 1024);
-            mma_bf16_pair(d_tmem, ad, bd, idesc, (kt > 0 || k > 0) ? 1u : 0u);
-          }
-          mma_commit_pair(cluster_addr(&empty_bar[s], 0));
-          mma_commit_pair(cluster_addr(&empty_bar[s], 1));
-        }
-        if (!ok) {
-          abort_flag = 1;
-          break;
-        }
-        mma_commit_pair(cluster_addr(&acc_full[acc], 0));
-        mma_commit_pair(cluster_addr(&acc_full[acc], 1));
-      }
-    }
-  } else {
-    // ---- epilogue (both CTAs): this CTA's 128 rows of the pair tile ----
-    const int quarter = warp & 3;
-    int i = 0;
-    for (int t = pair; t < ntiles; t += npairs, ++i) {
-      const int acc = i & 1;
-      const uint32_t use = (uint32_t)i >> 1;
-      if (!wait_or_abort(&acc_full[acc], use & 1u, abort_v)) {
-        abort_flag = 1;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int m0 = (t % n_mb) * PM + (int)rank * 128, n0 = (t / n_mb) * BN;
-      const int row = m0 + quarter * 32 + lane;
-      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * TMEM_COLS;
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(taddr + c, r);
-        const int col = n0 + c;
-        float cv[16];
-        if (g.beta != 0.0f && g.C) {
-          const uint4* cp = reinterpret_cast<const uint4*>(g.C + (size_t)row * g.ldc + col);
-          const uint4 c0 = __ldg(cp), c1 = __ldg(cp + 1);
-          const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            cv[2 * q] = __uint_as_float(w[q] << 16);
-            cv[2 * q + 1] = __uint_as_float(w[q] & 0xFFFF0000u);
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < 16; ++q) cv[q] = 0.0f;
-        }
-        uint32_t o[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float v0 = __fmaf_rn(g.alpha, __uint_as_float(r[2 * q]), __fmul_rn(g.beta, cv[2 * q]));
-          const float v1 = __fmaf_rn(g.alpha, __uint_as_float(r[2 * q + 1]), __fmul_rn(g.beta, cv[2 * q + 1]));
-          o[q] = f_to_bf16_rne(v0) | (f_to_bf16_rne(v1) << 16);
-        }
-        uint4* dp = reinterpret_cast<uint4*>(g.D + (size_t)row * g.ldd + col);
-        dp[0] = make_uint4(o[0], o[1], o[2], o[3]);
-        dp[1] = make_uint4(o[4], o[5], o[6], o[7]);
-      }
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      mbar_arrive_cl(cluster_addr(&acc_empty[acc], 0));
-    }
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  if (abort_flag && rank == 0) {
-    // drain the leader's tensor-core work (bounded) before the memory is released
-    if (threadIdx.x == 32) {
-      mma_commit_pair(cluster_addr(&drain, 0));
-      mbar_wait(&drain, 0);
-    }
-  }
-  if (abort_flag && threadIdx.x == 0 && g.err) atomicExch(g.err, 1);
-  __syncthreads();
-  // no CTA of the pair leaves while the other may still touch its memory
-  cluster_sync_all();
-  if (warp == 1) {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_ALLOC) : "memory");
-  }
-}
-
 // ---- host: tensor maps ----
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
@@ -646,17 +404,10 @@ int launch_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B,
   g.beta = beta;
   g.err = err;
   g.sym = sym ? 1 : 0;
-  // The pair kernel is correct (same parity tests) but measured no faster
-  // than the single-CTA kernel on the Newton–Schulz shapes (both about
-  // 1.05-1.1 PFLOP/s on 4096 x 14336 chains), so the single-CTA kernel is
-  // dispatched; the pair path is kept for tuning its pipeline depth.
-  const bool use_pair = false && (M % PM) == 0 && !sym;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
     attr_err = cudaFuncSetAttribute(ns_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(ns_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PSMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return check_cuda(attr_err, "advopt_ns_gemm: smem attribute");
   static int sms = 0;
@@ -665,17 +416,7 @@ int launch_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void* B,
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       sms = 148;
   }
-  if (use_pair) {
-    // tensor maps of this CTA's halves: A boxes of 128 rows, B boxes of 128 columns
-    rc = make_map(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BK, 128);
-    if (rc != ADVOPT_OK) return rc;
-    if (b_mn_major) rc = make_map(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 64, BK);
-    else rc = make_map(&mb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, BK, 128);
-    if (rc != ADVOPT_OK) return rc;
-    const int ntiles = (M / PM) * (N / BN);
-    const int pairs = ntiles < sms / 2 ? ntiles : sms / 2;
-    ns_gemm_pair_kernel<<<2 * pairs, THREADS, PSMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, g, b_mn_major);
-  } else {
+  {
     const int ntiles = sym ? (N / BN) * (N / BN + 1) : (M / BM) * (N / BN);
     const int grid = ntiles < sms ? ntiles : sms;
     ns_gemm_kernel<<<grid, THREADS, SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(ma, mb, g, b_mn_major);

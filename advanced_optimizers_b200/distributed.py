@@ -50,9 +50,18 @@ def lpt_partition(costs, world: int):
     return owner
 
 
+# Rates that turn a tensor's work into seconds, so that Newton-Schulz matrices
+# and elementwise tensors of one optimizer are balanced on one scale: the
+# tcgen05 chain's sustained bf16 rate and the elementwise kernels' HBM rate.
+NS_FLOPS_PER_S = 1.1e15
+HBM_BYTES_PER_S = 3.0e12
+
+
 def default_cost(optimizer_cls, group: dict, p: torch.Tensor) -> float:
-    """Bytes touched per step for the elementwise optimizers; for the Muon
-    family, the Newton–Schulz FLOPs of matrices routed to the Muon path."""
+    """Estimated seconds of the tensor's step: HBM bytes (param and grad, plus
+    about as much again of state) at the elementwise kernels' rate, plus, for
+    the Muon family's matrices, the Newton–Schulz FLOPs at the chain's rate."""
+    elem = p.numel() * p.element_size() * 4 / HBM_BYTES_PER_S
     name = getattr(optimizer_cls, "__name__", "")
     if name in ("Muon_adv", "AdaMuon_adv") and p.ndim >= 2:
         if group.get("use_muon") is not None:
@@ -64,9 +73,9 @@ def default_cost(optimizer_cls, group: dict, p: torch.Tensor) -> float:
         if muon:
             rows = p.shape[0]
             cols = p.numel() // max(1, rows)
-            return float(ns_flops(min(rows, cols), max(rows, cols), group.get("ns_steps", 5),
-                                  group.get("accelerated_ns", False)))
-    return float(p.numel() * p.element_size())
+            return elem + float(ns_flops(min(rows, cols), max(rows, cols), group.get("ns_steps", 5),
+                                         group.get("accelerated_ns", False))) / NS_FLOPS_PER_S
+    return elem
 
 
 class FlatParams:
@@ -114,6 +123,61 @@ class FlatParams:
         return works
 
 
+class LocalSegments:
+    """Storage of this rank's tensors only, for runs whose parameters do not
+    fit replicated on every rank: per gather bucket and dtype one flat
+    segment holding the rank's owned tensors (views, 128-byte aligned), padded
+    to the largest rank's segment so that a bucket's all-gather is one
+    `all_gather_into_tensor` into a transient rank-ordered buffer.  The buffer
+    is reused by every bucket: the gathered parameters stream through it (to
+    `consume(bucket, dtype, buffer, segment)` when given) rather than being
+    kept."""
+
+    def __init__(self, shapes, dtypes, owner, bucket, world: int, rank: int, device, group=None):
+        self.world, self.rank, self.group = world, rank, group
+        self.views = {}       # tensor index -> owned view
+        self.segments = []    # per bucket: {dtype: (flat, seg)}
+        n_buckets = max(bucket, default=0) + 1
+        recv = {}
+        for k in range(n_buckets):
+            per = {}
+            for dt in sorted({dtypes[i] for i in range(len(shapes)) if bucket[i] == k}, key=str):
+                used = [0] * world
+                offs = {}
+                for i in range(len(shapes)):
+                    if bucket[i] != k or dtypes[i] != dt:
+                        continue
+                    n = math.prod(shapes[i])
+                    offs[i] = used[owner[i]]
+                    used[owner[i]] += math.ceil(n / ALIGN_ELEMS) * ALIGN_ELEMS
+                seg = max(max(used), ALIGN_ELEMS)
+                flat = torch.zeros(seg, dtype=dt, device=device)
+                for i, off in offs.items():
+                    if owner[i] == rank:
+                        self.views[i] = flat[off: off + math.prod(shapes[i])].view(shapes[i])
+                per[dt] = (flat, seg)
+                recv[dt] = max(recv.get(dt, 0), world * seg)
+            self.segments.append(per)
+        self.recv = {dt: torch.empty(n, dtype=dt, device=device) for dt, n in recv.items()}
+
+    @torch.no_grad()
+    def all_gather(self, k: int, consume=None, async_op: bool = False):
+        works = []
+        for dt, (flat, seg) in self.segments[k].items():
+            buf = self.recv[dt][: self.world * seg]
+            if dist.get_backend(self.group) == "nccl":
+                w = dist.all_gather_into_tensor(buf, flat, group=self.group, async_op=async_op)
+            else:
+                w = dist.all_gather(list(buf.split(seg)), flat, group=self.group, async_op=async_op)
+            if async_op:
+                works.append(w)
+            if consume is not None:
+                if async_op:
+                    w.wait()
+                consume(k, dt, buf, seg)
+        return works
+
+
 def gather_buckets(sizes, owner, world: int, bucket_bytes: Optional[int]):
     """Split every rank's owned tensors (in parameter order) into the same
     number of consecutive buckets of about `bucket_bytes` each, by byte
@@ -152,7 +216,8 @@ class ShardedOptimizer:
 
     def __init__(self, optimizer_cls, params, *, process_group=None,
                  cost: Optional[Callable[[dict, torch.Tensor], float]] = None, flat: bool = True,
-                 bucket_bytes: Optional[int] = 1 << 30, reserve_sms: int = 0, **kwargs):
+                 bucket_bytes: Optional[int] = 1 << 30, reserve_sms: int = 0, replicate_params: bool = True,
+                 device=None, gather_consumer=None, **kwargs):
         if not (dist.is_available() and dist.is_initialized()):
             raise RuntimeError("ShardedOptimizer needs an initialised torch.distributed process group")
         self.group = process_group
@@ -176,11 +241,23 @@ class ShardedOptimizer:
         # asynchronously while the next bucket is stepped.  Prodigy keeps one
         # bucket (its d estimate couples every tensor of the step).
         sizes = [p.numel() * p.element_size() for p in self.all_params]
-        overlap = flat and self.world > 1 and not self.is_prodigy
+        overlap = (flat or not replicate_params) and self.world > 1 and not self.is_prodigy
         self.bucket = gather_buckets(sizes, self.owner, self.world, bucket_bytes if overlap else None)
         n_buckets = max(self.bucket, default=0) + 1
         self.flats = []
-        if flat:
+        self.local = None
+        self.gather_consumer = gather_consumer
+        if not replicate_params:
+            # only the owned tensors exist on this rank (the others may be meta
+            # tensors: their shapes and dtypes place them); the owned ones are
+            # new Parameters, views of this rank's bucket segments
+            dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+            self.local = LocalSegments([tuple(p.shape) for p in self.all_params], [p.dtype for p in self.all_params],
+                                       self.owner, self.bucket, self.world, self.rank, dev, process_group)
+            for g in groups:
+                g["params"] = [self._materialize(p) for p in g["params"]]
+            self.all_params = [p for g in groups for p in g["params"]]
+        elif flat:
             for k in range(n_buckets):
                 idx = [i for i in range(len(self.all_params)) if self.bucket[i] == k]
                 self.flats.append(FlatParams([self.all_params[i] for i in idx], [self.owner[i] for i in idx],
@@ -220,6 +297,17 @@ class ShardedOptimizer:
                 opt._process_group = process_group
             self.optimizers.append(opt)
 
+    def _materialize(self, p):
+        i = next(k for k, q in enumerate(self.all_params) if q is p)
+        if self.owner[i] != self.rank:
+            return p
+        return torch.nn.Parameter(self.local.views[i], requires_grad=p.requires_grad)
+
+    def owned_params(self):
+        """This rank's parameters (with replicate_params=False, the only ones
+        that hold storage)."""
+        return [p for i, p in enumerate(self.all_params) if self.owner[i] == self.rank]
+
     @property
     def optimizer(self):
         """The inner optimizer of this rank when there is one bucket (the
@@ -249,8 +337,14 @@ class ShardedOptimizer:
 
     @torch.no_grad()
     def gather(self):
-        """Bring every rank's updated tensors to all ranks."""
+        """Bring every rank's updated tensors to all ranks (with
+        replicate_params=False: stream them through the transient buffer)."""
         if self.world == 1:
+            return
+        if self.local is not None:
+            for k in range(len(self.optimizers)):
+                for w in self.local.all_gather(k, self.gather_consumer, async_op=self.gather_consumer is None):
+                    w.wait()
             return
         if self.flats:
             for f in self.flats:
@@ -290,9 +384,15 @@ class ShardedOptimizer:
                 self._empty_k += 1
             if self.world > 1 and self.flats:
                 works += self.flats[k].all_gather(async_op=True)
+            elif self.world > 1 and self.local is not None:
+                # stream the bucket's gathered parameters through the transient
+                # buffer; the gathers run in order on the collective stream, so
+                # the next bucket's may reuse it (a consumer reads each one
+                # before the next is issued)
+                works += self.local.all_gather(k, self.gather_consumer, async_op=self.gather_consumer is None)
         for w in works:
             w.wait()
-        if self.world > 1 and not self.flats:
+        if self.world > 1 and not self.flats and self.local is None:
             self.gather()
         return loss
 

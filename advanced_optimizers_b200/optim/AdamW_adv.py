@@ -15,6 +15,7 @@ import torch
 from .. import _lib as L
 from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, init_adam_state
 from ._common import load_state_dict_exact, reject
+from ._kourkoutas import KourkoutasBeta
 
 
 class AdamW_adv(torch.optim.Optimizer):
@@ -72,7 +73,6 @@ class AdamW_adv(torch.optim.Optimizer):
         if nnmf_factor:
             state_precision = "factored"
         reject(orthogonal_gradient != "disabled", "orthogonal_gradient")
-        reject(kourkoutas_beta, "kourkoutas_beta")
         reject(spectral_normalization, "spectral_normalization")
         reject(state_precision not in SUPPORTED_PRECISIONS, f"state_precision='{state_precision}'")
         reject(centered_wd and centered_wd_mode not in ("full", "float8", "int8", "int4"),
@@ -98,12 +98,17 @@ class AdamW_adv(torch.optim.Optimizer):
         super().__init__(params, defaults)
         self._runner = AdamFamilyRunner(seed=42)
         self._ids = {}
+        # Kourkoutas-beta's layer map is built once, before the first step
+        # (Kourkoutas.py:25-57)
+        self.kourkoutas_helper = KourkoutasBeta(self) if kourkoutas_beta else None
         self.init_step()
 
     # ---- reference API surface ----
     def load_state_dict(self, state_dict: dict) -> None:
         load_state_dict_exact(self, state_dict)
         self._runner.invalidate()
+        if self.kourkoutas_helper is not None:
+            self.kourkoutas_helper.loaded()
 
     @property
     def supports_fused_back_pass(self):
@@ -154,11 +159,16 @@ class AdamW_adv(torch.optim.Optimizer):
                        normed_momentum=group.get("normed_momentum", False), cautious_wd=group.get("cautious_wd", False),
                        fisher_wd=group.get("fisher_wd", False), centered_wd=group.get("centered_wd", 0.0),
                        centered_wd_mode=group.get("centered_wd_mode", "float8"),
-                       stochastic_rounding=self.stochastic_rounding)
+                       stochastic_rounding=self.stochastic_rounding,
+                       kourkoutas=self.kourkoutas_helper if group.get("kourkoutas_beta", False) else None)
 
     def _step_params(self, gi, group, params):
         for p in params:
             self._init_state(p, group)
+        if group.get("kourkoutas_beta", False):
+            # prepare once per step, before the first param of a Kourkoutas
+            # group (AdamW_adv.py:291-295)
+            self.kourkoutas_helper.maybe_prepare(self.state[params[0]]["step"], params[0].device)
         by_dtype = {}
         for p in params:
             by_dtype.setdefault((p.dtype, p.device), []).append(p)

@@ -2,14 +2,20 @@
 
 The elementwise step and the slice statistics of every parameter run in the
 Adam-family kernel (algo PRODIGY); the per-tensor statistics are folded into
-the group's d_numerator / d_denom on the device in parameter order, then
-`calculate_d` runs on the host in double precision exactly as the reference
-does.  With `fsdp_in_use` (or a flattened FSDP parameter) and an initialised
-process group, the two sums are all-reduced over torch.distributed (NCCL on
-GPUs) before `calculate_d` (Prodigy_adv.py:550-554).
+the group's d_numerator / d_denom on the device in parameter order.  d itself
+lives on the device (advopt_prodigy_dev): the step's scalars are derived from
+it there and `calculate_d` runs there in double precision with the
+reference's arithmetic, so a step never waits for the GPU.  The param groups'
+'d', 'd_max' and 'd_numerator' are filled in when read (that read waits for
+the step that produced them, like the reference's `.item()`), and values
+written to them are uploaded before the next step.  With `fsdp_in_use` (or a
+flattened FSDP parameter) and an initialised process group, the two sums are
+all-reduced over torch.distributed (NCCL on GPUs) before `calculate_d`
+(Prodigy_adv.py:550-554).
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Callable, Optional
 
@@ -18,8 +24,70 @@ import torch
 import torch.distributed as dist
 
 from .. import _lib as L
+from .._device import stream_handle
 from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, init_adam_state
 from ._common import load_state_dict_exact, reject
+from ._kourkoutas import KourkoutasBeta
+
+
+class _DeviceDGroup(dict):
+    """A Prodigy param group whose d, d_max and d_numerator are kept on the
+    device.  Reading one waits for the step that produced it; writing one
+    (or d0) is uploaded before the next step.  Copies and pickles are plain
+    dicts with the current values."""
+
+    LAZY = ("d", "d_max", "d_numerator")
+    WATCH = ("d", "d0", "d_max", "d_numerator")
+
+    def __init__(self, group, owner):
+        super().__init__(group)
+        self._owner = owner
+
+    def _pull(self):
+        o = getattr(self, "_owner", None)
+        if o is not None:
+            o._pull_d()
+
+    def __getitem__(self, key):
+        if key in self.LAZY:
+            self._pull()
+        return dict.__getitem__(self, key)
+
+    def get(self, key, default=None):
+        if key in self.LAZY:
+            self._pull()
+        return dict.get(self, key, default)
+
+    def items(self):
+        self._pull()
+        return dict.items(self)
+
+    def values(self):
+        self._pull()
+        return dict.values(self)
+
+    def copy(self):
+        self._pull()
+        return dict(dict.items(self))
+
+    def __repr__(self):
+        self._pull()
+        return dict.__repr__(self)
+
+    def __setitem__(self, key, value):
+        if key in self.WATCH:
+            self._pull()
+            o = getattr(self, "_owner", None)
+            if o is not None:
+                o._d_dirty = True
+        dict.__setitem__(self, key, value)
+
+    def raw(self, key):
+        """The host copy without waiting (internal)."""
+        return dict.__getitem__(self, key)
+
+    def __reduce__(self):
+        return (dict, (self.copy(),))
 
 
 class Prodigy_adv(torch.optim.Optimizer):
@@ -83,7 +151,6 @@ class Prodigy_adv(torch.optim.Optimizer):
         if nnmf_factor:
             state_precision = "factored"
         reject(orthogonal_gradient != "disabled", "orthogonal_gradient")
-        reject(kourkoutas_beta, "kourkoutas_beta")
         reject(state_precision not in SUPPORTED_PRECISIONS, f"state_precision='{state_precision}'")
         defaults = {
             "lr": lr, "betas": betas, "eps": eps, "weight_decay": weight_decay,
@@ -108,14 +175,36 @@ class Prodigy_adv(torch.optim.Optimizer):
         self.device = self.param_groups[0]["params"][0].device
         self._runner = AdamFamilyRunner(seed=42)
         self._ids = {}
-        self._first = True
         self._carry_scale = 1.0      # 0 on the ranks of a sharded run that do not carry the numerator
         self._process_group = None   # group of the d all-reduce (default group when None)
+        # d on the device: advopt_prodigy_dev (4 doubles, 2 sums, 5 launch scalars)
+        self._dblock = torch.zeros(L.PRODIGY_DEV_BYTES // 8, dtype=torch.float64, device=self.device)
+        self._dsums = self._dblock.view(torch.float32)[L.PRODIGY_DEV_SUMS // 4:L.PRODIGY_DEV_SUMS // 4 + 2]
+        self._dhost = torch.zeros(4, dtype=torch.float64, pin_memory=True)
+        self._d_pending = None       # event of the last d read-back not yet folded into the groups
+        self._d_dirty = True         # host group values to upload before the next step
+        self._sums_ready = False
+        self._wrap_groups()
+        self.kourkoutas_helper = KourkoutasBeta(self) if kourkoutas_beta else None
         self.init_step()
 
+    def _wrap_groups(self):
+        self.param_groups = [g if isinstance(g, _DeviceDGroup) else _DeviceDGroup(g, self)
+                             for g in self.param_groups]
+        self._d_dirty = True
+
+    def add_param_group(self, param_group: dict) -> None:
+        super().add_param_group(param_group)
+        if hasattr(self, "_dblock"):
+            self._wrap_groups()
+
     def load_state_dict(self, state_dict: dict) -> None:
+        self._pull_d()
         load_state_dict_exact(self, state_dict)
+        self._wrap_groups()
         self._runner.invalidate()
+        if self.kourkoutas_helper is not None:
+            self.kourkoutas_helper.loaded()
 
     @property
     def supports_fused_back_pass(self):
@@ -133,14 +222,53 @@ class Prodigy_adv(torch.optim.Optimizer):
         return None
 
     def init_step(self):
-        """Prodigy_adv.py:246-257: beta3 and the accumulators of the next step."""
+        """Prodigy_adv.py:246-257: beta1, beta2 and beta3 of the next step.
+        The accumulators' reset (d_numerator * beta3, 0) is made on the
+        device by calculate_d."""
         g = self.param_groups[0]
         self.beta1, self.beta2_default = g["betas"]
         self.beta3 = g["beta3"]
         if self.beta3 is None:
             self.beta3 = math.sqrt(self.beta2_default)
-        if not self._first:
-            self._d_num_carry = float(np.float32(g.get("d_numerator", 0.0) * self.beta3)) * self._carry_scale
+
+    # ---- d on the device ----
+    def _pull_d(self):
+        """Fold the last read-back of d, d_max and d_numerator into the
+        groups (waits for the step that produced them)."""
+        ev = self._d_pending
+        if ev is None:
+            return
+        ev.synchronize()
+        self._d_pending = None
+        d, _, d_max, d_num = self._dhost.tolist()
+        for g in self.param_groups:
+            for key, v in (("d", d), ("d_max", d_max), ("d_numerator", d_num)):
+                dict.__setitem__(g, key, v)
+
+    def _push_d(self):
+        """Upload the groups' d, d0, d_max and d_numerator (first step, and
+        after they were written); the first upload also starts the sums, from
+        d_numerator without beta3 as the reference's first step does
+        (Prodigy_adv.py:333-335)."""
+        if not self._d_dirty:
+            return
+        g0 = self.param_groups[0]
+        vals = [g0.raw("d"), g0.raw("d0"), g0.raw("d_max"), g0.raw("d_numerator")]
+        for g in self.param_groups[1:]:
+            if g.raw("d") != vals[0] or g.raw("d0") != vals[1]:
+                raise NotImplementedError("Prodigy_adv on B200 keeps one d for all param groups; "
+                                          "the groups hold different d or d0")
+        self._dblock[:4].copy_(torch.tensor(vals, dtype=torch.float64))
+        if not self._sums_ready:
+            self._dsums[0] = float(np.float32(vals[3])) * self._carry_scale
+            self._dsums[1] = 0.0
+            self._sums_ready = True
+        self._d_dirty = False
+
+    def _set_carry(self, value: float):
+        """Set the next step's carried d_numerator (its first sum) directly."""
+        self._push_d()
+        self._dsums[0] = float(value)
 
     def _tid(self, p):
         t = self._ids.get(id(p))
@@ -170,21 +298,16 @@ class Prodigy_adv(torch.optim.Optimizer):
             state["p0"] = torch.tensor(0, device=p.device, dtype=p.dtype)
 
     def _cfg(self, group, stats):
-        pd = dict(d=group["d"], d0=group["d0"], beta3=self.beta3, safeguard_warmup=group["safeguard_warmup"],
-                  slice_p=group["slice_p"], stats=stats)
+        pd = dict(d=group.raw("d"), d0=group.raw("d0"), beta3=self.beta3, safeguard_warmup=group["safeguard_warmup"],
+                  slice_p=group["slice_p"], stats=stats, dev=self._dblock)
         return AdamCfg(algo=L.ALGO_PRODIGY, lr=group["lr"], betas=group["betas"], eps=group["eps"],
                        weight_decay=group["weight_decay"], precision=group["actual_state_precision"],
                        nesterov=group.get("nesterov", False), nesterov_coef=group.get("nesterov_coef"),
                        use_atan2=group["use_atan2"], cautious_wd=group.get("cautious_wd", False),
                        fisher_wd=group.get("fisher_wd", False), centered_wd=group.get("centered_wd", 0.0),
                        centered_wd_mode=group.get("centered_wd_mode", "float8"),
-                       stochastic_rounding=self.stochastic_rounding, prodigy=pd)
-
-    def _ensure_sums(self):
-        if not hasattr(self, "_sums"):
-            self._sums = torch.zeros(2, dtype=torch.float32, device=self.device)
-            self._d_num_carry = float(np.float32(self.param_groups[0].get("d_numerator", 0.0))) * self._carry_scale
-            self._first = False
+                       stochastic_rounding=self.stochastic_rounding, prodigy=pd,
+                       kourkoutas=self.kourkoutas_helper if group.get("kourkoutas_beta", False) else None)
 
     def _step_params(self, gi, group, params):
         for p in params:
@@ -196,6 +319,11 @@ class Prodigy_adv(torch.optim.Optimizer):
             for p in params:
                 self.state[p].pop("s", None)
                 self.state[p].pop("p0", None)
+        if group.get("kourkoutas_beta", False):
+            # once per step, before the first param of a Kourkoutas group
+            # (Prodigy_adv.py:337-342); v's weight is d * d * (1 - beta2)
+            self.kourkoutas_helper.maybe_prepare(self.state[params[0]]["step"], params[0].device,
+                                                 d_dev=int(self._dblock.data_ptr()))
         by_dtype = {}
         for p in params:
             by_dtype.setdefault((p.dtype, p.device), []).append(p)
@@ -203,13 +331,13 @@ class Prodigy_adv(torch.optim.Optimizer):
         for (dt, dev), ps in by_dtype.items():
             key = (gi, dt, dev, tuple(id(p) for p in ps), stats)
             self._runner.run(key, ps, [self.state[p] for p in ps], [self._tid(p) for p in ps], cfg,
-                             prodigy_sums=self._sums)
+                             prodigy_sums=self._dsums)
 
     @torch.no_grad()
     def step_parameter(self, p: torch.Tensor, group: dict, i: int | None = None):
         if p.grad is None:
             return
-        self._ensure_sums()
+        self._push_d()
         gi = next(k for k, g in enumerate(self.param_groups) if g is group)
         self._step_params(gi, group, [p])
 
@@ -219,9 +347,7 @@ class Prodigy_adv(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
-        self._ensure_sums()
-        self._sums[0] = self._d_num_carry
-        self._sums[1] = 0.0
+        self._push_d()
         for gi, group in enumerate(self.param_groups):
             params = [p for p in group["params"] if p.grad is not None]
             if params:
@@ -232,29 +358,39 @@ class Prodigy_adv(torch.optim.Optimizer):
         return loss
 
     def calculate_d(self):
-        """Prodigy_adv.py:540-576 on the host, from the device sums."""
+        """Prodigy_adv.py:540-576 on the device (advopt_prodigy_update_d),
+        followed by the reset of the sums that init_step makes in the
+        reference (d_numerator * beta3 carried, d_denom 0).  Nothing is read
+        back here: the groups' d, d_max and d_numerator are filled in when
+        read."""
+        self._push_d()
         g_group = self.param_groups[0]
         active = not (g_group.get("prodigy_steps", 0) > 0 and g_group["k"] >= g_group["prodigy_steps"])
-        if active:
-            d_max, d_coef, growth_rate = g_group["d_max"], g_group["d_coef"], g_group["growth_rate"]
-            if self.fsdp_in_use and dist.is_available() and dist.is_initialized():
-                dist.all_reduce(self._sums, op=dist.ReduceOp.SUM, group=self._process_group)
-            gn, gd = self._sums.tolist()
-            d_hat = g_group["d"]
-            if gd > 0:
-                d_hat = d_coef * gn / gd
-                if g_group.get("d_limiter", False):
-                    d_hat = min(g_group["d"] * (2 ** 0.25), d_hat)
-                if g_group["d"] == g_group["d0"]:
-                    g_group["d"] = max(g_group["d"], d_hat)
-                d_max = max(d_max, d_hat)
-                g_group["d"] = min(d_max, g_group["d"] * growth_rate)
-            for group in self.param_groups:
-                group["d_numerator"] = gn
-                group["d"] = g_group["d"]
-                group["d_max"] = d_max
+        if active and self.fsdp_in_use and dist.is_available() and dist.is_initialized():
+            dist.all_reduce(self._dsums, op=dist.ReduceOp.SUM, group=self._process_group)
+        # init_step's beta3 for the carry (Prodigy_adv.py:249-256)
+        beta3 = g_group["beta3"]
+        if beta3 is None:
+            beta3 = math.sqrt(g_group["betas"][1])
+        a = L.ProdigyDArgs()
+        a.dev = int(self._dblock.data_ptr())
+        a.active = 1 if active else 0
+        a.d_limiter = 1 if g_group.get("d_limiter", False) else 0
+        a.d_coef = float(g_group["d_coef"])
+        a.growth_rate = float(g_group["growth_rate"])
+        a.limiter_factor = 2 ** 0.25
+        a.beta3 = float(beta3)
+        a.carry_scale = float(self._carry_scale)
+        L.check(L.lib().advopt_prodigy_update_d(ctypes.byref(a), stream_handle(self.device)),
+                "advopt_prodigy_update_d")
+        self._runner.launch_count += 1
+        # read-back for the groups, folded in when one of them is read
+        self._dhost.copy_(self._dblock[:4], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self._d_pending = ev
         for group in self.param_groups:
-            group["k"] += 1
+            dict.__setitem__(group, "k", group["k"] + 1)
 
     def check_errors(self):
         self._runner.check_errors()

@@ -17,6 +17,7 @@ import torch
 from .. import _lib as L
 from .._device import DeviceTable, aligned16, dtype_code, ptr, require_cuda_tensor, stream_handle, upload_static
 from .._plan import effective_shape, plan as plan_pieces
+from ._common import ErrorWatch
 
 A_ATAN2 = 4 / math.pi
 SHIFTER = [1, 2, 4, 8, 16, 32, 64, 128]
@@ -149,7 +150,7 @@ class AdamCfg:
     def __init__(self, *, algo, lr, betas, eps, weight_decay, precision, nesterov=False, nesterov_coef=None,
                  use_bias_correction=True, use_atan2=False, normed_momentum=False, cautious_wd=False,
                  fisher_wd=False, centered_wd=0.0, centered_wd_mode="float8", stochastic_rounding=True,
-                 prodigy=None):
+                 prodigy=None, kourkoutas=None):
         self.algo = algo
         self.lr = float(lr)
         self.beta1, self.beta2 = float(betas[0]), float(betas[1])
@@ -166,7 +167,10 @@ class AdamCfg:
         self.centered_wd = float(centered_wd)
         self.centered_wd_mode = centered_wd_mode
         self.sr = bool(stochastic_rounding)
-        self.prodigy = prodigy   # dict: d, d0, beta3, safeguard_warmup, slice_p, stats (bool)
+        # dict: d, d0, beta3, safeguard_warmup, slice_p, stats (bool), dev (the
+        # advopt_prodigy_dev block: d on the device; d and d0 above are then unused)
+        self.prodigy = prodigy
+        self.kourkoutas = kourkoutas   # KourkoutasBeta of the optimizer, or None
 
 
 class GroupPlan:
@@ -228,7 +232,9 @@ class GroupPlan:
                 d["aux0"][i] = ptr(st["anchor_data"])
                 d["aux1"][i] = ptr(st.get("anchor_scale"))
                 d["aux2"][i] = ptr(st.get("anchor_min"))
-            if cfg.prodigy is not None:
+            if cfg.prodigy is not None and cfg.prodigy["stats"]:
+                # s and p0 exist while the d estimate runs (Prodigy_adv.py:
+                # 494-509); after prodigy_steps they are freed
                 d["aux0"][i] = ptr(st["s"])
                 d["aux1"][i] = ptr(st["p0"])
                 d["slice_p"][i] = cfg.prodigy["slice_p"]
@@ -290,8 +296,21 @@ class GroupPlan:
         self.stats = torch.zeros(max(1, 2 * self.n_pieces), dtype=torch.float64, device=self.device) \
             if need_stats else None
         self.table = DeviceTable(self.descs.nbytes, self.device)
-        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.err = None   # the runner's device error word (set by AdamFamilyRunner.get_plan)
         self.eps_cache = [None] * n
+        # Kourkoutas-beta: each tensor's layer and the per-piece sums of g*g
+        self.params = list(params)
+        self.layer_dev = None
+        self.gsq = None
+        self.math_bf16 = cfg.precision == "auto" and self.pdt == L.DT_BF16
+        # Prodigy with d on the device: per-tensor (eps_t, wd_t, cwd_t) in double
+        self.pconsts_host = None
+        self.pconsts_dev = None
+
+    def kourkoutas_tables(self, kk):
+        if self.layer_dev is None:
+            self.layer_dev = upload_static(np.asarray(kk.layer_table(self.params), np.int32), self.device)
+            self.gsq = torch.zeros(max(1, self.n_pieces), dtype=torch.float64, device=self.device)
 
     def launch_struct(self, cfg: AdamCfg, flags: int, seed: int) -> L.AdamLaunch:
         s = L.AdamLaunch()
@@ -311,6 +330,12 @@ class GroupPlan:
         s.seed = seed
         s.stages = self.stages
         s.err = int(self.err.data_ptr())
+        kk = cfg.kourkoutas
+        if kk is not None and kk.n:
+            self.kourkoutas_tables(kk)
+            s.layer_beta2 = int(kk.beta2.data_ptr())
+            s.layer_of_tensor = int(self.layer_dev.data_ptr())
+            s.piece_gsq = int(self.gsq.data_ptr())
         return s
 
 
@@ -328,21 +353,20 @@ class AdamFamilyRunner:
         self.kernel_events = None  # list to collect (start, end) CUDA events around the main launch
         self.launch_count = 0      # kernels launched so far (for launch accounting)
         self.reserve_sms = 0       # SMs the step's grid leaves free (see GroupPlan)
+        self.errors = ErrorWatch("an Adam-family step kernel")
 
     def invalidate(self):
         self.plans.clear()
 
     def check_errors(self):
         """Raise if a kernel reported a bounded wait that gave up (synchronises)."""
-        for pl in self.plans.values():
-            if int(pl.err.item()) != 0:
-                raise L.AdvOptError("an optimizer kernel gave up waiting for its shared-memory copies; "
-                                    "the step's results are invalid")
+        self.errors.check(sync=True)
 
     def get_plan(self, key, params, states, ids, cfg):
         pl = self.plans.get(key)
         if pl is None or any(pl.descs["param"][i] != ptr(p) for i, p in enumerate(params)):
             pl = GroupPlan(params, states, ids, cfg, self.reserve_sms)
+            pl.err = self.errors.word(pl.device)
             self.plans[key] = pl
         return pl
 
@@ -352,6 +376,8 @@ class AdamFamilyRunner:
         for p in params:
             require_cuda_tensor(p, "param")
             require_cuda_tensor(p.grad, "grad")
+        # an earlier step's kernels that gave up are reported here, without a sync
+        self.errors.check()
         pl = self.get_plan(key, params, states, ids, cfg)
         d = pl.descs
         for i, p in enumerate(params):
@@ -364,6 +390,8 @@ class AdamFamilyRunner:
         # per-tensor scalars in the reference's arithmetic (Python floats, cast to fp32)
         lr = cfg.lr
         step_cache = {}
+        pdev = cfg.algo == L.ALGO_PRODIGY and cfg.prodigy.get("dev") is not None
+        pconsts = np.zeros((len(params), 3), np.float64) if pdev else None
         for i, (p, st) in enumerate(zip(params, states)):
             t = st["step"]
             if cfg.algo == L.ALGO_PRODIGY:
@@ -387,9 +415,11 @@ class AdamFamilyRunner:
                 ss, sbc2 = sc
                 lr_wd = lr
             eps = cfg.eps if cfg.eps is not None else 1.0 / math.sqrt(p.numel())
+            wd, cwd = adjust_wds(cfg.weight_decay, cfg.centered_wd, p)
+            if pdev:
+                pconsts[i] = (eps, wd, cwd)
             if cfg.algo == L.ALGO_PRODIGY:
                 eps = cfg.prodigy["d"] * eps
-            wd, cwd = adjust_wds(cfg.weight_decay, cfg.centered_wd, p)
             d["step_size"][i] = ss
             d["sqrt_bc2"][i] = sbc2
             d["eps"][i] = eps
@@ -443,7 +473,28 @@ class AdamFamilyRunner:
                     if d[field][i] == 0:
                         raise ValueError(f"injected noise missing for tensor {i} ({field})")
         pl.table.upload(d)
+        stream = stream_handle(pl.device)
+        lib = L.lib()
+        if pdev:
+            # the d-dependent scalars and table fields from the device d
+            if pl.pconsts_host is None or not np.array_equal(pl.pconsts_host, pconsts):
+                pl.pconsts_host = pconsts
+                pl.pconsts_dev = upload_static(pconsts, pl.device)
+            pa = L.ProdigyScalarArgs()
+            pa.dev = int(cfg.prodigy["dev"].data_ptr())
+            pa.tensors = pl.table.ptr
+            pa.tensor_consts = int(pl.pconsts_dev.data_ptr())
+            pa.n_tensors = pl.n
+            pa.safeguard_warmup = 1 if cfg.prodigy["safeguard_warmup"] else 0
+            pa.lr = float(cfg.lr)
+            pa.beta1 = float(cfg.beta1)
+            pa.beta2 = float(cfg.beta2)
+            pa.step_scale = A_ATAN2 if cfg.use_atan2 else 1.0
+            L.check(lib.advopt_prodigy_scalars(ctypes.byref(pa), stream), "advopt_prodigy_scalars")
+            self.launch_count += 1
         s = pl.launch_struct(cfg, flags, self.seed)
+        if pdev:
+            s.prodigy = int(cfg.prodigy["dev"].data_ptr())
         nc = cfg.nesterov_coef
         nv_coef = cfg.beta1 if nc is None else nc
         s.beta1 = f32(cfg.beta1)
@@ -463,8 +514,6 @@ class AdamFamilyRunner:
                 s.flags |= L.F_PRODIGY_STATS
         else:
             s.c_v = f32(1.0 - cfg.beta2)
-        stream = stream_handle(pl.device)
-        lib = L.lib()
         if cfg.fisher:
             if not cfg.use_atan2:
                 st_s = L.AdamLaunch.from_buffer_copy(s)
@@ -476,8 +525,14 @@ class AdamFamilyRunner:
         if self.kernel_events is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record(torch.cuda.current_stream(pl.device))
+        kk = cfg.kourkoutas if (cfg.kourkoutas is not None and cfg.kourkoutas.n) else None
+        if kk is not None:
+            s.flags |= L.F_GRAD_SQ
         L.check(lib.advopt_adam_step(ctypes.byref(s), stream), "advopt_adam_step")
         self.launch_count += 1
+        if kk is not None:
+            kk.accumulate(pl, stream)
+            self.launch_count += 1
         if self.kernel_events is not None:
             ev1.record(torch.cuda.current_stream(pl.device))
             self.kernel_events.append((ev0, ev1, pl))
@@ -492,6 +547,7 @@ class AdamFamilyRunner:
             L.check(lib.advopt_prodigy_finish(ctypes.byref(s), int(prodigy_sums.data_ptr()), coef, s_bf16, stream),
                     "advopt_prodigy_finish")
             self.launch_count += 1
+        self.errors.after_launch(pl.device)
         for st in states:
             st["step"] += 1
         if noise_keep:

@@ -10,6 +10,53 @@ def reject(cond, what: str):
         raise NotImplementedError(f"{what} is not supported by the B200 optimizer kernels")
 
 
+class ErrorWatch:
+    """Device error words of one runner (one int32 per device) that its
+    kernels set when a bounded wait gives up, surfaced without a per-step
+    synchronisation: after every launch the word is copied into pinned host
+    memory behind a CUDA event, and the next launch (or `check(sync=True)`)
+    raises once such a copy shows it set.  A step whose kernels gave up has
+    left its parameters partly updated; the error says so at the following
+    step at the latest."""
+
+    def __init__(self, what: str):
+        self.what = what
+        self.words = {}   # device -> [device word, pinned copy, event or None]
+
+    def word(self, device, existing: torch.Tensor | None = None) -> torch.Tensor:
+        """The device's error word (`existing`, if given, becomes it)."""
+        w = self.words.get(device)
+        if w is None or (existing is not None and w[0] is not existing):
+            w = [existing if existing is not None else torch.zeros(1, dtype=torch.int32, device=device),
+                 torch.zeros(1, dtype=torch.int32, pin_memory=True), None]
+            self.words[device] = w
+        return w[0]
+
+    def after_launch(self, device) -> None:
+        w = self.words.get(device)
+        if w is None:
+            return
+        w[1].copy_(w[0], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(device))
+        w[2] = ev
+
+    def check(self, sync: bool = False) -> None:
+        for dev, w in self.words.items():
+            if sync:
+                torch.cuda.synchronize(dev)
+                bad = int(w[0].item()) != 0
+            else:
+                ev = w[2]
+                if ev is None or not ev.query():
+                    continue
+                bad = int(w[1][0]) != 0
+            if bad:
+                from .. import _lib as L
+                raise L.AdvOptError(f"{self.what} gave up waiting for its shared-memory copies (bounded wait); "
+                                    "the parameters of that step are only partly updated")
+
+
 def fix_loaded_state_dtype(state: dict, p: torch.Tensor, group: dict) -> None:
     """state_util.fix_loaded_state_dtype (state_util.py:181-263): undo
     torch's load_state_dict casting of quantised / factored states."""

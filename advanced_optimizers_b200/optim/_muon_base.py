@@ -138,10 +138,13 @@ class MuonFamilyBase(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        # chains of an earlier step that gave up are reported here, without a sync
+        self._muon_runner.errors.check()
         for gi, group in enumerate(self.param_groups):
             params = [p for p in group["params"] if p.grad is not None]
             if params:
                 self._step_params(gi, group, params)
+        self._muon_runner.after_step()
         self._test_noise = None
         return loss
 

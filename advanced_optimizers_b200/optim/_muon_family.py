@@ -20,6 +20,7 @@ import torch
 from .. import _lib as L
 from .._device import dtype_code, ptr, require_cuda_tensor, stream_handle
 from ._adam_family import adjust_wds, f32, init_state_tensor
+from ._common import ErrorWatch
 
 NS_ALIGN = 256   # the GEMM's N tile; also a multiple of its M (128) and K (64) tiles
 
@@ -172,6 +173,7 @@ class MuonMatrixRunner:
         self.ws = {}
         self.launch_count = 0
         self.gemm_events = None   # (start, end, algorithmic flops, executed flops) of each NS chain
+        self.errors = ErrorWatch("a Newton-Schulz GEMM")
 
     def workspace(self, device) -> NSWorkspace:
         # one workspace per device, shared by every runner: the chains of all
@@ -181,13 +183,16 @@ class MuonMatrixRunner:
             ws = NSWorkspace(device)
             _DEVICE_WS[device] = ws
         self.ws[device] = ws
+        self.errors.word(device, ws.err)
         return ws
 
     def check_errors(self):
-        for ws in self.ws.values():
-            if int(ws.err.item()) != 0:
-                raise L.AdvOptError("a Newton-Schulz GEMM gave up waiting for its shared-memory copies; "
-                                    "the step's results are invalid")
+        self.errors.check(sync=True)
+
+    def after_step(self):
+        """Queue the non-blocking read-back of the error words (once per step)."""
+        for dev in self.ws:
+            self.errors.after_launch(dev)
 
     @torch.no_grad()
     def step_matrix(self, p, state, *, adamuon: bool, lr: float, beta1: float, beta2: float, eps, nesterov: bool,

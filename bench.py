@@ -118,64 +118,126 @@ def measured_peaks():
 # CPU baseline: the oracle (CPU restatement of the reference's step)
 # ---------------------------------------------------------------------------
 
-def oracle_sample_step(sample_shapes, seed=0):
-    """Time one oracle step over `sample_shapes`; returns (seconds, elements)."""
-    from oracle import oracle as O
-    rng = np.random.default_rng(seed)
-    hp = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, nesterov=True, precision="int8_sr")
-    items = []
-    for sh in sample_shapes:
-        n = math.prod(sh)
-        p = O.round_bf16((rng.standard_normal(n, dtype=np.float32) * 0.02).reshape(sh))
-        g = rng.standard_normal(n, dtype=np.float32) * 1e-3
-        g = np.where(rng.random(n) < 0.01, g * 100, g).astype(np.float32)
-        g = O.round_bf16(g.reshape(sh))
-        st = O.adamw_init_state(sh, "bf16", "int8_sr", True, 0.9)
-        pad = ((n + 2047) // 2048) * 2048
-        nz = {k: rng.integers(0, 65536, m, dtype=np.int32) for k, m in (("exp_avg", pad), ("exp_avg_sq", pad),
-                                                                           ("param", n))}
-        items.append((p, g, st, nz))
-    t0 = time.perf_counter()
-    for p, g, st, nz in items:
-        O.adam_family_step(p, "bf16", g, st, hp, nz, algo="adamw")
-    dt = time.perf_counter() - t0
-    return dt, sum(math.prod(s) for s in sample_shapes)
+def llama3_8b_distinct():
+    """The distinct Llama-3-8B tensor shapes and how many of the 291 tensors
+    have each (embed/lm_head, q/o, k/v, gate/up, down, RMSNorm weights)."""
+    d, kv, ffn, V = 4096, 1024, 14336, 128256
+    return [((V, d), 2), ((d, d), 64), ((kv, d), 64), ((ffn, d), 64), ((d, ffn), 32), ((d,), 65)]
 
 
-def cpu_baseline(total_elems):
-    from oracle import oracle as O
-    sample = [(4096, 4096), (4096,)]
-    dt, n = oracle_sample_step(sample)
-    steps_per_s = (n / total_elems) / dt
-    return {"value": steps_per_s, "unit": "optimizer steps/s", "cores": O.num_threads(), "kind": "port",
-            "sample": f"one oracle step over a q_proj 4096x4096 + a 4096 norm ({n} of {total_elems} elements, "
-                      f"{dt:.2f} s), scaled by element count"}
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+class OracleSample:
+    """One oracle step per distinct Llama-3-8B shape, the way the reference
+    runs its step: tensor after tensor, each op using every host core (the
+    oracle's C primitives are OpenMP loops; its numpy parts run on one).  A
+    full step's time is the sum over the 291 tensors of the measured time of
+    their shape.  Shapes above 64M elements (the 525M-element embedding) are
+    timed on a slab of whole rows and scaled by the element count (said in
+    `describe()`), which keeps a sample to seconds."""
+
+    def __init__(self, seed=0, cores=None, max_elems=64 << 20):
+        from oracle import oracle as O
+        self.O = O
+        self.cores = int(cores or host_cores())
+        O.set_num_threads(self.cores)
+        try:
+            import psutil
+            avail = psutil.virtual_memory().available
+        except Exception:
+            avail = 64 << 30
+        rng = np.random.default_rng(seed)
+        self.hp = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, nesterov=True, precision="int8_sr")
+        self.items = []
+        self.slabbed = []
+        for sh, mult in llama3_8b_distinct():
+            n = math.prod(sh)
+            scale = 1.0
+            # at most max_elems per timed item (and what host memory holds:
+            # float32 inputs, draws and the step's temporaries, ~64 B/element):
+            # larger shapes are timed on a slab of whole rows
+            cap = min(max_elems, int(0.5 * avail) // 64)
+            if n > cap:
+                k = math.ceil(n / cap)
+                sh = (max(1, sh[0] // k),) + tuple(sh[1:])
+                scale = n / math.prod(sh)
+                self.slabbed.append((sh, scale))
+                n = math.prod(sh)
+            p = O.round_bf16((rng.standard_normal(n, dtype=np.float32) * 0.02).reshape(sh))
+            g = rng.standard_normal(n, dtype=np.float32) * 1e-3
+            g = np.where(rng.random(n, dtype=np.float32) < 0.01, g * 100, g).astype(np.float32)
+            g = O.round_bf16(g.reshape(sh))
+            st = O.adamw_init_state(sh, "bf16", "int8_sr", True, 0.9)
+            pad = ((n + 2047) // 2048) * 2048
+            nz = {"exp_avg": rng.integers(0, 65536, pad, dtype=np.int32),
+                  "exp_avg_sq": rng.integers(0, 65536, pad, dtype=np.int32),
+                  "param": rng.integers(0, 65536, n, dtype=np.int32)}
+            self.items.append((sh, mult, scale, p, g, st, nz))
+
+    def run(self):
+        """One sample: (wall seconds of the sample, seconds of one full step)."""
+        full = 0.0
+        t_all = time.perf_counter()
+        for sh, mult, scale, p, g, st, nz in self.items:
+            t0 = time.perf_counter()
+            self.O.adam_family_step(p, "bf16", g, st, self.hp, nz, algo="adamw")
+            full += (time.perf_counter() - t0) * scale * mult
+        return time.perf_counter() - t_all, full
+
+    def describe(self, sample_s):
+        s = (f"each sample: one oracle step per distinct Llama-3-8B shape (embed 128256x4096, q/o 4096x4096, "
+             f"k/v 1024x4096, gate/up 14336x4096, down 4096x14336, norm 4096), in sequence, {self.cores} OpenMP "
+             f"threads in the C primitives; full step = sum over the 291 tensors of their shape's time "
+             f"(sample {sample_s:.1f} s)")
+        if self.slabbed:
+            s += "; timed on row slabs scaled by element count: " + ", ".join(
+                f"{list(sh)} x{sc:.0f}" for sh, sc in self.slabbed)
+        return s
+
+
+def cpu_baseline():
+    """The oracle's step on this host (one warm-up sample, one timed)."""
+    smp = OracleSample()
+    smp.run()
+    wall, full = smp.run()
+    return {"value": 1.0 / full, "unit": "optimizer steps/s", "cores": smp.cores, "kind": "port",
+            "sample": smp.describe(wall), "full_step_s": full}
 
 
 def run_reference(args):
+    """The reference's CPU step on this host's cores (the oracle port: the
+    reference is a Python package that does not travel), rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from oracle import oracle as O
     shapes = llama3_8b_shapes()
     total = sum(math.prod(s) for s in shapes)
-    sample = [(4096, 4096), (4096,)]
+    smp = OracleSample()
     for _ in range(args.warmup):
-        oracle_sample_step(sample)
-    ts = []
-    for k in range(args.steps):
-        dt, n = oracle_sample_step(sample, seed=k)
-        ts.append(dt * total / n)     # seconds for one full step, extrapolated by element count
-    sec = float(np.mean(ts))
-    value = 1.0 / sec
+        smp.run()
+    walls, fulls = [], []
+    for _ in range(args.steps):
+        w, f = smp.run()
+        walls.append(w)
+        fulls.append(f)
+    full = float(np.mean(fulls))
+    value = 1.0 / full
     out = {"impl": "reference", "metric": "optimizer steps/s at Llama-3-8B shapes", "value": value,
            "unit": "optimizer steps/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-           "ms_per_step": sec * 1000, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+           # the timed samples' own wall time; full_step_ms is the whole step they stand for
+           "ms_per_step": float(np.mean(walls)) * 1000, "full_step_ms": full * 1000,
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
            "dtype": "f32", "data": "synthetic",
-           "config": {"workload": WORKLOAD, "params": total, "tensors": len(shapes)},
-           "cpu_baseline": {"value": value, "unit": "optimizer steps/s", "cores": O.num_threads(), "kind": "port",
-                            "sample": "each step: one oracle step over a q_proj 4096x4096 + a 4096 norm, "
-                                      "extrapolated to all 8.03e9 elements by element count"},
+           "config": {"workload": WORKLOAD, "params": total, "tensors": len(shapes),
+                      "parallelism": f"per-tensor sharding x{args.gpus}",
+                      "l2": "inputs larger than L2 (about 40 GB resident per step)"},
+           "cpu_baseline": {"value": value, "unit": "optimizer steps/s", "cores": smp.cores, "kind": "port",
+                            "sample": smp.describe(float(np.mean(walls)))},
            "e2e": {"value": value, "unit": "optimizer steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -271,17 +333,54 @@ def run_ours(args):
     ms_per_step = elapsed_ms / args.steps
     value = 1000.0 / ms_per_step   # whole-job optimizer steps/s (every rank takes part in each step)
 
+    # sharded: the same step without the parameter all-gather (each rank's
+    # kernels only), and the all-gather alone, beside the full step above
+    split = None
+    if world > 1:
+        def timed(fn, n):
+            torch.cuda.synchronize()
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(n):
+                fn()
+            b.record()
+            torch.cuda.synchronize()
+            t = torch.tensor([a.elapsed_time(b) / n], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        def step_only():
+            for o in opts:
+                o.step()
+
+        only = timed(step_only, args.steps)
+        gather = timed(sharded.gather, args.steps)
+        moved = sum(fl.numel() * fl.element_size() for f in sharded.flats for fl, _ in f.buffers)
+        recv = moved * (world - 1) / world
+        split = {"step_only_ms": only, "step_only_value": 1000.0 / only, "step_plus_gather_ms": ms_per_step,
+                 "gather_only_ms": gather, "gather_bytes_received_per_rank": recv,
+                 "gather_gbs_per_rank": recv / (gather * 1e-3) / 1e9 if gather > 0 else 0.0,
+                 "nvlink_peer_copy_gbs": 770.0}
+
     # ---- e2e: grads copied host->device every step, one result read back ----
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, owned, step, world, dev, opt if world == 1 else None, sharded)
-    ns = None
-    if not args.no_ns:
+    ns = prodigy = None
+    if not (args.no_ns and args.no_prodigy):
         del opt, opts, owned, params, step, sharded
         torch.cuda.empty_cache()
+    if not args.no_ns:
         ns = run_ns_leg(args, world, rank, dev)
+    if not args.no_prodigy:
+        prodigy = run_prodigy_leg(args, world, rank, dev)
+    adamuon70 = None
+    if world >= 4 and not args.no_70b:
+        adamuon70 = run_adamuon70b_leg(args, world, rank, dev)
     if rank == 0:
-        emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, launches, clocks, e2e, ns)
+        emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, launches, clocks, e2e, ns,
+             prodigy, adamuon70, split)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -294,32 +393,42 @@ def muon_shapes(layers=32):
 
 
 def run_ns_leg(args, world, rank, dev):
-    """Muon_adv (momentum 0.95, 5 quintic Newton-Schulz iterations, bf16
-    'auto' states) over every hidden matrix; with N ranks the matrices are
-    split by Newton-Schulz FLOPs (ShardedOptimizer) and the updated params
-    all-gathered."""
+    """The Muon_adv step of the Llama-3-8B configuration: Muon (momentum 0.95,
+    5 quintic Newton-Schulz iterations, bf16 'auto' states) on every hidden
+    matrix, and Muon's auxiliary AdamW with fp32 states
+    (adam_state_precision='fp32') on the two 128256x4096 embeddings and the 65
+    RMSNorm weights, all in one optimizer step.  With N ranks the tensors are
+    split by Newton-Schulz FLOPs / bytes (ShardedOptimizer) and the updated
+    params all-gathered."""
     import torch.distributed as dist
     import advanced_optimizers_b200 as A
     from advanced_optimizers_b200.optim._muon_family import ns_flops
     shapes = muon_shapes(args.layers)
     flops = [ns_flops(min(s), max(s), 5, False) for s in shapes]
+    d, V = 4096, 128256
+    adam_shapes = ([(V, d), (V, d)] if not args.no_embed else []) + [(d,)] * (2 * args.layers + 1)
     gen = torch.Generator(device=dev).manual_seed(4321 + rank)
     params = [torch.nn.Parameter(torch.empty(sh, dtype=torch.bfloat16, device=dev)) for sh in shapes]
-    groups = [dict(params=params, optim_type="muon")]
+    aparams = [torch.nn.Parameter(torch.empty(sh, dtype=torch.bfloat16, device=dev)) for sh in adam_shapes]
+    groups = [dict(params=params, optim_type="muon"), dict(params=aparams, optim_type="adam")]
+    kw = dict(lr=1e-3, beta1=0.95, adam_state_precision="fp32")
     if world > 1:
-        sharded = A.ShardedOptimizer(A.Muon_adv, groups, lr=1e-3, beta1=0.95)
+        sharded = A.ShardedOptimizer(A.Muon_adv, groups, **kw)
         owner = sharded.owner
     else:
         sharded = None
-        owner = [0] * len(shapes)
-    owned = [params[i] for i in range(len(shapes)) if owner[i] == rank]
+        owner = [0] * (len(shapes) + len(adam_shapes))
+    allp = params + aparams
+    owned = [allp[i] for i in range(len(allp)) if owner[i] == rank]
     with torch.no_grad():
         for p in owned:
             p.normal_(0, 0.02, generator=gen)
     for p in owned:
         p.grad = torch.empty_like(p).normal_(0, 1e-3, generator=gen)
-    opts = ([o for o in sharded.optimizers if o is not None] if sharded is not None else
-            [A.Muon_adv([dict(params=owned, optim_type="muon")], lr=1e-3, beta1=0.95)])
+    if sharded is not None:
+        opts = [o for o in sharded.optimizers if o is not None]
+    else:
+        opts = [A.Muon_adv([dict(params=params, optim_type="muon"), dict(params=aparams, optim_type="adam")], **kw)]
     opt = opts[0]
 
     def step():
@@ -328,15 +437,18 @@ def run_ns_leg(args, world, rank, dev):
         else:
             opt.step()
 
-    warm = 1
-    steps = 2
+    warm = 2
+    steps = 5
     for _ in range(warm):
         step()
     torch.cuda.synchronize()
+    for o in opts:
+        o.check_errors()
     if world > 1:
         dist.barrier()
     for o in opts:
         o._muon_runner.gemm_events = []
+        o._adam_runner.kernel_events = []
     l0 = sum(o.launch_count for o in opts)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -349,26 +461,31 @@ def run_ns_leg(args, world, rank, dev):
     gemm_ms = sum(e[0].elapsed_time(e[1]) for e in gev) / steps
     fl = sum(e[2] for e in gev) / steps      # the reference's FLOP count of the chains
     fx = sum(e[3] for e in gev) / steps      # FLOPs the tensor cores execute (symmetric products halved)
+    aux_ms = sum(a.elapsed_time(b) for o in opts for a, b, _ in o._adam_runner.kernel_events) / steps
     for o in opts:
         o._muon_runner.gemm_events = None
+        o._adam_runner.kernel_events = None
     launches = sum(o.launch_count for o in opts) - l0
     if world > 1:
-        t = torch.tensor([ms, gemm_ms], device=dev, dtype=torch.float64)
+        t = torch.tensor([ms, gemm_ms, aux_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, gemm_ms = (float(x) for x in t.tolist())
+        ms, gemm_ms, aux_ms = (float(x) for x in t.tolist())
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peak, kind = float(json.load(f)["bf16_tflops_sustained"]), "measured sustained"
     except Exception:
         peak, kind = 1400.0, "fallback sustained"
     total_flops = sum(flops)
-    del opt, opts, owned, params, sharded
+    n_aux = sum(math.prod(s) for s in adam_shapes)
+    del opt, opts, owned, params, aparams, allp, sharded
     torch.cuda.empty_cache()
-    return {"workload": f"Muon_adv over {len(shapes)} Llama-3-8B hidden matrices (q/o 4096x4096, k/v 1024x4096, "
-                        "gate/up 14336x4096, down 4096x14336), momentum 0.95, 5 quintic Newton-Schulz "
-                        "iterations, bf16 'auto' states", "steps": steps, "warmup": warm,
+    return {"workload": f"Muon_adv step: Muon over {len(shapes)} Llama-3-8B hidden matrices (q/o 4096x4096, "
+                        "k/v 1024x4096, gate/up 14336x4096, down 4096x14336), momentum 0.95, 5 quintic "
+                        f"Newton-Schulz iterations, bf16 'auto' states; auxiliary AdamW (fp32 states) over "
+                        f"{len(adam_shapes)} embedding / RMSNorm tensors ({n_aux} elements)",
+            "steps": steps, "warmup": warm,
             "ms_per_step": ms, "value": 1000.0 / ms, "unit": "optimizer steps/s",
-            "ns_ms_per_step": gemm_ms,
+            "ns_ms_per_step": gemm_ms, "aux_adam_ms_per_step": aux_ms,
             "roofline": {"bound": "tensor", "achieved": (fx / (gemm_ms * 1e-3)) / 1e12 if gemm_ms > 0 else 0.0,
                          "peak": peak, "unit": "TFLOP/s",
                          "frac": ((fx / (gemm_ms * 1e-3)) / 1e12) / peak if gemm_ms > 0 else 0.0,
@@ -380,6 +497,220 @@ def run_ns_leg(args, world, rank, dev):
                                  "b A + c A A on the blocks on or above the diagonal) / its chain time; "
                                  "algorithmic_tflops = the reference's FLOP count 5(4m^2n+2m^3) / the same time"},
             "gpu_launches": launches}
+
+
+def gpt_1p3b_shapes(layers=24):
+    """A 1.3B GPT-style shape list (d_model 2048, ffn 8192, vocab 50304,
+    tied embeddings): embedding, per layer fused qkv 6144x2048, out 2048x2048,
+    fc 8192x2048, proj 2048x8192 and two LayerNorm weights, then the final
+    LayerNorm; 1.311e9 elements in 146 tensors."""
+    d, ffn, V = 2048, 8192, 50304
+    s = [(V, d)]
+    for _ in range(layers):
+        s += [(3 * d, d), (d, d), (ffn, d), (d, ffn), (d,), (d,)]
+    return s + [(d,)]
+
+
+def prodigy_bytes(shapes, slice_p=11):
+    """Mandatory HBM bytes of one Prodigy_adv bf16_sr step: bf16 p read+write,
+    bf16 g read, bf16 m and v read+write (14 B/element), plus every
+    slice_p-th element's bf16 s read+write and bf16 p0 read."""
+    tot = 0
+    for sh in shapes:
+        n = math.prod(sh)
+        tot += 14 * n + 6 * ((n + slice_p - 1) // slice_p)
+    return tot
+
+
+def run_prodigy_leg(args, world, rank, dev):
+    """Prodigy_adv(state_precision='bf16_sr', d0=1e-6) over the 1.3B GPT
+    shapes; bf16 params ~N(0, 0.02^2), grads ~N(0, 1e-3^2) times a per-step
+    scale drawn log-uniform in [1e-4, 1e-2].  Each step ends in the d
+    estimate: with N ranks the owners' two sums are all-reduced (one 2-float
+    NCCL all-reduce) and the updated params all-gathered."""
+    import torch.distributed as dist
+    import advanced_optimizers_b200 as A
+    shapes = gpt_1p3b_shapes(args.prodigy_layers)
+    gen = torch.Generator(device=dev).manual_seed(777 + rank)
+    params = [torch.nn.Parameter(torch.empty(sh, dtype=torch.bfloat16, device=dev)) for sh in shapes]
+    kw = dict(state_precision="bf16_sr", d0=1e-6)
+    if world > 1:
+        sharded = A.ShardedOptimizer(A.Prodigy_adv, params, **kw)
+        owner = sharded.owner
+    else:
+        sharded = None
+        owner = [0] * len(shapes)
+    owned = [params[i] for i in range(len(shapes)) if owner[i] == rank]
+    with torch.no_grad():
+        for p in owned:
+            p.normal_(0, 0.02, generator=gen)
+    base = [torch.empty_like(p).normal_(0, 1e-3, generator=gen) for p in owned]
+    opts = [o for o in sharded.optimizers if o is not None] if sharded is not None else [A.Prodigy_adv(owned, **kw)]
+    rng = np.random.default_rng(99)
+    scales = [float(10 ** rng.uniform(-4, -2)) for _ in range(64)]
+
+    def step(k):
+        with torch.no_grad():
+            for p, b in zip(owned, base):
+                p.grad = b * scales[k % len(scales)]
+        if sharded is not None:
+            sharded.step()
+        else:
+            opts[0].step()
+
+    warm, steps = 3, 10
+    for k in range(warm):
+        step(k)
+    torch.cuda.synchronize()
+    for o in opts:
+        o.check_errors()
+    if world > 1:
+        dist.barrier()
+    # the grads of each step are set before its clock starts
+    tot = 0.0
+    kms = 0.0
+    for k in range(steps):
+        with torch.no_grad():
+            for p, b in zip(owned, base):
+                p.grad = b * scales[(warm + k) % len(scales)]
+        for o in opts:
+            o._runner.kernel_events = []
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        if sharded is not None:
+            sharded.step()
+        else:
+            opts[0].step()
+        e1.record()
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+        kms += sum(a.elapsed_time(b) for o in opts for a, b, _ in o._runner.kernel_events)
+        for o in opts:
+            o._runner.kernel_events = None
+    ms, kernel_ms = tot / steps, kms / steps
+    if world > 1:
+        t = torch.tensor([ms, kernel_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, kernel_ms = (float(x) for x in t.tolist())
+    d_val = float(opts[0].param_groups[0]["d"]) if opts else 0.0
+    mine = [shapes[i] for i in range(len(shapes)) if owner[i] == rank]
+    alg = prodigy_bytes(mine)
+    peak, peak_kind = measured_peaks()
+    achieved = alg / (kernel_ms * 1e-3) / 1e9 if kernel_ms > 0 else 0.0
+    del opts, owned, params, base, sharded
+    torch.cuda.empty_cache()
+    return {"workload": "Prodigy_adv(state_precision='bf16_sr', d0=1e-6), 1.3B GPT shapes (d_model 2048, "
+                        f"{args.prodigy_layers} layers, ffn 8192, vocab 50304, tied embedding), bf16, "
+                        "grads x log-uniform[1e-4, 1e-2] per step",
+            "params": sum(math.prod(s) for s in shapes), "tensors": len(shapes),
+            "steps": steps, "warmup": warm, "ms_per_step": ms, "value": 1000.0 / ms, "unit": "optimizer steps/s",
+            "d_after": d_val,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "kernel": "adam_fast_kernel<BF16_SR, bf16, Prodigy>",
+                         "kernel_ms": kernel_ms, "algorithmic_bytes": alg}}
+
+
+def llama3_70b_matrices(layers=80):
+    """Llama-3-70B 2-D weights: per layer q/o 8192x8192, k/v 1024x8192,
+    gate/up 28672x8192, down 8192x28672, plus the 128256x8192 embedding; 561
+    matrices, 6.95e10 elements."""
+    d, kv, ffn, V = 8192, 1024, 28672, 128256
+    s = [(V, d)]
+    for _ in range(layers):
+        s += [(d, d), (kv, d), (kv, d), (d, d), (ffn, d), (ffn, d), (d, ffn)]
+    return s
+
+
+def run_adamuon70b_leg(args, world, rank, dev):
+    """AdaMuon_adv(accelerated_ns=True (CANS), state_precision='int8_sr') over
+    the Llama-3-70B 2-D weights, states and Newton-Schulz work sharded per
+    tensor.  The bf16 model (139 GB) does not fit replicated next to the
+    states, so each rank holds only the tensors it owns
+    (ShardedOptimizer(replicate_params=False)); after each bucket is stepped
+    its updated params stream through one transient all-gather buffer.
+    Runs with 4 or more ranks (about 105 GB per rank at 4, 55 GB at 8)."""
+    import torch.distributed as dist
+    import advanced_optimizers_b200 as A
+    from advanced_optimizers_b200.optim._muon_family import ns_flops
+    shapes = llama3_70b_matrices()
+    meta = [torch.nn.Parameter(torch.empty(sh, dtype=torch.bfloat16, device="meta")) for sh in shapes]
+    kw = dict(lr=1e-3, accelerated_ns=True, state_precision="int8_sr")
+    sharded = A.ShardedOptimizer(A.AdaMuon_adv, [dict(params=meta, optim_type="muon")], replicate_params=False,
+                                 **kw)
+    gen = torch.Generator(device=dev).manual_seed(7000 + rank)
+    owned = sharded.owned_params()
+    with torch.no_grad():
+        for p in owned:
+            p.normal_(0, 0.02, generator=gen)
+    for p in owned:
+        p.grad = torch.empty_like(p).normal_(0, 1e-3, generator=gen)
+    opts = [o for o in sharded.optimizers if o is not None]
+    warm, steps = 1, 2
+    for _ in range(warm):
+        sharded.step()
+    torch.cuda.synchronize()
+    for o in opts:
+        o.check_errors()
+    dist.barrier()
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for o in opts:
+        o._muon_runner.gemm_events = []
+    ms = timed(sharded.step)
+    gev = [e for o in opts for e in o._muon_runner.gemm_events]
+    gemm_ms = sum(e[0].elapsed_time(e[1]) for e in gev) / steps
+    fx = sum(e[3] for e in gev) / steps
+    for o in opts:
+        o._muon_runner.gemm_events = None
+
+    def step_only():
+        for o in opts:
+            o.step()
+
+    ms_step_only = timed(step_only)
+    t = torch.tensor([gemm_ms, fx], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    gemm_ms_max = float(t[0])
+    tf = torch.tensor([fx], device=dev, dtype=torch.float64)
+    dist.all_reduce(tf, op=dist.ReduceOp.SUM)
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, kind = float(json.load(f)["bf16_tflops_sustained"]), "measured sustained"
+    except Exception:
+        peak, kind = 1400.0, "fallback sustained"
+    total_flops = sum(ns_flops(min(s), max(s), 5, True) for s in shapes)
+    own_bytes = sum(p.numel() for p in owned) * 2
+    del opts, owned, sharded, meta
+    torch.cuda.empty_cache()
+    return {"workload": "AdaMuon_adv(accelerated_ns=True, state_precision='int8_sr') over the 561 Llama-3-70B 2-D "
+                        "weights (6.95e10 elements), bf16, states and Newton-Schulz work sharded per tensor, params "
+                        "not replicated (streamed bucket all-gathers)",
+            "n_gpus": world, "steps": steps, "warmup": warm,
+            "ms_per_step": ms, "value": 1000.0 / ms, "unit": "optimizer steps/s",
+            "step_only_ms": ms_step_only, "ns_ms_per_step_max_rank": gemm_ms_max,
+            "owned_param_bytes_rank0": own_bytes,
+            "roofline": {"bound": "tensor", "achieved": (tf.item() / world / (gemm_ms_max * 1e-3)) / 1e12
+                         if gemm_ms_max > 0 else 0.0, "peak": peak, "unit": "TFLOP/s",
+                         "frac": (tf.item() / world / (gemm_ms_max * 1e-3)) / 1e12 / peak if gemm_ms_max > 0 else 0.0,
+                         "peak_kind": kind, "kernel": "ns_gemm_kernel (tcgen05, 128x256 tiles), CANS chain",
+                         "algorithmic_flops_per_step": total_flops,
+                         "note": "achieved = executed tensor-core FLOPs per rank (mean over ranks) / the slowest "
+                                 "rank's chain time"}}
 
 
 def run_e2e(args, owned, step, world, dev, opt=None, sharded=None):
@@ -449,7 +780,8 @@ def run_e2e(args, owned, step, world, dev, opt=None, sharded=None):
             "d2h_bytes_per_step": readback.numel() * 2}
 
 
-def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, launches, clocks, e2e, ns=None):
+def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, launches, clocks, e2e, ns=None,
+         prodigy=None, adamuon70=None, split=None):
     if True:
         alg = algorithmic_bytes([shapes[i] for i in mine])
         peak, peak_kind = measured_peaks()
@@ -469,16 +801,23 @@ def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, la
                          "frac": achieved / peak, "traffic": TRAFFIC_PER_ALG_BYTE * alg,
                          "traffic_note": "dram bytes per launch scaled from the 2-layer ncu capture",
                          "peak_kind": peak_kind,
-                         "kernel": "adam_fast_kernel<INT8_SR, bf16, AdamW, Philox, flags compiled in>", "kernel_ms": kernel_avg_ms,
+                         "kernel": "adam_fast_kernel<INT8_SR, bf16, AdamW, Philox, flags compiled in>",
+                         "kernel_ms": kernel_avg_ms,
                          "algorithmic_bytes": alg},
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,
         }
         if ns is not None:
-            out["muon_ns"] = ns
+            out["muon_step"] = ns
+        if prodigy is not None:
+            out["prodigy_step"] = prodigy
+        if adamuon70 is not None:
+            out["adamuon_70b_step"] = adamuon70
+        if split is not None:
+            out["sharded"] = split
         if world == 1 and not args.no_cpu_baseline:
-            out["cpu_baseline"] = cpu_baseline(total)
+            out["cpu_baseline"] = cpu_baseline()
         print(json.dumps(out), flush=True)
 
 
@@ -492,7 +831,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--layers", type=int, default=32, help="decoder layers (32 = the full model; fewer for profiling)")
     ap.add_argument("--no-embed", action="store_true", help="leave out embed/lm_head (profiling only)")
-    ap.add_argument("--no-ns", action="store_true", help="skip the Muon Newton-Schulz leg")
+    ap.add_argument("--no-ns", action="store_true", help="skip the Muon_adv step leg")
+    ap.add_argument("--no-prodigy", action="store_true", help="skip the Prodigy_adv step leg")
+    ap.add_argument("--prodigy-layers", type=int, default=24,
+                    help="layers of the 1.3B GPT shapes in the Prodigy_adv leg (24 = the full model; fewer for profiling)")
+    ap.add_argument("--no-70b", action="store_true", help="skip the AdaMuon Llama-3-70B leg (4+ GPUs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define ADVOPT_ABI_VERSION 1
+#define ADVOPT_ABI_VERSION 3
 
 /* ---- error codes ---- */
 #define ADVOPT_OK 0
@@ -63,6 +63,7 @@ extern "C" {
 #define ADVOPT_F_FISHER_STATS (1u << 9)/* this launch only accumulates sum((p*ws)^2) */
 #define ADVOPT_F_ANCHORS (1u << 10)    /* some tensor carries a centered-WD anchor */
 #define ADVOPT_F_NO_WD (1u << 11)      /* no tensor of the launch has weight decay (optional hint) */
+#define ADVOPT_F_GRAD_SQ (1u << 12)    /* also write each piece's sum of g*g to piece_gsq (Kourkoutas-beta) */
 
 /* per-tensor flags */
 #define ADVOPT_T_FACTORED (1u << 0)    /* second moment as rank-1 factors (factored_2nd) */
@@ -124,6 +125,25 @@ typedef struct advopt_piece {
   int32_t slot;
 } advopt_piece;
 
+/* Prodigy's d estimate, resident in device memory (one per optimizer).  The
+ * doubles are the param group's Python floats d, d0, d_max, d_numerator;
+ * sums are the running d_numerator (carried, times beta3) and d_denom of the
+ * current step (Prodigy_adv.py:246-257, 333-335); the five floats are the
+ * step's launch scalars written by advopt_prodigy_scalars. */
+typedef struct advopt_prodigy_dev {
+  double d;
+  double d0;
+  double d_max;
+  double d_numerator;
+  float sums[2];
+  float c_v;                 /* float(d * d * (1 - beta2))                     */
+  float c_m;                 /* float(d * (1 - beta1))                         */
+  float d_f;                 /* float(d)                                       */
+  float s_alpha;             /* float((d / d0) * d) or float((d / d0) * dlr)  */
+  float coef;                /* float((d / d0) * dlr): d_numerator's add       */
+  float pad;
+} advopt_prodigy_dev;
+
 /* One launch over one parameter group (all scalars already rounded to fp32
  * the way the reference's scalar arguments are). */
 typedef struct advopt_adam_launch {
@@ -153,6 +173,15 @@ typedef struct advopt_adam_launch {
   float d;                            /* Prodigy d (grad.mul(d) without momentum) */
   int32_t stages;                     /* fast path: shared-memory ring depth (2..4); 0 = general kernel */
   uint64_t seed;                      /* Philox key                           */
+  /* Kourkoutas-beta (both NULL otherwise): tensor t's v update uses
+   * beta2 = layer_beta2[2 * layer_of_tensor[t]] and (1 - beta2) =
+   * layer_beta2[2 * layer_of_tensor[t] + 1] instead of beta2 / c_v. */
+  const float* layer_beta2;           /* [n_layers][2], written by advopt_kourkoutas_prepare */
+  const int32_t* layer_of_tensor;     /* [n_tensors]                          */
+  double* piece_gsq;                  /* ADVOPT_F_GRAD_SQ: [n_pieces] sum of g*g of the grad the step uses */
+  /* Prodigy with d on the device: c_v, c_m, d and s_alpha are read from here
+   * instead of the fields above (NULL: the fields above) */
+  const advopt_prodigy_dev* prodigy;
 } advopt_adam_launch;
 
 /* Adam-family step for one group.  Replaces AdamW_adv.step/_step_parameter
@@ -168,10 +197,52 @@ int advopt_adam_step(const advopt_adam_launch* launch, void* stream);
 int advopt_factored_finish(const advopt_adam_launch* launch, const int32_t* tensor_index,
                            int32_t n_factored, int32_t max_d2, void* stream);
 
+/*
+ * Kourkoutas-beta (Kourkoutas.py:6-257), layer-wise dynamic beta2.  A layer is
+ * a set of tensors (by default those of one shape); its state is a float32
+ * EMA of the pooled grad norm.
+ *   prepare (once per optimizer step, before the launches): for each layer
+ *     pooled = sqrt(acc); ema = ema*alpha + pooled*(1-alpha);
+ *     raw = pooled / (ema + tiny_spike); sun = raw / (1 + raw);
+ *     target = beta2_max - (beta2_max - beta2_min) * sun;
+ *     beta2 = (1-w)*beta2_max + w*target  (w = min(1, step / k_warmup_steps));
+ *     layer_beta2[l] = (beta2, float(1 - double(beta2))); acc = 0;
+ *     all in float32 with each Python-double scalar rounded to float32 first,
+ *     as the reference's 0-dim tensor ops do (Kourkoutas.py:131-187);
+ *   accumulate (after each launch that set ADVOPT_F_GRAD_SQ): for each tensor
+ *     in order, the sum of its pieces' piece_gsq (rounded to float32, or to
+ *     bf16 when the step squares and sums a bf16 grad) is added to its layer's
+ *     acc: the next step's pooled norm (Kourkoutas.py:231-247).
+ */
+typedef struct advopt_kourkoutas_args {
+  float* acc;                   /* [n_layers] pooled squared-norm accumulators  */
+  float* ema;                   /* [n_layers] kourkoutas_r_ema                   */
+  float* layer_beta2;           /* [n_layers][2] (beta2, 1 - beta2)              */
+  const int32_t* layer_of_tensor; /* accumulate: [n_tensors] of the launch      */
+  const double* piece_gsq;      /* accumulate: the launch's per-piece sums        */
+  const advopt_piece* pieces;   /* accumulate: the launch's pieces                */
+  int32_t n_layers;
+  int32_t n_tensors;
+  int32_t n_pieces;
+  int32_t gsq_bf16;             /* accumulate: the step squares a bf16 grad       */
+  float beta2_max, beta2_min_gap; /* beta2_max, float(beta2_max - beta2_min)     */
+  float ema_alpha, one_minus_alpha; /* float(alpha), float(1 - alpha)            */
+  float tiny_spike;
+  float w, one_minus_w_bmax;    /* float(w), float((1 - w) * beta2_max)            */
+  float pad;
+  double cv_scale;              /* prepare: layer_beta2[2l+1] = float(cv_scale * (1 - beta2));
+                                   1 for AdamW, d*d for Prodigy (Prodigy_adv.py:413) */
+  const double* d_dev;          /* prepare: when set, cv_scale = d_dev[0] * d_dev[0] (Prodigy's d on the device) */
+} advopt_kourkoutas_args;
+
+int advopt_kourkoutas_prepare(const advopt_kourkoutas_args* args, void* stream);
+int advopt_kourkoutas_accumulate(const advopt_kourkoutas_args* args, void* stream);
+
 /* Prodigy: fold the per-piece statistics into the group's running sums in
  * parameter order (Prodigy_adv.py:505-509).  `sums` (device, 2 floats) holds
  * d_numerator (already decayed by beta3) and d_denom on entry and exit.
- * `coef` = (d/d0)*dlr as float, `s_is_bf16` says whether s is stored in bf16. */
+ * `coef` = (d/d0)*dlr as float (taken from launch->prodigy->coef when that is
+ * set), `s_is_bf16` says whether s is stored in bf16. */
 int advopt_prodigy_finish(const advopt_adam_launch* launch, float* sums, float coef,
                           int32_t s_is_bf16, void* stream);
 
@@ -179,6 +250,40 @@ int advopt_prodigy_finish(const advopt_adam_launch* launch, float* sums, float c
  * tensor's 1/max(1, rms) (update_util.py:26-36), written to fisher_clip of a
  * device copy of the tensor table. */
 int advopt_fisher_finish(const advopt_adam_launch* launch, advopt_adam_tensor* tensors_rw, void* stream);
+
+/* Prodigy with d on the device, step part: from dev->d, the launch scalars
+ * into dev (c_v, c_m, d_f, s_alpha, coef) and the d-dependent fields of the
+ * group's device tensor table, in the reference's double arithmetic
+ * (Prodigy_adv.py:345-346, 404-520): step_size = float(dlr [* 4/pi]),
+ * eps = float(d * eps_t), wd = float(wd_t * dlr), cwd = float(cwd_t * dlr),
+ * with dlr = d * lr.  One thread; launched after the table upload. */
+typedef struct advopt_prodigy_scalar_args {
+  advopt_prodigy_dev* dev;
+  advopt_adam_tensor* tensors;    /* device table of the launch              */
+  const double* tensor_consts;    /* device [n_tensors][3]: eps_t (eps or 1/sqrt(numel)), wd_t, cwd_t */
+  int32_t n_tensors;
+  int32_t safeguard_warmup;
+  double lr, beta1, beta2;
+  double step_scale;              /* 4/pi under atan2, else 1               */
+} advopt_prodigy_scalar_args;
+
+int advopt_prodigy_scalars(const advopt_prodigy_scalar_args* args, void* stream);
+
+/* Prodigy with d on the device, end of step: calculate_d (Prodigy_adv.py:
+ * 540-572) when `active`, in double precision with Python's min/max, then
+ * init_step's carry (Prodigy_adv.py:246-257): sums = {float(d_numerator *
+ * beta3) * carry_scale, 0}.  One thread. */
+typedef struct advopt_prodigy_d_args {
+  advopt_prodigy_dev* dev;
+  int32_t active;                 /* prodigy_steps <= 0 or k < prodigy_steps */
+  int32_t d_limiter;
+  double d_coef, growth_rate;
+  double limiter_factor;          /* 2 ** 0.25                               */
+  double beta3;
+  double carry_scale;             /* 1, or 0 on the ranks that do not carry the numerator */
+} advopt_prodigy_d_args;
+
+int advopt_prodigy_update_d(const advopt_prodigy_d_args* args, void* stream);
 
 /* Lion_adv step for one group (Lion_adv.py:213-278, lion_k.py:23-24). */
 typedef struct advopt_lion_tensor {

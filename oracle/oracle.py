@@ -69,12 +69,19 @@ def _lib():
                 fn.argtypes = args
                 fn.restype = None
             lib.orc_num_threads.restype = ctypes.c_int
+            lib.orc_set_num_threads.argtypes = [ctypes.c_int]
+            lib.orc_set_num_threads.restype = None
             _LIB = lib
     return _LIB
 
 
 def num_threads() -> int:
     return int(_lib().orc_num_threads())
+
+
+def set_num_threads(n: int) -> None:
+    """Threads of the C primitives' OpenMP loops."""
+    _lib().orc_set_num_threads(int(n))
 
 
 def _c(a, dtype=np.float32):
@@ -546,6 +553,9 @@ def adam_family_step(p, p_dt, g, state, hp, noise, *, algo="adamw"):
         step_size = hp["lr"] / bc1
     grad = upcast(T(g, p_dt), prec)
     shape = np.shape(p)
+    if "kourkoutas" in hp:
+        # the grad's squared norm for the next step's beta2 (AdamW_adv.py:336-338)
+        hp["kourkoutas"].accumulate(shape, grad)
 
     def v_path():
         if factored_2nd:
@@ -555,10 +565,13 @@ def adam_family_step(p, p_dt, g, state, hp, noise, *, algo="adamw"):
         else:
             v = get_state(state, "exp_avg_sq", prec, p_dt, non_neg=True)
             gv = grad
+        # Kourkoutas-beta replaces beta2 in the v update only (the bias
+        # correction keeps group['betas'][1]; AdamW_adv.py:291-304)
+        b2 = hp.get("beta2_dyn", beta2)
         if algo == "prodigy":
-            v = v.mul_s(beta2).addcmul(gv, gv, d * d * (1.0 - beta2))
+            v = v.mul_s(b2).addcmul(gv, gv, d * d * (1.0 - b2))
         else:
-            v = v.mul_s(beta2).addcmul(gv, gv, 1.0 - beta2)
+            v = v.mul_s(b2).addcmul(gv, gv, 1.0 - b2)
         if factored_2nd:
             d1, d2 = state["effective_shape"]
             state["mu_v_nmf"], state["mv_v_nmf"] = nnmf(np.abs(v.v).reshape(d1, d2))
@@ -770,6 +783,53 @@ def rms_adjustment(u: T, rms_rescaling, lr):
         return T(u.v * scale.v[0], u.dt)
     r, c = u.v.shape[-2], u.v.shape[-1]
     return u.mul_s(lr * math.sqrt(max(1, r / c)))
+
+
+class Kourkoutas:
+    """Kourkoutas.py:6-257 (KourkoutasHelper) for the default layer key (the
+    param's shape): a float32 EMA of each layer's pooled grad norm and, per
+    step, beta2 = beta2_max - (beta2_max - beta2_min) * sun(raw) with
+    raw = pooled / (ema + tiny_spike), sun(x) = x / (1 + x), blended in over
+    k_warmup_steps.  The pooled norm is that of the PREVIOUS step's grads
+    (accumulated while stepping, reset by prepare)."""
+
+    def __init__(self, shapes, beta2_max, beta2_min, ema_alpha, tiny_spike, k_warmup_steps):
+        self.keys = []
+        for sh in shapes:
+            if tuple(sh) not in self.keys:
+                self.keys.append(tuple(sh))
+        self.acc = {k: f32(0.0) for k in self.keys}
+        self.ema = {k: f32(0.0) for k in self.keys}
+        self.beta2 = {}
+        self.b2max, self.b2min, self.alpha, self.tiny, self.kw = beta2_max, beta2_min, ema_alpha, tiny_spike, k_warmup_steps
+
+    def prepare(self, current_step):
+        """Kourkoutas.py:131-197: every op on float32 0-dim tensors with the
+        Python scalar rounded to float32."""
+        for k in self.keys:
+            pooled = np.sqrt(f32(self.acc[k]))
+            e = f32(self.ema[k] * f32(self.alpha))
+            # add_(pooled, alpha=1 - ema_alpha): ATen's fused add-with-alpha
+            e = T(np.array([e], np.float32), "f32").add_alpha(T(np.array([pooled], np.float32), "f32"),
+                                                              1.0 - self.alpha).v[0]
+            self.ema[k] = f32(e)
+            raw = f32(pooled / f32(self.ema[k] + f32(self.tiny)))
+            sun = f32(raw / f32(f32(1.0) + raw))
+            target = f32(f32(self.b2max) - f32(f32(self.b2max - self.b2min) * sun))
+            weight = min(1.0, current_step / self.kw) if self.kw > 0 else 1.0
+            b2 = f32(f32((1.0 - weight) * self.b2max) + f32(f32(weight) * target))
+            self.beta2[k] = float(b2)
+            self.acc[k] = f32(0.0)
+
+    def accumulate(self, shape, grad):
+        """Kourkoutas.py:231-247: torch.sum(grad.pow(2)).float() added to the
+        layer's float32 accumulator (a bf16 grad squares and sums in bf16)."""
+        if grad.dt == "bf16":
+            sq = round_bf16(np.float32(np.sum(round_bf16(grad.v.astype(np.float32) ** 2).astype(np.float64))))
+        else:
+            sq = np.float32(np.sum((grad.v.astype(np.float32) ** 2).astype(np.float32).astype(np.float64)))
+        k = tuple(shape)
+        self.acc[k] = f32(self.acc[k] + f32(sq))
 
 
 def is_suitable_for_muon(shape, min_dim_size=4, max_aspect_ratio=128.0):

@@ -178,3 +178,13 @@ int orc_num_threads(void) {
   return 1;
 #endif
 }
+
+/* Threads of the OpenMP loops above (overrides OMP_NUM_THREADS, which a
+ * launcher such as torchrun sets to 1). */
+void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}

@@ -20,7 +20,8 @@ ADAMW_DEFAULTS = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, f
                       cautious_wd=False, use_bias_correction=True, stochastic_rounding=True,
                       use_atan2=False, nesterov=False, nesterov_coef=None, normed_momentum=False,
                       centered_wd=0.0, centered_wd_mode="float8", state_precision="auto",
-                      factored_2nd=False)
+                      factored_2nd=False, kourkoutas_beta=False, beta2_min=0.9, ema_alpha=0.95,
+                      tiny_spike=1e-9, k_warmup_steps=0)
 MUON_DEFAULTS = dict(lr=1e-3, beta1=0.95, weight_decay=0.0, cautious_wd=False, nesterov=True,
                      nesterov_coef=None, ns_steps=5, ns_eps=1e-7, ns_coeffs=(3.4445, -4.7750, 2.0315),
                      stochastic_rounding=True, rms_rescaling=True, state_precision="auto",
@@ -35,7 +36,8 @@ PRODIGY_DEFAULTS = dict(lr=1.0, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, 
                         nesterov_coef=None, state_precision="auto", factored_2nd=False, beta3=None,
                         d0=1e-6, d_coef=1.0, growth_rate=float("inf"), safeguard_warmup=False,
                         slice_p=11, prodigy_steps=0, d_limiter=False, centered_wd=0.0,
-                        centered_wd_mode="float8")
+                        centered_wd_mode="float8", kourkoutas_beta=False, beta2_min=0.9, ema_alpha=0.95,
+                        tiny_spike=1e-9, k_warmup_steps=0)
 LION_DEFAULTS = dict(lr=1e-4, betas=(0.9, 0.99), weight_decay=0.0, cautious_wd=False, stochastic_rounding=True)
 
 
@@ -110,8 +112,12 @@ def replay(name, steps=None, pin_d=False, teacher=False):
     kinds = route_kinds(meta)
     states = []
     group = None
+    kk = None
     if cls == "AdamW_adv":
         hp = _adam_hp(kw)
+        if hp.get("kourkoutas_beta"):
+            kk = O.Kourkoutas(shapes, hp["betas"][1], hp["beta2_min"], hp["ema_alpha"], hp["tiny_spike"],
+                              hp["k_warmup_steps"])
         for i, sh in enumerate(shapes):
             st = O.adamw_init_state(sh, dt, hp["precision"], hp["factored_2nd"], hp["betas"][0])
             if hp["centered_wd"]:
@@ -135,6 +141,9 @@ def replay(name, steps=None, pin_d=False, teacher=False):
     elif cls == "Prodigy_adv":
         hp = dict(PRODIGY_DEFAULTS)
         hp.update(kw)
+        if hp.get("kourkoutas_beta"):
+            kk = O.Kourkoutas(shapes, hp["betas"][1], hp["beta2_min"], hp["ema_alpha"], hp["tiny_spike"],
+                              hp["k_warmup_steps"])
         hp["betas"] = tuple(hp["betas"])
         hp["precision"] = hp["state_precision"]
         group = dict(d=hp["d0"], d0=hp["d0"], d_max=hp["d0"], d_numerator=0.0, d_coef=hp["d_coef"],
@@ -173,11 +182,21 @@ def replay(name, steps=None, pin_d=False, teacher=False):
                     fk = f"st_{s - 1}_{i}_{key}"
                     if fk in z.files and isinstance(states[i][key], np.ndarray):
                         states[i][key] = np.array(z[fk]).astype(states[i][key].dtype).reshape(states[i][key].shape)
+        if kk is not None:
+            if teacher and s > 0:
+                for i, sh in enumerate(shapes):
+                    fk = f"st_{s - 1}_{i}_kourkoutas_r_ema"
+                    if fk in z.files:
+                        kk.ema[tuple(sh)] = np.float32(z[fk])
+            kk.prepare(s)
         for i, sh in enumerate(shapes):
             g = values(z[f"g_{s}_{i}"], dt).reshape(sh)
             r = draws(z, s, i)
             if cls == "AdamW_adv":
-                ps[i] = O.adam_family_step(ps[i], dt, g, states[i], hp, r, algo="adamw")
+                hp_i = hp if kk is None else dict(hp, beta2_dyn=kk.beta2[tuple(sh)], kourkoutas=kk)
+                ps[i] = O.adam_family_step(ps[i], dt, g, states[i], hp_i, r, algo="adamw")
+                if kk is not None:
+                    states[i]["kourkoutas_r_ema"] = np.array(kk.ema[tuple(sh)], np.float32)
             elif cls in ("Muon_adv", "AdaMuon_adv"):
                 if kinds[i] == "muon":
                     fn = O.muon_step if cls == "Muon_adv" else O.adamuon_step
@@ -186,7 +205,11 @@ def replay(name, steps=None, pin_d=False, teacher=False):
                     ps[i] = O.adam_family_step(ps[i], dt, g, states[i], aux, r, algo="auxadam")
             elif cls == "Prodigy_adv":
                 hp_s = dict(hp, d=group["d"], k=group["k"], beta3=group["beta3"])
+                if kk is not None:
+                    hp_s.update(beta2_dyn=kk.beta2[tuple(sh)], kourkoutas=kk)
                 ps[i], stats = O.adam_family_step(ps[i], dt, g, states[i], hp_s, r, algo="prodigy")
+                if kk is not None:
+                    states[i]["kourkoutas_r_ema"] = np.array(kk.ema[tuple(sh)], np.float32)
                 if stats is not None:
                     d_num = np.float32(d_num + np.float32(stats[0]))
                     d_den = np.float32(d_den + np.float32(stats[1]))

@@ -143,6 +143,16 @@ CASES = {
     "adamw_centered_int4": dict(cls="AdamW_adv", dtype="bf16", shapes=[(64, 33), (50,)],
                                 kw=dict(state_precision="fp32", centered_wd=0.1, centered_wd_mode="int4"),
                                 steps=3),
+    # Kourkoutas-beta: layer-wise dynamic beta2 from the pooled grad norms of the
+    # previous step (layers = params of one shape), with and without warm-up
+    "adamw_kourkoutas_fp32": dict(cls="AdamW_adv", dtype="f32",
+                                  shapes=[(64, 32), (64, 32), (50,), (50,), (96, 48)],
+                                  kw=dict(state_precision="fp32", kourkoutas_beta=True, beta2_min=0.9,
+                                          ema_alpha=0.9, k_warmup_steps=2, weight_decay=0.01), steps=4),
+    "adamw_kourkoutas_int8_f2nd": dict(cls="AdamW_adv", dtype="bf16",
+                                       shapes=[(300, 70), (300, 70), (96,), (37,)],
+                                       kw=dict(state_precision="int8_sr", factored_2nd=True, nesterov=True,
+                                               kourkoutas_beta=True, beta2_min=0.88), steps=4, outliers=True),
     # centered weight decay with the reference's default anchor storage (float8_e4m3fn)
     "adamw_centered_float8": dict(cls="AdamW_adv", dtype="bf16", shapes=[(64, 33), (50,)],
                                   kw=dict(state_precision="fp32", centered_wd=0.1, weight_decay=0.01), steps=3),
@@ -175,6 +185,15 @@ CASES = {
     "prodigy_fp32_wd": dict(cls="Prodigy_adv", dtype="f32", shapes=[(120, 40), (40,)],
                             kw=dict(state_precision="fp32", d0=1e-4, weight_decay=0.01, slice_p=5,
                                     nesterov=True), steps=3, log_scale=True),
+    # the d estimate stops after prodigy_steps: s and p0 are freed, d is frozen
+    "prodigy_steps_bf16": dict(cls="Prodigy_adv", dtype="bf16", shapes=[(120, 40), (40,)],
+                               kw=dict(state_precision="bf16_sr", d0=1e-4, slice_p=7, prodigy_steps=2),
+                               steps=4, log_scale=True),
+    # Kourkoutas-beta under Prodigy: v's weight is d * d * (1 - beta2_dyn)
+    "prodigy_kourkoutas_fp32": dict(cls="Prodigy_adv", dtype="f32", shapes=[(120, 40), (120, 40), (40,), (64, 64)],
+                                    kw=dict(state_precision="fp32", d0=1e-4, slice_p=5, kourkoutas_beta=True,
+                                            beta2_min=0.88, ema_alpha=0.9, k_warmup_steps=2),
+                                    steps=4, log_scale=True),
     # config 5 semantics (AdaMuon CANS, int8_sr)
     "adamuon_cans_int8": dict(cls="AdaMuon_adv", dtype="bf16",
                               groups=[dict(shapes=[(64, 48), (48, 96)], optim_type="muon"),

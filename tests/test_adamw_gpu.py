@@ -136,3 +136,58 @@ def test_adamw_matches_oracle_large(case):
                 if key in ostate[i]:
                     ostate[i][key] = to_numpy(opt.state[p][key])
             p_o[i] = O.from_bf16_bits(to_numpy(p)).reshape(sh) if dt == "bf16" else to_numpy(p).reshape(sh)
+
+
+def test_bit_exact_against_oracle_llama_shapes():
+    """The Llama-3-8B configuration (int8_sr + factored_2nd + Nesterov, bf16,
+    outlier grads) on a q/k/gate-shaped subset plus a norm, two steps,
+    injected random integers shared with the oracle: int8 codes, block scales
+    and every parameter bit-identical to the oracle (the update's square root
+    and divisions are correctly rounded), factors within 2e-6."""
+    import advanced_optimizers_b200 as A
+    rng = np.random.default_rng(21)
+    shapes = [(4096, 4096), (1024, 4096), (14336, 512), (4096,)]
+    hp = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, nesterov=True, precision="int8_sr")
+    p_np = [O.round_bf16((rng.standard_normal(sh, dtype=np.float32) * 0.02)) for sh in shapes]
+    params = [torch.nn.Parameter(torch.from_numpy(v.copy()).cuda().to(torch.bfloat16)) for v in p_np]
+    opt = A.AdamW_adv(params, state_precision="int8_sr", factored_2nd=True, nesterov=True)
+    states = [O.adamw_init_state(sh, "bf16", "int8_sr", True, 0.9) for sh in shapes]
+    for step in range(2):
+        noise = []
+        for i, sh in enumerate(shapes):
+            g = (rng.standard_normal(sh, dtype=np.float32) * 1e-3)
+            g = np.where(rng.random(sh) < 0.01, g * 100, g).astype(np.float32)
+            g = O.round_bf16(g)
+            params[i].grad = torch.from_numpy(g).cuda().to(torch.bfloat16)
+            n = int(np.prod(sh))
+            pad = ((n + 2047) // 2048) * 2048
+            nz = {"exp_avg": rng.integers(0, 65536, pad, dtype=np.int32),
+                  "exp_avg_sq": rng.integers(0, 65536, pad, dtype=np.int32),
+                  "param": rng.integers(0, 65536, n, dtype=np.int32)}
+            noise.append(nz)
+            p_np[i] = O.adam_family_step(p_np[i], "bf16", g, states[i], hp, nz, algo="adamw")
+        opt.set_test_noise({p: {k: torch.from_numpy(v).cuda() for k, v in nz.items()} for p, nz in zip(params, noise)})
+        opt.step()
+        torch.cuda.synchronize()
+        opt.check_errors()
+        for i, sh in enumerate(shapes):
+            what = f"step {step} {sh}"
+            st = opt.state[params[i]]
+            np.testing.assert_array_equal(to_numpy(st["exp_avg"]), states[i]["exp_avg"], err_msg=f"{what}: m codes")
+            np.testing.assert_array_equal(to_numpy(st["exp_avg_scale"]), states[i]["exp_avg_scale"],
+                                          err_msg=f"{what}: m scales")
+            if "mu_v_nmf" in states[i]:
+                check_fp32(to_numpy(st["mu_v_nmf"]), states[i]["mu_v_nmf"], 2e-6, f"{what}: mu_v_nmf")
+                check_fp32(to_numpy(st["mv_v_nmf"]), states[i]["mv_v_nmf"], 2e-6, f"{what}: mv_v_nmf")
+                # the next step starts from the oracle's factors on both sides
+                st["mu_v_nmf"].copy_(torch.from_numpy(states[i]["mu_v_nmf"]))
+                st["mv_v_nmf"].copy_(torch.from_numpy(states[i]["mv_v_nmf"]))
+            else:
+                np.testing.assert_array_equal(to_numpy(st["exp_avg_sq"]), states[i]["exp_avg_sq"],
+                                              err_msg=f"{what}: v codes")
+            mine = to_numpy(params[i]).reshape(-1)
+            ref = O.bf16_bits(p_np[i]).reshape(-1)
+            nd = int(np.count_nonzero(mine != ref))
+            assert nd == 0, f"{what}: {nd} params differ"
+            # both sides continue from the oracle's params
+            params[i].data.copy_(torch.from_numpy(O.bf16_bits(p_np[i]).view(np.int16)).cuda().view(torch.bfloat16))

@@ -51,7 +51,7 @@ def test_matches_reference_golden(name):
             ref = z[f"d_{s - 1}"]
             for g in opt.param_groups:
                 g["d"], g["d_max"], g["d_numerator"] = float(ref[0]), float(ref[1]), float(ref[2])
-            opt._d_num_carry = float(np.float32(float(ref[2]) * opt.beta3))
+            opt._set_carry(float(np.float32(float(ref[2]) * opt.beta3)))
         opt.set_test_noise({p: _draws(z, s, i) for i, p in enumerate(params)})
         opt.step()
         torch.cuda.synchronize()

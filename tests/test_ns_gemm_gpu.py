@@ -61,8 +61,13 @@ def test_symmetric_products_at_llama_shapes(m, k):
     Newton-Schulz shapes), then B = b A + c A A with the quintic
     coefficients.  Every element — the computed blocks on or above the
     diagonal and the mirrored stores below it — is checked against the fp32
-    product with the tolerance of the general GEMM test, and D must be
-    exactly symmetric."""
+    product, and D must be exactly symmetric.  Per element the tolerance is
+    one bf16 ulp of the result plus the fp32 accumulation-order error, which
+    scales with the magnitudes summed rather than with the result: on the
+    diagonal of b A + c A A the two terms cancel (c (A A)_ii ~ 9, b A_ii ~ -9,
+    result ~ 0.2 at 4096 x 14336), so the accumulation term is
+    2^-12 (|c| |A| |A| + |b| |A|): K u, the worst-case bound of a K = 4096-term
+    float32 sum (the tensor cores measured about 2^-13.5 there)."""
     from advanced_optimizers_b200 import _lib as L
     g = torch.Generator(device="cuda").manual_seed(m + k)
     X = (torch.randn(m, k, generator=g, device="cuda") / (m * k) ** 0.25).bfloat16()
@@ -80,12 +85,14 @@ def test_symmetric_products_at_llama_shapes(m, k):
                                    c, b, err.data_ptr(), s), "advopt_ns_gemm_sym")
     torch.cuda.synchronize()
     assert int(err.item()) == 0
-    for D, ref32, what in ((A, X.float() @ X.float().t(), "X X^T"),
-                           (B, c * (A.float() @ A.float()) + b * A.float(), "b A + c A A")):
+    Xa, Aa = X.float().abs(), A.float().abs()
+    for D, ref32, mag, what in ((A, X.float() @ X.float().t(), Xa @ Xa.t(), "X X^T"),
+                                (B, c * (A.float() @ A.float()) + b * A.float(), abs(c) * (Aa @ Aa) + abs(b) * Aa,
+                                 "b A + c A A")):
         assert torch.equal(D.view(torch.int16), D.t().contiguous().view(torch.int16)), f"{what}: not symmetric"
         diff = (D.float() - ref32).abs()
         rms = float(ref32.pow(2).mean().sqrt())
-        bad = diff > 2.0 ** -8 * ref32.abs() + 1e-3 * rms
+        bad = diff > 2.0 ** -8 * ref32.abs() + 2.0 ** -12 * mag + 1e-3 * rms
         nb = int(bad.sum())
         if nb:
             r, cidx = torch.nonzero(bad)[0].tolist()

@@ -175,3 +175,68 @@ def test_prodigy_rank_without_tensors_follows_the_d_schedule(prodigy_steps):
     assert list(out.values()).count("empty") == 1
     expect = 5 if prodigy_steps <= 0 else min(5, prodigy_steps)
     assert owners == [expect] * 2
+
+
+def _stream_worker(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ps, grads = _make()
+        # every rank describes the whole model by shape only
+        meta = [torch.nn.Parameter(torch.empty(p.shape, device="meta")) for p in ps]
+        got = {}
+
+        def consume(k, dt, buf, seg):
+            got[k] = buf.clone()
+
+        opt = ShardedOptimizer(PlainSGD, meta, lr=0.5, replicate_params=False, device="cpu", bucket_bytes=512,
+                               gather_consumer=consume)
+        own = opt.owned_params()
+        idx = [i for i in range(len(ps)) if opt.owner[i] == rank]
+        assert all(not p.is_meta for p in own)
+        assert all(opt.all_params[i].is_meta for i in range(len(ps)) if opt.owner[i] != rank)
+        with torch.no_grad():
+            for i, p in zip(idx, own):
+                p.copy_(ps[i])
+        for i, p in zip(idx, own):
+            p.grad = grads[i].clone()
+        opt.step()
+        # unpack every gathered bucket into per-tensor values (rank-ordered segments)
+        vals = {}
+        for k in got:
+            seg = opt.local.segments[k][torch.float32][1]
+            for r in range(world):
+                off = 0
+                for i in range(len(ps)):
+                    if opt.bucket[i] == k and opt.owner[i] == r:
+                        n = ps[i].numel()
+                        vals[i] = got[k][r * seg + off: r * seg + off + n].view(ps[i].shape).clone()
+                        off += -(-n // 64) * 64
+        out[rank] = vals
+        out[f"n_buckets{rank}"] = len(opt.optimizers)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_streamed_gather_without_replicated_params():
+    """replicate_params=False: each rank materialises only its own tensors
+    (the rest stay meta), steps them, and every bucket's all-gather streams
+    the whole updated model through one transient buffer, bucket by bucket;
+    the gathered values equal a single-process step."""
+    world = 2
+    port = _free_port()
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_stream_worker, args=(world, port, out), nprocs=world, join=True)
+    assert out["n_buckets0"] == out["n_buckets1"] > 1
+    ref, grads = _make()
+    opt = PlainSGD(ref, lr=0.5)
+    for p, g in zip(ref, grads):
+        p.grad = g
+    opt.step()
+    for r in range(world):
+        vals = out[r]
+        assert sorted(vals) == list(range(len(ref)))
+        for i, p in enumerate(ref):
+            assert torch.equal(vals[i], p.detach()), (r, i)
