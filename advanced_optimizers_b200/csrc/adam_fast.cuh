@@ -643,6 +643,12 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
         if (NOISE_IN) return noise_words_k<true>(K, T, arr, stream, k0, nv);
         return philox4x32_10_k(U4{P.gbase + ((uint32_t)toff >> 3), stream << 24, P.tensor_id, P.step}, K);
       };
+      SliceAt sl;          // this thread's first Prodigy slice point in the chunk
+      sl.e = kVec;
+      if (pstats) {
+        const int first = srem ? (int)(slice_p - srem) : 0;
+        if (first < nv) slice_fetch<PBF>(T, k0, first, slice_p, si32, sl);
+      }
       FastIn<PREC, PBF> in;
       in.mu = pre_mu;
       in.mva = pre_a;
@@ -705,34 +711,20 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
       }
 
       if (pstats) {
-        // Prodigy slice statistics on p before the update (Prodigy_adv.py:494-509)
-        int next = srem ? (int)(slice_p - srem) : 0;   // next slice point at or after k0
+        // Prodigy slice statistics on g and p before the update
+        // (Prodigy_adv.py:494-509): the prefetched first point, then any
+        // further ones (slice_p < 8)
+        for (int e = sl.e; e < nv;) {
+          float gv = 0.0f, pv = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          if (e < nv && e == next) {
-            next += (int)slice_p;
-            const float2 gp = pair_of<LY::BPP, true>(in.g, e >> 1), pp = pair_of<LY::BPP, true>(in.p, e >> 1);
-            const float gv = (e & 1) ? gp.y : gp.x;
-            const float pv = (e & 1) ? pp.y : pp.x;
-            const int64_t si = si32 ? (int64_t)((uint32_t)(k0 + e) / slice_p) : (k0 + e) / (int64_t)slice_p;
-            float p0v = 0.0f;
-            if (!(T.flags & ADVOPT_T_P0_SCALAR))
-              p0v = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux1)[si]) : static_cast<const float*>(T.aux1)[si];
-            st0 += (double)gv * (double)__fsub_rn(p0v, pv);
-            const float s_old = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux0)[si])
-                                    : static_cast<const float*>(T.aux0)[si];
-            float s1 = __fmul_rn(s_old, L.beta3);
-            if (PBF) s1 = round_bf16(s1);
-            float s2 = __fmaf_rn(gv, s_alpha, s1);
-            if (PBF) {
-              const uint32_t b = f_to_bf16_rne(s2);
-              static_cast<uint16_t*>(T.aux0)[si] = (uint16_t)b;
-              s2 = bf16_to_f(b);
-            } else {
-              static_cast<float*>(T.aux0)[si] = s2;
-            }
-            st1 += (double)fabsf(s2);
+          for (int j = 0; j < 8; j += 2) {
+            const float2 gp = pair_of<LY::BPP, true>(in.g, j >> 1), pp = pair_of<LY::BPP, true>(in.p, j >> 1);
+            if (e == j) { gv = gp.x; pv = pp.x; }
+            if (e == j + 1) { gv = gp.y; pv = pp.y; }
           }
+          slice_apply<PBF>(T, sl, gv, pv, L.beta3, s_alpha, st0, st1);
+          e += (int)slice_p;
+          if (e < nv) slice_fetch<PBF>(T, k0, e, slice_p, si32, sl);
         }
         srem += srem_step;
         if (srem >= slice_p) srem -= slice_p;

@@ -320,6 +320,50 @@ __device__ __forceinline__ uint2 quantize8(const float (&x)[8], float bmax, cons
   return make_uint2(pack4_bytes(c[0], c[1], c[2], c[3]), pack4_bytes(c[4], c[5], c[6], c[7]));
 }
 
+// ---------------------------------------------------------------------------
+// Prodigy slice statistics (Prodigy_adv.py:494-509): every slice_p-th
+// element k of a tensor adds g_k * (p0[k / slice_p] - p_k) to d_numerator's
+// dot product and updates s[k / slice_p] = s * beta3 + g_k * s_alpha, whose
+// |.| goes to d_denom.  A thread's slice point in a chunk has its s and p0
+// entries fetched before the chunk's arithmetic (their latency then overlaps
+// it) and is applied once per thread, not once per unrolled element, so the
+// lanes of a warp that hold a slice point do it together.
+// ---------------------------------------------------------------------------
+struct SliceAt {
+  int e;          // offset in the thread's 8 elements (>= 8: none)
+  int64_t si;     // slice index k / slice_p
+  float p0;
+  float s;
+};
+
+template <bool PBF>
+__device__ __forceinline__ void slice_fetch(const TensorRegs& T, int64_t k0, int e, uint32_t slice_p, bool si32,
+                                            SliceAt& S) {
+  S.e = e;
+  S.si = si32 ? (int64_t)((uint32_t)(k0 + e) / slice_p) : (k0 + e) / (int64_t)slice_p;
+  S.p0 = 0.0f;
+  if (!(T.flags & ADVOPT_T_P0_SCALAR))
+    S.p0 = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux1)[S.si]) : static_cast<const float*>(T.aux1)[S.si];
+  S.s = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux0)[S.si]) : static_cast<const float*>(T.aux0)[S.si];
+}
+
+template <bool PBF>
+__device__ __forceinline__ void slice_apply(const TensorRegs& T, const SliceAt& S, float gv, float pv, float beta3,
+                                            float s_alpha, double& st0, double& st1) {
+  st0 += (double)gv * (double)__fsub_rn(S.p0, pv);
+  float s1 = __fmul_rn(S.s, beta3);
+  if (PBF) s1 = round_bf16(s1);
+  float s2 = __fmaf_rn(gv, s_alpha, s1);
+  if (PBF) {
+    const uint32_t b = f_to_bf16_rne(s2);
+    static_cast<uint16_t*>(T.aux0)[S.si] = (uint16_t)b;
+    s2 = bf16_to_f(b);
+  } else {
+    static_cast<float*>(T.aux0)[S.si] = s2;
+  }
+  st1 += (double)fabsf(s2);
+}
+
 template <int PREC, bool PBF, int ALGO, bool EXT, bool NOISE_IN>
 __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_launch L) {
   using TR = StateTraits<PREC, PBF>;
@@ -469,9 +513,11 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
       }
       U4 nzp{0u, 0u, 0u, 0u};
       if (sr && !fstats) nzp = noise_words<NOISE_IN>(L, T, T.nz_p, kNoiseP, k0, nv);
-      int slice_next = 0;  // offset of the next Prodigy slice point from k0
+      SliceAt sl;          // this thread's first Prodigy slice point in the chunk
+      sl.e = kVec;
       if (pstats) {
-        slice_next = srem ? (int)(slice_p - srem) : 0;
+        const int first = srem ? (int)(slice_p - srem) : 0;
+        if (first < nv) slice_fetch<PBF>(T, k0, first, slice_p, si32, sl);
         srem += srem_step;
         if (srem >= slice_p) srem -= slice_p;
       }
@@ -534,29 +580,6 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
         amax_m = fmaxf(amax_m, fabsf(m_new[e]));
         vmax = fmaxf(vmax, v[e]);
 
-        // Prodigy slice statistics on p before its update (Prodigy_adv.py:501-509)
-        if (pstats && ok && e == slice_next) {
-          slice_next += (int)slice_p;
-          const int64_t si = si32 ? (int64_t)((uint32_t)(k0 + e) / slice_p) : (k0 + e) / (int64_t)slice_p;
-          float p0v = 0.0f;
-          if (!(T.flags & ADVOPT_T_P0_SCALAR))
-            p0v = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux1)[si]) : static_cast<const float*>(T.aux1)[si];
-          st0 += (double)gi * (double)__fsub_rn(p0v, p[e]);
-          const float s_old = PBF ? bf16_to_f(static_cast<const uint16_t*>(T.aux0)[si])
-                                  : static_cast<const float*>(T.aux0)[si];
-          float s1 = __fmul_rn(s_old, L.beta3);
-          if (PBF) s1 = round_bf16(s1);
-          float s2 = __fmaf_rn(gi, s_alpha, s1);
-          if (PBF) {
-            const uint32_t b = f_to_bf16_rne(s2);
-            static_cast<uint16_t*>(T.aux0)[si] = (uint16_t)b;
-            s2 = bf16_to_f(b);
-          } else {
-            static_cast<float*>(T.aux0)[si] = s2;
-          }
-          st1 += (double)fabsf(s2);
-        }
-
         // Fisher weight decay scaler (update_util.py:15-36)
         float ws = 0.0f;
         if (fisher || fstats) {
@@ -580,6 +603,19 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
           const float pn = __fadd_rn(pcv, -ui);
           // bf16 + SR: add the noise to the bit pattern; the pack below keeps the high half
           pout[e] = PBF ? (__float_as_uint(pn) + noise_at(nzp, e)) : __float_as_uint(pn);
+        }
+      }
+      // Prodigy slice statistics on g and p before its update (Prodigy_adv.py:501-509):
+      // the prefetched first point, then any further ones (slice_p < 8)
+      if (pstats) {
+        for (int e = sl.e; e < nv;) {
+          float gv = 0.0f, pv = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (j == e) { gv = g[j]; pv = p[j]; }
+          slice_apply<PBF>(T, sl, gv, pv, L.beta3, s_alpha, st0, st1);
+          e += (int)slice_p;
+          if (e < nv) slice_fetch<PBF>(T, k0, e, slice_p, si32, sl);
         }
       }
       if (!fstats) {

@@ -104,7 +104,6 @@ class AdaMuon_adv(MuonFamilyBase):
         reject(approx_mars, "approx_mars")
         reject(spectral_normalization or adam_spectral_normalization, "spectral_normalization")
         reject(centered_wd, "centered_wd for AdaMuon_adv")
-        reject(adam_kourkoutas_beta, "adam_kourkoutas_beta")
         reject(not auto_projection and kappa_p not in (1.0, 2.0), f"kappa_p={kappa_p}")
         defaults = {
             "lr": lr, "betas": betas, "weight_decay": weight_decay, "cautious_wd": cautious_wd,

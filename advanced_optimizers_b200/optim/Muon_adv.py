@@ -105,7 +105,6 @@ class Muon_adv(MuonFamilyBase):
         reject(approx_mars, "approx_mars")
         reject(spectral_normalization or adam_spectral_normalization, "spectral_normalization")
         reject(centered_wd, "centered_wd for Muon_adv")
-        reject(adam_kourkoutas_beta, "adam_kourkoutas_beta")
         defaults = {
             "lr": lr, "beta1": beta1, "weight_decay": weight_decay, "cautious_wd": cautious_wd,
             "nesterov": nesterov, "nesterov_coef": nesterov_coef, "ns_steps": ns_steps, "ns_eps": ns_eps,

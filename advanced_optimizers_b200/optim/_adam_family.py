@@ -150,7 +150,7 @@ class AdamCfg:
     def __init__(self, *, algo, lr, betas, eps, weight_decay, precision, nesterov=False, nesterov_coef=None,
                  use_bias_correction=True, use_atan2=False, normed_momentum=False, cautious_wd=False,
                  fisher_wd=False, centered_wd=0.0, centered_wd_mode="float8", stochastic_rounding=True,
-                 prodigy=None, kourkoutas=None):
+                 prodigy=None, kourkoutas=None, kourkoutas_apply=True):
         self.algo = algo
         self.lr = float(lr)
         self.beta1, self.beta2 = float(betas[0]), float(betas[1])
@@ -171,6 +171,9 @@ class AdamCfg:
         # advopt_prodigy_dev block: d on the device; d and d0 above are then unused)
         self.prodigy = prodigy
         self.kourkoutas = kourkoutas   # KourkoutasBeta of the optimizer, or None
+        # False: the grads' squared norms are pooled but the v update keeps
+        # beta2 (the hybrid optimizers' auxiliary Adam under bias correction)
+        self.kourkoutas_apply = bool(kourkoutas_apply)
 
 
 class GroupPlan:
@@ -333,8 +336,9 @@ class GroupPlan:
         kk = cfg.kourkoutas
         if kk is not None and kk.n:
             self.kourkoutas_tables(kk)
-            s.layer_beta2 = int(kk.beta2.data_ptr())
-            s.layer_of_tensor = int(self.layer_dev.data_ptr())
+            if cfg.kourkoutas_apply:
+                s.layer_beta2 = int(kk.beta2.data_ptr())
+                s.layer_of_tensor = int(self.layer_dev.data_ptr())
             s.piece_gsq = int(self.gsq.data_ptr())
         return s
 

@@ -8,6 +8,7 @@ import torch
 from .. import _lib as L
 from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, init_adam_state
 from ._common import load_state_dict_exact, reject
+from ._kourkoutas import KourkoutasBeta
 from ._muon_family import MuonMatrixRunner, init_muon_state, is_suitable_for_muon
 
 
@@ -22,10 +23,17 @@ class MuonFamilyBase(torch.optim.Optimizer):
         self._mstep = {}
         self._test_noise = None
         self.init_step()
+        # Kourkoutas-beta of the auxiliary Adam, built after the states as the
+        # reference does (Muon_adv.py:248-252): a group holding a Muon param
+        # has had adam_kourkoutas_beta switched off by then
+        self.kourkoutas_helper = (KourkoutasBeta(self, prefix="adam_")
+                                  if any(g.get("adam_kourkoutas_beta", False) for g in self.param_groups) else None)
 
     def load_state_dict(self, state_dict: dict) -> None:
         load_state_dict_exact(self, state_dict)
         self._adam_runner.invalidate()
+        if self.kourkoutas_helper is not None:
+            self.kourkoutas_helper.loaded()
 
     @property
     def supports_fused_back_pass(self):
@@ -85,8 +93,21 @@ class MuonFamilyBase(torch.optim.Optimizer):
             state["is_muon"] = False
 
     def _adam_cfg(self, group):
-        """Muon_AuxAdam._adam_step_parameter's hyperparameters (Muon_AuxAdam.py:70-192)."""
-        return AdamCfg(algo=L.ALGO_AUXADAM, lr=group["lr"], betas=group["adam_betas"], eps=group["adam_eps"],
+        """Muon_AuxAdam._adam_step_parameter's hyperparameters (Muon_AuxAdam.py:70-192).
+
+        Kourkoutas-beta (Muon_adv.py:377-391, AdaMuon_adv.py:425-441): with a
+        helper, every auxiliary-Adam param pools its grad norm into its layer
+        (by layer key, whatever its group).  The dynamic beta2 reaches the v
+        update only without bias correction (with it, adam_betas is read
+        again after the lookup); then params outside every layer take
+        group['betas'][1] where the group has 'betas' (AdaMuon), else
+        adam_betas[1] (Kourkoutas.py:250-257)."""
+        kk = self.kourkoutas_helper
+        bc = group.get("adam_use_bias_correction", True)
+        betas = group["adam_betas"]
+        if kk is not None and not bc and group.get("betas") is not None:
+            betas = (betas[0], group["betas"][1])
+        return AdamCfg(algo=L.ALGO_AUXADAM, lr=group["lr"], betas=betas, eps=group["adam_eps"],
                        weight_decay=group["adam_weight_decay"],
                        precision=group.get("adam_actual_state_precision", group.get("adam_state_precision", "auto")),
                        nesterov=group.get("adam_nesterov", False), nesterov_coef=group.get("adam_nesterov_coef"),
@@ -94,7 +115,8 @@ class MuonFamilyBase(torch.optim.Optimizer):
                        use_atan2=group.get("adam_use_atan2", False), cautious_wd=group.get("cautious_wd", False),
                        fisher_wd=group.get("adam_fisher_wd", False), centered_wd=group.get("centered_wd", 0.0),
                        centered_wd_mode=group.get("centered_wd_mode", "float8"),
-                       stochastic_rounding=self.stochastic_rounding)
+                       stochastic_rounding=self.stochastic_rounding,
+                       kourkoutas=kk, kourkoutas_apply=not bc)
 
     def _muon_hp(self, group, p):
         raise NotImplementedError
@@ -108,6 +130,9 @@ class MuonFamilyBase(torch.optim.Optimizer):
             by_dtype = {}
             for p in adam:
                 by_dtype.setdefault((p.dtype, p.device), []).append(p)
+            if self.kourkoutas_helper is not None:
+                # once per step, before the first auxiliary-Adam param (Muon_adv.py:382-384)
+                self.kourkoutas_helper.maybe_prepare(self.state[adam[0]]["step"], adam[0].device)
             cfg = self._adam_cfg(group)
             if self._test_noise is not None:
                 self._adam_runner.test_noise = {k: v for k, v in self._test_noise.items()

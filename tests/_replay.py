@@ -28,7 +28,9 @@ MUON_DEFAULTS = dict(lr=1e-3, beta1=0.95, weight_decay=0.0, cautious_wd=False, n
                      accelerated_ns=False, cns_a_bound=None, centered_wd=0.0, centered_wd_mode="float8",
                      adam_betas=(0.9, 0.99), adam_eps=1e-8, adam_weight_decay=0.0, adam_fisher_wd=False,
                      adam_use_bias_correction=True, adam_use_atan2=False, adam_nesterov=False,
-                     adam_nesterov_coef=None, adam_state_precision="auto", adam_factored_2nd=False)
+                     adam_nesterov_coef=None, adam_state_precision="auto", adam_factored_2nd=False,
+                     adam_kourkoutas_beta=False, adam_beta2_min=0.9, adam_ema_alpha=0.95, adam_tiny_spike=1e-9,
+                     adam_k_warmup_steps=0)
 ADAMUON_DEFAULTS = dict(MUON_DEFAULTS, betas=(0.95, 0.95), eps=1e-8, use_atan2=False, factored_2nd=False,
                         kappa_p=1.0, auto_projection=True)
 PRODIGY_DEFAULTS = dict(lr=1.0, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, fisher_wd=False,
@@ -138,6 +140,20 @@ def replay(name, steps=None, pin_d=False, teacher=False):
                 states.append(st)
             else:
                 states.append(O.adamw_init_state(sh, dt, aux["precision"], aux["factored_2nd"], aux["betas"][0]))
+        kk_members = set()
+        if base.get("adam_kourkoutas_beta"):
+            # the helper is built after the states: groups holding a Muon param
+            # have lost the flag by then (Muon_adv.py:248-252, 353)
+            layer_shapes, k = [], 0
+            for gm in meta["groups"]:
+                idx = list(range(k, k + gm["n"]))
+                if all(kinds[j] != "muon" for j in idx):
+                    layer_shapes += [shapes[j] for j in idx]
+                    kk_members.update(idx)
+                k += gm["n"]
+            if layer_shapes:
+                kk = O.Kourkoutas(layer_shapes, aux["betas"][1], base["adam_beta2_min"], base["adam_ema_alpha"],
+                                  base["adam_tiny_spike"], base["adam_k_warmup_steps"])
     elif cls == "Prodigy_adv":
         hp = dict(PRODIGY_DEFAULTS)
         hp.update(kw)
@@ -202,7 +218,21 @@ def replay(name, steps=None, pin_d=False, teacher=False):
                     fn = O.muon_step if cls == "Muon_adv" else O.adamuon_step
                     ps[i] = fn(ps[i], dt, g, states[i], base, r)
                 else:
-                    ps[i] = O.adam_family_step(ps[i], dt, g, states[i], aux, r, algo="auxadam")
+                    aux_i = aux
+                    if kk is not None:
+                        # pooled by layer key whatever the group; the dynamic
+                        # beta2 only without bias correction, else beta2 of
+                        # 'betas' (AdaMuon) or adam_betas (Muon_adv.py:377-391,
+                        # Muon_AuxAdam.py:76-78, Kourkoutas.py:250-257)
+                        if tuple(sh) in kk.keys:
+                            aux_i = dict(aux, kourkoutas=kk)
+                            if not aux["use_bias_correction"]:
+                                aux_i["beta2_dyn"] = kk.beta2[tuple(sh)]
+                        elif not aux["use_bias_correction"] and cls == "AdaMuon_adv":
+                            aux_i = dict(aux, beta2_dyn=base["betas"][1])
+                    ps[i] = O.adam_family_step(ps[i], dt, g, states[i], aux_i, r, algo="auxadam")
+                    if i in kk_members:
+                        states[i]["kourkoutas_r_ema"] = np.array(kk.ema[tuple(sh)], np.float32)
             elif cls == "Prodigy_adv":
                 hp_s = dict(hp, d=group["d"], k=group["k"], beta3=group["beta3"])
                 if kk is not None:

@@ -178,6 +178,24 @@ CASES = {
                             groups=[dict(shapes=[(64, 48), (48,), (2, 64), (600, 4), (8, 4, 3), (1, 64), (40, 96)],
                                          optim_type=None)],
                             kw=dict(lr=1e-3, adam_state_precision="fp32"), steps=2),
+    # Kourkoutas-beta on the auxiliary Adam: the mixed third group loses the
+    # flag at state creation; its 1-D param still pools into the (48,) layer.
+    # With bias correction the v update keeps adam_betas[1].
+    "muon_kourkoutas_bc": dict(cls="Muon_adv", dtype="bf16",
+                               groups=[dict(shapes=[(64, 48), (48, 96)], optim_type="muon"),
+                                       dict(shapes=[(100, 32), (100, 32), (48,)], optim_type="adam"),
+                                       dict(shapes=[(48,), (40, 96)], optim_type=None)],
+                               kw=dict(lr=1e-3, adam_state_precision="fp32", adam_kourkoutas_beta=True,
+                                       adam_beta2_min=0.88, adam_ema_alpha=0.9, adam_k_warmup_steps=1), steps=4),
+    # without bias correction the dynamic beta2 reaches v; an auxiliary param
+    # outside every layer takes AdaMuon's betas[1]
+    "adamuon_kourkoutas_nobc": dict(cls="AdaMuon_adv", dtype="bf16",
+                                    groups=[dict(shapes=[(64, 48)], optim_type="muon"),
+                                            dict(shapes=[(100, 32), (48,)], optim_type="adam"),
+                                            dict(shapes=[(48,), (33,), (64, 48)], optim_type=None)],
+                                    kw=dict(lr=1e-3, adam_state_precision="fp32", adam_kourkoutas_beta=True,
+                                            adam_use_bias_correction=False, adam_beta2_min=0.88,
+                                            adam_ema_alpha=0.9), steps=4),
     # config 4 semantics (Prodigy bf16_sr)
     "prodigy_bf16sr": dict(cls="Prodigy_adv", dtype="bf16", shapes=[(120, 40), (40,), (64, 64)],
                            kw=dict(state_precision="bf16_sr", d0=1e-6, slice_p=11), steps=3,
