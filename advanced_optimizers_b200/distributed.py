@@ -270,14 +270,27 @@ class ShardedOptimizer:
             self._empty_k = 0
             self._empty_prodigy_steps = int(dict(kwargs, **{k: v for k, v in groups[0].items()
                                                             if k != "params"}).get("prodigy_steps", 0))
+        # the user's groups (global param indices, options) for the state
+        # dict in the reference's layout
+        self._group_meta = []
+        k0 = 0
+        for g in groups:
+            n = len(g["params"])
+            self._group_meta.append({"indices": list(range(k0, k0 + n)),
+                                     "opts": dict(kwargs, **{k: v for k, v in g.items() if k != "params"})})
+            k0 += n
+        self._inner_src = []   # per inner optimizer: the user group of each of its groups
         self.optimizers = []
         for k in range(n_buckets):
             own = {id(p) for i, p in enumerate(self.all_params) if self.owner[i] == self.rank and self.bucket[i] == k}
             owned_groups = []
-            for g in groups:
+            src = []
+            for gi, g in enumerate(groups):
                 ps = [p for p in g["params"] if id(p) in own]
                 if ps:
                     owned_groups.append(dict(g, params=ps))
+                    src.append(gi)
+            self._inner_src.append(src)
             opt = optimizer_cls(owned_groups, **kwargs) if owned_groups else None
             if opt is not None and hasattr(opt, "_ids"):
                 # Philox streams keyed by the tensor's global index: the sharded
@@ -402,6 +415,61 @@ class ShardedOptimizer:
                 p.grad = None
             elif p.grad is not None:
                 p.grad.zero_()
+
+    def full_state_dict(self, dst: int = 0):
+        """The state dict one `optimizer_cls` over all the params would
+        return (torch.optim's layout, which the reference's checkpoints use,
+        state_util.py:181-263): global param indices, the user's groups, every
+        owner's states gathered to rank `dst` as CPU tensors.  A collective:
+        every rank calls it; ranks other than `dst` get None.  Loadable at any
+        world size (`load_full_state_dict`) and by a single-process optimizer."""
+        local_state, group_opts = {}, {}
+        for opt, src in zip(self.optimizers, self._inner_src):
+            if opt is None:
+                continue
+            sd = opt.state_dict()
+            local_params = [p for g in opt.param_groups for p in g["params"]]
+            for li, st in sd["state"].items():
+                local_state[self._index(local_params[li])] = {
+                    k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in st.items()}
+            for g, s in zip(sd["param_groups"], src):
+                group_opts.setdefault(s, {k: v for k, v in g.items() if k != "params"})
+        parts = [None] * self.world if self.rank == dst else None
+        dist.gather_object((local_state, group_opts), parts, dst=dst, group=self.group)
+        if self.rank != dst:
+            return None
+        state, opts = {}, {}
+        for ls, go in parts:
+            state.update(ls)
+            for s, o in go.items():
+                opts.setdefault(s, o)
+        param_groups = []
+        for s, meta in enumerate(self._group_meta):
+            pg = dict(opts.get(s, meta["opts"]))
+            pg["params"] = list(meta["indices"])
+            param_groups.append(pg)
+        return {"state": {i: state[i] for i in sorted(state)}, "param_groups": param_groups}
+
+    def load_full_state_dict(self, sd):
+        """Load a state dict in torch.optim's layout (from `full_state_dict`,
+        a single-process optimizer, or the reference's own `state_dict()`):
+        each rank takes its owned params' entries and its groups' options."""
+        for opt, src in zip(self.optimizers, self._inner_src):
+            if opt is None:
+                continue
+            local_params = [p for g in opt.param_groups for p in g["params"]]
+            state = {}
+            for li, p in enumerate(local_params):
+                gi = self._index(p)
+                if gi in sd["state"]:
+                    state[li] = sd["state"][gi]
+            groups, li = [], 0
+            for g, s in zip(opt.param_groups, src):
+                pg = {k: v for k, v in sd["param_groups"][s].items() if k != "params"}
+                pg["params"] = list(range(li, li + len(g["params"])))
+                li += len(g["params"])
+                groups.append(pg)
+            opt.load_state_dict({"state": state, "param_groups": groups})
 
     def state_dict(self):
         if len(self.optimizers) == 1:

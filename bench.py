@@ -358,7 +358,12 @@ def run_ours(args):
         gather = timed(sharded.gather, args.steps)
         moved = sum(fl.numel() * fl.element_size() for f in sharded.flats for fl, _ in f.buffers)
         recv = moved * (world - 1) / world
-        split = {"step_only_ms": only, "step_only_value": 1000.0 / only, "step_plus_gather_ms": ms_per_step,
+        # each rank's own Adam kernel time in the full step (partition balance)
+        mine_k = torch.tensor([kernel_avg_ms], device=dev, dtype=torch.float64)
+        all_k = [torch.zeros_like(mine_k) for _ in range(world)]
+        dist.all_gather(all_k, mine_k)
+        split = {"per_rank_kernel_ms": [float(x.item()) for x in all_k],
+                 "step_only_ms": only, "step_only_value": 1000.0 / only, "step_plus_gather_ms": ms_per_step,
                  "gather_only_ms": gather, "gather_bytes_received_per_rank": recv,
                  "gather_gbs_per_rank": recv / (gather * 1e-3) / 1e9 if gather > 0 else 0.0,
                  "nvlink_peer_copy_gbs": 770.0}
@@ -466,7 +471,14 @@ def run_ns_leg(args, world, rank, dev):
         o._muon_runner.gemm_events = None
         o._adam_runner.kernel_events = None
     launches = sum(o.launch_count for o in opts) - l0
+    per_rank = [[gemm_ms, aux_ms]]
     if world > 1:
+        # each rank's own chain and auxiliary-Adam kernel time: the balance of
+        # the partition (the step waits for the slowest rank)
+        mine = torch.tensor([gemm_ms, aux_ms], device=dev, dtype=torch.float64)
+        allr = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        per_rank = [x.tolist() for x in allr]
         t = torch.tensor([ms, gemm_ms, aux_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, gemm_ms, aux_ms = (float(x) for x in t.tolist())
@@ -486,6 +498,7 @@ def run_ns_leg(args, world, rank, dev):
             "steps": steps, "warmup": warm,
             "ms_per_step": ms, "value": 1000.0 / ms, "unit": "optimizer steps/s",
             "ns_ms_per_step": gemm_ms, "aux_adam_ms_per_step": aux_ms,
+            "per_rank_ns_aux_ms": per_rank,
             "roofline": {"bound": "tensor", "achieved": (fx / (gemm_ms * 1e-3)) / 1e12 if gemm_ms > 0 else 0.0,
                          "peak": peak, "unit": "TFLOP/s",
                          "frac": ((fx / (gemm_ms * 1e-3)) / 1e12) / peak if gemm_ms > 0 else 0.0,

@@ -86,6 +86,11 @@ def _worker(rank, world, port, name, out):
         out[rank] = [p.detach().cpu() for p in ps]
         if name == "prodigy" and opt.optimizer is not None:
             out[f"d{rank}"] = opt.optimizer.param_groups[0]["d"]
+        if name == "adamw_buckets":
+            # the owners' states gathered into the single-process layout
+            sd = opt.full_state_dict()
+            if rank == 0:
+                out["sd"] = sd
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -109,6 +114,25 @@ def test_sharded_matches_single_process(name):
                 assert int(da.max()) <= 1, f"rank {r} tensor {i}: {int(da.max())} bf16 ulps"
             else:
                 assert torch.equal(a, b), f"rank {r} tensor {i} differs"
+    if name == "adamw_buckets":
+        sd, want = out["sd"], opt.state_dict()
+        assert sorted(sd["state"]) == sorted(want["state"])
+        assert [g["params"] for g in sd["param_groups"]] == [g["params"] for g in want["param_groups"]]
+        for i, st in want["state"].items():
+            for key, val in st.items():
+                got = sd["state"][i][key]
+                if not torch.is_tensor(val):
+                    assert got == val, (i, key)
+                elif key in ("mu_v_nmf", "mv_v_nmf"):
+                    # float32 column sums over another piece cut
+                    torch.testing.assert_close(got, val.cpu(), rtol=2e-6, atol=0)
+                else:
+                    assert torch.equal(got, val.cpu()), (i, key)
+        # and a single-process optimizer resumes from it
+        opt2 = _make("adamw", [torch.nn.Parameter(p.detach().clone()) for p in ps], False)
+        opt2.load_state_dict(sd)
+        assert torch.equal(opt2.state[opt2.param_groups[0]["params"][0]]["exp_avg"].cpu(),
+                           want["state"][0]["exp_avg"].cpu())
     if name == "prodigy":
         d_ref = opt.param_groups[0]["d"]
         for r in range(world):

@@ -4,6 +4,7 @@ The optimizer here is a stand-in (plain SGD on CPU tensors) because the B200
 classes run only on CUDA; what is tested is the partition, the rank-ordered
 flat parameter storage and the all-gather: after a sharded step every rank
 holds exactly the parameters a single process would have."""
+import copy
 import os
 import socket
 
@@ -240,3 +241,95 @@ def test_streamed_gather_without_replicated_params():
         assert sorted(vals) == list(range(len(ref)))
         for i, p in enumerate(ref):
             assert torch.equal(vals[i], p.detach()), (r, i)
+
+
+class MomentumSGD(torch.optim.Optimizer):
+    """Stand-in with per-param state (a buffer and a step count)."""
+
+    def __init__(self, params, lr=0.1, momentum=0.9):
+        super().__init__(params, dict(lr=lr, momentum=momentum))
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        for g in self.param_groups:
+            for p in g["params"]:
+                if p.grad is None:
+                    continue
+                st = self.state[p]
+                if "buf" not in st:
+                    st["buf"] = torch.zeros_like(p)
+                    st["step"] = 0
+                st["buf"].mul_(g["momentum"]).add_(p.grad)
+                st["step"] += 1
+                p.add_(st["buf"], alpha=-g["lr"])
+
+
+def _groups(ps):
+    return [dict(params=ps[:3], lr=0.3), dict(params=ps[3:])]
+
+
+def _full_sd_worker(rank, world, port, single_sd, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ps, grads = _make()
+        opt = ShardedOptimizer(MomentumSGD, _groups(ps), lr=0.5, bucket_bytes=512)
+        for step in range(2):
+            for p, g in zip(ps, grads):
+                p.grad = g * (step + 1)
+            opt.step()
+        sd = opt.full_state_dict()
+        if rank == 0:
+            out["sd"] = sd
+        else:
+            out["other"] = sd
+        # a second sharded optimizer, bucketed differently, resumes from the
+        # single-process optimizer's state dict and takes the third step
+        ps2, _ = _make()
+        with torch.no_grad():
+            for a, b in zip(ps2, single_sd["params"]):
+                a.copy_(b)
+        opt2 = ShardedOptimizer(MomentumSGD, _groups(ps2), lr=0.5, bucket_bytes=None)
+        # (torch.optim's load_state_dict keeps same-device tensors as given:
+        # load a copy, the parent's dict lives in shared memory)
+        opt2.load_full_state_dict(copy.deepcopy(single_sd["sd"]))
+        for p, g in zip(ps2, grads):
+            p.grad = g * 3
+        opt2.step()
+        out[rank] = [p.detach().clone() for p in ps2]
+    finally:
+        dist.destroy_process_group()
+
+
+def test_full_state_dict_in_the_single_process_layout():
+    """full_state_dict() gathers every owner's states under global indices
+    with the user's groups: equal to one unsharded optimizer's state_dict();
+    load_full_state_dict() takes such a dict at another bucketing and the
+    next step matches the unsharded optimizer's."""
+    ref, grads = _make()
+    opt = MomentumSGD(_groups(ref), lr=0.5)
+    for step in range(2):
+        for p, g in zip(ref, grads):
+            p.grad = g * (step + 1)
+        opt.step()
+    single = {"sd": opt.state_dict(), "params": [p.detach().clone() for p in ref]}
+    world = 2
+    port = _free_port()
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_full_sd_worker, args=(world, port, single, out), nprocs=world, join=True)
+    sd, want = out["sd"], single["sd"]
+    assert out["other"] is None
+    assert sorted(sd["state"]) == sorted(want["state"])
+    for i, st in want["state"].items():
+        assert sd["state"][i]["step"] == st["step"]
+        assert torch.equal(sd["state"][i]["buf"], st["buf"]), i
+    assert [g["params"] for g in sd["param_groups"]] == [g["params"] for g in want["param_groups"]]
+    assert [g["lr"] for g in sd["param_groups"]] == [0.3, 0.5]
+    for p, g in zip(ref, grads):
+        p.grad = g * 3
+    opt.step()
+    for r in range(world):
+        for a, b in zip(out[r], ref):
+            assert torch.equal(a, b.detach()), r
