@@ -15,7 +15,7 @@ import numpy as np
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libadvopt.so")
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # ---- constants mirrored from include/advopt.h ----
 DT_F32, DT_BF16 = 0, 1
@@ -116,6 +116,10 @@ MU_NOISE_IN = 1 << 4
 MU_RMS = 1 << 5
 MU_TRANSPOSED = 1 << 6
 MU_ATAN2 = 1 << 7
+MU_MARS = 1 << 8
+MU_NORMUON = 1 << 9
+MU_VFACT = 1 << 10
+VCOL_SPLIT = 16
 ST_F32, ST_BF16, ST_BF16_SR, ST_Q8 = 0, 1, 2, 3
 
 
@@ -131,6 +135,11 @@ class MuonArgs(ctypes.Structure):
         ("tensor_id", ctypes.c_uint32), ("step", ctypes.c_uint32), ("flags", ctypes.c_uint32),
         ("m_storage", ctypes.c_int32), ("v_storage", ctypes.c_int32), ("param_bf16", ctypes.c_int32),
         ("math_bf16", ctypes.c_int32), ("update_bf16", ctypes.c_int32),
+        ("last_grad", ctypes.c_uint64), ("mars_factor", ctypes.c_float), ("nm_w", ctypes.c_float),
+        ("nm_eps", ctypes.c_float), ("pad0", ctypes.c_int32),
+        ("row_v", ctypes.c_uint64), ("row_den", ctypes.c_uint64),
+        ("v_row", ctypes.c_uint64), ("v_col", ctypes.c_uint64), ("v_full", ctypes.c_uint64),
+        ("v_sums", ctypes.c_uint64), ("d1", ctypes.c_int64), ("d2", ctypes.c_int64),
     ]
 
 

@@ -91,6 +91,27 @@ __device__ __forceinline__ float load_grad(const Args& a, int64_t k) {
   return a.param_bf16 ? bf16_to_f(static_cast<const uint16_t*>(a.grad)[k]) : static_cast<const float*>(a.grad)[k];
 }
 
+// approx MARS-M (Muon_util.py:333-347): c = (g - last).mul_(f).add_(g), each
+// op rounding to the grad's dtype (bf16 under 'auto' with bf16 params, else
+// f32); last_grad (the param's dtype) takes g.
+template <bool MBF>
+__device__ __forceinline__ float mars(const Args& a, int64_t k, float g) {
+  const bool pbf = a.param_bf16 != 0;
+  const float lg = pbf ? bf16_to_f(static_cast<const uint16_t*>(a.last_grad)[k])
+                       : static_cast<const float*>(a.last_grad)[k];
+  float t = __fsub_rn(g, lg);
+  if (MBF) t = round_bf16(t);
+  t = __fmul_rn(t, a.mars_factor);
+  if (MBF) t = round_bf16(t);
+  t = __fadd_rn(t, g);
+  if (MBF) t = round_bf16(t);
+  if (pbf)
+    static_cast<uint16_t*>(a.last_grad)[k] = (uint16_t)f_to_bf16_rne(g);
+  else
+    static_cast<float*>(a.last_grad)[k] = g;
+  return t;
+}
+
 // ---- stage 0: momentum, Nesterov, sign, momentum store, X0, sum(X0^2) ----
 // RAW (stage 6): X0 = bf16(grad) only, for a bare Newton–Schulz call.
 template <bool MBF, bool RAW>
@@ -109,7 +130,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const Args a) {
       const int64_t k = k0 + e;
       mn[e] = 0.0f;
       if (k < a.numel) {
-        const float g = load_grad(a, k);
+        float g = load_grad(a, k);
+        if (!RAW && (a.flags & ADVOPT_MU_MARS)) g = mars<MBF>(a, k, g);
         float u = g;
         if (!RAW) {
           const float m0 = load_state(a.m, k, st, a.m_scale, false);
@@ -604,6 +626,227 @@ __global__ void __launch_bounds__(256) adamuon_apply_kernel(const Args a) {
   }
 }
 
+// Row index of element k0 of the flattened [rows][cols] update, advanced one
+// element at a time (8 consecutive elements a thread; a row may end inside).
+struct RowCursor {
+  int64_t r, c, cols;
+  __device__ __forceinline__ RowCursor(int64_t k0, int64_t cols_) : cols(cols_) {
+    r = k0 / cols_;
+    c = k0 - r * cols_;
+  }
+  __device__ __forceinline__ void next() {
+    if (++c == cols) { c = 0; ++r; }
+  }
+};
+
+// ---- stage 7: NorMuon row statistics (Muon_util.py:349-360) ----
+//   v[r] = lerp(v[r], mean_c(u^2), 1 - beta2)  (u^2 in the update's dtype, the
+//   mean in float32);  den[r] = sqrt(v[r]) + eps.  One warp per row.
+__global__ void __launch_bounds__(256) normuon_rows_kernel(const Args a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool ubf = a.update_bf16 != 0;
+  for (int64_t r = (int64_t)blockIdx.x * kWarps + warp; r < a.rows; r += (int64_t)gridDim.x * kWarps) {
+    const uint16_t* row = a.u + r * a.cols;
+    double s = 0.0;
+    for (int64_t c = lane; c < a.cols; c += 32) {
+      const float x = bf16_to_f(row[c]);
+      float q = __fmul_rn(x, x);
+      if (ubf) q = round_bf16(q);
+      s += (double)q;
+    }
+    s = warp_sum_d(s);
+    if (lane == 0) {
+      const float mean = __fdiv_rn((float)s, (float)a.cols);
+      const float v = lerp_t(a.row_v[r], mean, a.nm_w);
+      a.row_v[r] = v;
+      a.row_den[r] = __fadd_rn(__fsqrt_rn(v), a.nm_eps);
+    }
+  }
+}
+
+// u' = u / den[row], computed in float32 and stored in the update's dtype
+__device__ __forceinline__ float normuon_u(const Args& a, float u, int64_t r) {
+  const float q = __fdiv_rn(u, a.row_den[r]);
+  return a.update_bf16 ? round_bf16(q) : q;
+}
+
+// ---- stage 8: per-chunk sum(u'^2) of the NorMuon update ----
+__global__ void __launch_bounds__(256) normuon_stats_kernel(const Args a) {
+  __shared__ double redd[kWarps];
+  const int64_t nchunks = (a.numel + kChunk - 1) / kChunk;
+  for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const int64_t k0 = c * kChunk + threadIdx.x * 8;
+    double ss = 0.0;
+    if (k0 < a.numel) {
+      RowCursor rc(k0, a.cols);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (k0 + e < a.numel) {
+          const float up = normuon_u(a, bf16_to_f(a.u[k0 + e]), rc.r);
+          ss += (double)up * (double)up;
+        }
+        rc.next();
+      }
+    }
+    const double s = block_sum_d(ss, redd, 256);
+    if (threadIdx.x == 0) a.partial[c] = s;
+  }
+}
+
+// ---- stage 9: p updated with u' * scale (NorMuon) ----
+__global__ void __launch_bounds__(256) normuon_apply_kernel(const Args a) {
+  const float sc = a.scalars[1];
+  const bool ubf = a.update_bf16 != 0;
+  const bool need_r = a.param_bf16 && (a.flags & ADVOPT_MU_SR);
+  const int64_t groups = (a.numel + 7) / 8;
+  for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k0 = gi * 8;
+    uint32_t r[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (need_r) noise8(a, a.noise_p, kNoiseP, k0, a.numel, r);
+    RowCursor rc(k0, a.cols);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int64_t k = k0 + e;
+      if (k < a.numel) {
+        float u = __fmul_rn(normuon_u(a, bf16_to_f(a.u[k]), rc.r), sc);
+        if (ubf) u = round_bf16(u);
+        apply_one(a, k, u, r[e]);
+      }
+      rc.next();
+    }
+  }
+}
+
+// AdaMuon factored second moment (AdaMuon_adv.py:617-631), in float32:
+//   v = outer(v_row, v_col)[i][j] * beta2 + (1 - beta2) * u * u
+//   u' = u / R(sqrt(v) + eps)   (atan2: atan2(u, R(sqrt(v))))
+// with R the update's dtype; (i, j) = divmod(k, d2) in the effective shape.
+__device__ __forceinline__ float vfact_u(const Args& a, float u, float v) {
+  const bool ubf = a.update_bf16 != 0;
+  float den = __fsqrt_rn(v);
+  float q;
+  if (a.flags & ADVOPT_MU_ATAN2) {
+    if (ubf) den = round_bf16(den);
+    q = atan2f(u, den);
+  } else {
+    den = __fadd_rn(den, a.eps);
+    if (ubf) den = round_bf16(den);
+    q = __fdiv_rn(u, den);
+  }
+  return ubf ? round_bf16(q) : q;
+}
+
+// ---- stage 10a: v (into v_full) and per-chunk sum(u'^2) ----
+__global__ void __launch_bounds__(256) vfact_stats_kernel(const Args a) {
+  __shared__ double redd[kWarps];
+  const int64_t nchunks = (a.numel + kChunk - 1) / kChunk;
+  for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const int64_t k0 = c * kChunk + threadIdx.x * 8;
+    double ss = 0.0;
+    if (k0 < a.numel) {
+      RowCursor rc(k0, a.d2);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int64_t k = k0 + e;
+        if (k < a.numel) {
+          const float u = bf16_to_f(a.u[k]);
+          float v = __fmul_rn(__fmul_rn(a.v_row[rc.r], a.v_col[rc.c]), a.beta2);
+          v = __fmaf_rn(__fmul_rn(a.c_v, u), u, v);
+          a.v_full[k] = v;
+          const float up = vfact_u(a, u, v);
+          ss += (double)up * (double)up;
+        }
+        rc.next();
+      }
+    }
+    const double s = block_sum_d(ss, redd, 256);
+    if (threadIdx.x == 0) a.partial[c] = s;
+  }
+}
+
+// ---- stage 10b: row sums of v (one warp per row of the effective shape) ----
+__global__ void __launch_bounds__(256) vfact_rows_kernel(const Args a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t i = (int64_t)blockIdx.x * kWarps + warp; i < a.d1; i += (int64_t)gridDim.x * kWarps) {
+    const float* row = a.v_full + i * a.d2;
+    double s = 0.0;
+    for (int64_t j = lane; j < a.d2; j += 32) s += (double)row[j];
+    s = warp_sum_d(s);
+    if (lane == 0) a.v_sums[i] = s;
+  }
+}
+
+// ---- stage 10c: column partial sums over ADVOPT_VCOL_SPLIT row ranges ----
+__global__ void __launch_bounds__(256) vfact_cols_kernel(const Args a) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int split = blockIdx.y;
+  if (j >= a.d2) return;
+  const int64_t i0 = a.d1 * split / ADVOPT_VCOL_SPLIT, i1 = a.d1 * (split + 1) / ADVOPT_VCOL_SPLIT;
+  double s = 0.0;
+  for (int64_t i = i0; i < i1; ++i) s += (double)a.v_full[i * a.d2 + j];
+  a.v_sums[a.d1 + (int64_t)split * a.d2 + j] = s;
+}
+
+// ---- stage 10d: the new factors (factorization_util.py:60-80): row and
+// column sums as float32, the factor of the smaller dimension divided by
+// max(its total, 1e-12).  One CTA of 1024. ----
+__global__ void __launch_bounds__(1024) vfact_finish_kernel(const Args a) {
+  __shared__ double red[32];
+  __shared__ float scale_s;
+  const double* rows = a.v_sums;
+  const double* cols = a.v_sums + a.d1;
+  const bool by_rows = a.d1 < a.d2;
+  double t = 0.0;
+  if (by_rows) {
+    for (int64_t i = threadIdx.x; i < a.d1; i += blockDim.x) t += rows[i];
+  } else {
+    for (int64_t j = threadIdx.x; j < a.d2; j += blockDim.x) {
+      double cj = 0.0;
+      for (int sp = 0; sp < ADVOPT_VCOL_SPLIT; ++sp) cj += cols[(int64_t)sp * a.d2 + j];
+      t += cj;
+    }
+  }
+  t = block_sum_d(t, red, 1024);
+  if (threadIdx.x == 0) {
+    const float tf = (float)t;
+    scale_s = tf > 1e-12f ? tf : 1e-12f;
+  }
+  __syncthreads();
+  const float sc = scale_s;
+  for (int64_t i = threadIdx.x; i < a.d1; i += blockDim.x) {
+    const float r = (float)rows[i];
+    a.v_row[i] = by_rows ? __fdiv_rn(r, sc) : r;
+  }
+  for (int64_t j = threadIdx.x; j < a.d2; j += blockDim.x) {
+    double cj = 0.0;
+    for (int sp = 0; sp < ADVOPT_VCOL_SPLIT; ++sp) cj += cols[(int64_t)sp * a.d2 + j];
+    const float c = (float)cj;
+    a.v_col[j] = by_rows ? c : __fdiv_rn(c, sc);
+  }
+}
+
+// ---- stage 11: p updated with u' * scale (AdaMuon factored) ----
+__global__ void __launch_bounds__(256) vfact_apply_kernel(const Args a) {
+  const float sc = a.scalars[1];
+  const bool ubf = a.update_bf16 != 0;
+  const bool need_r = a.param_bf16 && (a.flags & ADVOPT_MU_SR);
+  const int64_t groups = (a.numel + 7) / 8;
+  for (int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; gi < groups; gi += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k0 = gi * 8;
+    uint32_t r[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (need_r) noise8(a, a.noise_p, kNoiseP, k0, a.numel, r);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int64_t k = k0 + e;
+      if (k < a.numel) {
+        float u = __fmul_rn(vfact_u(a, bf16_to_f(a.u[k]), a.v_full[k]), sc);
+        if (ubf) u = round_bf16(u);
+        apply_one(a, k, u, r[e]);
+      }
+    }
+  }
+}
+
 }  // namespace muon
 }  // namespace advopt
 
@@ -650,7 +893,7 @@ extern "C" int advopt_muon_stage(const advopt_muon_args* ap, int32_t stage, void
     case 6: {
       if (!a.ns) return set_error(ADVOPT_E_INVALID, "advopt_muon_stage: null workspace");
       const unsigned gp = grid_for(nchunks);
-      if (vec && a.param_bf16 && (stage == 6 || a.m_storage != ADVOPT_ST_Q8)) {
+      if (vec && a.param_bf16 && (stage == 6 || (a.m_storage != ADVOPT_ST_Q8 && !(a.flags & ADVOPT_MU_MARS)))) {
         if (stage == 6) prep_vec_kernel<false, true, ADVOPT_ST_BF16><<<gp, 256, 0, s>>>(a);
         else if (a.m_storage == ADVOPT_ST_F32)
           a.math_bf16 ? prep_vec_kernel<true, false, ADVOPT_ST_F32><<<gp, 256, 0, s>>>(a)
@@ -719,6 +962,33 @@ extern "C" int advopt_muon_stage(const advopt_muon_args* ap, int32_t stage, void
       }
       break;
     }
+    case 7:
+    case 8:
+    case 9:
+      if (!a.row_v || !a.row_den) return set_error(ADVOPT_E_INVALID, "advopt_muon_stage: NorMuon buffers missing");
+      if (stage == 7) {
+        normuon_rows_kernel<<<grid_for((a.rows + kWarps - 1) / kWarps), 256, 0, s>>>(a);
+      } else if (stage == 8) {
+        normuon_stats_kernel<<<grid_for(nchunks), 256, 0, s>>>(a);
+        scale_kernel<<<1, 1024, 0, s>>>(a, nchunks);
+      } else {
+        normuon_apply_kernel<<<grid_for((a.numel + 8 * 256 - 1) / (8 * 256)), 256, 0, s>>>(a);
+      }
+      break;
+    case 10:
+    case 11:
+      if (!a.v_row || !a.v_col || !a.v_full || !a.v_sums || a.d1 <= 0 || a.d2 <= 0 || a.d1 * a.d2 != a.numel)
+        return set_error(ADVOPT_E_INVALID, "advopt_muon_stage: AdaMuon factored second moment missing");
+      if (stage == 10) {
+        vfact_stats_kernel<<<grid_for(nchunks), 256, 0, s>>>(a);
+        scale_kernel<<<1, 1024, 0, s>>>(a, nchunks);
+        vfact_rows_kernel<<<grid_for((a.d1 + kWarps - 1) / kWarps), 256, 0, s>>>(a);
+        vfact_cols_kernel<<<dim3((unsigned)((a.d2 + 255) / 256), ADVOPT_VCOL_SPLIT), 256, 0, s>>>(a);
+        vfact_finish_kernel<<<1, 1024, 0, s>>>(a);
+      } else {
+        vfact_apply_kernel<<<grid_for((a.numel + 8 * 256 - 1) / (8 * 256)), 256, 0, s>>>(a);
+      }
+      break;
     default:
       return set_error(ADVOPT_E_INVALID, "advopt_muon_stage: unknown stage");
   }

@@ -435,7 +435,7 @@ class ShardedOptimizer:
             for g, s in zip(sd["param_groups"], src):
                 group_opts.setdefault(s, {k: v for k, v in g.items() if k != "params"})
         parts = [None] * self.world if self.rank == dst else None
-        dist.gather_object((local_state, group_opts), parts, dst=dst, group=self.group)
+        dist.gather_object((local_state, group_opts), parts, dst=dst, group=self._object_group())
         if self.rank != dst:
             return None
         state, opts = {}, {}
@@ -449,6 +449,16 @@ class ShardedOptimizer:
             pg["params"] = list(meta["indices"])
             param_groups.append(pg)
         return {"state": {i: state[i] for i in sorted(state)}, "param_groups": param_groups}
+
+    def _object_group(self):
+        """The group for Python-object collectives: a gloo group over the
+        default group's ranks when the collectives run on NCCL (the states
+        are CPU tensors by then; no device copies), else the group itself."""
+        if self.group is not None or dist.get_backend(self.group) == "gloo":
+            return self.group
+        if getattr(self, "_cpu_group", None) is None:
+            self._cpu_group = dist.new_group(backend="gloo")
+        return self._cpu_group
 
     def load_full_state_dict(self, sd):
         """Load a state dict in torch.optim's layout (from `full_state_dict`,

@@ -98,10 +98,7 @@ class AdaMuon_adv(MuonFamilyBase):
         reject(state_precision in ("factored", "fp16"), f"state_precision='{state_precision}'")
         reject(adam_state_precision in ("factored", "fp16") or adam_nnmf_factor,
                f"adam_state_precision='{adam_state_precision}'")
-        reject(factored_2nd, "factored_2nd on the AdaMuon path")
         reject(low_rank_ortho, "low_rank_ortho")
-        reject(normuon_variant, "normuon_variant")
-        reject(approx_mars, "approx_mars")
         reject(spectral_normalization or adam_spectral_normalization, "spectral_normalization")
         reject(centered_wd, "centered_wd for AdaMuon_adv")
         reject(not auto_projection and kappa_p not in (1.0, 2.0), f"kappa_p={kappa_p}")
@@ -131,6 +128,10 @@ class AdaMuon_adv(MuonFamilyBase):
         self._init_lr = lr if lr > 0 else 1
         super().__init__(params, defaults)
         self._setup()
+
+    def _normuon_hp(self, group):
+        """AdaMuon_adv.py:558-559, 614-615: normuon_update(update, v, beta2, eps)."""
+        return (1 - group["betas"][1], group["eps"])
 
     def _muon_hp(self, group, p):
         """AdaMuon_adv._muon_step_parameter's hyperparameters (AdaMuon_adv.py:492-659)."""

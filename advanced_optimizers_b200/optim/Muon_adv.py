@@ -101,8 +101,6 @@ class Muon_adv(MuonFamilyBase):
         reject(adam_state_precision in ("factored", "fp16") or adam_nnmf_factor,
                f"adam_state_precision='{adam_state_precision}'")
         reject(low_rank_ortho, "low_rank_ortho")
-        reject(normuon_variant, "normuon_variant")
-        reject(approx_mars, "approx_mars")
         reject(spectral_normalization or adam_spectral_normalization, "spectral_normalization")
         reject(centered_wd, "centered_wd for Muon_adv")
         defaults = {
@@ -131,6 +129,10 @@ class Muon_adv(MuonFamilyBase):
         self._init_lr = lr if lr > 0 else 1
         super().__init__(params, defaults)
         self._setup()
+
+    def _normuon_hp(self, group):
+        """Muon_adv.py:505: normuon_update(update, v, beta2_normuon, normuon_eps)."""
+        return (1 - group["beta2_normuon"], group["normuon_eps"])
 
     def _muon_hp(self, group, p):
         """Muon_adv._muon_step_parameter's hyperparameters (Muon_adv.py:443-555)."""

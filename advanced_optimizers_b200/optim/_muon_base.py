@@ -78,7 +78,7 @@ class MuonFamilyBase(torch.optim.Optimizer):
             req = group["state_precision"]
             reject(req not in SUPPORTED_PRECISIONS, f"state_precision='{req}' on the Muon path")
             group["actual_state_precision"] = req
-            init_muon_state(p, state, req, self._adamuon)
+            init_muon_state(p, state, req, self._adamuon, group)
             group["adam_kourkoutas_beta"] = False
             state["is_muon"] = True
         else:
@@ -121,6 +121,10 @@ class MuonFamilyBase(torch.optim.Optimizer):
     def _muon_hp(self, group, p):
         raise NotImplementedError
 
+    def _normuon_hp(self, group):
+        """(1 - beta2, eps) of NorMuon's row-wise second moment."""
+        raise NotImplementedError
+
     def _step_params(self, gi, group, params):
         for p in params:
             self._init_state(p, group)
@@ -146,9 +150,14 @@ class MuonFamilyBase(torch.optim.Optimizer):
             t = self._mstep.get(id(p), 0)
             self._mstep[id(p)] = t + 1
             nz = None if self._test_noise is None else self._test_noise.get(id(p), {})
-            self._muon_runner.step_matrix(p, self.state[p], adamuon=self._adamuon, tensor_id=self._tid(p), step=t,
+            st = self.state[p]
+            self._muon_runner.step_matrix(p, st, adamuon=self._adamuon, tensor_id=self._tid(p), step=t,
                                           noise=nz, sr=self.stochastic_rounding,
-                                          precision=group["actual_state_precision"], **hp)
+                                          precision=group["actual_state_precision"],
+                                          normuon=self._normuon_hp(group) if "normuon_v" in st else None,
+                                          mars_factor=(group["mars_gamma"] * hp["beta1"] / (1.0 - hp["beta1"])
+                                                       if "last_grad" in st else None),
+                                          vfact=bool(st.get("factored_2nd", False)), **hp)
 
     @torch.no_grad()
     def step_parameter(self, p: torch.Tensor, group: dict, i: int | None = None):

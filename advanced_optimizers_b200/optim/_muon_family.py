@@ -19,7 +19,8 @@ import torch
 
 from .. import _lib as L
 from .._device import dtype_code, ptr, require_cuda_tensor, stream_handle
-from ._adam_family import adjust_wds, f32, init_state_tensor
+from .._plan import effective_shape
+from ._adam_family import SHIFTER, adjust_wds, f32, init_state_tensor
 from ._common import ErrorWatch
 
 NS_ALIGN = 256   # the GEMM's N tile; also a multiple of its M (128) and K (64) tiles
@@ -100,6 +101,16 @@ class NSWorkspace:
         self.part_cap = 0
         self.scalars = torch.zeros(4, dtype=torch.float32, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.aux = {}
+
+    def scratch(self, key: str, n: int, dtype) -> int:
+        """Address of a scratch array of at least n elements (NorMuon row
+        denominators, AdaMuon's factored v and its sums), grown on demand."""
+        t = self.aux.get(key)
+        if t is None or t.numel() < n or t.dtype != dtype:
+            t = torch.empty(max(1, n), dtype=dtype, device=self.device)
+            self.aux[key] = t
+        return int(t.data_ptr())
 
     def ensure(self, numel: int, m_pad: int, n_pad: int):
         need_ns = 2 * m_pad * n_pad + 2 * m_pad * m_pad
@@ -198,7 +209,12 @@ class MuonMatrixRunner:
     def step_matrix(self, p, state, *, adamuon: bool, lr: float, beta1: float, beta2: float, eps, nesterov: bool,
                     nesterov_coef, ns_steps: int, ns_eps, ns_coeffs, cns: bool, cns_a_bound, rms_rescaling: bool,
                     use_atan2: bool, sign_projection: bool, weight_decay: float, cautious_wd: bool, sr: bool,
-                    precision: str, tensor_id: int, step: int, noise=None):
+                    precision: str, tensor_id: int, step: int, noise=None, normuon=None, mars_factor=None,
+                    vfact: bool = False):
+        """One matrix.  normuon: (1 - beta2, eps) of the NorMuon row-wise
+        second moment (state['normuon_v']); mars_factor: approx MARS-M's
+        gamma * beta1 / (1 - beta1) (state['last_grad']); vfact: AdaMuon's
+        factored second moment (state['mu_vbuf_nmf'], state['mv_vbuf_nmf'])."""
         require_cuda_tensor(p, "param")
         require_cuda_tensor(p.grad, "grad")
         if p.ndim < 2:
@@ -221,10 +237,23 @@ class MuonMatrixRunner:
         mb = state["momentum_buffer"]
         a.m = ptr(mb)
         a.m_scale = ptr(state.get("momentum_buffer_scale"))
-        if adamuon:
+        if adamuon and not vfact and normuon is None:
             vb = state["second_momentum_buffer"]
             a.v = ptr(vb)
             a.v_scale = ptr(state.get("second_momentum_buffer_scale"))
+        if mars_factor is not None:
+            a.last_grad = ptr(state["last_grad"])
+            a.mars_factor = f32(mars_factor)
+        if normuon is not None:
+            a.nm_w, a.nm_eps = f32(normuon[0]), f32(normuon[1])
+            a.row_v = ptr(state["normuon_v"])
+            a.row_den = ws.scratch("row_den", rows, torch.float32)
+        if vfact:
+            d1, d2 = state["effective_shape"]
+            a.d1, a.d2 = d1, d2
+            a.v_row, a.v_col = ptr(state["mu_vbuf_nmf"]), ptr(state["mv_vbuf_nmf"])
+            a.v_full = ws.scratch("v_full", numel, torch.float32)
+            a.v_sums = ws.scratch("v_sums", d1 + L.VCOL_SPLIT * d2, torch.float64)
         a.x0, a.ns, a.u = ptrs["x0"], ptrs["x"], ptrs["u"]
         a.partial, a.scalars = ptr(ws.partial), ptr(ws.scalars)
         a.numel, a.rows, a.cols = numel, rows, cols
@@ -239,12 +268,14 @@ class MuonMatrixRunner:
         a.ns_eps = f32(ns_eps if ns_eps is not None else 1.0 / math.sqrt(numel))
         wd, _ = adjust_wds(weight_decay, 0.0, p)
         a.wd = f32(wd * lr) if wd != 0 else 0.0
-        step_scale = lr * (4 / math.pi) if (adamuon and use_atan2) else lr
+        # NorMuon replaces AdaMuon's second moment, atan2 included (AdaMuon_adv.py:635)
+        step_scale = lr * (4 / math.pi) if (adamuon and use_atan2 and normuon is None) else lr
         if rms_rescaling:
             a.scale_const = f32(step_scale * 0.2 * math.sqrt(numel))
         else:
-            # AdaMuon rescales in the param's shape, Muon in the flattened one
-            r, c = (p.shape[-2], p.shape[-1]) if adamuon else (rows, cols)
+            # AdaMuon rescales in the param's shape, Muon (and AdaMuon's
+            # NorMuon branch, AdaMuon_adv.py:614-616) in the flattened one
+            r, c = (p.shape[-2], p.shape[-1]) if (adamuon and normuon is None) else (rows, cols)
             a.scale_const = f32(step_scale * math.sqrt(max(1, r / c)))
         a.tensor_id = tensor_id & 0xFFFFFFFF
         a.step = step & 0xFFFFFFFF
@@ -261,8 +292,14 @@ class MuonMatrixRunner:
             flags |= L.MU_RMS
         if rows > cols:
             flags |= L.MU_TRANSPOSED
-        if adamuon and use_atan2:
+        if adamuon and use_atan2 and normuon is None:
             flags |= L.MU_ATAN2
+        if mars_factor is not None:
+            flags |= L.MU_MARS
+        if normuon is not None:
+            flags |= L.MU_NORMUON
+        if vfact:
+            flags |= L.MU_VFACT
         keep = []
         if noise is not None:
             flags |= L.MU_NOISE_IN
@@ -277,7 +314,7 @@ class MuonMatrixRunner:
                     setattr(a, field, ptr(t))
         a.flags = flags
         a.m_storage = storage_code(precision, p)
-        a.v_storage = storage_code(precision, p) if adamuon else 0
+        a.v_storage = storage_code(precision, p) if (adamuon and not vfact and normuon is None) else 0
         auto_bf16 = precision == "auto" and pbf
         a.param_bf16 = 1 if pbf else 0
         a.math_bf16 = 1 if auto_bf16 else 0
@@ -295,7 +332,18 @@ class MuonMatrixRunner:
             self.gemm_events.append((ev0, ev1, ns_flops(m, n, ns_steps, cns),
                                      ns_flops_executed(m_pad, n_pad, ns_steps, cns)))
         a.ns_result = final
-        if adamuon:
+        if normuon is not None:
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 7, stream), "advopt_muon_stage (NorMuon rows)")
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 8, stream), "advopt_muon_stage (NorMuon statistics)")
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 9, stream), "advopt_muon_stage (NorMuon update)")
+            self.launch_count += 3 + 1 + 1 + 2 + 1
+        elif vfact:
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 10, stream), "advopt_muon_stage (AdaMuon factored v)")
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 11, stream), "advopt_muon_stage (AdaMuon update)")
+            self.launch_count += 3 + 1 + 5 + 1
+        elif adamuon:
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 4, stream), "advopt_muon_stage (AdaMuon statistics)")
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 5, stream), "advopt_muon_stage (AdaMuon update)")
@@ -358,11 +406,29 @@ def newton_schulz(G: torch.Tensor, steps: int = 5, eps: float | None = 1e-7,
     return out if G.dtype == torch.bfloat16 else out.to(G.dtype)
 
 
-def init_muon_state(p, state, precision: str, adamuon: bool):
+def init_muon_state(p, state, precision: str, adamuon: bool, group=None):
     """Muon_adv.__init_state / AdaMuon_adv.__init_state, non-factored
-    (Muon_adv.py:304-330, AdaMuon_adv.py:334-359)."""
+    (Muon_adv.py:304-345, AdaMuon_adv.py:361-397): the momentum; AdaMuon's
+    second moment, full or factored (effective shape, mu_vbuf_nmf /
+    mv_vbuf_nmf, shifter) unless NorMuon replaces it; NorMuon's row-wise
+    normuon_v; MARS-M's last_grad."""
+    group = group or {}
+    normuon = bool(group.get("normuon_variant", False))
     state["factored"] = False
     init_state_tensor(state, "momentum_buffer", p, precision)
     if adamuon:
-        state["factored_2nd"] = False
-        init_state_tensor(state, "second_momentum_buffer", p, precision, non_neg=True)
+        use_f2 = bool(group.get("factored_2nd", False)) and not normuon and not (
+            p.ndim == 1 and not group.get("vector_reshape", False))
+        state["factored_2nd"] = use_f2
+        if use_f2:
+            d1, d2 = effective_shape(p.numel())
+            state["effective_shape"] = (d1, d2)
+            state["mu_vbuf_nmf"] = torch.zeros(d1, device=p.device, dtype=torch.float32)
+            state["mv_vbuf_nmf"] = torch.zeros(d2, device=p.device, dtype=torch.float32)
+            state["shifter"] = torch.tensor(SHIFTER, device=p.device, dtype=torch.uint8)
+        elif not normuon:
+            init_state_tensor(state, "second_momentum_buffer", p, precision, non_neg=True)
+    if normuon and p.ndim >= 2:
+        state["normuon_v"] = torch.zeros(p.shape[0], device=p.device, dtype=torch.float32)
+    if group.get("approx_mars", False):
+        state["last_grad"] = torch.zeros_like(p, device=p.device, dtype=p.dtype)

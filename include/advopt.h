@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define ADVOPT_ABI_VERSION 3
+#define ADVOPT_ABI_VERSION 4
 
 /* ---- error codes ---- */
 #define ADVOPT_OK 0
@@ -362,6 +362,9 @@ int advopt_ns_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void*
 #define ADVOPT_MU_RMS (1u << 5)       /* rms_rescaling */
 #define ADVOPT_MU_TRANSPOSED (1u << 6)/* rows > cols: the workspace holds X^T */
 #define ADVOPT_MU_ATAN2 (1u << 7)     /* AdaMuon use_atan2 */
+#define ADVOPT_MU_MARS (1u << 8)      /* approx_mars: g' = (g - last_grad) * mars_factor + g */
+#define ADVOPT_MU_NORMUON (1u << 9)   /* normuon_variant: stages 7, 8, 9 */
+#define ADVOPT_MU_VFACT (1u << 10)    /* AdaMuon factored_2nd: stages 10, 11 */
 
 /* storage codes of momentum_buffer / second_momentum_buffer */
 #define ADVOPT_ST_F32 0
@@ -408,8 +411,33 @@ typedef struct advopt_muon_args {
   int32_t param_bf16;        /* 1: bf16 params, 0: f32                           */
   int32_t math_bf16;         /* 1: momentum and AdaMuon math in bf16 ('auto', bf16 params) */
   int32_t update_bf16;       /* 1: the orthogonalised update is bf16 (else f32)  */
+  /* approx MARS-M (Muon_util.py:333-347) */
+  void* last_grad;           /* state['last_grad'] (param dtype), rewritten      */
+  float mars_factor;         /* float(mars_gamma * beta1 / (1 - beta1))          */
+  /* NorMuon (Muon_util.py:349-360): row-wise second moment after the chain */
+  float nm_w;                /* lerp weight 1 - beta2 (Muon: beta2_normuon)      */
+  float nm_eps;              /* normuon_eps (AdaMuon: eps)                        */
+  int32_t pad0;
+  float* row_v;              /* state['normuon_v'] [rows] f32, rewritten          */
+  float* row_den;            /* scratch [rows]: sqrt(v) + eps                    */
+  /* AdaMuon factored_2nd (AdaMuon_adv.py:617-631): v = outer(v_row, v_col) */
+  float* v_row;              /* mu_vbuf_nmf [d1], rewritten                      */
+  float* v_col;              /* mv_vbuf_nmf [d2], rewritten                      */
+  float* v_full;             /* scratch f32 [numel]: the updated v               */
+  double* v_sums;            /* scratch f64 [d1 + kVColSplit * d2]: row sums, column partials */
+  int64_t d1, d2;            /* effective shape (factorization_util.py:43-50)    */
 } advopt_muon_args;
 
+/* column partial sums of the AdaMuon factored v: d1 rows are cut into this
+ * many row ranges, each summed per column; the finish adds them in order */
+#define ADVOPT_VCOL_SPLIT 16
+
+/* Stages (one matrix per call sequence):
+ *   0 momentum / X0 / norm / workspace load     6 the same for a bare Newton–Schulz call
+ *   1 U store + RMS scale, 2 Muon update        3 U store only
+ *   4 AdaMuon statistics + scale, 5 AdaMuon second moment + update
+ *   7 NorMuon rows (v, sqrt(v) + eps per row), 8 NorMuon statistics + scale, 9 NorMuon update
+ *   10 AdaMuon factored statistics + scale + new factors, 11 AdaMuon factored update */
 int advopt_muon_stage(const advopt_muon_args* args, int32_t stage, void* stream);
 
 /* The stochastic-rounding noise generator.  No reference counterpart: the

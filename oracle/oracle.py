@@ -785,6 +785,30 @@ def rms_adjustment(u: T, rms_rescaling, lr):
     return u.mul_s(lr * math.sqrt(max(1, r / c)))
 
 
+def approx_mars(grad: T, state, p_dt, mars_gamma, beta1):
+    """Muon_util.approx_mars (Muon_util.py:333-347): c = (g - last).mul_(f).add_(g)
+    with f = gamma * beta1 / (1 - beta1), each op rounding to the grad's dtype;
+    last_grad (the param's dtype) takes the current grad."""
+    f = mars_gamma * beta1 / (1.0 - beta1)
+    last = T(state["last_grad"].astype(np.float32) if p_dt == "f32" else from_bf16_bits(state["last_grad"]), p_dt)
+    c = grad.add(last.neg(), dt=grad.dt).mul_s(f).add(grad, dt=grad.dt)
+    state["last_grad"] = grad.v.astype(np.float32) if p_dt == "f32" else bf16_bits(grad.v)
+    return c
+
+
+def normuon_update(u: T, state, beta2, eps):
+    """Muon_util.normuon_update (Muon_util.py:349-360) on the 2-D update:
+    v = lerp(v, mean(u^2 over each row) [u^2 in u's dtype, the mean in
+    float32], 1 - beta2); u = u / (sqrt(v) + eps), computed in float32 and
+    stored in u's dtype."""
+    sq = T(u.v * u.v, u.dt)
+    mean = np.float32(sq.v.astype(np.float64).sum(axis=1).astype(np.float32) / np.float32(u.v.shape[1]))
+    v = T(state["normuon_v"].astype(np.float32), "f32").lerp(T(mean, "f32"), 1 - beta2)
+    state["normuon_v"] = v.v.copy()
+    den = (np.sqrt(v.v) + f32(eps)).astype(np.float32)
+    return T(u.v / den[:, None], u.dt)
+
+
 class Kourkoutas:
     """Kourkoutas.py:6-257 (KourkoutasHelper) for the default layer key (the
     param's shape): a float32 EMA of each layer's pooled grad norm and, per
@@ -853,6 +877,8 @@ def muon_step(p, p_dt, g, state, hp, noise):
     prec = hp["precision"]
     beta1 = hp["beta1"]
     grad = upcast(T(g, p_dt), prec)
+    if hp.get("approx_mars", False):
+        grad = approx_mars(grad, state, p_dt, hp.get("mars_gamma", 0.025), beta1)
     m = get_state(state, "momentum_buffer", prec, p_dt)
     m = m.lerp(grad, 1 - beta1)
     if hp.get("nesterov", True):
@@ -864,6 +890,8 @@ def muon_step(p, p_dt, g, state, hp, noise):
     shape = np.shape(p)
     upd = T(upd.v.reshape(shape[0], -1), upd.dt)
     upd = newton_schulz(upd, hp["ns_steps"], hp["ns_eps"], hp["ns_coeffs"], hp.get("accelerated_ns", False), hp.get("cns_a_bound"))
+    if hp.get("normuon_variant", False):
+        upd = normuon_update(upd, state, hp.get("beta2_normuon", 0.95), hp.get("normuon_eps", 1e-8))
     upd = rms_adjustment(upd, hp.get("rms_rescaling", True), hp["lr"])
     upd = T(upd.v.reshape(shape), upd.dt)
     return apply_parameter_update(p, p_dt, upd, state, lr=hp["lr"], wd=hp.get("weight_decay", 0.0),
@@ -879,6 +907,8 @@ def adamuon_step(p, p_dt, g, state, hp, noise):
     grad = upcast(T(g, p_dt), prec)
     shape = np.shape(p)
     eps = hp["eps"] if hp["eps"] is not None else 1.0 / math.sqrt(grad.v.size)
+    if hp.get("approx_mars", False):
+        grad = approx_mars(grad, state, p_dt, hp.get("mars_gamma", 0.025), beta1)
     m = get_state(state, "momentum_buffer", prec, p_dt)
     m = m.lerp(grad, 1 - beta1)
     if hp.get("nesterov", True):
@@ -894,9 +924,15 @@ def adamuon_step(p, p_dt, g, state, hp, noise):
         upd = upd.sign()
     upd = T(upd.v.reshape(shape[0], -1), upd.dt)
     upd = newton_schulz(upd, hp["ns_steps"], hp["ns_eps"], hp["ns_coeffs"], hp.get("accelerated_ns", False), hp.get("cns_a_bound"))
+    normuon = hp.get("normuon_variant", False)
+    if normuon:
+        # replaces the second moment (AdaMuon_adv.py:614-616)
+        upd = normuon_update(upd, state, beta2, hp["eps"])
     upd = T(upd.v.reshape(shape), upd.dt)
-    atan2 = hp.get("use_atan2", False)
-    if state.get("factored_2nd", False):
+    atan2 = hp.get("use_atan2", False) and not normuon
+    if normuon:
+        pass
+    elif state.get("factored_2nd", False):
         d1, d2 = state["effective_shape"]
         uf = upd.to("f32")
         v = T(unnmf(state["mu_vbuf_nmf"], state["mv_vbuf_nmf"]), "f32")

@@ -30,7 +30,8 @@ MUON_DEFAULTS = dict(lr=1e-3, beta1=0.95, weight_decay=0.0, cautious_wd=False, n
                      adam_use_bias_correction=True, adam_use_atan2=False, adam_nesterov=False,
                      adam_nesterov_coef=None, adam_state_precision="auto", adam_factored_2nd=False,
                      adam_kourkoutas_beta=False, adam_beta2_min=0.9, adam_ema_alpha=0.95, adam_tiny_spike=1e-9,
-                     adam_k_warmup_steps=0)
+                     adam_k_warmup_steps=0, normuon_variant=False, beta2_normuon=0.95, normuon_eps=1e-8,
+                     approx_mars=False, mars_gamma=0.025)
 ADAMUON_DEFAULTS = dict(MUON_DEFAULTS, betas=(0.95, 0.95), eps=1e-8, use_atan2=False, factored_2nd=False,
                         kappa_p=1.0, auto_projection=True)
 PRODIGY_DEFAULTS = dict(lr=1.0, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, fisher_wd=False,
@@ -135,8 +136,18 @@ def replay(name, steps=None, pin_d=False, teacher=False):
             if kinds[i] == "muon":
                 st = {}
                 O.init_state_tensor(st, "momentum_buffer", sh, base["precision"], dt)
-                if cls == "AdaMuon_adv":
+                if cls == "AdaMuon_adv" and base.get("factored_2nd") and not base["normuon_variant"]:
+                    d1, d2 = O.effective_shape(int(np.prod(sh)))
+                    st["effective_shape"] = (d1, d2)
+                    st["factored_2nd"] = True
+                    st["mu_vbuf_nmf"] = np.zeros(d1, np.float32)
+                    st["mv_vbuf_nmf"] = np.zeros(d2, np.float32)
+                elif cls == "AdaMuon_adv" and not base["normuon_variant"]:
                     O.init_state_tensor(st, "second_momentum_buffer", sh, base["precision"], dt, non_neg=True)
+                if base["normuon_variant"]:
+                    st["normuon_v"] = np.zeros(sh[0], np.float32)
+                if base["approx_mars"]:
+                    st["last_grad"] = np.zeros(sh, np.uint16 if dt == "bf16" else np.float32)
                 states.append(st)
             else:
                 states.append(O.adamw_init_state(sh, dt, aux["precision"], aux["factored_2nd"], aux["betas"][0]))

@@ -196,6 +196,24 @@ CASES = {
                                     kw=dict(lr=1e-3, adam_state_precision="fp32", adam_kourkoutas_beta=True,
                                             adam_use_bias_correction=False, adam_beta2_min=0.88,
                                             adam_ema_alpha=0.9), steps=4),
+    # NorMuon (row-wise second moment after Newton-Schulz) and approximated
+    # MARS-M (grad correction from the previous grad)
+    "muon_normuon_mars": dict(cls="Muon_adv", dtype="bf16",
+                              groups=[dict(shapes=[(64, 48), (48, 96), (8, 4, 3)], optim_type="muon"),
+                                      dict(shapes=[(48,)], optim_type="adam")],
+                              kw=dict(lr=1e-3, normuon_variant=True, approx_mars=True, mars_gamma=0.05), steps=3),
+    "muon_normuon_fp32_states": dict(cls="Muon_adv", dtype="bf16",
+                                     groups=[dict(shapes=[(64, 48), (48, 96)], optim_type="muon")],
+                                     kw=dict(lr=1e-3, normuon_variant=True, state_precision="fp32",
+                                             beta2_normuon=0.9), steps=3),
+    "adamuon_normuon_mars": dict(cls="AdaMuon_adv", dtype="bf16",
+                                 groups=[dict(shapes=[(64, 48), (40, 96)], optim_type="muon"),
+                                         dict(shapes=[(48,)], optim_type="adam")],
+                                 kw=dict(lr=1e-3, normuon_variant=True, approx_mars=True), steps=3),
+    # AdaMuon's factored second moment (mu_vbuf_nmf / mv_vbuf_nmf)
+    "adamuon_factored_2nd": dict(cls="AdaMuon_adv", dtype="bf16",
+                                 groups=[dict(shapes=[(64, 48), (48, 96), (40, 30)], optim_type="muon")],
+                                 kw=dict(lr=1e-3, factored_2nd=True), steps=3),
     # config 4 semantics (Prodigy bf16_sr)
     "prodigy_bf16sr": dict(cls="Prodigy_adv", dtype="bf16", shapes=[(120, 40), (40,), (64, 64)],
                            kw=dict(state_precision="bf16_sr", d0=1e-6, slice_p=11), steps=3,

@@ -136,7 +136,8 @@ def test_matches_reference_golden(name):
                 rk = f"st_{s}_{i}_{key}"
                 if not (torch.is_tensor(val) and rk in z.files):
                     continue
-                if muon and key.startswith("second_momentum_buffer"):
+                if muon and key.startswith(("second_momentum_buffer", "normuon_v", "mu_vbuf_nmf", "mv_vbuf_nmf")):
+                    # statistics of the chain's output
                     check_second_moment(key, to_numpy(val), z[rk], f"{what} {key}")
                 else:
                     pk = f"st_{s - 1}_{i}_{key}" if s > 0 else f"st0_{i}_{key}"

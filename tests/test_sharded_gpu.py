@@ -4,6 +4,7 @@ bit-identical (Philox streams are keyed by the tensor's global index);
 Prodigy_adv's d is within 1e-5 relative (its two sums are all-reduced in a
 different order) and its params within 1 bf16 ulp.  Skipped with fewer than
 two GPUs."""
+import io
 import os
 import socket
 
@@ -88,9 +89,13 @@ def _worker(rank, world, port, name, out):
             out[f"d{rank}"] = opt.optimizer.param_groups[0]["d"]
         if name == "adamw_buckets":
             # the owners' states gathered into the single-process layout
+            # (handed to the parent as bytes: no tensor sharing across the
+            # process boundary)
             sd = opt.full_state_dict()
             if rank == 0:
-                out["sd"] = sd
+                buf = io.BytesIO()
+                torch.save(sd, buf)
+                out["sd"] = buf.getvalue()
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -115,7 +120,7 @@ def test_sharded_matches_single_process(name):
             else:
                 assert torch.equal(a, b), f"rank {r} tensor {i} differs"
     if name == "adamw_buckets":
-        sd, want = out["sd"], opt.state_dict()
+        sd, want = torch.load(io.BytesIO(out["sd"]), weights_only=False), opt.state_dict()
         assert sorted(sd["state"]) == sorted(want["state"])
         assert [g["params"] for g in sd["param_groups"]] == [g["params"] for g in want["param_groups"]]
         for i, st in want["state"].items():
