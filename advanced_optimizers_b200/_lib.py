@@ -119,6 +119,7 @@ MU_ATAN2 = 1 << 7
 MU_MARS = 1 << 8
 MU_NORMUON = 1 << 9
 MU_VFACT = 1 << 10
+MU_LOWRANK = 1 << 11
 VCOL_SPLIT = 16
 ST_F32, ST_BF16, ST_BF16_SR, ST_Q8 = 0, 1, 2, 3
 
@@ -187,6 +188,10 @@ def lib():
             "advopt_kourkoutas_accumulate": ([ctypes.POINTER(KourkoutasArgs), P], ctypes.c_int),
             "advopt_prodigy_scalars": ([ctypes.POINTER(ProdigyScalarArgs), P], ctypes.c_int),
             "advopt_prodigy_update_d": ([ctypes.POINTER(ProdigyDArgs), P], ctypes.c_int),
+            "advopt_lr_sketch": ([P, ctypes.c_int64, ctypes.c_int64, U64, U32, U32, P], ctypes.c_int),
+            "advopt_lr_gemm": ([P, P, P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, I32, P], ctypes.c_int),
+            "advopt_lr_qr_work": ([ctypes.c_int64, ctypes.c_int64], ctypes.c_int64),
+            "advopt_lr_qr": ([P, P, ctypes.c_int64, ctypes.c_int64, P, P], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -218,7 +223,8 @@ def exported_symbols():
             "advopt_lion_step", "advopt_sizeof", "advopt_abi_version", "advopt_last_error",
             "advopt_adam_occupancy", "advopt_adam_step_noalloc", "advopt_ns_gemm", "advopt_ns_gemm_sym", "advopt_muon_stage", "advopt_philox4x32_10",
             "advopt_noise_fill", "advopt_ns_chain", "advopt_kourkoutas_prepare", "advopt_kourkoutas_accumulate",
-            "advopt_prodigy_scalars", "advopt_prodigy_update_d"]
+            "advopt_prodigy_scalars", "advopt_prodigy_update_d", "advopt_lr_sketch", "advopt_lr_gemm",
+            "advopt_lr_qr_work", "advopt_lr_qr"]
 
 
 _OCC_CACHE = {}

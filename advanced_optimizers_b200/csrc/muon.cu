@@ -16,6 +16,17 @@
 //   stage 5  adamuon_apply  second_momentum_buffer store + param update
 //   stage 6  prep_kernel<RAW> X0 = bf16(grad) for a bare Newton–Schulz call,
 //            then norm_kernel and load_kernel as in stage 0
+//   stage 7  normuon_rows   NorMuon: per-row lerp of mean(u^2) into normuon_v,
+//                           sqrt(v) + eps per row (Muon_util.py:349-360)
+//   stage 8  normuon_stats  per-chunk sum(u'^2), u' = u / den[row], and scale_kernel
+//   stage 9  normuon_apply  param update with u' * scale
+//   stage 10 vfact_*        AdaMuon factored_2nd: v = outer(row, col) * beta2 +
+//                           (1-beta2) u^2 into a scratch, sum(u'^2) and
+//                           scale_kernel, then the new row / column factors
+//   stage 11 vfact_apply    param update with u' * scale
+//   stage 13 u_stats        sum(U^2) of U already in `u` (low-rank chain) and scale_kernel
+//   MARS-M (flag) corrects the grad inside stage 0; with ADVOPT_MU_LOWRANK
+//   stage 0 ends after X0 (the chain runs on the low-rank projection).
 //
 // One launch sequence handles one matrix.  Chunks of 2048 elements (the int8
 // block) map to CTAs of 256 threads x 8 consecutive elements, so one Philox
@@ -693,6 +704,24 @@ __global__ void __launch_bounds__(256) normuon_stats_kernel(const Args a) {
   }
 }
 
+// ---- stage 13: per-chunk sum(U^2) of U in `u` (after a low-rank chain) ----
+__global__ void __launch_bounds__(256) u_stats_kernel(const Args a) {
+  __shared__ double redd[kWarps];
+  const int64_t nchunks = (a.numel + kChunk - 1) / kChunk;
+  for (int64_t c = blockIdx.x; c < nchunks; c += gridDim.x) {
+    const int64_t k0 = c * kChunk + threadIdx.x * 8;
+    double ss = 0.0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (k0 + e < a.numel) {
+        const float f = bf16_to_f(a.u[k0 + e]);
+        ss += (double)f * (double)f;
+      }
+    const double s = block_sum_d(ss, redd, 256);
+    if (threadIdx.x == 0) a.partial[c] = s;
+  }
+}
+
 // ---- stage 9: p updated with u' * scale (NorMuon) ----
 __global__ void __launch_bounds__(256) normuon_apply_kernel(const Args a) {
   const float sc = a.scalars[1];
@@ -911,6 +940,8 @@ extern "C" int advopt_muon_stage(const advopt_muon_args* ap, int32_t stage, void
       } else {
         prep_kernel<false, false><<<gp, 256, 0, s>>>(a);
       }
+      // low-rank: X0 feeds the sketch products; the chain runs on the projection
+      if (a.flags & ADVOPT_MU_LOWRANK) break;
       norm_kernel<<<1, 1024, 0, s>>>(a, nchunks);
       if (vec && a.cols % 8 == 0 && tr)
         load_vec_t_kernel<<<dim3((unsigned)(a.n_pad / kTile), (unsigned)(a.m_pad / kTile)), 256, 0, s>>>(a);
@@ -974,6 +1005,10 @@ extern "C" int advopt_muon_stage(const advopt_muon_args* ap, int32_t stage, void
       } else {
         normuon_apply_kernel<<<grid_for((a.numel + 8 * 256 - 1) / (8 * 256)), 256, 0, s>>>(a);
       }
+      break;
+    case 13:
+      u_stats_kernel<<<grid_for(nchunks), 256, 0, s>>>(a);
+      scale_kernel<<<1, 1024, 0, s>>>(a, nchunks);
       break;
     case 10:
     case 11:

@@ -100,7 +100,6 @@ class Muon_adv(MuonFamilyBase):
         reject(state_precision in ("factored", "fp16"), f"state_precision='{state_precision}'")
         reject(adam_state_precision in ("factored", "fp16") or adam_nnmf_factor,
                f"adam_state_precision='{adam_state_precision}'")
-        reject(low_rank_ortho, "low_rank_ortho")
         reject(spectral_normalization or adam_spectral_normalization, "spectral_normalization")
         reject(centered_wd, "centered_wd for Muon_adv")
         defaults = {

@@ -157,7 +157,9 @@ class MuonFamilyBase(torch.optim.Optimizer):
                                           normuon=self._normuon_hp(group) if "normuon_v" in st else None,
                                           mars_factor=(group["mars_gamma"] * hp["beta1"] / (1.0 - hp["beta1"])
                                                        if "last_grad" in st else None),
-                                          vfact=bool(st.get("factored_2nd", False)), **hp)
+                                          vfact=bool(st.get("factored_2nd", False)),
+                                          low_rank=group["ortho_rank"] if group.get("low_rank_ortho", False) else None,
+                                          **hp)
 
     @torch.no_grad()
     def step_parameter(self, p: torch.Tensor, group: dict, i: int | None = None):

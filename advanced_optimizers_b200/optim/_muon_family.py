@@ -210,11 +210,12 @@ class MuonMatrixRunner:
                     nesterov_coef, ns_steps: int, ns_eps, ns_coeffs, cns: bool, cns_a_bound, rms_rescaling: bool,
                     use_atan2: bool, sign_projection: bool, weight_decay: float, cautious_wd: bool, sr: bool,
                     precision: str, tensor_id: int, step: int, noise=None, normuon=None, mars_factor=None,
-                    vfact: bool = False):
+                    vfact: bool = False, low_rank=None):
         """One matrix.  normuon: (1 - beta2, eps) of the NorMuon row-wise
         second moment (state['normuon_v']); mars_factor: approx MARS-M's
         gamma * beta1 / (1 - beta1) (state['last_grad']); vfact: AdaMuon's
-        factored second moment (state['mu_vbuf_nmf'], state['mv_vbuf_nmf'])."""
+        factored second moment (state['mu_vbuf_nmf'], state['mv_vbuf_nmf']);
+        low_rank: ortho_rank of the low-rank chain (Muon_util.py:239-270)."""
         require_cuda_tensor(p, "param")
         require_cuda_tensor(p.grad, "grad")
         if p.ndim < 2:
@@ -228,8 +229,18 @@ class MuonMatrixRunner:
         m, n = min(rows, cols), max(rows, cols)
         m_pad, n_pad = round_up(m, NS_ALIGN), round_up(n, NS_ALIGN)
         ws = self.workspace(p.device)
-        ws.ensure(numel, m_pad, n_pad)
-        ptrs = ws.pointers(numel, m_pad, n_pad)
+        if low_rank is not None:
+            # the chain runs on the [r][cols] projection only
+            if not (precision == "auto" and dtype_code(p.dtype) == L.DT_BF16):
+                raise NotImplementedError("low_rank_ortho needs a bf16 update (state_precision='auto' with bf16 "
+                                          "params) on the B200 kernels")
+            r = min(int(low_rank), rows, cols)
+            m2, n2 = min(r, cols), max(r, cols)
+            ws_m, ws_n = round_up(m2, NS_ALIGN), round_up(n2, NS_ALIGN)
+        else:
+            ws_m, ws_n = m_pad, n_pad
+        ws.ensure(numel, ws_m, ws_n)
+        ptrs = ws.pointers(numel, ws_m, ws_n)
         stream = stream_handle(p.device)
 
         a = L.MuonArgs()
@@ -300,6 +311,8 @@ class MuonMatrixRunner:
             flags |= L.MU_NORMUON
         if vfact:
             flags |= L.MU_VFACT
+        if low_rank is not None:
+            flags |= L.MU_LOWRANK
         keep = []
         if noise is not None:
             flags |= L.MU_NOISE_IN
@@ -322,29 +335,43 @@ class MuonMatrixRunner:
 
         lib = L.lib()
         L.check(lib.advopt_muon_stage(ctypes.byref(a), 0, stream), "advopt_muon_stage (prep)")
+        # eps and the CANS bound come from the full shape, low rank or not (Muon_util.py:225-237)
         bound = cns_a_bound if cns_a_bound is not None else default_cns_bound(rows, cols)
         if self.gemm_events is not None:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record(torch.cuda.current_stream(p.device))
-        final = run_ns_chain(ws, ptrs, m_pad, n_pad, ns_steps, ns_coeffs, cns, bound, stream)
+        if low_rank is not None:
+            sketch = None if noise is None else noise.get("sketch")
+            self._low_rank_chain(a, ws, ptrs, r, ws_m, ws_n, ns_steps, ns_coeffs, cns, bound, stream, sketch)
+            flops = (ns_flops(m2, n2, ns_steps, cns) + 6 * rows * cols * r,
+                     ns_flops_executed(ws_m, ws_n, ns_steps, cns) + 6 * rows * cols * r)
+        else:
+            a.ns_result = run_ns_chain(ws, ptrs, m_pad, n_pad, ns_steps, ns_coeffs, cns, bound, stream)
+            flops = (ns_flops(m, n, ns_steps, cns), ns_flops_executed(m_pad, n_pad, ns_steps, cns))
         if self.gemm_events is not None:
             ev1.record(torch.cuda.current_stream(p.device))
-            self.gemm_events.append((ev0, ev1, ns_flops(m, n, ns_steps, cns),
-                                     ns_flops_executed(m_pad, n_pad, ns_steps, cns)))
-        a.ns_result = final
-        if normuon is not None:
-            L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")
+            self.gemm_events.append((ev0, ev1) + flops)
+        u_ready = low_rank is not None       # the low-rank chain leaves U in `u`
+        if u_ready and normuon is None and not vfact and not adamuon:
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 13, stream), "advopt_muon_stage (U statistics)")
+            L.check(lib.advopt_muon_stage(ctypes.byref(a), 2, stream), "advopt_muon_stage (update)")
+            self.launch_count += 2 + 2
+        elif normuon is not None:
+            if not u_ready:
+                L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 7, stream), "advopt_muon_stage (NorMuon rows)")
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 8, stream), "advopt_muon_stage (NorMuon statistics)")
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 9, stream), "advopt_muon_stage (NorMuon update)")
             self.launch_count += 3 + 1 + 1 + 2 + 1
         elif vfact:
-            L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")
+            if not u_ready:
+                L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 10, stream), "advopt_muon_stage (AdaMuon factored v)")
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 11, stream), "advopt_muon_stage (AdaMuon update)")
             self.launch_count += 3 + 1 + 5 + 1
         elif adamuon:
-            L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")
+            if not u_ready:
+                L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (U)")
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 4, stream), "advopt_muon_stage (AdaMuon statistics)")
             L.check(lib.advopt_muon_stage(ctypes.byref(a), 5, stream), "advopt_muon_stage (AdaMuon update)")
             self.launch_count += 3 + 1 + 2 + 1
@@ -355,6 +382,48 @@ class MuonMatrixRunner:
         self.launch_count += ns_launches(ns_steps, cns)
         if keep:
             torch.cuda.current_stream(p.device).synchronize()
+
+    def _low_rank_chain(self, a, ws, ptrs, r, m_pad2, n_pad2, ns_steps, ns_coeffs, cns, bound, stream, sketch):
+        """Muon_util.py:239-270 on X0 = the update in bf16 ([rows][cols], after
+        stage 0): MG = X0 S, Q = qr(MG), P = Q^T X0, the chain on P, U = Q NS(P)
+        into `u`."""
+        lib = L.lib()
+        rows, cols = a.rows, a.cols
+        x0 = ptrs["x0"]
+        s_ptr = ws.scratch("lr_sketch", cols * r, torch.bfloat16)
+        if sketch is not None:
+            t = sketch.to(device=ws.device).reshape(-1)
+            if t.dtype != torch.bfloat16:
+                # the reference's bf16 bit patterns, as integers
+                t = t.to(torch.int32).to(torch.int16).view(torch.bfloat16)
+            if t.numel() != cols * r:
+                raise ValueError(f"injected sketch has {t.numel()} entries, {cols * r} needed")
+            ws.aux["lr_sketch"][: cols * r].copy_(t)
+        else:
+            L.check(lib.advopt_lr_sketch(s_ptr, cols, r, a.seed, a.tensor_id, a.step, stream), "advopt_lr_sketch")
+        mg = ws.scratch("lr_mg", rows * r, torch.bfloat16)
+        q = ws.scratch("lr_q", rows * r, torch.bfloat16)
+        pp = ws.scratch("lr_p", r * cols, torch.bfloat16)
+        oo = ws.scratch("lr_o", r * cols, torch.bfloat16)
+        work = ws.scratch("lr_work", int(lib.advopt_lr_qr_work(rows, r)), torch.float64)
+        L.check(lib.advopt_lr_gemm(mg, x0, s_ptr, rows, r, cols, 0, stream), "advopt_lr_gemm (M S)")
+        L.check(lib.advopt_lr_qr(q, mg, rows, r, work, stream), "advopt_lr_qr")
+        L.check(lib.advopt_lr_gemm(pp, q, x0, r, cols, rows, 1, stream), "advopt_lr_gemm (Q^T M)")
+        # the ordinary chain on P [r][cols]: stage 6 (P -> workspace), chain, stage 3 (-> oo)
+        b = L.MuonArgs.from_buffer_copy(a)
+        b.grad = pp
+        b.param, b.m = 0, 0
+        b.u = oo
+        b.rows, b.cols, b.numel = r, cols, r * cols
+        b.m_pad, b.n_pad, b.ld_ns = m_pad2, n_pad2, n_pad2
+        b.ns = ptrs["x"]
+        b.param_bf16 = 1
+        b.flags = L.MU_TRANSPOSED if r > cols else 0
+        L.check(lib.advopt_muon_stage(ctypes.byref(b), 6, stream), "advopt_muon_stage (low-rank load)")
+        b.ns_result = run_ns_chain(ws, ptrs, m_pad2, n_pad2, ns_steps, ns_coeffs, cns, bound, stream)
+        L.check(lib.advopt_muon_stage(ctypes.byref(b), 3, stream), "advopt_muon_stage (low-rank U)")
+        L.check(lib.advopt_lr_gemm(a.u, q, oo, rows, cols, r, 0, stream), "advopt_lr_gemm (Q NS(P))")
+        self.launch_count += (0 if sketch is not None else 1) + 3 + 10 + 1 + 3 + 1 + 1
 
 
 _NS_RUNNER = None

@@ -365,6 +365,7 @@ int advopt_ns_gemm(void* D, int32_t ldd, const void* A, int32_t lda, const void*
 #define ADVOPT_MU_MARS (1u << 8)      /* approx_mars: g' = (g - last_grad) * mars_factor + g */
 #define ADVOPT_MU_NORMUON (1u << 9)   /* normuon_variant: stages 7, 8, 9 */
 #define ADVOPT_MU_VFACT (1u << 10)    /* AdaMuon factored_2nd: stages 10, 11 */
+#define ADVOPT_MU_LOWRANK (1u << 11)  /* low_rank_ortho: stage 0 stops after X0 (no norm, no workspace load) */
 
 /* storage codes of momentum_buffer / second_momentum_buffer */
 #define ADVOPT_ST_F32 0
@@ -432,12 +433,28 @@ typedef struct advopt_muon_args {
  * many row ranges, each summed per column; the finish adds them in order */
 #define ADVOPT_VCOL_SPLIT 16
 
+/* Low-rank Newton–Schulz (Muon_util.py:239-270), bf16 operands, float32
+ * accumulation, one rounding of each product to bf16:
+ *   advopt_lr_sketch  S [n][r] ~ N(0, 1) (Philox4x32-10, Box–Muller), the sketch
+ *   advopt_lr_gemm    D [M][N] = op(A) B; op(A) = A [M][K], or A^T with A stored [K][M] (trans_a)
+ *   advopt_lr_qr      Q [m][r] = the Q factor of A [m][r] (shifted CholeskyQR3 in float64;
+ *                     `work` holds advopt_lr_qr_work(m, r) doubles)
+ * The host chain: MG = M S, Q = qr(MG), P = Q^T M, the ordinary chain on P
+ * (stage 6 with P as its input, then stage 3), U = Q NS(P). */
+int advopt_lr_sketch(uint16_t* S, int64_t n, int64_t r, uint64_t seed, uint32_t tensor_id, uint32_t step,
+                     void* stream);
+int advopt_lr_gemm(uint16_t* D, const uint16_t* A, const uint16_t* B, int64_t M, int64_t N, int64_t K,
+                   int32_t trans_a, void* stream);
+int64_t advopt_lr_qr_work(int64_t m, int64_t r);
+int advopt_lr_qr(uint16_t* Q, const uint16_t* A, int64_t m, int64_t r, double* work, void* stream);
+
 /* Stages (one matrix per call sequence):
  *   0 momentum / X0 / norm / workspace load     6 the same for a bare Newton–Schulz call
  *   1 U store + RMS scale, 2 Muon update        3 U store only
  *   4 AdaMuon statistics + scale, 5 AdaMuon second moment + update
  *   7 NorMuon rows (v, sqrt(v) + eps per row), 8 NorMuon statistics + scale, 9 NorMuon update
- *   10 AdaMuon factored statistics + scale + new factors, 11 AdaMuon factored update */
+ *   10 AdaMuon factored statistics + scale + new factors, 11 AdaMuon factored update
+ *   13 sum(U^2) of the U already in `u` + RMS scale (Muon after a low-rank chain) */
 int advopt_muon_stage(const advopt_muon_args* args, int32_t stage, void* stream);
 
 /* The stochastic-rounding noise generator.  No reference counterpart: the

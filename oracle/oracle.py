@@ -742,14 +742,43 @@ def _mm_bf16(a, b, alpha=1.0, beta=0.0, c=None):
     return round_bf16(out)
 
 
-def newton_schulz(G: T, steps=5, eps=1e-7, coeffs=(3.4445, -4.7750, 2.0315), cns=False, cns_a_bound=None):
-    """Muon_util.newton_schulz / _newton_schulz_iteration (standard path):
-    returns T in G's dtype."""
+def _mm_dt(a, b, dt):
+    """torch.matmul in `dt`: bf16 operands accumulate in float32 and round the
+    output once to bf16; float32 is a float32 product."""
+    out = np.matmul(a.astype(np.float32), b.astype(np.float32)).astype(np.float32)
+    return round_bf16(out) if dt == "bf16" else out
+
+
+def low_rank_newton_schulz(G: T, sketch, steps, eps, coeffs, cns, cns_a_bound):
+    """Muon_util.newton_schulz, low-rank path (Muon_util.py:239-270): MG =
+    G @ sketch, Q from the QR of MG in float32 (cast back to G's dtype), the
+    chain on Q^T G, then Q @ result.  eps and the CANS bound come from G's
+    full shape.  QR is unique up to the signs of Q's columns, and the result
+    does not depend on them (NS(D X) = D NS(X) for a diagonal D of +-1)."""
+    M = G.v
+    S = from_bf16_bits(sketch) if G.dt == "bf16" else np.asarray(sketch, np.float32)
+    S = S.reshape(M.shape[1], -1)
+    MG = _mm_dt(M, S, G.dt)
+    Q, _ = np.linalg.qr(MG.astype(np.float32))
+    Q = Q.astype(np.float32)
+    if G.dt == "bf16":
+        Q = round_bf16(Q)
+    P = T(_mm_dt(Q.T, M, G.dt), G.dt)
+    O = newton_schulz(P, steps, eps, coeffs, cns, cns_a_bound)
+    return T(_mm_dt(Q, O.v, G.dt), G.dt)
+
+
+def newton_schulz(G: T, steps=5, eps=1e-7, coeffs=(3.4445, -4.7750, 2.0315), cns=False, cns_a_bound=None,
+                  sketch=None):
+    """Muon_util.newton_schulz / _newton_schulz_iteration (standard path, or
+    the low-rank path when a sketch is given): returns T in G's dtype."""
     M, N = G.v.shape
     if eps is None:
         eps = 1 / math.sqrt(G.v.size)
     if cns_a_bound is None:
         cns_a_bound = default_cns_bound(M, N)
+    if sketch is not None:
+        return low_rank_newton_schulz(G, sketch, steps, eps, coeffs, cns, cns_a_bound)
     X = round_bf16(G.v)
     transposed = X.shape[0] > X.shape[1]
     if transposed:
@@ -889,7 +918,8 @@ def muon_step(p, p_dt, g, state, hp, noise):
     set_state(state, "momentum_buffer", m, prec, noise.get("momentum_buffer"))
     shape = np.shape(p)
     upd = T(upd.v.reshape(shape[0], -1), upd.dt)
-    upd = newton_schulz(upd, hp["ns_steps"], hp["ns_eps"], hp["ns_coeffs"], hp.get("accelerated_ns", False), hp.get("cns_a_bound"))
+    upd = newton_schulz(upd, hp["ns_steps"], hp["ns_eps"], hp["ns_coeffs"], hp.get("accelerated_ns", False), hp.get("cns_a_bound"),
+                            sketch=noise.get("sketch") if hp.get("low_rank_ortho", False) else None)
     if hp.get("normuon_variant", False):
         upd = normuon_update(upd, state, hp.get("beta2_normuon", 0.95), hp.get("normuon_eps", 1e-8))
     upd = rms_adjustment(upd, hp.get("rms_rescaling", True), hp["lr"])
@@ -923,7 +953,8 @@ def adamuon_step(p, p_dt, g, state, hp, noise):
     if kappa == 1.0:
         upd = upd.sign()
     upd = T(upd.v.reshape(shape[0], -1), upd.dt)
-    upd = newton_schulz(upd, hp["ns_steps"], hp["ns_eps"], hp["ns_coeffs"], hp.get("accelerated_ns", False), hp.get("cns_a_bound"))
+    upd = newton_schulz(upd, hp["ns_steps"], hp["ns_eps"], hp["ns_coeffs"], hp.get("accelerated_ns", False), hp.get("cns_a_bound"),
+                            sketch=noise.get("sketch") if hp.get("low_rank_ortho", False) else None)
     normuon = hp.get("normuon_variant", False)
     if normuon:
         # replaces the second moment (AdaMuon_adv.py:614-616)

@@ -31,7 +31,7 @@ MUON_DEFAULTS = dict(lr=1e-3, beta1=0.95, weight_decay=0.0, cautious_wd=False, n
                      adam_nesterov_coef=None, adam_state_precision="auto", adam_factored_2nd=False,
                      adam_kourkoutas_beta=False, adam_beta2_min=0.9, adam_ema_alpha=0.95, adam_tiny_spike=1e-9,
                      adam_k_warmup_steps=0, normuon_variant=False, beta2_normuon=0.95, normuon_eps=1e-8,
-                     approx_mars=False, mars_gamma=0.025)
+                     approx_mars=False, mars_gamma=0.025, low_rank_ortho=False, ortho_rank=128)
 ADAMUON_DEFAULTS = dict(MUON_DEFAULTS, betas=(0.95, 0.95), eps=1e-8, use_atan2=False, factored_2nd=False,
                         kappa_p=1.0, auto_projection=True)
 PRODIGY_DEFAULTS = dict(lr=1.0, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, fisher_wd=False,
@@ -81,6 +81,8 @@ def draws(z, step, i):
     for k in z.files:
         if k.startswith(pre):
             out[k[len(pre):]] = z[k].astype(np.int32)
+    if f"sk_{step}_{i}" in z.files:
+        out["sketch"] = z[f"sk_{step}_{i}"]      # low-rank Newton-Schulz sketch (the update's dtype)
     return out
 
 

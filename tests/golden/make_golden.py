@@ -49,6 +49,7 @@ class DrawRecorder:
         self.draws = []
         self._orig_sr = pu._get_random_int_for_sr
         self._orig_8 = pu._get_random_int_for_8bit_sr
+        self._orig_sk = pu._get_random_noise_for_low_rank_ortho
 
         self.param_index = {}
 
@@ -74,8 +75,14 @@ class DrawRecorder:
             self.draws.append((*label(), r.clone()))
             return r
 
+        def sketch(source, ortho_rank):
+            r = self._orig_sk(source, ortho_rank)
+            self.draws.append(("sketch", label()[1], r.clone()))
+            return r
+
         pu._get_random_int_for_sr = sr
         pu._get_random_int_for_8bit_sr = b8
+        pu._get_random_noise_for_low_rank_ortho = sketch
 
     def take(self):
         d, self.draws = self.draws, []
@@ -84,6 +91,7 @@ class DrawRecorder:
     def restore(self):
         self.pu._get_random_int_for_sr = self._orig_sr
         self.pu._get_random_int_for_8bit_sr = self._orig_8
+        self.pu._get_random_noise_for_low_rank_ortho = self._orig_sk
 
 
 def make_params(shapes, dtype, seed, ln_ones=False):
@@ -210,6 +218,14 @@ CASES = {
                                  groups=[dict(shapes=[(64, 48), (40, 96)], optim_type="muon"),
                                          dict(shapes=[(48,)], optim_type="adam")],
                                  kw=dict(lr=1e-3, normuon_variant=True, approx_mars=True), steps=3),
+    # low-rank Newton-Schulz: Gaussian sketch, QR, projected chain
+    "muon_low_rank": dict(cls="Muon_adv", dtype="bf16",
+                          groups=[dict(shapes=[(96, 64), (64, 160), (40, 96)], optim_type="muon")],
+                          kw=dict(lr=1e-3, low_rank_ortho=True, ortho_rank=16), steps=2),
+    "adamuon_low_rank_cans": dict(cls="AdaMuon_adv", dtype="bf16",
+                                  groups=[dict(shapes=[(96, 64), (64, 160)], optim_type="muon")],
+                                  kw=dict(lr=1e-3, low_rank_ortho=True, ortho_rank=24, accelerated_ns=True),
+                                  steps=2),
     # AdaMuon's factored second moment (mu_vbuf_nmf / mv_vbuf_nmf)
     "adamuon_factored_2nd": dict(cls="AdaMuon_adv", dtype="bf16",
                                  groups=[dict(shapes=[(64, 48), (48, 96), (40, 30)], optim_type="muon")],
@@ -296,6 +312,11 @@ def run_case(name, spec, adv_optm, pu):
             # are stored as uint16.  `order_{s}` keeps the draw order.
             order = []
             for lab, idx, r in draws:
+                if lab == "sketch":
+                    # low-rank Newton-Schulz: the Gaussian sketch, in the update's dtype
+                    out[f"sk_{s}_{idx}"] = bits(r)
+                    order.append(f"{idx}:{lab}")
+                    continue
                 out[f"r_{s}_{idx}_{lab}"] = r.numpy().astype(np.uint16).reshape(-1)
                 order.append(f"{idx}:{lab}")
             out[f"order_{s}"] = np.array(json.dumps(order))

@@ -39,7 +39,11 @@ QUINTIC = (3.4445, -4.7750, 2.0315)
 
 def _draws(z, s, i):
     pre = f"r_{s}_{i}_"
-    return {k[len(pre):]: torch.from_numpy(z[k].astype(np.int32)).cuda() for k in z.files if k.startswith(pre)}
+    out = {k[len(pre):]: torch.from_numpy(z[k].astype(np.int32)).cuda() for k in z.files if k.startswith(pre)}
+    if f"sk_{s}_{i}" in z.files:
+        # the low-rank chain's Gaussian sketch (bf16 bits)
+        out["sketch"] = torch.from_numpy(z[f"sk_{s}_{i}"].view(np.int16).copy()).view(torch.bfloat16).cuda()
+    return out
 
 
 def check_ns_param(mine, ref, old, dt, what, adamuon=False):
@@ -323,3 +327,50 @@ def test_philox_mode_runs_and_is_deterministic():
     deq = outs[0][1].float().reshape(-1) * sc
     assert torch.all((deq - m_true).abs() <= sc * 1.0001 + 1e-12)
     assert not torch.equal(outs[0][0], p0)
+
+
+@pytest.mark.parametrize("adamuon", [False, True])
+def test_low_rank_with_device_sketch_matches_oracle(adamuon):
+    """Low-rank Newton-Schulz (ortho_rank 64) without injected noise: the
+    device draws its Gaussian sketch from Philox (advopt_lr_sketch, read back
+    here for the oracle), takes the QR by shifted CholeskyQR3 and runs the
+    chain on the [64][cols] projection; params within the chain's tolerance
+    of the oracle (which takes numpy's Householder QR) on a tall, a wide and
+    a ragged matrix.  The sketch itself is N(0, 1) to within sampling error."""
+    import ctypes
+    import advanced_optimizers_b200 as A
+    from advanced_optimizers_b200 import _lib as L
+    rng = np.random.default_rng(12)
+    shapes = [(1536, 512), (512, 1536), (300, 700)]
+    r = 64
+    ps0 = [O.round_bf16((rng.standard_normal(sh) * 0.02).astype(np.float32)) for sh in shapes]
+    params = [torch.nn.Parameter(torch.from_numpy(v.copy()).cuda().to(torch.bfloat16)) for v in ps0]
+    hp = _oracle_hp(adamuon, precision="auto", low_rank_ortho=True, ortho_rank=r, stochastic_rounding=False)
+    kw = dict(lr=hp["lr"], nesterov=hp["nesterov"], state_precision="auto", low_rank_ortho=True, ortho_rank=r,
+              stochastic_rounding=False)
+    if adamuon:
+        opt = A.AdaMuon_adv([dict(params=params, optim_type="muon")], betas=hp["betas"], **kw)
+    else:
+        opt = A.Muon_adv([dict(params=params, optim_type="muon")], beta1=hp["beta1"], **kw)
+    stream = torch.cuda.current_stream().cuda_stream
+    for i, (p, sh) in enumerate(zip(params, shapes)):
+        g = O.round_bf16((rng.standard_normal(sh) * 1e-3).astype(np.float32))
+        p.grad = torch.from_numpy(g.copy()).cuda().to(torch.bfloat16)
+        # the sketch the device draws for this tensor at step 0
+        sk = torch.empty((sh[1], min(r, *sh)), dtype=torch.bfloat16, device="cuda")
+        L.check(L.lib().advopt_lr_sketch(sk.data_ptr(), sk.shape[0], sk.shape[1], 42, opt._tid(p), 0, stream),
+                "advopt_lr_sketch")
+        skf = sk.float().cpu().numpy()
+        assert abs(skf.mean()) < 0.05 and abs(skf.std() - 1.0) < 0.05
+        st = {}
+        O.init_state_tensor(st, "momentum_buffer", sh, "auto", "bf16")
+        if adamuon:
+            O.init_state_tensor(st, "second_momentum_buffer", sh, "auto", "bf16", non_neg=True)
+        step_fn = O.adamuon_step if adamuon else O.muon_step
+        p._oracle = step_fn(ps0[i].copy(), "bf16", g, st, hp, {"sketch": O.bf16_bits(skf)})
+    opt.step()
+    torch.cuda.synchronize()
+    opt.check_errors()
+    for i, p in enumerate(params):
+        mine = p.detach().float().cpu().numpy()
+        check_ns_param(mine, p._oracle, ps0[i], "bf16", f"low rank {shapes[i]}", adamuon)
