@@ -434,13 +434,16 @@ def newton_schulz(G: torch.Tensor, steps: int = 5, eps: float | None = 1e-7,
                   coeffs: tuple[float, float, float] = (3.4445, -4.7750, 2.0315), cns: bool = False,
                   cns_a_bound: float | None = None, low_rank_ortho: bool = False, ortho_rank: int = 128,
                   G_sketch=None, compiled: bool = False) -> torch.Tensor:
-    """Muon_util.newton_schulz (Muon_util.py:193-283), standard path, on the
-    tcgen05 GEMM chain: X = bf16(G) (transposed if rows > cols), divided by
+    """Muon_util.newton_schulz (Muon_util.py:193-283) on the tcgen05 GEMM
+    chain: X = bf16(G) (transposed if rows > cols), divided by
     max(||X||_F, eps), then `steps` quintic or CANS iterations in bf16 with
-    fp32 accumulation; returns a new tensor in G's dtype."""
+    fp32 accumulation; returns a new tensor in G's dtype.  With
+    low_rank_ortho (bf16 G), the chain runs on Q^T G for the Q factor of
+    G @ G_sketch (a [cols][r] sketch; drawn N(0, 1) when None) and the result
+    is Q NS(Q^T G)."""
     global _NS_RUNNER
-    if low_rank_ortho:
-        raise NotImplementedError("low_rank_ortho is not supported by the B200 optimizer kernels")
+    if low_rank_ortho and G.dtype != torch.bfloat16:
+        raise NotImplementedError("low_rank_ortho needs a bf16 matrix on the B200 kernels")
     if G.ndim != 2:
         raise NotImplementedError("newton_schulz takes one 2-D matrix")
     require_cuda_tensor(G, "G")
@@ -455,8 +458,13 @@ def newton_schulz(G: torch.Tensor, steps: int = 5, eps: float | None = 1e-7,
     ws = _NS_RUNNER.workspace(G.device)
     m, n = min(rows, cols), max(rows, cols)
     m_pad, n_pad = round_up(m, NS_ALIGN), round_up(n, NS_ALIGN)
-    ws.ensure(numel, m_pad, n_pad)
-    ptrs = ws.pointers(numel, m_pad, n_pad)
+    r = min(int(ortho_rank), rows, cols) if low_rank_ortho else 0
+    if r > 0:
+        ws_m, ws_n = round_up(min(r, cols), NS_ALIGN), round_up(max(r, cols), NS_ALIGN)
+    else:
+        ws_m, ws_n = m_pad, n_pad
+    ws.ensure(numel, ws_m, ws_n)
+    ptrs = ws.pointers(numel, ws_m, ws_n)
     stream = stream_handle(G.device)
     a = L.MuonArgs()
     a.grad = ptr(G)
@@ -468,8 +476,14 @@ def newton_schulz(G: torch.Tensor, steps: int = 5, eps: float | None = 1e-7,
     a.flags = L.MU_TRANSPOSED if rows > cols else 0
     a.param_bf16 = 1 if G.dtype == torch.bfloat16 else 0
     lib = L.lib()
-    L.check(lib.advopt_muon_stage(ctypes.byref(a), 6, stream), "advopt_muon_stage (load)")
     bound = cns_a_bound if cns_a_bound is not None else default_cns_bound(rows, cols)
+    if r > 0:
+        a.flags |= L.MU_LOWRANK
+        a.seed = _NS_RUNNER.seed
+        L.check(lib.advopt_muon_stage(ctypes.byref(a), 6, stream), "advopt_muon_stage (X0)")
+        _NS_RUNNER._low_rank_chain(a, ws, ptrs, r, ws_m, ws_n, steps, coeffs, cns, bound, stream, G_sketch)
+        return out
+    L.check(lib.advopt_muon_stage(ctypes.byref(a), 6, stream), "advopt_muon_stage (load)")
     a.ns_result = run_ns_chain(ws, ptrs, m_pad, n_pad, steps, coeffs, cns, bound, stream)
     L.check(lib.advopt_muon_stage(ctypes.byref(a), 3, stream), "advopt_muon_stage (store)")
     return out if G.dtype == torch.bfloat16 else out.to(G.dtype)
