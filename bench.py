@@ -373,7 +373,8 @@ def run_ours(args):
     if not args.no_e2e:
         e2e = run_e2e(args, owned, step, world, dev, opt if world == 1 else None, sharded)
     ns = prodigy = None
-    if not (args.no_ns and args.no_prodigy):
+    if not (args.no_ns and args.no_prodigy and (world < 4 or args.no_70b)):
+        # the other legs need the memory of the AdamW leg
         del opt, opts, owned, params, step, sharded
         torch.cuda.empty_cache()
     if not args.no_ns:
