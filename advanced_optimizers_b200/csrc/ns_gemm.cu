@@ -29,6 +29,7 @@
 #include <cmath>
 #include <cstdio>
 #include <mutex>
+#include <unordered_map>
 #include <utility>
 
 #include "advopt.h"
@@ -350,8 +351,8 @@ int get_encode() {
 
 // 2-D bf16 tensor map: rows x cols row-major with leading dimension ld
 // (elements); box = box_cols x box_rows, 128-byte swizzle.
-int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
-             uint32_t box_rows) {
+int encode_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
+               uint32_t box_rows) {
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {ld * 2};
   const cuuint32_t box[2] = {box_cols, box_rows};
@@ -360,6 +361,49 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, u
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(ADVOPT_E_INVALID, "cuTensorMapEncodeTiled rejected a Newton-Schulz operand");
+  return ADVOPT_OK;
+}
+
+// The chain's operands are the same workspace buffers step after step, so
+// their tensor maps are encoded once and kept (a host-side cache keyed by
+// every encoding argument; cleared when it grows past 4096 entries).
+struct MapKey {
+  uintptr_t base;
+  uint64_t rows, cols, ld;
+  uint32_t box_cols, box_rows;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && ld == o.ld && box_cols == o.box_cols &&
+           box_rows == o.box_rows;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = k.base * 0x9E3779B97F4A7C15ull;
+    h ^= (k.rows * 0xC2B2AE3D27D4EB4Full) + (h << 6) + (h >> 2);
+    h ^= (k.cols * 0x165667B19E3779F9ull) + (h << 6) + (h >> 2);
+    h ^= (k.ld + ((uint64_t)k.box_cols << 32 | k.box_rows)) + (h << 6) + (h >> 2);
+    return (size_t)h;
+  }
+};
+
+int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
+             uint32_t box_rows) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  const MapKey key{reinterpret_cast<uintptr_t>(base), rows, cols, ld, box_cols, box_rows};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *map = it->second;
+      return ADVOPT_OK;
+    }
+  }
+  const int rc = encode_map(map, base, rows, cols, ld, box_cols, box_rows);
+  if (rc != ADVOPT_OK) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, *map);
   return ADVOPT_OK;
 }
 

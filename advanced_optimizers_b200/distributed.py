@@ -32,7 +32,7 @@ from typing import Callable, Iterable, Optional
 import torch
 import torch.distributed as dist
 
-from .optim._muon_family import is_suitable_for_muon, ns_flops
+from .optim._muon_family import is_suitable_for_muon, ns_time_estimate
 
 ALIGN_ELEMS = 64   # every parameter view starts on a 128-byte boundary (bf16)
 
@@ -50,17 +50,17 @@ def lpt_partition(costs, world: int):
     return owner
 
 
-# Rates that turn a tensor's work into seconds, so that Newton-Schulz matrices
-# and elementwise tensors of one optimizer are balanced on one scale: the
-# tcgen05 chain's sustained bf16 rate and the elementwise kernels' HBM rate.
-NS_FLOPS_PER_S = 1.1e15
+# The elementwise kernels' HBM rate, which turns a tensor's bytes into
+# seconds on the scale of the Newton-Schulz time estimate (ns_time_estimate:
+# waves of GEMM tiles, so that small matrices that fill few SMs weigh what
+# they take).
 HBM_BYTES_PER_S = 3.0e12
 
 
 def default_cost(optimizer_cls, group: dict, p: torch.Tensor) -> float:
     """Estimated seconds of the tensor's step: HBM bytes (param and grad, plus
     about as much again of state) at the elementwise kernels' rate, plus, for
-    the Muon family's matrices, the Newton–Schulz FLOPs at the chain's rate."""
+    the Muon family's matrices, the Newton–Schulz chain's estimated time."""
     elem = p.numel() * p.element_size() * 4 / HBM_BYTES_PER_S
     name = getattr(optimizer_cls, "__name__", "")
     if name in ("Muon_adv", "AdaMuon_adv") and p.ndim >= 2:
@@ -73,8 +73,8 @@ def default_cost(optimizer_cls, group: dict, p: torch.Tensor) -> float:
         if muon:
             rows = p.shape[0]
             cols = p.numel() // max(1, rows)
-            return elem + float(ns_flops(min(rows, cols), max(rows, cols), group.get("ns_steps", 5),
-                                         group.get("accelerated_ns", False))) / NS_FLOPS_PER_S
+            return elem + ns_time_estimate(min(rows, cols), max(rows, cols), group.get("ns_steps", 5),
+                                           group.get("accelerated_ns", False))
     return elem
 
 

@@ -173,6 +173,35 @@ def ns_flops_executed(m_pad: int, n_pad: int, steps: int, cns: bool) -> int:
     return steps * per_iter
 
 
+# the chain's GEMM tiles (128 x 256) per second on one SM at a full wave:
+# a sustained ~1.3 PFLOP/s over 148 SMs
+NS_TILE_FLOPS_PER_SM_S = 1.3e15 / 148
+NS_SMS = 148
+# per matrix: the chain's launches and the elementwise stages around it
+# (measured on B200: a 1024 x 4096 chain takes 0.42 ms in a step against
+# 0.23 ms of tile waves)
+NS_CHAIN_OVERHEAD_S = 0.19e-3
+
+
+def ns_time_estimate(m: int, n: int, steps: int, cns: bool) -> float:
+    """Seconds of the chain on an m x n matrix (m <= n), counted in waves of
+    the persistent GEMM's 128 x 256 tiles over 148 SMs: a small matrix (the
+    1024-row k / v projections) fills few SMs, which its FLOP count alone
+    does not show.  X X^T and b A + c A A run on the upper 256 x 256 blocks."""
+    m_pad, n_pad = round_up(m, NS_ALIGN), round_up(n, NS_ALIGN)
+    nb = m_pad // 256
+    sym_tiles = nb * (nb + 1)                   # 2 tiles of 128 x 256 per upper block
+
+    def gemm(tiles, k):
+        waves = -(-tiles // NS_SMS)
+        return waves * 2.0 * 128 * 256 * k / NS_TILE_FLOPS_PER_SM_S
+
+    per_iter = gemm(sym_tiles, n_pad) + gemm((m_pad // 128) * (n_pad // 256), m_pad)
+    if not cns:
+        per_iter += gemm(sym_tiles, m_pad)
+    return steps * per_iter + NS_CHAIN_OVERHEAD_S
+
+
 _DEVICE_WS = {}
 
 
