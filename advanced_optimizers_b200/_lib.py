@@ -192,6 +192,11 @@ def lib():
             "advopt_lr_gemm": ([P, P, P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, I32, P], ctypes.c_int),
             "advopt_lr_qr_work": ([ctypes.c_int64, ctypes.c_int64], ctypes.c_int64),
             "advopt_lr_qr": ([P, P, ctypes.c_int64, ctypes.c_int64, P, P], ctypes.c_int),
+            "advopt_ipc_get_handle": ([P, P, ctypes.POINTER(U64)], ctypes.c_int),
+            "advopt_ipc_open": ([P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+            "advopt_ipc_close": ([P], ctypes.c_int),
+            "advopt_enable_peer": ([I32], ctypes.c_int),
+            "advopt_copy_async": ([P, P, U64, P], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -224,7 +229,8 @@ def exported_symbols():
             "advopt_adam_occupancy", "advopt_adam_step_noalloc", "advopt_ns_gemm", "advopt_ns_gemm_sym", "advopt_muon_stage", "advopt_philox4x32_10",
             "advopt_noise_fill", "advopt_ns_chain", "advopt_kourkoutas_prepare", "advopt_kourkoutas_accumulate",
             "advopt_prodigy_scalars", "advopt_prodigy_update_d", "advopt_lr_sketch", "advopt_lr_gemm",
-            "advopt_lr_qr_work", "advopt_lr_qr"]
+            "advopt_lr_qr_work", "advopt_lr_qr", "advopt_ipc_get_handle", "advopt_ipc_open", "advopt_ipc_close",
+            "advopt_enable_peer", "advopt_copy_async"]
 
 
 _OCC_CACHE = {}

@@ -26,12 +26,14 @@ all-reduce (Prodigy_adv.py:550-554), which the Prodigy class keeps.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Callable, Iterable, Optional
 
 import torch
 import torch.distributed as dist
 
+from . import _lib as L
 from .optim._muon_family import is_suitable_for_muon, ns_time_estimate
 
 ALIGN_ELEMS = 64   # every parameter view starts on a 128-byte boundary (bf16)
@@ -123,6 +125,107 @@ class FlatParams:
         return works
 
 
+class PeerPull:
+    """The parameter gather on this GPU's copy engines: each rank maps the
+    other ranks' flat buffers (CUDA IPC) and pulls their segments with one
+    cudaMemcpyAsync per peer segment on a side stream, so the gather takes no
+    SMs from the step's kernels (an NCCL all-gather runs as kernels beside
+    them and slows them by about a quarter).
+
+    Ordering, with one 1-element NCCL all-reduce as a fence: after a bucket's
+    kernels, a fence on the side stream (every rank has written its segment)
+    precedes the pulls of that bucket; the caller's stream waits for the side
+    stream at the end of the step; a fence on the caller's stream at the
+    start of the next step (every rank has finished reading) precedes the
+    next writes to this rank's segments."""
+
+    def __init__(self, flats, world: int, rank: int, group, device):
+        self.world, self.rank, self.group = world, rank, group
+        lib = L.lib()
+        self.bases = []
+        self.peer = {}       # (bucket, buffer, rank) -> address of that rank's flat buffer
+        # every step below ends in an agreement among the ranks, so that a
+        # failure on one rank (no IPC for its allocations) makes all of them
+        # fall back together rather than diverge in their collectives
+        try:
+            local = []
+            for fp in flats:
+                row = []
+                for flat, seg in fp.buffers:
+                    h = ctypes.create_string_buffer(64)
+                    off = ctypes.c_uint64(0)
+                    L.check(lib.advopt_ipc_get_handle(flat.data_ptr(), h, ctypes.byref(off)), "advopt_ipc_get_handle")
+                    row.append((h.raw, int(off.value)))
+                local.append(row)
+        except Exception:
+            local = None
+        everyone = [None] * world
+        dist.all_gather_object(everyone, local, group=group)
+        if any(e is None for e in everyone):
+            raise RuntimeError("a rank cannot export its parameter buffers over CUDA IPC")
+        ok = True
+        try:
+            for q in range(world):
+                if q == rank:
+                    continue
+                for k, row in enumerate(everyone[q]):
+                    for j, (h, off) in enumerate(row):
+                        base = ctypes.c_void_p(0)
+                        L.check(lib.advopt_ipc_open(h, ctypes.byref(base)), "advopt_ipc_open")
+                        self.bases.append(base.value)
+                        self.peer[(k, j, q)] = base.value + off
+        except Exception:
+            ok = False
+        oks = [None] * world
+        dist.all_gather_object(oks, ok, group=group)
+        if not all(oks):
+            self.close()
+            raise RuntimeError("a rank cannot map the other ranks' parameter buffers")
+        self.flats = flats
+        self.side = torch.cuda.Stream(device)
+        self.fence = torch.zeros(1, dtype=torch.float32, device=device)
+
+    def begin_step(self):
+        """Fence on the caller's stream: every rank has finished pulling the
+        previous step's segments."""
+        dist.all_reduce(self.fence, group=self.group)
+
+    def pull_bucket(self, k: int):
+        """After bucket k's kernels (on the caller's stream): fence, then pull
+        the other ranks' segments of its buffers on the side stream."""
+        lib = L.lib()
+        self.side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.side):
+            dist.all_reduce(self.fence, group=self.group)
+            sh = self.side.cuda_stream
+            for j, (flat, seg) in enumerate(self.flats[k].buffers):
+                es = flat.element_size()
+                nbytes = seg * es
+                for q in range(self.world):
+                    if q == self.rank:
+                        continue
+                    L.check(lib.advopt_copy_async(flat.data_ptr() + q * nbytes, self.peer[(k, j, q)] + q * nbytes,
+                                                  nbytes, sh), "advopt_copy_async")
+
+    def end_step(self):
+        torch.cuda.current_stream().wait_stream(self.side)
+
+    def close(self):
+        if not self.bases:
+            return
+        torch.cuda.synchronize()
+        lib = L.lib()
+        for b in self.bases:
+            lib.advopt_ipc_close(b)
+        self.bases = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class LocalSegments:
     """Storage of this rank's tensors only, for runs whose parameters do not
     fit replicated on every rank: per gather bucket and dtype one flat
@@ -211,13 +314,16 @@ class ShardedOptimizer:
     the partition cost.  `bucket_bytes` sizes the gather buckets (None: one
     bucket, gathered after the whole step); with more than one bucket the
     elementwise kernels leave `reserve_sms` SMs free so that the all-gather of
-    the previous bucket runs beside them.  Every rank must call step() (it
-    ends in collectives)."""
+    the previous bucket runs beside them.  `gather`: "copy" pulls the other
+    ranks' segments of the replicated flat buffers with the copy engines over
+    CUDA IPC mappings (PeerPull), "nccl" all-gathers them with NCCL, "auto"
+    takes "copy" where every rank can map the others' buffers.  Every rank
+    must call step() (it ends in collectives)."""
 
     def __init__(self, optimizer_cls, params, *, process_group=None,
                  cost: Optional[Callable[[dict, torch.Tensor], float]] = None, flat: bool = True,
                  bucket_bytes: Optional[int] = 1 << 30, reserve_sms: int = 0, replicate_params: bool = True,
-                 device=None, gather_consumer=None, **kwargs):
+                 device=None, gather_consumer=None, gather: str = "auto", **kwargs):
         if not (dist.is_available() and dist.is_initialized()):
             raise RuntimeError("ShardedOptimizer needs an initialised torch.distributed process group")
         self.group = process_group
@@ -309,6 +415,16 @@ class ShardedOptimizer:
                 opt._carry_scale = 1.0 if self.rank == 0 else 0.0
                 opt._process_group = process_group
             self.optimizers.append(opt)
+        self.peer = None
+        if (self.world > 1 and self.flats and gather in ("auto", "copy")
+                and dist.get_backend(process_group) == "nccl"):
+            try:
+                self.peer = PeerPull(self.flats, self.world, self.rank, process_group,
+                                     self.flats[0].buffers[0][0].device)
+            except RuntimeError:
+                if gather == "copy":
+                    raise
+                self.peer = None
 
     def _materialize(self, p):
         i = next(k for k, q in enumerate(self.all_params) if q is p)
@@ -359,7 +475,12 @@ class ShardedOptimizer:
                 for w in self.local.all_gather(k, self.gather_consumer, async_op=self.gather_consumer is None):
                     w.wait()
             return
-        if self.flats:
+        if self.peer is not None:
+            self.peer.begin_step()
+            for k in range(len(self.flats)):
+                self.peer.pull_bucket(k)
+            self.peer.end_step()
+        elif self.flats:
             for f in self.flats:
                 f.all_gather()
         else:
@@ -382,6 +503,8 @@ class ShardedOptimizer:
             with torch.enable_grad():
                 loss = closure()
         works = []
+        if self.peer is not None:
+            self.peer.begin_step()
         for k, opt in enumerate(self.optimizers):
             if bucket_events is not None:
                 torch.cuda.current_stream().wait_event(bucket_events[k])
@@ -395,7 +518,9 @@ class ShardedOptimizer:
                     dist.all_reduce(torch.zeros(2, dtype=torch.float32, device=self.all_params[0].device),
                                     op=dist.ReduceOp.SUM, group=self.group)
                 self._empty_k += 1
-            if self.world > 1 and self.flats:
+            if self.peer is not None:
+                self.peer.pull_bucket(k)
+            elif self.world > 1 and self.flats:
                 works += self.flats[k].all_gather(async_op=True)
             elif self.world > 1 and self.local is not None:
                 # stream the bucket's gathered parameters through the transient
@@ -405,6 +530,8 @@ class ShardedOptimizer:
                 works += self.local.all_gather(k, self.gather_consumer, async_op=self.gather_consumer is None)
         for w in works:
             w.wait()
+        if self.peer is not None:
+            self.peer.end_step()
         if self.world > 1 and not self.flats and self.local is None:
             self.gather()
         return loss

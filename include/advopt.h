@@ -448,6 +448,18 @@ int advopt_lr_gemm(uint16_t* D, const uint16_t* A, const uint16_t* B, int64_t M,
 int64_t advopt_lr_qr_work(int64_t m, int64_t r);
 int advopt_lr_qr(uint16_t* Q, const uint16_t* A, int64_t m, int64_t r, double* work, void* stream);
 
+/* Peer copies for the sharded parameter gather (copy engines, no SMs):
+ *   advopt_ipc_get_handle  the CUDA IPC handle (64 bytes) of the allocation holding
+ *                          ptr, and ptr's byte offset in it
+ *   advopt_ipc_open        map another process's allocation; advopt_ipc_close unmaps it
+ *   advopt_enable_peer     peer access to another device of this process
+ *   advopt_copy_async      device-to-device cudaMemcpyAsync on `stream` */
+int advopt_ipc_get_handle(const void* ptr, void* handle_out, uint64_t* offset_out);
+int advopt_ipc_open(const void* handle, void** base_out);
+int advopt_ipc_close(void* base);
+int advopt_enable_peer(int32_t peer_device);
+int advopt_copy_async(void* dst, const void* src, uint64_t bytes, void* stream);
+
 /* Stages (one matrix per call sequence):
  *   0 momentum / X0 / norm / workspace load     6 the same for a bare Newton–Schulz call
  *   1 U store + RMS scale, 2 Muon update        3 U store only

@@ -2,8 +2,9 @@
 single-process step.  AdamW_adv (int8_sr + factored_2nd) and Muon_adv are
 bit-identical (Philox streams are keyed by the tensor's global index);
 Prodigy_adv's d is within 1e-5 relative (its two sums are all-reduced in a
-different order) and its params within 1 bf16 ulp.  Skipped with fewer than
-two GPUs."""
+different order) and its params within 1 bf16 ulp.  The gather runs on the
+copy engines (CUDA IPC pulls) by default; one case uses the NCCL all-gather.
+Skipped with fewer than two GPUs."""
 import io
 import os
 import socket
@@ -36,7 +37,8 @@ def _params(dev):
 def _make(name, params, sharded):
     import advanced_optimizers_b200 as A
     buckets = name.endswith("_buckets")
-    name = name.replace("_buckets", "")
+    nccl = "_nccl" in name
+    name = name.replace("_buckets", "").replace("_nccl", "")
     if name == "adamw":
         cls, args, kw = A.AdamW_adv, params, dict(state_precision="int8_sr", factored_2nd=True, nesterov=True)
     elif name == "prodigy":
@@ -48,6 +50,9 @@ def _make(name, params, sharded):
     if sharded:
         # small gather buckets: several asynchronous all-gathers per step
         extra = dict(bucket_bytes=256 << 10) if buckets else {}
+        if nccl:
+            # the NCCL all-gather instead of the copy-engine pulls
+            extra["gather"] = "nccl"
         return A.ShardedOptimizer(cls, args, **kw, **extra)
     return cls(args, **kw)
 
@@ -102,7 +107,7 @@ def _worker(rank, world, port, name, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("name", ["adamw", "muon", "prodigy", "adamw_buckets", "muon_buckets"])
+@pytest.mark.parametrize("name", ["adamw", "muon", "prodigy", "adamw_buckets", "muon_buckets", "adamw_nccl_buckets"])
 def test_sharded_matches_single_process(name):
     world = 2
     mgr = mp.Manager()
@@ -110,7 +115,7 @@ def test_sharded_matches_single_process(name):
     mp.spawn(_worker, args=(world, _free_port(), name, out), nprocs=world, join=True)
     ps, grads = _params(torch.device("cuda", 0))
     opt = _make(name, ps, False)
-    _run(name.replace("_buckets", ""), ps, grads, opt)
+    _run(name.replace("_buckets", "").replace("_nccl", ""), ps, grads, opt)
     ref = [p.detach().cpu() for p in ps]
     for r in range(world):
         for i, (a, b) in enumerate(zip(out[r], ref)):
