@@ -6,9 +6,10 @@ factored_2nd=True, nesterov=True) over Llama-3-8B parameter shapes in bf16
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Prints one JSON line (rank 0).  With N > 1 (torchrun) every rank owns a
-byte-balanced share of the tensors (per-tensor sharding) and steps only
-those, then the updated bf16 parameters are all-gathered over NCCL; the
-timed step includes that all-gather.  `--impl reference` times the CPU
+time-balanced share of the tensors (per-tensor sharding) and steps only
+those, then every rank pulls the others' updated bf16 parameters with its
+copy engines over NVLink (CUDA IPC mappings; NCCL fences order the pulls);
+the timed step includes that gather.  `--impl reference` times the CPU
 restatement of the reference's step (oracle/) on this host's cores.
 """
 from __future__ import annotations
@@ -64,19 +65,25 @@ def algorithmic_bytes(shapes):
 
 
 def sample_clocks_start(path):
+    """nvidia-smi sampling every 50 ms, started before the warm-up so that it
+    is running when the timed region begins; each sample carries its time."""
     try:
         f = open(path, "w")
         p = subprocess.Popen(
-            ["nvidia-smi", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+            ["nvidia-smi", "--query-gpu=timestamp,index,clocks.sm,clocks.max.sm,power.draw,"
+             "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-             "--format=csv,noheader,nounits", "-lms", "200"], stdout=f, stderr=subprocess.DEVNULL)
+             "--format=csv,noheader,nounits", "-lms", "50"], stdout=f, stderr=subprocess.DEVNULL)
         return p, f
     except Exception:
         return None, None
 
 
-def sample_clocks_stop(proc, f, path, gpu_index):
+def sample_clocks_stop(proc, f, path, gpu_index, t0=None, t1=None):
+    """Median SM clock and the throttle reasons seen between host times t0 and
+    t1 (the timed region); a region shorter than the sampling period takes
+    the sample nearest to it."""
+    import datetime
     if proc is None:
         return None
     proc.terminate()
@@ -85,24 +92,37 @@ def sample_clocks_stop(proc, f, path, gpu_index):
     except Exception:
         proc.kill()
     f.close()
-    sm, mx, reasons = [], [], set()
-    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    rows = []
     for line in open(path):
         parts = [x.strip() for x in line.split(",")]
-        if len(parts) < 9 or parts[0] != str(gpu_index):
+        if len(parts) < 10 or parts[1] != str(gpu_index):
             continue
         try:
-            sm.append(float(parts[1]))
-            mx.append(float(parts[2]))
+            ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            ts = None
+        try:
+            rows.append((ts, float(parts[2]), float(parts[3]), parts[6:10]))
         except ValueError:
             continue
-        for nm, val in zip(names, parts[5:9]):
+    if not rows:
+        return None
+    timed = [r for r in rows if r[0] is not None]
+    if t0 is None or len(timed) < len(rows):
+        inside = rows
+    else:
+        inside = [r for r in timed if t0 - 0.05 <= r[0] <= t1 + 0.05]
+        if not inside:
+            mid = 0.5 * (t0 + t1)
+            inside = [min(timed, key=lambda r: abs(r[0] - mid))]
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    reasons = set()
+    for r in inside:
+        for nm, val in zip(names, r[3]):
             if val.lower() == "active":
                 reasons.add(nm)
-    if not sm:
-        return None
-    return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(max(mx)), "reasons": sorted(reasons),
-            "samples": len(sm)}
+    return {"sm_mhz": float(np.median([r[1] for r in inside])), "sm_max_mhz": float(max(r[2] for r in inside)),
+            "reasons": sorted(reasons), "samples": len(inside)}
 
 
 def measured_peaks():
@@ -295,14 +315,14 @@ def run_ours(args):
         else:
             opt.step()
 
+    clock_path = os.path.join(tempfile.gettempdir(), f"advopt_clocks_{rank}.csv")
+    proc, fh = sample_clocks_start(clock_path)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
 
-    clock_path = os.path.join(tempfile.gettempdir(), f"advopt_clocks_{rank}.csv")
-    proc, fh = sample_clocks_start(clock_path)
     for o in opts:
         o._runner.kernel_events = []
     launches0 = sum(o._runner.launch_count for o in opts)
@@ -310,15 +330,18 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_clock0 = time.time()
     e0.record()
     for _ in range(args.steps):
         step()
     e1.record()
     torch.cuda.synchronize()
+    t_clock1 = time.time()
     if world > 1:
         dist.barrier()
     clocks = sample_clocks_stop(proc, fh, clock_path, torch.cuda.get_device_properties(dev).index
-                                if hasattr(torch.cuda.get_device_properties(dev), "index") else local)
+                                if hasattr(torch.cuda.get_device_properties(dev), "index") else local,
+                                t_clock0, t_clock1)
     elapsed_ms = e0.elapsed_time(e1)
     kev = [e for o in opts for e in o._runner.kernel_events]
     for o in opts:
@@ -808,8 +831,8 @@ def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, la
             "config": {"workload": WORKLOAD if (args.layers == 32 and not args.no_embed) else
                        f"profiling subset: {args.layers} layers" + ("" if not args.no_embed else ", no embeddings"),
                        "params": total, "tensors": len(shapes),
-                       "parallelism": f"per-tensor sharding x{world}" + (" + bucketed asynchronous bf16 all-gathers of the"
-                                                                 " flat params" if world > 1 else ""),
+                       "parallelism": f"per-tensor sharding x{world}" + (" + bucketed copy-engine pulls of the peers'"
+                                                                 " bf16 params (NVLink)" if world > 1 else ""),
                        "l2": "inputs larger than L2 (about 40 GB resident per step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": TRAFFIC_PER_ALG_BYTE * alg,
