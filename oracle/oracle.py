@@ -317,6 +317,55 @@ def nnmf(matrix):
     return mu, mv
 
 
+SHIFTER = np.array([1, 2, 4, 8, 16, 32, 64, 128], np.uint8)
+
+
+def pack_signs(mask):
+    """_pack_bools (factorization_util.py:87-95): bit j of byte b of row i is
+    column 8*b + j; the last byte of a row is zero-padded."""
+    mask = np.asarray(mask, bool)
+    d1, d2 = mask.shape
+    pd2 = (d2 + 7) // 8
+    pad = np.zeros((d1, pd2 * 8), np.uint8)
+    pad[:, :d2] = mask
+    return (pad.reshape(d1, pd2, 8) * SHIFTER).sum(axis=2, dtype=np.uint8)
+
+
+def unpack_signs(packed, d2):
+    """_unpack_bools (factorization_util.py:98-104)."""
+    packed = np.asarray(packed, np.uint8)
+    return ((packed[:, :, None] & SHIFTER[None, None, :]) != 0).reshape(packed.shape[0], -1)[:, :d2]
+
+
+def reconstruct_signed(mu, mv, sign, d2):
+    """_reconstruct_state(signed=True) (factorization_util.py:9-19):
+    outer(mu, mv), negated where the sign bit is clear."""
+    full = unnmf(mu, mv)
+    return np.where(unpack_signs(sign, d2), full, -full).astype(np.float32)
+
+
+def factorize_signed(m):
+    """_factorize_state(signed=True) (factorization_util.py:25-32):
+    (mu, mv, sign) of a full momentum; the sign bit is m > 0."""
+    m = np.asarray(m, np.float32)
+    sign = pack_signs(m > 0)
+    mu, mv = nnmf(np.abs(m))
+    return mu, mv, sign
+
+
+def init_factored(st, shape, has_m, m_keys=("mu_m_nmf", "mv_m_nmf", "sign")):
+    """The 'factored' state of one tensor (AdamW_adv.py:242-256): signed
+    rank-1 m (when betas[0] > 0) and rank-1 v over the effective shape."""
+    d1, d2 = effective_shape(int(np.prod(shape)))
+    st["factored"] = True
+    st["effective_shape"] = (d1, d2)
+    if has_m:
+        st[m_keys[0]] = np.zeros(d1, np.float32)
+        st[m_keys[1]] = np.zeros(d2, np.float32)
+        st[m_keys[2]] = np.zeros((d1, (d2 + 7) // 8), np.uint8)
+        st["shifter"] = SHIFTER.copy()
+
+
 # ---------------------------------------------------------------------------
 # weight decay and the final update (param_update.py:15-156)
 # ---------------------------------------------------------------------------
@@ -445,6 +494,70 @@ def _apply_weight_decay(pc: T, uc: T, state, scaled_wd, scaled_cwd, cautious, cw
     return pc
 
 
+def _rdiv(s, t: T) -> T:
+    """python scalar / tensor: torch evaluates it as reciprocal(t) * s."""
+    return T(f32(1.0) / t.v, t.dt).mul_s(s)
+
+
+def _state_vals(a):
+    return (from_bf16_bits(a), "bf16") if a.dtype == np.uint16 else (np.asarray(a, np.float32), "f32")
+
+
+def _store_like(a, v):
+    return bf16_bits(v).reshape(a.shape) if a.dtype == np.uint16 else np.asarray(v, np.float32).reshape(a.shape)
+
+
+def max_abs_normalization(upd: T, lr) -> T:
+    """scaled_optm.py:160-168: update * (lr / max(|update|)), in the update's dtype."""
+    norm = T(np.maximum(np.max(np.abs(upd.v)), f32(1e-12)).reshape(1), upd.dt)
+    return T(upd.v * _rdiv(lr, norm).v[0], upd.dt)
+
+
+def spectral_normalization(upd: T, state, lr, target_scale) -> T:
+    """scaled_optm.py:255-295: one power-iteration step on the update viewed
+    as (d_out, d_in) in the singular vectors' dtype, then
+    update * lr * target_scale / max(sigma, 1/(sqrt(d_out)+sqrt(d_in))).
+    The matrix-vector products and norms are summed in float64 and rounded
+    once to that dtype (the reference's accumulation order is not pinned)."""
+    u0, sdt = _state_vals(state["spectral_u"])
+    v0, _ = _state_vals(state["spectral_v"])
+    d_out = u0.size
+    d_in = upd.v.size // d_out
+    U = upd.to(sdt).v.reshape(d_out, d_in)
+    U64 = U.astype(np.float64)
+
+    def rnd(x):
+        return T(np.asarray(x, np.float32).reshape(-1), sdt).v
+
+    v_raw = rnd(U64.T @ u0.astype(np.float64))
+    v_norm = rnd(np.sqrt(np.sum(v_raw.astype(np.float64) ** 2)))[0]
+    cand_v = rnd(v_raw / np.maximum(v_norm, rnd(1e-8)[0]))
+    next_v = cand_v if v_norm >= 1e-6 else v0
+    state["spectral_v"] = _store_like(state["spectral_v"], next_v)
+    u_raw = rnd(U64 @ next_v.astype(np.float64))
+    u_norm = rnd(np.sqrt(np.sum(u_raw.astype(np.float64) ** 2)))[0]
+    cand_u = rnd(u_raw / np.maximum(u_norm, rnd(1e-8)[0]))
+    next_u = cand_u if u_norm >= 1e-6 else u0
+    state["spectral_u"] = _store_like(state["spectral_u"], next_u)
+    sigma = rnd(np.dot(next_u.astype(np.float64), u_raw.astype(np.float64)))[0]
+    eps = 1.0 / (math.sqrt(d_out) + math.sqrt(d_in))
+    sig = T(np.array([sigma if sigma >= eps else eps], np.float32), sdt)     # clamp_min_(eps)
+    scale = _rdiv(target_scale, sig).mul_s(lr)
+    return T(U.reshape(-1) * scale.v[0], sdt)
+
+
+def scale_update(shape, upd: T, lr, state) -> T:
+    """scale_update (scaled_optm.py:35-72) for params without DoRA / OFT /
+    LoRA markers: max-abs scaling for 1-D, spectral scaling with target
+    sqrt(d_out / d_in) otherwise."""
+    if len(shape) < 2:
+        return max_abs_normalization(upd, lr)
+    d_out = shape[0]
+    d_in = int(np.prod(shape)) // d_out
+    out = spectral_normalization(upd, state, lr, math.sqrt(d_out / d_in))
+    return T(out.v.reshape(upd.v.shape), out.dt)
+
+
 def fisher_wd_scaler(p: T, denom: T, atan2: bool):
     """update_util.py:15-36 (AdamW/Prodigy call it with eps=None)."""
     if atan2:
@@ -497,10 +610,18 @@ def init_anchor(p_vals, p_dt, mode):
 # ---------------------------------------------------------------------------
 
 def adamw_init_state(shape, p_dt, precision, factored_2nd, beta1, vector_reshape=False):
-    """AdamW_adv.py:221-277 (non-'factored' precisions)."""
+    """AdamW_adv.py:221-277.  Under 'factored' a 2-D (or larger) param keeps
+    signed rank-1 m and rank-1 v; a 1-D one float32 m and v."""
     st = {"step": 0}
     is_vector = len(shape) == 1 and not vector_reshape
     st["factored"] = False
+    if precision == "factored":
+        if not is_vector:
+            init_factored(st, shape, beta1 > 0)
+            st["mu_v_nmf"] = np.zeros(st["effective_shape"][0], np.float32)
+            st["mv_v_nmf"] = np.zeros(st["effective_shape"][1], np.float32)
+            return st
+        precision = "fp32"
     st["factored_2nd"] = bool(factored_2nd and not is_vector)
     if beta1 > 0:
         init_state_tensor(st, "exp_avg", shape, precision, p_dt)
@@ -529,6 +650,11 @@ def adam_family_step(p, p_dt, g, state, hp, noise, *, algo="adamw"):
     makes for them.  Returns new p values (and prodigy stats).
     """
     prec = hp["precision"]           # group['actual_state_precision']
+    grad_prec = prec
+    if prec == "factored":
+        # float32 states and math for every tensor of a 'factored' group
+        # (state_util.py:165-179; AdamW_adv.py:236-239)
+        prec = "fp32"
     beta1, beta2 = hp["betas"]
     step = state["step"]
     factored_2nd = state.get("factored_2nd", False)
@@ -551,7 +677,7 @@ def adam_family_step(p, p_dt, g, state, hp, noise, *, algo="adamw"):
         else:
             bc1, sqrt_bc2 = 1, 1
         step_size = hp["lr"] / bc1
-    grad = upcast(T(g, p_dt), prec)
+    grad = upcast(T(g, p_dt), grad_prec)
     shape = np.shape(p)
     if "kourkoutas" in hp:
         # the grad's squared norm for the next step's beta2 (AdamW_adv.py:336-338)
@@ -604,7 +730,50 @@ def adam_family_step(p, p_dt, g, state, hp, noise, *, algo="adamw"):
                 den = den.add_s(eps)
         return den
 
-    if algo == "auxadam":                     # Muon_AuxAdam.py:139-180
+    if state.get("factored", False):
+        # state_precision='factored' (AdamW_adv.py:342-399, Muon_AuxAdam.py:86-133,
+        # Prodigy_adv.py:387-434): m rebuilt from its signed rank-1 factors,
+        # v from its rank-1 factors, both refactorised after their update
+        d1, d2 = state["effective_shape"]
+        gv = T(grad.to("f32").v.reshape(d1, d2), "f32")
+        b2 = hp.get("beta2_dyn", beta2)
+
+        def fm(gin):
+            m = T(reconstruct_signed(state["mu_m_nmf"], state["mv_m_nmf"], state["sign"], d2), "f32")
+            if algo == "prodigy":
+                m = m.mul_s(beta1).add_alpha(gin, d * (1.0 - beta1))
+            else:
+                m = m.lerp(gin, 1.0 - beta1)
+            state["mu_m_nmf"], state["mv_m_nmf"], state["sign"] = factorize_signed(m.v)
+            if nesterov:
+                c = beta1 if nv_coef is None else nv_coef
+                m = m.lerp(gin, 1 - c)
+            return m
+
+        def fv():
+            v = T(unnmf(state["mu_v_nmf"], state["mv_v_nmf"]), "f32")
+            v = v.mul_s(b2).addcmul(gv, gv, (d * d * (1.0 - b2)) if algo == "prodigy" else (1.0 - b2))
+            state["mu_v_nmf"], state["mv_v_nmf"] = nnmf(np.abs(v.v))
+            return T(np.abs(v.v), "f32")
+
+        if algo == "adamw":
+            v = fv()
+            den = make_denom(v)
+            if normed:
+                gv = gv.atan2(den) if atan2 else gv.div(den)
+            upd = fm(gv) if use_mt else gv.clone()
+        else:
+            upd = fm(gv) if use_mt else None
+            v = fv()
+            den = make_denom(v)
+            if upd is None:
+                upd = gv.mul_s(d) if algo == "prodigy" else gv.clone()
+        if not normed:
+            upd = upd.atan2(den) if atan2 else upd.div(den)
+        upd = T(upd.v.reshape(shape), upd.dt)
+        den = T(den.v.reshape(shape), den.dt)
+        normed = True    # the division is done
+    elif algo == "auxadam":                   # Muon_AuxAdam.py:139-180
         upd = m_path(grad) if use_mt else grad.clone()
         v = v_path()
         den = make_denom(v)
@@ -631,7 +800,10 @@ def adam_family_step(p, p_dt, g, state, hp, noise, *, algo="adamw"):
     if hp.get("fisher_wd", False):
         wd_scaler = fisher_wd_scaler(T(p, p_dt), den, atan2)
     scaling = step_size * (4 / math.pi) if atan2 else step_size
-    upd = upd.mul_s(scaling)
+    if hp.get("spectral", False):
+        upd = scale_update(shape, upd, scaling, state)   # AdamW_adv.py:459-463
+    else:
+        upd = upd.mul_s(scaling)
 
     stats = None
     if algo == "prodigy":                      # Prodigy_adv.py:495-511
@@ -690,15 +862,41 @@ def prodigy_calculate_d(group, d_numerator, d_denom):
 # Lion_adv (Lion_adv.py:213-278, lion_k.py:5-24)
 # ---------------------------------------------------------------------------
 
+def lion_init_state(shape, p_dt, nnmf_factor, vector_reshape=False):
+    """Lion_adv.py:156-181: signed rank-1 m for 2-D params under nnmf_factor,
+    else m in the param dtype."""
+    st = {"step": 0}
+    if nnmf_factor and not (len(shape) == 1 and not vector_reshape):
+        init_factored(st, shape, True)
+    else:
+        st["factored"] = False
+        st["exp_avg"] = np.zeros(shape, np.uint16 if p_dt == "bf16" else np.float32)
+    return st
+
+
 def lion_step(p, p_dt, g, state, hp, noise):
     beta1, beta2 = hp["betas"]
     grad = T(g, p_dt)
-    m = T(from_bf16_bits(state["exp_avg"]) if state["exp_avg"].dtype == np.uint16 else state["exp_avg"], p_dt)
-    upd = grad.lerp(m, beta1)
-    m = m.lerp(grad, 1 - beta2)
-    state["exp_avg"] = bf16_bits(m.v) if p_dt == "bf16" else m.v.copy()
+    shape = np.shape(p)
+    if state.get("factored", False):
+        # Lion_adv.py:232-254: float32 grad, m from its signed rank-1 factors
+        d1, d2 = state["effective_shape"]
+        gv = T(grad.v.reshape(d1, d2), "f32")
+        m = T(reconstruct_signed(state["mu_m_nmf"], state["mv_m_nmf"], state["sign"], d2), "f32")
+        upd = gv.lerp(m, beta1)
+        m = m.lerp(gv, 1 - beta2)
+        state["mu_m_nmf"], state["mv_m_nmf"], state["sign"] = factorize_signed(m.v)
+        upd = T(upd.v.reshape(shape), "f32")
+    else:
+        m = T(from_bf16_bits(state["exp_avg"]) if state["exp_avg"].dtype == np.uint16 else state["exp_avg"], p_dt)
+        upd = grad.lerp(m, beta1)
+        m = m.lerp(grad, 1 - beta2)
+        state["exp_avg"] = bf16_bits(m.v) if p_dt == "bf16" else m.v.copy()
     upd = upd.sign()
-    upd = upd.mul_s(hp["lr"])
+    if hp.get("spectral", False):
+        upd = scale_update(shape, upd, hp["lr"], state)    # Lion_adv.py:273-276
+    else:
+        upd = upd.mul_s(hp["lr"])
     state["step"] = state.get("step", 0) + 1
     return apply_parameter_update(p, p_dt, upd, state, lr=hp["lr"], wd=hp.get("weight_decay", 0.0),
                                   cautious=hp.get("cautious_wd", False),

@@ -21,7 +21,7 @@ ADAMW_DEFAULTS = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, f
                       use_atan2=False, nesterov=False, nesterov_coef=None, normed_momentum=False,
                       centered_wd=0.0, centered_wd_mode="float8", state_precision="auto",
                       factored_2nd=False, kourkoutas_beta=False, beta2_min=0.9, ema_alpha=0.95,
-                      tiny_spike=1e-9, k_warmup_steps=0)
+                      tiny_spike=1e-9, k_warmup_steps=0, nnmf_factor=False, spectral_normalization=False)
 MUON_DEFAULTS = dict(lr=1e-3, beta1=0.95, weight_decay=0.0, cautious_wd=False, nesterov=True,
                      nesterov_coef=None, ns_steps=5, ns_eps=1e-7, ns_coeffs=(3.4445, -4.7750, 2.0315),
                      stochastic_rounding=True, rms_rescaling=True, state_precision="auto",
@@ -31,7 +31,8 @@ MUON_DEFAULTS = dict(lr=1e-3, beta1=0.95, weight_decay=0.0, cautious_wd=False, n
                      adam_nesterov_coef=None, adam_state_precision="auto", adam_factored_2nd=False,
                      adam_kourkoutas_beta=False, adam_beta2_min=0.9, adam_ema_alpha=0.95, adam_tiny_spike=1e-9,
                      adam_k_warmup_steps=0, normuon_variant=False, beta2_normuon=0.95, normuon_eps=1e-8,
-                     approx_mars=False, mars_gamma=0.025, low_rank_ortho=False, ortho_rank=128)
+                     approx_mars=False, mars_gamma=0.025, low_rank_ortho=False, ortho_rank=128,
+                     adam_nnmf_factor=False, adam_spectral_normalization=False)
 ADAMUON_DEFAULTS = dict(MUON_DEFAULTS, betas=(0.95, 0.95), eps=1e-8, use_atan2=False, factored_2nd=False,
                         kappa_p=1.0, auto_projection=True)
 PRODIGY_DEFAULTS = dict(lr=1.0, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, fisher_wd=False,
@@ -41,7 +42,8 @@ PRODIGY_DEFAULTS = dict(lr=1.0, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, 
                         slice_p=11, prodigy_steps=0, d_limiter=False, centered_wd=0.0,
                         centered_wd_mode="float8", kourkoutas_beta=False, beta2_min=0.9, ema_alpha=0.95,
                         tiny_spike=1e-9, k_warmup_steps=0)
-LION_DEFAULTS = dict(lr=1e-4, betas=(0.9, 0.99), weight_decay=0.0, cautious_wd=False, stochastic_rounding=True)
+LION_DEFAULTS = dict(lr=1e-4, betas=(0.9, 0.99), weight_decay=0.0, cautious_wd=False, stochastic_rounding=True,
+                     nnmf_factor=False, spectral_normalization=False)
 
 
 def list_cases():
@@ -96,12 +98,23 @@ def _adam_hp(kw, aux=False, precision=None):
                     stochastic_rounding=d["stochastic_rounding"], use_atan2=d["adam_use_atan2"],
                     nesterov=d["adam_nesterov"], nesterov_coef=d["adam_nesterov_coef"],
                     centered_wd=d["centered_wd"], centered_wd_mode=d["centered_wd_mode"],
-                    precision=d["adam_state_precision"], factored_2nd=d["adam_factored_2nd"])
+                    precision="factored" if d["adam_nnmf_factor"] else d["adam_state_precision"],
+                    factored_2nd=d["adam_factored_2nd"], spectral=d["adam_spectral_normalization"])
     d = dict(ADAMW_DEFAULTS)
     d.update(kw)
     d["betas"] = tuple(d["betas"])
-    d["precision"] = d["state_precision"]
+    d["precision"] = "factored" if d["nnmf_factor"] else d["state_precision"]
+    d["spectral"] = d["spectral_normalization"]
     return d
+
+
+def inject_initial(z, states):
+    """States the reference draws at construction (the spectral singular
+    vectors, from its torch generator) are taken from the fixture."""
+    for i, st in enumerate(states):
+        for key in ("spectral_u", "spectral_v"):
+            if f"st0_{i}_{key}" in z.files:
+                st[key] = np.array(z[f"st0_{i}_{key}"])
 
 
 def replay(name, steps=None, pin_d=False, teacher=False):
@@ -174,7 +187,8 @@ def replay(name, steps=None, pin_d=False, teacher=False):
             kk = O.Kourkoutas(shapes, hp["betas"][1], hp["beta2_min"], hp["ema_alpha"], hp["tiny_spike"],
                               hp["k_warmup_steps"])
         hp["betas"] = tuple(hp["betas"])
-        hp["precision"] = hp["state_precision"]
+        hp["precision"] = "factored" if hp.get("nnmf_factor") else hp["state_precision"]
+        hp["spectral"] = hp.get("spectral_normalization", False)
         group = dict(d=hp["d0"], d0=hp["d0"], d_max=hp["d0"], d_numerator=0.0, d_coef=hp["d_coef"],
                      growth_rate=hp["growth_rate"], d_limiter=hp["d_limiter"], k=0,
                      prodigy_steps=hp["prodigy_steps"],
@@ -192,10 +206,12 @@ def replay(name, steps=None, pin_d=False, teacher=False):
         hp = dict(LION_DEFAULTS)
         hp.update(kw)
         hp["betas"] = tuple(hp["betas"])
+        hp["spectral"] = hp["spectral_normalization"]
         for i, sh in enumerate(shapes):
-            states.append({"step": 0, "exp_avg": np.zeros(sh, np.uint16 if dt == "bf16" else np.float32)})
+            states.append(O.lion_init_state(sh, dt, hp["nnmf_factor"]))
     else:
         raise KeyError(cls)
+    inject_initial(z, states)
 
     d_num_carry = np.float32(0.0)
     for s in range(nsteps):

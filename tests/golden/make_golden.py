@@ -255,6 +255,46 @@ CASES = {
                       kw=dict(lr=1e-4, weight_decay=0.01), steps=3),
     "lion_fp32_cautious": dict(cls="Lion_adv", dtype="f32", shapes=[(64, 32), (32,)],
                                kw=dict(lr=1e-4, weight_decay=0.1, cautious_wd=True), steps=3),
+    # state_precision='factored': m as signed rank-1 factors (1-bit sign), v as
+    # rank-1 factors; 1-D params keep fp32 states.  Effective shapes (150, 140),
+    # (64, 64), (40, 33) (a ragged last sign byte) and a 3-D param.
+    "adamw_factored_bf16": dict(cls="AdamW_adv", dtype="bf16",
+                                shapes=[(300, 70), (64, 64), (96,), (40, 33), (8, 4, 3)],
+                                kw=dict(state_precision="factored", nesterov=True, weight_decay=0.01),
+                                steps=3, outliers=True),
+    "adamw_factored_f32_atan2": dict(cls="AdamW_adv", dtype="f32", shapes=[(64, 48), (50,), (40, 33)],
+                                     kw=dict(nnmf_factor=True, use_atan2=True, cautious_wd=True,
+                                             weight_decay=0.05), steps=3),
+    "adamw_factored_normed": dict(cls="AdamW_adv", dtype="bf16", shapes=[(64, 48), (50,)],
+                                  kw=dict(state_precision="factored", betas=(0.9, 0.99), normed_momentum=True),
+                                  steps=3),
+    "prodigy_factored_bf16": dict(cls="Prodigy_adv", dtype="bf16", shapes=[(120, 40), (40,), (40, 33)],
+                                  kw=dict(state_precision="factored", d0=1e-6, slice_p=11, nesterov=True),
+                                  steps=3, log_scale=True),
+    "lion_factored_bf16": dict(cls="Lion_adv", dtype="bf16", shapes=[(64, 32), (32,), (40, 33)],
+                               kw=dict(lr=1e-4, weight_decay=0.01, nnmf_factor=True), steps=3),
+    "lion_factored_f32_cautious": dict(cls="Lion_adv", dtype="f32", shapes=[(64, 48), (40, 33)],
+                                       kw=dict(lr=1e-4, weight_decay=0.1, cautious_wd=True, nnmf_factor=True),
+                                       steps=3),
+    "muon_aux_factored": dict(cls="Muon_adv", dtype="bf16",
+                              groups=[dict(shapes=[(64, 48)], optim_type="muon"),
+                                      dict(shapes=[(100, 32), (48,), (40, 33)], optim_type="adam")],
+                              kw=dict(lr=1e-3, adam_state_precision="factored", adam_nesterov=True), steps=3),
+    # spectral normalisation (one power-iteration step per 2-D update, max-abs
+    # scaling for 1-D updates); the initial singular vectors are recorded in st0
+    "adamw_spectral_bf16": dict(cls="AdamW_adv", dtype="bf16", shapes=[(64, 48), (48,), (40, 96), (8, 4, 3)],
+                                kw=dict(state_precision="auto", spectral_normalization=True, weight_decay=0.01),
+                                steps=3),
+    "adamw_spectral_factored_f32": dict(cls="AdamW_adv", dtype="f32", shapes=[(64, 48), (50,)],
+                                        kw=dict(state_precision="factored", spectral_normalization=True,
+                                                cautious_wd=True, weight_decay=0.05), steps=3),
+    "lion_spectral_bf16": dict(cls="Lion_adv", dtype="bf16", shapes=[(64, 32), (32,)],
+                               kw=dict(lr=1e-4, weight_decay=0.01, spectral_normalization=True), steps=3),
+    "muon_aux_spectral": dict(cls="Muon_adv", dtype="bf16",
+                              groups=[dict(shapes=[(64, 48)], optim_type="muon"),
+                                      dict(shapes=[(100, 32), (48,)], optim_type="adam")],
+                              kw=dict(lr=1e-3, adam_state_precision="fp32", adam_spectral_normalization=True),
+                              steps=3),
 }
 
 

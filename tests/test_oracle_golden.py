@@ -94,6 +94,15 @@ def test_oracle_matches_reference(name):
             what = f"{name} step {s} param {i} {key}"
             if key in ("shifter", "anchor_data", "anchor_scale", "anchor_min"):
                 np.testing.assert_array_equal(val.reshape(-1), ref.reshape(-1), err_msg=what)
+            elif key in ("spectral_u", "spectral_v"):
+                # unit vectors from matrix-vector products whose summation
+                # order the reference does not fix: within 1e-5 (fp32) or
+                # 1 bf16 ulp of the largest element
+                vv = O.from_bf16_bits(val) if val.dtype == np.uint16 else val
+                rr = O.from_bf16_bits(ref) if ref.dtype == np.uint16 else ref
+                tol = (2.0 ** -8 if val.dtype == np.uint16 else 1e-5) * np.max(np.abs(rr))
+                err = np.max(np.abs(np.asarray(vv, np.float64) - np.asarray(rr, np.float64)))
+                assert err <= tol, f"{what}: max error {err:.3g} above {tol:.3g}"
             elif is_ns_param and key.startswith(("second_momentum_buffer", "normuon_v", "mu_vbuf_nmf", "mv_vbuf_nmf")):
                 # statistics of the Newton-Schulz output (bf16 GEMM chain)
                 if val.dtype in (np.int8, np.uint8):
