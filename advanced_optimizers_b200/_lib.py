@@ -15,7 +15,7 @@ import numpy as np
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_PKG, "libadvopt.so")
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 # ---- constants mirrored from include/advopt.h ----
 DT_F32, DT_BF16 = 0, 1
@@ -34,18 +34,24 @@ F_FISHER_STATS = 1 << 9
 F_ANCHORS = 1 << 10
 F_NO_WD = 1 << 11
 F_GRAD_SQ = 1 << 12
+F_EMIT_UPDATE = 1 << 13
+F_FACT_M = 1 << 14
 T_FACTORED = 1 << 0
 T_VEC = 1 << 1
 T_P0_SCALAR = 1 << 2
+T_FACT_M = 1 << 3
 T_ANCHOR_SHIFT = 4
+T_UPD_BF16 = 1 << 7
 ANCHOR = {"none": 0, "full": 1, "float8": 2, "int8": 3, "int4": 4}
 
-# advopt_adam_tensor (192 bytes)
+# advopt_adam_tensor (232 bytes)
 ADAM_TENSOR_DT = np.dtype([
     ("param", "<u8"), ("grad", "<u8"), ("exp_avg", "<u8"), ("exp_avg_scale", "<u8"),
     ("exp_avg_sq", "<u8"), ("exp_avg_sq_scale", "<u8"), ("row_factor", "<u8"), ("col_factor", "<u8"),
     ("col_partial", "<u8"), ("aux0", "<u8"), ("aux1", "<u8"), ("aux2", "<u8"),
     ("noise_v", "<u8"), ("noise_m", "<u8"), ("noise_p", "<u8"),
+    ("m_row_factor", "<u8"), ("m_col_factor", "<u8"), ("m_col_partial", "<u8"), ("m_sign", "<u8"),
+    ("update_out", "<u8"),
     ("numel", "<i8"), ("d1", "<i8"), ("d2", "<i8"),
     ("step_size", "<f4"), ("sqrt_bc2", "<f4"), ("eps", "<f4"), ("wd", "<f4"), ("cwd", "<f4"),
     ("fisher_clip", "<f4"),

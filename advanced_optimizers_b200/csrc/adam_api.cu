@@ -5,29 +5,35 @@
 namespace advopt {
 
 // ---------------------------------------------------------------------------
-// factored_2nd finish: column sums from the partials, then normalise one
-// factor (factorization_util.py:60-80).  Kernel A sums partial rows in slot
-// order (float64) into mv; kernel B normalises mu (d1 < d2) or mv by its total.
-// Both leave the factors untouched when the step's error word is set: a CTA
-// whose bounded wait gave up has not written its column partials.
+// factored_2nd / 'factored' finish: column sums from the partials, then
+// normalise one factor (factorization_util.py:60-80).  Kernel A sums partial
+// rows in slot order (float64) into mv; kernel B normalises mu (d1 < d2) or
+// mv by its total.  blockIdx.z / blockIdx.y = 1 does the same for the signed
+// momentum's |m| factors of ADVOPT_T_FACT_M tensors.  Both leave the factors
+// untouched when the step's error word is set: a CTA whose bounded wait gave
+// up has not written its column partials.
 // ---------------------------------------------------------------------------
 __global__ void factored_cols_kernel(const advopt_adam_tensor* tensors, const int32_t* index, const int32_t* err) {
   if (err && *err) return;
   const advopt_adam_tensor* t = tensors + index[blockIdx.y];
+  const bool mom = blockIdx.z == 1;
+  if (mom && (!(t->flags & ADVOPT_T_FACT_M) || !t->m_col_partial)) return;
   const int64_t d2 = t->d2;
   const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= d2) return;
   double acc = 0.0;
-  const float* src = t->col_partial + j;
+  const float* src = (mom ? t->m_col_partial : t->col_partial) + j;
   for (int s = 0; s < t->n_slots; ++s) acc += (double)src[(int64_t)s * d2];
-  t->col_factor[j] = (float)acc;
+  (mom ? t->m_col_factor : t->col_factor)[j] = (float)acc;
 }
 
 __global__ void factored_norm_kernel(const advopt_adam_tensor* tensors, const int32_t* index, const int32_t* err) {
   if (err && *err) return;
   const advopt_adam_tensor* t = tensors + index[blockIdx.x];
+  const bool mom = blockIdx.y == 1;
+  if (mom && (!(t->flags & ADVOPT_T_FACT_M) || !t->m_col_partial)) return;
   const int64_t d1 = t->d1, d2 = t->d2;
-  float* vec = d1 < d2 ? t->row_factor : t->col_factor;
+  float* vec = mom ? (d1 < d2 ? t->m_row_factor : t->m_col_factor) : (d1 < d2 ? t->row_factor : t->col_factor);
   const int64_t n = d1 < d2 ? d1 : d2;
   __shared__ double part[32];
   double acc = 0.0;
@@ -233,17 +239,21 @@ extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
   if (L->smem_floats < 0 || L->smem_floats > 56832)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: shared memory request above 227 KB (factored d2 too large)");
   if (L->stages < 0 || L->stages > 4) return set_error(ADVOPT_E_INVALID, "advopt_adam_step: stages must be 0..4");
+  if ((L->flags & ADVOPT_F_FACT_M) && L->precision != ADVOPT_PREC_FP32)
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: factored momentum needs ADVOPT_PREC_FP32");
+  if ((L->flags & ADVOPT_F_EMIT_UPDATE) && (L->flags & (ADVOPT_F_FISHER | ADVOPT_F_FISHER_STATS)))
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: update emission with Fisher weight decay");
   return check_cuda(run_adam(*L, static_cast<cudaStream_t>(stream)), "advopt_adam_step");
 }
 
 namespace advopt {
 cudaError_t run_factored_finish(const advopt_adam_tensor* tensors, const int32_t* index, int n_factored, int max_d2,
                                 const int32_t* err, cudaStream_t s) {
-  dim3 ga((unsigned)((max_d2 + 255) / 256), (unsigned)n_factored);
+  dim3 ga((unsigned)((max_d2 + 255) / 256), (unsigned)n_factored, 2u);
   factored_cols_kernel<<<ga, 256, 0, s>>>(tensors, index, err);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  factored_norm_kernel<<<n_factored, 1024, 0, s>>>(tensors, index, err);
+  factored_norm_kernel<<<dim3((unsigned)n_factored, 2u), 1024, 0, s>>>(tensors, index, err);
   return cudaGetLastError();
 }
 }  // namespace advopt

@@ -52,6 +52,11 @@ struct TensorRegs {
   const int32_t* nz_v;
   const int32_t* nz_m;
   const int32_t* nz_p;
+  float* mrow;
+  float* mcol;
+  float* mcolpart;
+  uint8_t* msign;
+  void* upd;
   int64_t numel, d1, d2;
   float step_size, sqrt_bc2, eps, wd, cwd, fisher_clip;
   uint32_t tensor_id, step, flags, slice_p;
@@ -62,6 +67,8 @@ __device__ __forceinline__ void load_tensor(const advopt_adam_tensor* t, TensorR
   r.v = t->exp_avg_sq; r.v_scale = t->exp_avg_sq_scale; r.row = t->row_factor; r.col = t->col_factor;
   r.colpart = t->col_partial; r.aux0 = t->aux0; r.aux1 = t->aux1; r.aux2 = t->aux2;
   r.nz_v = t->noise_v; r.nz_m = t->noise_m; r.nz_p = t->noise_p;
+  r.mrow = t->m_row_factor; r.mcol = t->m_col_factor; r.mcolpart = t->m_col_partial; r.msign = t->m_sign;
+  r.upd = t->update_out;
   r.numel = t->numel; r.d1 = t->d1; r.d2 = t->d2;
   r.step_size = t->step_size; r.sqrt_bc2 = t->sqrt_bc2; r.eps = t->eps; r.wd = t->wd; r.cwd = t->cwd;
   r.fisher_clip = t->fisher_clip;
@@ -230,6 +237,10 @@ struct Raw {
   Words<StoreBytes<kStore>::v> m, v;
   float mv[8];
   float mu, ms, vs;
+  // signed rank-1 momentum (fast factored path): the thread's sign byte and factors
+  float fmv[8];
+  float fmu;
+  uint32_t fsgn;
 };
 
 struct ChunkPos {
@@ -241,7 +252,8 @@ struct ChunkPos {
 
 template <int PREC, bool PBF, int ALGO, bool EXT>
 __device__ __forceinline__ void load_raw(const TensorRegs& T, const ChunkPos& cp, int tid, bool fact, bool ffast,
-                                         bool has_m, bool vec, Raw<PBF, StateTraits<PREC, PBF>::kStore>& R) {
+                                         bool has_m, bool vec, bool factm,
+                                         Raw<PBF, StateTraits<PREC, PBF>::kStore>& R) {
   constexpr int kStore = StateTraits<PREC, PBF>::kStore;
   constexpr int SB = StoreBytes<kStore>::v;
   const int64_t k0 = cp.cs + tid * kVec;
@@ -250,7 +262,20 @@ __device__ __forceinline__ void load_raw(const TensorRegs& T, const ChunkPos& cp
   const int64_t blk = cp.cs >> 11;
   ld_words<PBF ? 2 : 4>(T.grad, k0, nv, v8, R.g);
   ld_words<PBF ? 2 : 4>(T.param, k0, nv, v8, R.p);
-  if (has_m) {
+  if (factm) {
+    // signed rank-1 momentum: the generic path reads its factors per element
+    if (ffast) {
+      const int64_t cc = cp.c0 + tid * kVec;
+      const bool second = cc >= T.d2;
+      const int64_t col = second ? cc - T.d2 : cc;
+      R.fmu = nv > 0 ? T.mrow[cp.r0 + (second ? 1 : 0)] : 0.0f;
+      R.fsgn = nv > 0 ? (uint32_t)T.msign[k0 >> 3] : 0u;    // 8 elements = one sign byte
+      const float4 a = *reinterpret_cast<const float4*>(T.mcol + col);
+      const float4 b = *(reinterpret_cast<const float4*>(T.mcol + col) + 1);
+      R.fmv[0] = a.x; R.fmv[1] = a.y; R.fmv[2] = a.z; R.fmv[3] = a.w;
+      R.fmv[4] = b.x; R.fmv[5] = b.y; R.fmv[6] = b.z; R.fmv[7] = b.w;
+    }
+  } else if (has_m) {
     ld_words<SB>(T.m, k0, nv, v8, R.m);
     if (kStore == 2) R.ms = T.m_scale[blk];
   }
@@ -377,7 +402,13 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
   float* colacc = reinterpret_cast<float*>(dsm4);
   float* vbuf = colacc + L.gen_offset;
   float* segs = vbuf + kChunk;
-  __shared__ float red[2][kWarps][4];         // per-chunk block reductions (double-buffered)
+  // signed rank-1 momentum ('factored' launches, fp32 only): the same three
+  // areas again for |m|, after the second moment's
+  constexpr bool kFM = PREC == ADVOPT_PREC_FP32;
+  float* colacc_m = colacc + L.gen_offset + 2 * kChunk + 4;
+  float* mbuf = colacc_m + L.gen_offset;
+  float* msegs = mbuf + kChunk;
+  __shared__ float red[2][kWarps][6];         // per-chunk block reductions (double-buffered)
   __shared__ double dred[kWarps][2];
   __shared__ TensorRegs Ts;                   // the piece's tensor descriptor
 
@@ -401,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
   const float beta1 = L.beta1, w_m = L.w_m, w_nest = L.w_nest, c_m = pdev ? L.prodigy->c_m : L.c_m;
   float beta2 = L.beta2, c_v = c_v0;      // per tensor under Kourkoutas-beta
   const bool gsq = (F & ADVOPT_F_GRAD_SQ) && !fstats;
+  const bool emit = F & ADVOPT_F_EMIT_UPDATE;
   __shared__ double gred[kWarps];
   auto Rm = [](float x) { return kMBF ? round_bf16(x) : x; };  // rounding of m / update / grad ops
   int parity = 0;
@@ -423,18 +455,27 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
     const bool vec = T.flags & ADVOPT_T_VEC;
     const bool has_anchor = EXT && (((T.flags >> ADVOPT_T_ANCHOR_SHIFT) & 7u) != 0);
     const bool fact_sums = fact && !fstats;   // factored row/column sums (skipped by the Fisher pass)
+    // signed rank-1 momentum (state_precision='factored', AdamW_adv.py:342-399)
+    const bool factm = kFM && has_m && fact && (T.flags & ADVOPT_T_FACT_M);
+    const bool fm_sums = factm && !fstats;
     const int64_t d2 = fact ? T.d2 : 1;
+    const int64_t pd2 = (d2 + 7) >> 3;        // sign bytes per row
     // fast factored path: each column at most once per chunk, each thread's 8
-    // elements in one row, 8-aligned factor columns
-    const bool ffast = fact && d2 >= kChunk && (d2 % 8) == 0 && ((reinterpret_cast<uintptr_t>(T.col) & 15) == 0);
+    // elements in one row (one sign byte), 8-aligned factor columns
+    const bool ffast = fact && d2 >= kChunk && (d2 % 8) == 0 && ((reinterpret_cast<uintptr_t>(T.col) & 15) == 0) &&
+                       (!factm || (reinterpret_cast<uintptr_t>(T.mcol) & 15) == 0);
+    const bool upd_bf16 = T.flags & ADVOPT_T_UPD_BF16;
     const bool vbf = kMBF && !fact;  // v math in bf16 ('auto' bf16, not factored)
     const float rcp_sbc2 = __frcp_rn(T.sqrt_bc2);
     const float step_size = T.step_size, eps = T.eps, sbc2 = T.sqrt_bc2, wd = T.wd, cwd = T.cwd;
     if (fact_sums) {
       for (int j = tid; j < (int)d2; j += kThreads) colacc[j] = 0.0f;
+      if (fm_sums)
+        for (int j = tid; j < (int)d2; j += kThreads) colacc_m[j] = 0.0f;
       __syncthreads();
     }
     double row_carry = 0.0;  // thread 0: running sum of the row in progress
+    double row_carry_m = 0.0;
     double st0 = 0.0, st1 = 0.0;
     const uint32_t slice_p = T.slice_p ? T.slice_p : 1u;
     // Prodigy: running remainder of this thread's first element mod slice_p
@@ -449,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
     cp.r0 = fact ? pc.begin / d2 : 0;
     cp.c0 = fact ? pc.begin - cp.r0 * d2 : 0;
     Raw<PBF, kStore> cur;
-    load_raw<PREC, PBF, ALGO, EXT>(T, cp, tid, fact, ffast, has_m, vec, cur);
+    load_raw<PREC, PBF, ALGO, EXT>(T, cp, tid, fact, ffast, has_m, vec, factm, cur);
 
     while (true) {
       // next chunk's position, and its loads in flight during this chunk
@@ -469,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
       Raw<PBF, kStore> nxt;
       if (has_next) {
         np.clen = (int)min((int64_t)kChunk, pc.end - np.cs);
-        load_raw<PREC, PBF, ALGO, EXT>(T, np, tid, fact, ffast, has_m, vec, nxt);
+        load_raw<PREC, PBF, ALGO, EXT>(T, np, tid, fact, ffast, has_m, vec, factm, nxt);
       }
 
       const int clen = cp.clen;
@@ -482,7 +523,30 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
       float g[8], p[8], m[8], vh[8];
       unpack8<PBF ? 2 : 4>(cur.g, g);
       unpack8<PBF ? 2 : 4>(cur.p, p);
-      if (has_m) {
+      if (factm) {
+        // _reconstruct_state(signed=True): outer(mu, mv), negated where the
+        // sign bit is clear (factorization_util.py:9-19)
+        if (ffast) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float a = __fmul_rn(cur.fmu, cur.fmv[e]);
+            m[e] = ((cur.fsgn >> e) & 1u) ? a : -a;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            m[e] = 0.0f;
+            if (e < nv) {
+              const int64_t cc = c0 + tid * kVec + e;
+              const int64_t dr = cc / d2;
+              const int64_t col = cc - dr * d2;
+              const float a = __fmul_rn(T.mrow[r0 + dr], T.mcol[col]);
+              const uint32_t byte = T.msign[(r0 + dr) * pd2 + (col >> 3)];
+              m[e] = ((byte >> (col & 7)) & 1u) ? a : -a;
+            }
+          }
+        }
+      } else if (has_m) {
         unpack8<SB, true>(cur.m, m);
         if (kStore == 2) {
 #pragma unroll
@@ -527,6 +591,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
       float m_new[8], v[8];
       float amax_m = 0.0f, vmax = 0.0f;
       uint32_t pout[8];
+      float uemit[8];
       if (gsq) {
         // torch.sum(grad.pow(2)) of the grad the step uses: squares in bf16
         // for a bf16 grad under 'auto' (Kourkoutas.py:241-245)
@@ -576,6 +641,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
           ui = (ALGO == ADVOPT_ALGO_PRODIGY) ? Rm(__fmul_rn(gi, d_f)) : gi;
         }
         if (!normed) ui = atan2m ? Rm(atan2f(ui, du)) : Rm(__fdiv_rn(ui, du));
+        if (emit) uemit[e] = ui;   // the update before its scaling (AdamW_adv.py:459-461)
         ui = Rm(__fmul_rn(ui, step_size));
         amax_m = fmaxf(amax_m, fabsf(m_new[e]));
         vmax = fmaxf(vmax, v[e]);
@@ -618,7 +684,16 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
           if (e < nv) slice_fetch<PBF>(T, k0, e, slice_p, si32, sl);
         }
       }
-      if (!fstats) {
+      if (emit) {
+        if (upd_bf16) {
+          uint32_t b[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) b[e] = f_to_bf16_rne(uemit[e]);
+          store8_bf16(T.upd, k0, nv, v8, b);
+        } else {
+          store8_f32(T.upd, k0, nv, v8, uemit);
+        }
+      } else if (!fstats) {
         if (PBF) {
           Words<2> o;
 #pragma unroll
@@ -676,17 +751,65 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
         }
       }
 
+      // ---- signed rank-1 momentum: sign bits, |m| row sums and column partials
+      // (_factorize_state(signed=True), factorization_util.py:25-32) ----
+      float mrs0 = 0.0f, mrs1 = 0.0f;
+      if (fm_sums) {
+        if (ffast) {
+          const int64_t cc = c0 + tid * kVec;
+          const bool second = cc >= d2;
+          const int64_t col = second ? cc - d2 : cc;
+          float am[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) am[e] = fabsf(m_new[e]);
+          if (nv > 0) {
+            uint32_t sb = 0u;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sb |= (m_new[e] > 0.0f ? 1u : 0u) << e;
+            T.msign[k0 >> 3] = (uint8_t)sb;
+            float4* ca = reinterpret_cast<float4*>(colacc_m + col);
+            float4 a = ca[0], b = ca[1];
+            a.x = __fadd_rn(a.x, am[0]); a.y = __fadd_rn(a.y, am[1]); a.z = __fadd_rn(a.z, am[2]); a.w = __fadd_rn(a.w, am[3]);
+            b.x = __fadd_rn(b.x, am[4]); b.y = __fadd_rn(b.y, am[5]); b.z = __fadd_rn(b.z, am[6]); b.w = __fadd_rn(b.w, am[7]);
+            ca[0] = a;
+            ca[1] = b;
+          }
+          const float s = __fadd_rn(__fadd_rn(__fadd_rn(am[0], am[1]), __fadd_rn(am[2], am[3])),
+                                    __fadd_rn(__fadd_rn(am[4], am[5]), __fadd_rn(am[6], am[7])));
+          if (second) mrs1 = s; else mrs0 = s;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (e < nv) {
+              mbuf[tid * kVec + e] = fabsf(m_new[e]);
+              // one atomic per element on the 4-byte word that holds its sign byte
+              const int64_t cc = c0 + tid * kVec + e;
+              const int64_t dr = cc / d2;
+              const int64_t col = cc - dr * d2;
+              const int64_t byte = (r0 + dr) * pd2 + (col >> 3);
+              unsigned int* w = reinterpret_cast<unsigned int*>(T.msign) + (byte >> 2);
+              const unsigned int bit = 1u << (((unsigned)(byte & 3) << 3) + (unsigned)(col & 7));
+              if (m_new[e] > 0.0f) atomicOr(w, bit); else atomicAnd(w, ~bit);
+            }
+          }
+        }
+      }
+
       // ---- block reductions (one barrier per chunk) ----
       {
         const float a = (has_m && kStore == 2) ? warp_max(amax_m) : 0.0f;
         const float b = (!fact && kStore == 2) ? warp_max(vmax) : 0.0f;
         const float c = ffast ? warp_sum(rsum0) : 0.0f;
         const float d = ffast ? warp_sum(rsum1) : 0.0f;
+        const float e5 = (ffast && fm_sums) ? warp_sum(mrs0) : 0.0f;
+        const float f6 = (ffast && fm_sums) ? warp_sum(mrs1) : 0.0f;
         if (lane == 0) {
           red[parity][warp][0] = a;
           red[parity][warp][1] = b;
           red[parity][warp][2] = c;
           red[parity][warp][3] = d;
+          red[parity][warp][4] = e5;
+          red[parity][warp][5] = f6;
         }
       }
       __syncthreads();
@@ -705,45 +828,62 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
               T.row[r0] = (float)row_carry;
               row_carry = (double)s1;
             }
-          }
-        } else {
-          // generic: each column's elements in this chunk, summed in order by
-          // the thread that owns its first occurrence
-          const int ncol = (int)min((int64_t)clen, d2);
-          for (int pp = tid; pp < ncol; pp += kThreads) {
-            float acc = 0.0f;
-            for (int q = pp; q < clen; q += (int)d2) acc = __fadd_rn(acc, vbuf[q]);
-            int64_t j = c0 + pp;
-            if (j >= d2) j -= d2;
-            colacc[j] = __fadd_rn(colacc[j], acc);
-          }
-          // rows: segment s covers chunk positions [max(0, s*d2-c0), min(clen, (s+1)*d2-c0))
-          const int nseg = (int)((c0 + clen - 1) / d2) + 1;
-          for (int s = warp; s < nseg; s += kWarps) {
-            const int64_t lo = max((int64_t)0, (int64_t)s * d2 - c0);
-            const int64_t hi = min((int64_t)clen, (int64_t)(s + 1) * d2 - c0);
-            float acc = 0.0f;
-            for (int64_t q = lo + lane; q < hi; q += 32) acc = __fadd_rn(acc, vbuf[q]);
-            acc = warp_sum(acc);
-            if (lane == 0) segs[s] = acc;
-          }
-          __syncthreads();
-          if (tid == 0) {
-            for (int s = 0; s < nseg; ++s) {
-              row_carry += (double)segs[s];
-              if ((int64_t)(s + 1) * d2 - c0 <= clen) {   // row r0+s ends in this chunk
-                T.row[r0 + s] = (float)row_carry;
-                row_carry = 0.0;
+            if (fm_sums) {
+              float m0 = 0.0f, m1 = 0.0f;
+#pragma unroll
+              for (int w = 0; w < kWarps; ++w) {
+                m0 = __fadd_rn(m0, red[parity][w][4]);
+                m1 = __fadd_rn(m1, red[parity][w][5]);
+              }
+              row_carry_m += (double)m0;
+              if (clen >= d2 - c0) {
+                T.mrow[r0] = (float)row_carry_m;
+                row_carry_m = (double)m1;
               }
             }
           }
-          __syncthreads();
+        } else {
+          // generic: each column's elements in this chunk, summed in order by
+          // the thread that owns its first occurrence; rows by segment
+          auto gen_sums = [&](const float* buf, float* cacc, float* sg, float* rowp, double& carry) {
+            const int ncol = (int)min((int64_t)clen, d2);
+            for (int pp = tid; pp < ncol; pp += kThreads) {
+              float acc = 0.0f;
+              for (int q = pp; q < clen; q += (int)d2) acc = __fadd_rn(acc, buf[q]);
+              int64_t j = c0 + pp;
+              if (j >= d2) j -= d2;
+              cacc[j] = __fadd_rn(cacc[j], acc);
+            }
+            // rows: segment s covers chunk positions [max(0, s*d2-c0), min(clen, (s+1)*d2-c0))
+            const int nseg = (int)((c0 + clen - 1) / d2) + 1;
+            for (int s = warp; s < nseg; s += kWarps) {
+              const int64_t lo = max((int64_t)0, (int64_t)s * d2 - c0);
+              const int64_t hi = min((int64_t)clen, (int64_t)(s + 1) * d2 - c0);
+              float acc = 0.0f;
+              for (int64_t q = lo + lane; q < hi; q += 32) acc = __fadd_rn(acc, buf[q]);
+              acc = warp_sum(acc);
+              if (lane == 0) sg[s] = acc;
+            }
+            __syncthreads();
+            if (tid == 0) {
+              for (int s = 0; s < nseg; ++s) {
+                carry += (double)sg[s];
+                if ((int64_t)(s + 1) * d2 - c0 <= clen) {   // row r0+s ends in this chunk
+                  rowp[r0 + s] = (float)carry;
+                  carry = 0.0;
+                }
+              }
+            }
+            __syncthreads();
+          };
+          gen_sums(vbuf, colacc, segs, T.row, row_carry);
+          if (fm_sums) gen_sums(mbuf, colacc_m, msegs, T.mrow, row_carry_m);
         }
       }
 
       // ---- store the new moments (they need the block max) ----
       if (!fstats) {
-        if (has_m) {
+        if (has_m && !factm) {
           if (kStore == 2) {
             float bmax = 0.0f;
 #pragma unroll
@@ -803,6 +943,10 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
       __syncthreads();
       float* dst = T.colpart + (int64_t)pc.slot * d2;
       for (int j = tid; j < (int)d2; j += kThreads) dst[j] = colacc[j];
+      if (fm_sums) {
+        float* dm = T.mcolpart + (int64_t)pc.slot * d2;
+        for (int j = tid; j < (int)d2; j += kThreads) dm[j] = colacc_m[j];
+      }
       __syncthreads();
     }
     if (pstats || fstats) {
@@ -883,7 +1027,9 @@ cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
                               ADVOPT_F_ANCHORS);
   const bool nin = L.flags & ADVOPT_F_NOISE_IN;
   const size_t smem = (size_t)L.smem_floats * sizeof(float);
-  if (!ext && L.stages > 0) {
+  // signed rank-1 momentum and update emission live in the general kernel only
+  const bool general_only = L.flags & (ADVOPT_F_FACT_M | ADVOPT_F_EMIT_UPDATE);
+  if (!ext && !general_only && L.stages > 0) {
     if (nin) {
       auto kf = adam_fast_kernel<PREC, PBF, ALGO, true, kCfDyn>;
       cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

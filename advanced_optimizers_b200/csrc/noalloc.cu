@@ -162,6 +162,9 @@ extern "C" int advopt_adam_step_noalloc(const advopt_adam_tensor* tensor, const 
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step_noalloc: per-piece grad sums are not supported here");
   if (hp.layer_beta2 && !hp.layer_of_tensor)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step_noalloc: layer_beta2 without layer_of_tensor");
+  if ((hp.flags & (ADVOPT_F_FACT_M | ADVOPT_F_EMIT_UPDATE)) || (t.flags & ADVOPT_T_FACT_M))
+    return set_error(ADVOPT_E_INVALID,
+                     "advopt_adam_step_noalloc: factored momentum and update emission are not supported here");
   const bool fact = t.flags & ADVOPT_T_FACTORED;
   const int64_t d2 = fact ? t.d2 : 0;
   if (fact && (t.d1 <= 0 || d2 <= 0 || t.d1 * d2 != t.numel))

@@ -95,10 +95,13 @@ class AdaMuon_adv(MuonFamilyBase):
         if adam_state_precision not in VALID_PRECISIONS:
             raise ValueError(f"adam_state_precision must be one of {VALID_PRECISIONS}. Got {adam_state_precision}")
         reject(orthogonal_gradient != "disabled" or adam_orthogonal_gradient != "disabled", "orthogonal_gradient")
+        # 'factored' on the orthogonalised path: the reference's factored AdaMuon path fails (original_shape unset, AdaMuon_adv.py:578,657)
         reject(state_precision in ("factored", "fp16"), f"state_precision='{state_precision}'")
-        reject(adam_state_precision in ("factored", "fp16") or adam_nnmf_factor,
-               f"adam_state_precision='{adam_state_precision}'")
-        reject(spectral_normalization or adam_spectral_normalization, "spectral_normalization")
+        reject(adam_state_precision == "fp16", "adam_state_precision='fp16'")
+        # spectral normalisation of the orthogonalised update: the reference
+        # calls it without its target_scale argument and fails
+        reject(spectral_normalization, "spectral_normalization")
+        reject(adam_spectral_normalization, "adam_spectral_normalization")
         reject(centered_wd, "centered_wd for AdaMuon_adv")
         reject(not auto_projection and kappa_p not in (1.0, 2.0), f"kappa_p={kappa_p}")
         defaults = {

@@ -144,7 +144,7 @@ class AdamW_adv(torch.optim.Optimizer):
         if "step" in state:
             return
         req = group["state_precision"]
-        group["actual_state_precision"] = req
+        group["actual_state_precision"] = "auto" if req == "factored" else req
         init_adam_state(p, state, precision=req, factored_2nd=group.get("factored_2nd", False),
                         beta1=group["betas"][0], vector_reshape=group["vector_reshape"],
                         centered_wd=group.get("centered_wd", 0.0),
@@ -153,7 +153,7 @@ class AdamW_adv(torch.optim.Optimizer):
 
     def _cfg(self, group):
         return AdamCfg(algo=L.ALGO_ADAMW, lr=group["lr"], betas=group["betas"], eps=group["eps"],
-                       weight_decay=group["weight_decay"], precision=group["actual_state_precision"],
+                       weight_decay=group["weight_decay"], precision="factored" if group["state_precision"] == "factored" else group["actual_state_precision"],
                        nesterov=group.get("nesterov", False), nesterov_coef=group.get("nesterov_coef"),
                        use_bias_correction=group["use_bias_correction"], use_atan2=group["use_atan2"],
                        normed_momentum=group.get("normed_momentum", False), cautious_wd=group.get("cautious_wd", False),

@@ -97,10 +97,13 @@ class Muon_adv(MuonFamilyBase):
         if adam_state_precision not in VALID_PRECISIONS:
             raise ValueError(f"adam_state_precision must be one of {VALID_PRECISIONS}. Got {adam_state_precision}")
         reject(orthogonal_gradient != "disabled" or adam_orthogonal_gradient != "disabled", "orthogonal_gradient")
+        # 'factored' on the orthogonalised path: the reference's factored Muon path never applies lr to the update (Muon_adv.py:463-503)
         reject(state_precision in ("factored", "fp16"), f"state_precision='{state_precision}'")
-        reject(adam_state_precision in ("factored", "fp16") or adam_nnmf_factor,
-               f"adam_state_precision='{adam_state_precision}'")
-        reject(spectral_normalization or adam_spectral_normalization, "spectral_normalization")
+        reject(adam_state_precision == "fp16", "adam_state_precision='fp16'")
+        # spectral normalisation of the orthogonalised update: the reference
+        # calls it without its target_scale argument and fails
+        reject(spectral_normalization, "spectral_normalization")
+        reject(adam_spectral_normalization, "adam_spectral_normalization")
         reject(centered_wd, "centered_wd for Muon_adv")
         defaults = {
             "lr": lr, "beta1": beta1, "weight_decay": weight_decay, "cautious_wd": cautious_wd,

@@ -284,7 +284,7 @@ class Prodigy_adv(torch.optim.Optimizer):
         if "step" in state:
             return
         req = group["state_precision"]
-        group["actual_state_precision"] = req
+        group["actual_state_precision"] = "auto" if req == "factored" else req
         init_adam_state(p, state, precision=req, factored_2nd=group.get("factored_2nd", False),
                         beta1=group["betas"][0], vector_reshape=group["vector_reshape"],
                         centered_wd=group.get("centered_wd", 0.0),
@@ -301,7 +301,7 @@ class Prodigy_adv(torch.optim.Optimizer):
         pd = dict(d=group.raw("d"), d0=group.raw("d0"), beta3=self.beta3, safeguard_warmup=group["safeguard_warmup"],
                   slice_p=group["slice_p"], stats=stats, dev=self._dblock)
         return AdamCfg(algo=L.ALGO_PRODIGY, lr=group["lr"], betas=group["betas"], eps=group["eps"],
-                       weight_decay=group["weight_decay"], precision=group["actual_state_precision"],
+                       weight_decay=group["weight_decay"], precision="factored" if group["state_precision"] == "factored" else group["actual_state_precision"],
                        nesterov=group.get("nesterov", False), nesterov_coef=group.get("nesterov_coef"),
                        use_atan2=group["use_atan2"], cautious_wd=group.get("cautious_wd", False),
                        fisher_wd=group.get("fisher_wd", False), centered_wd=group.get("centered_wd", 0.0),

@@ -22,7 +22,7 @@ from ._common import ErrorWatch
 A_ATAN2 = 4 / math.pi
 SHIFTER = [1, 2, 4, 8, 16, 32, 64, 128]
 BLOCK = 2048
-SUPPORTED_PRECISIONS = ("auto", "fp32", "bf16_sr", "int8_sr")
+SUPPORTED_PRECISIONS = ("auto", "fp32", "bf16_sr", "int8_sr", "factored")
 FAST_COLS = 8192   # shared-memory column accumulator of the fast kernel (floats)
 
 
@@ -115,14 +115,56 @@ def anchor_code(state, mode) -> int:
     return L.ANCHOR["full"]
 
 
+def sign_storage(d1, packed_d2, device):
+    """A zeroed (d1, ceil(d2/8)) uint8 sign array whose storage is a whole
+    number of 4-byte words (the kernel sets sign bits with 32-bit atomics)."""
+    n = d1 * packed_d2
+    return torch.zeros(((n + 3) // 4) * 4, dtype=torch.uint8, device=device)[:n].view(d1, packed_d2)
+
+
+def ensure_sign_words(state, key="sign"):
+    """Re-home a sign array (e.g. one loaded from a checkpoint) into storage
+    that ends on a 4-byte word, keeping its values."""
+    t = state.get(key)
+    if t is None:
+        return
+    n = t.numel()
+    room = t.untyped_storage().nbytes() - t.storage_offset()
+    if t.is_contiguous() and t.data_ptr() % 4 == 0 and room >= ((n + 3) // 4) * 4:
+        return
+    s = sign_storage(t.shape[0], t.shape[1], t.device)
+    s.copy_(t)
+    state[key] = s
+
+
 @torch.no_grad()
 def init_adam_state(p, state, *, precision, factored_2nd, beta1, vector_reshape, centered_wd, centered_wd_mode,
                     fisher_wd):
-    """AdamW_adv.__init_state for the non-'factored' precisions (AdamW_adv.py:221-277);
-    Muon_AuxAdam._init_auxadam_state is the same with adam_* keys (Muon_AuxAdam.py:15-67)."""
+    """AdamW_adv.__init_state (AdamW_adv.py:221-277); Muon_AuxAdam._init_auxadam_state
+    is the same with adam_* keys (Muon_AuxAdam.py:15-67).  Under 'factored' a
+    param of two or more dims keeps m as signed rank-1 factors (mu_m_nmf,
+    mv_m_nmf, 1-bit sign) and v as rank-1 factors; a 1-D one float32 m and v."""
     state["step"] = 0
     is_vector = p.dim() == 1 and not vector_reshape
     state["factored"] = False
+    if precision == "factored":
+        if not is_vector:
+            d1, d2 = effective_shape(p.numel())
+            state["factored"] = True
+            state["factored_2nd"] = bool(factored_2nd)
+            state["effective_shape"] = (d1, d2)
+            if beta1 > 0:
+                state["mu_m_nmf"] = torch.zeros(d1, device=p.device, dtype=torch.float32)
+                state["mv_m_nmf"] = torch.zeros(d2, device=p.device, dtype=torch.float32)
+                state["sign"] = sign_storage(d1, (d2 + 7) // 8, p.device)
+                state["shifter"] = torch.tensor(SHIFTER, device=p.device, dtype=torch.uint8)
+            state["mu_v_nmf"] = torch.zeros(d1, device=p.device, dtype=torch.float32)
+            state["mv_v_nmf"] = torch.zeros(d2, device=p.device, dtype=torch.float32)
+            init_anchor(p, state, centered_wd, centered_wd_mode)
+            if fisher_wd:
+                state["wd_scaler"] = torch.tensor(1.0, device=p.device)
+            return
+        precision = "fp32"        # float32 states for 1-D params of a 'factored' group
     state["factored_2nd"] = bool(factored_2nd and not is_vector)
     if beta1 > 0:
         init_state_tensor(state, "exp_avg", p, precision)
@@ -191,6 +233,8 @@ class GroupPlan:
         prec = cfg.precision
         if prec == "auto" and self.pdt == L.DT_F32:
             prec = "fp32"
+        if prec == "factored":
+            prec = "fp32"          # float32 math and states throughout (state_util.py:165-179)
         self.precision = L.PREC[prec]
         self.descs = np.zeros(n, L.ADAM_TENSOR_DT)
         d = self.descs
@@ -198,15 +242,25 @@ class GroupPlan:
         max_d2 = 0
         any_generic = False
         self.has_anchor = False
+        self.any_fact_m = False
         vec_ok = []
         for i, (p, st) in enumerate(zip(self.params, self.states)):
             numel = p.numel()
             numels.append(numel)
             flags = 0
-            fact = bool(st.get("factored_2nd", False))
+            smmf = bool(st.get("factored", False))
+            fact = bool(st.get("factored_2nd", False)) or smmf
             m = st.get("exp_avg")
             v = st.get("exp_avg_sq")
             tensors = [p, m, v]
+            if smmf and "mu_m_nmf" in st:
+                # signed rank-1 momentum (state_precision='factored')
+                ensure_sign_words(st)
+                flags |= L.T_FACT_M
+                self.any_fact_m = True
+                d["m_row_factor"][i] = ptr(st["mu_m_nmf"])
+                d["m_col_factor"][i] = ptr(st["mv_m_nmf"])
+                d["m_sign"][i] = ptr(st["sign"])
             if fact:
                 d1, d2 = st["effective_shape"]
                 flags |= L.T_FACTORED
@@ -254,9 +308,11 @@ class GroupPlan:
         # fast path: no extended options and only wide factored tensors
         ext = cfg.use_atan2 or cfg.normed or cfg.fisher or self.has_anchor
         factors_aligned = all(aligned16(st["mu_v_nmf"], st["mv_v_nmf"]) for st in self.states
-                              if st.get("factored_2nd", False))
-        # the fast kernel keeps element offsets in 32 bits (tensors below 2^34 elements)
-        self.fast = (not ext) and (not any_generic) and factors_aligned and max(numels, default=0) < (1 << 34)
+                              if st.get("factored_2nd", False) or st.get("factored", False))
+        # the fast kernel keeps element offsets in 32 bits (tensors below 2^34
+        # elements); signed rank-1 momentum runs in the general kernel
+        self.fast = (not ext) and (not any_generic) and factors_aligned and max(numels, default=0) < (1 << 34) \
+            and not self.any_fact_m
         if self.fast:
             bpp = 2 if self.pdt == L.DT_BF16 else 4
             bps = {0: 4, 1: 2, 2: 1, 3: 2 if self.pdt == L.DT_BF16 else 4}[self.precision]
@@ -269,6 +325,14 @@ class GroupPlan:
             budget = per_cta - self.gen_offset * 4
             self.stages = int(max(2, min(4, budget // stage)))
             self.smem_floats = self.gen_offset + self.stages * stage // 4
+        elif self.any_fact_m:
+            # the second-moment and |m| areas: column sums + generic staging each
+            self.stages = 0
+            self.smem_floats = 2 * (self.gen_offset + 2 * 2048 + 4)
+            if self.smem_floats > 56832:
+                raise NotImplementedError(
+                    f"state_precision='factored' with an effective row of {max_d2} columns: the B200 kernel keeps "
+                    f"both factors' column sums in shared memory (at most 24316 columns)")
         else:
             self.stages = 0
             self.smem_floats = self.gen_offset + (2 * 2048 + 4 if any_generic else 0)
@@ -290,6 +354,10 @@ class GroupPlan:
                 self.scratch.append(buf)
                 d["col_partial"][i] = ptr(buf)
                 d["n_slots"][i] = n_slots[i]
+                if d["flags"][i] & L.T_FACT_M:
+                    mbuf = torch.empty(max(1, n_slots[i]) * d2, dtype=torch.float32, device=self.device)
+                    self.scratch.append(mbuf)
+                    d["m_col_partial"][i] = ptr(mbuf)
                 fact_idx.append(i)
         self.fact_idx = fact_idx
         self.fact_idx_dev = upload_static(np.asarray(fact_idx, np.int32), self.device) if fact_idx else None
@@ -447,6 +515,8 @@ class AdamFamilyRunner:
             flags |= L.F_ANCHORS
         if not d["wd"].any():
             flags |= L.F_NO_WD
+        if pl.any_fact_m:
+            flags |= L.F_FACT_M
         noise_keep = []
         if self.test_noise is not None:
             flags |= L.F_NOISE_IN

@@ -63,10 +63,15 @@ def fix_loaded_state_dtype(state: dict, p: torch.Tensor, group: dict) -> None:
     mode = group.get("centered_wd_mode", "full")
     if state.get("is_muon") is False:
         # auxiliary Adam state of Muon_adv / AdaMuon_adv: its own precision key
-        actual = group.get("adam_actual_state_precision", group.get("adam_state_precision", "auto"))
+        req = group.get("adam_state_precision", "auto")
+        actual = group.get("adam_actual_state_precision", req)
     else:
-        actual = group.get("actual_state_precision", group.get("state_precision", "auto"))
-    is_factored = state.get("factored", False) or actual == "factored"
+        req = group.get("state_precision", "auto")
+        actual = group.get("actual_state_precision", req)
+    # a 'factored' group keeps float32 states for its 1-D params too (the
+    # reference would cast them to the param dtype here: its group records
+    # 'auto' as the actual precision)
+    is_factored = state.get("factored", False) or actual == "factored" or req == "factored"
     if actual == "fp32":
         base = torch.float32
     elif actual == "bf16_sr":

@@ -84,15 +84,20 @@ class MuonFamilyBase(torch.optim.Optimizer):
         else:
             req = group.get("adam_state_precision", "auto")
             reject(req not in SUPPORTED_PRECISIONS, f"adam_state_precision='{req}'")
-            group["adam_actual_state_precision"] = req
-            init_adam_state(p, state, precision=req, factored_2nd=group.get("adam_factored_2nd", False),
+            # adam_nnmf_factor factors the 2-D params only; 1-D ones keep
+            # adam_state_precision (Muon_AuxAdam.py:24-34)
+            is_vec = p.dim() == 1 and not group.get("vector_reshape", False)
+            smmf = req == "factored" or (group.get("adam_nnmf_factor", False) and not is_vec)
+            group["adam_actual_state_precision"] = "auto" if req == "factored" else req
+            init_adam_state(p, state, precision="factored" if smmf else req,
+                            factored_2nd=group.get("adam_factored_2nd", False),
                             beta1=group["adam_betas"][0], vector_reshape=group.get("vector_reshape", False),
                             centered_wd=group.get("centered_wd", 0.0),
                             centered_wd_mode=group.get("centered_wd_mode", "float8"),
                             fisher_wd=group.get("adam_fisher_wd", False))
             state["is_muon"] = False
 
-    def _adam_cfg(self, group):
+    def _adam_cfg(self, group, factored=False):
         """Muon_AuxAdam._adam_step_parameter's hyperparameters (Muon_AuxAdam.py:70-192).
 
         Kourkoutas-beta (Muon_adv.py:377-391, AdaMuon_adv.py:425-441): with a
@@ -107,9 +112,11 @@ class MuonFamilyBase(torch.optim.Optimizer):
         betas = group["adam_betas"]
         if kk is not None and not bc and group.get("betas") is not None:
             betas = (betas[0], group["betas"][1])
+        req = group.get("adam_state_precision", "auto")
         return AdamCfg(algo=L.ALGO_AUXADAM, lr=group["lr"], betas=betas, eps=group["adam_eps"],
                        weight_decay=group["adam_weight_decay"],
-                       precision=group.get("adam_actual_state_precision", group.get("adam_state_precision", "auto")),
+                       precision="factored" if (factored or req == "factored") else
+                       group.get("adam_actual_state_precision", req),
                        nesterov=group.get("adam_nesterov", False), nesterov_coef=group.get("adam_nesterov_coef"),
                        use_bias_correction=group.get("adam_use_bias_correction", True),
                        use_atan2=group.get("adam_use_atan2", False), cautious_wd=group.get("cautious_wd", False),
@@ -137,13 +144,19 @@ class MuonFamilyBase(torch.optim.Optimizer):
             if self.kourkoutas_helper is not None:
                 # once per step, before the first auxiliary-Adam param (Muon_adv.py:382-384)
                 self.kourkoutas_helper.maybe_prepare(self.state[adam[0]]["step"], adam[0].device)
-            cfg = self._adam_cfg(group)
             if self._test_noise is not None:
                 self._adam_runner.test_noise = {k: v for k, v in self._test_noise.items()
                                                 if any(id(p) == k for p in adam)}
-            for (dt, dev), ps in by_dtype.items():
-                key = (gi, dt, dev, tuple(id(p) for p in ps))
-                self._adam_runner.run(key, ps, [self.state[p] for p in ps], [self._tid(p) for p in ps], cfg)
+            for (dt, dev), ps_all in by_dtype.items():
+                # factored tensors compute in float32; under adam_nnmf_factor
+                # the 1-D params of the group keep adam_state_precision
+                parts = {}
+                for p in ps_all:
+                    parts.setdefault(bool(self.state[p].get("factored", False)), []).append(p)
+                for fac, ps in parts.items():
+                    cfg = self._adam_cfg(group, factored=fac)
+                    key = (gi, dt, dev, fac, tuple(id(p) for p in ps))
+                    self._adam_runner.run(key, ps, [self.state[p] for p in ps], [self._tid(p) for p in ps], cfg)
             self._adam_runner.test_noise = None
         for p in muon:
             hp = self._muon_hp(group, p)

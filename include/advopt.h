@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define ADVOPT_ABI_VERSION 4
+#define ADVOPT_ABI_VERSION 5
 
 /* ---- error codes ---- */
 #define ADVOPT_OK 0
@@ -64,11 +64,17 @@ extern "C" {
 #define ADVOPT_F_ANCHORS (1u << 10)    /* some tensor carries a centered-WD anchor */
 #define ADVOPT_F_NO_WD (1u << 11)      /* no tensor of the launch has weight decay (optional hint) */
 #define ADVOPT_F_GRAD_SQ (1u << 12)    /* also write each piece's sum of g*g to piece_gsq (Kourkoutas-beta) */
+#define ADVOPT_F_EMIT_UPDATE (1u << 13)/* write each tensor's unscaled update to update_out and leave the
+                                          param alone (spectral normalisation finishes the step) */
+#define ADVOPT_F_FACT_M (1u << 14)     /* some tensor carries ADVOPT_T_FACT_M (needs ADVOPT_PREC_FP32) */
 
 /* per-tensor flags */
 #define ADVOPT_T_FACTORED (1u << 0)    /* second moment as rank-1 factors (factored_2nd) */
 #define ADVOPT_T_VEC (1u << 1)         /* all pointers 16-byte aligned: vector path allowed */
 #define ADVOPT_T_P0_SCALAR (1u << 2)   /* Prodigy p0 is the scalar 0 (all-zero param at init) */
+#define ADVOPT_T_FACT_M (1u << 3)      /* first moment as signed rank-1 factors + 1-bit signs
+                                          (state_precision='factored'; fp32 launches only) */
+#define ADVOPT_T_UPD_BF16 (1u << 7)    /* update_out holds bf16 (else float32) */
 #define ADVOPT_T_ANCHOR_SHIFT 4        /* 3 bits: centered-WD anchor storage */
 #define ADVOPT_ANCHOR_NONE 0
 #define ADVOPT_ANCHOR_FULL 1           /* anchor in the param dtype      */
@@ -97,6 +103,13 @@ typedef struct advopt_adam_tensor {
   const int32_t* noise_v;    /* injected SR noise for v  (ADVOPT_F_NOISE_IN)  */
   const int32_t* noise_m;    /* injected SR noise for m                       */
   const int32_t* noise_p;    /* injected SR noise for the param               */
+  float* m_row_factor;       /* ADVOPT_T_FACT_M: mu_m_nmf [d1] (rewritten in place) */
+  float* m_col_factor;       /* mv_m_nmf [d2] (rewritten by the finish)       */
+  float* m_col_partial;      /* scratch [n_slots][d2]                         */
+  uint8_t* m_sign;           /* sign [d1][ceil(d2/8)], bit j of byte b = column 8b+j; its
+                                storage is a whole number of 4-byte words, 4-byte aligned */
+  void* update_out;          /* ADVOPT_F_EMIT_UPDATE: the update before its step-size
+                                scaling, f32 or bf16 (ADVOPT_T_UPD_BF16), [numel] */
   int64_t numel;
   int64_t d1;                /* factored effective shape (d1, d2)             */
   int64_t d2;
@@ -191,9 +204,10 @@ typedef struct advopt_adam_launch {
  * (param_update.py:77-156) for every tensor of the group. */
 int advopt_adam_step(const advopt_adam_launch* launch, void* stream);
 
-/* Second half of factored_2nd: reduce the column partials into mv_v_nmf and
- * normalise one factor (factorization_util.py:60-80).  `tensor_index` lists
- * the factored tensors of the launch. */
+/* Second half of factored_2nd / 'factored': reduce the column partials into
+ * mv_v_nmf (and mv_m_nmf for ADVOPT_T_FACT_M tensors) and normalise one factor
+ * of each (factorization_util.py:60-80).  `tensor_index` lists the factored
+ * tensors of the launch. */
 int advopt_factored_finish(const advopt_adam_launch* launch, const int32_t* tensor_index,
                            int32_t n_factored, int32_t max_d2, void* stream);
 

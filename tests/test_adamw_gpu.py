@@ -81,6 +81,13 @@ def _oracle_state_from_torch(st):
     ([(1024, 4096), (4096,), (33, 65)], "bf16", dict(state_precision="int8_sr", weight_decay=0.1, lr=1e-2)),
     ([(768, 2304), (2304,), (50257, 64)], "f32",
      dict(state_precision="fp32", weight_decay=0.01)),
+    # state_precision='factored': signed rank-1 m on the fast factored layout
+    # (d2 = 1024 / 2048 / 4096 -> 2048 and 4096 take the one-byte-per-thread
+    # sign path) and on ragged rows (777 x 3 -> (777, 3), 1000 x 7)
+    pytest.param(([(4096, 1024), (2048, 2048), (96,), (1024, 4096), (777, 3), (1000, 7)], "bf16",
+                  dict(state_precision="factored", nesterov=True, weight_decay=0.01)), id="factored_bf16"),
+    pytest.param(([(4096, 4096), (4096,), (333, 12)], "f32",
+                  dict(state_precision="factored", cautious_wd=True, weight_decay=0.05)), id="factored_f32"),
 ])
 def test_adamw_matches_oracle_large(case):
     import advanced_optimizers_b200 as A
@@ -132,7 +139,7 @@ def test_adamw_matches_oracle_large(case):
                 if torch.is_tensor(val) and key in ostate[i] and isinstance(ostate[i][key], np.ndarray):
                     check_state(key, to_numpy(val), ostate[i][key], f"{what} {key}")
             # keep the oracle on the device's factors so later steps compare one step each
-            for key in ("mu_v_nmf", "mv_v_nmf"):
+            for key in ("mu_v_nmf", "mv_v_nmf", "mu_m_nmf", "mv_m_nmf", "sign"):
                 if key in ostate[i]:
                     ostate[i][key] = to_numpy(opt.state[p][key])
             p_o[i] = O.from_bf16_bits(to_numpy(p)).reshape(sh) if dt == "bf16" else to_numpy(p).reshape(sh)

@@ -25,7 +25,7 @@ def test_header_symbols_exported():
 def test_struct_sizes():
     from advanced_optimizers_b200 import _lib
     L = _lib.lib()
-    assert L.advopt_sizeof(0) == _lib.ADAM_TENSOR_DT.itemsize == 192
+    assert L.advopt_sizeof(0) == _lib.ADAM_TENSOR_DT.itemsize == 232
     assert L.advopt_sizeof(1) == _lib.PIECE_DT.itemsize == 24
     assert L.advopt_sizeof(2) == ctypes.sizeof(_lib.AdamLaunch)
     assert L.advopt_sizeof(3) == _lib.LION_TENSOR_DT.itemsize
