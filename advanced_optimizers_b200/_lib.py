@@ -20,7 +20,7 @@ ABI_VERSION = 5
 # ---- constants mirrored from include/advopt.h ----
 DT_F32, DT_BF16 = 0, 1
 PREC = {"fp32": 0, "bf16_sr": 1, "int8_sr": 2, "auto": 3}
-ALGO_ADAMW, ALGO_AUXADAM, ALGO_PRODIGY = 0, 1, 2
+ALGO_ADAMW, ALGO_AUXADAM, ALGO_PRODIGY, ALGO_LION = 0, 1, 2, 3
 F_NESTEROV = 1 << 0
 F_ATAN2 = 1 << 1
 F_NORMED = 1 << 2

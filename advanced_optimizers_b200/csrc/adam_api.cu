@@ -18,6 +18,7 @@ __global__ void factored_cols_kernel(const advopt_adam_tensor* tensors, const in
   const advopt_adam_tensor* t = tensors + index[blockIdx.y];
   const bool mom = blockIdx.z == 1;
   if (mom && (!(t->flags & ADVOPT_T_FACT_M) || !t->m_col_partial)) return;
+  if (!mom && !t->col_partial) return;     // factored Lion: no second moment
   const int64_t d2 = t->d2;
   const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= d2) return;
@@ -32,6 +33,7 @@ __global__ void factored_norm_kernel(const advopt_adam_tensor* tensors, const in
   const advopt_adam_tensor* t = tensors + index[blockIdx.x];
   const bool mom = blockIdx.y == 1;
   if (mom && (!(t->flags & ADVOPT_T_FACT_M) || !t->m_col_partial)) return;
+  if (!mom && !t->col_partial) return;
   const int64_t d1 = t->d1, d2 = t->d2;
   float* vec = mom ? (d1 < d2 ? t->m_row_factor : t->m_col_factor) : (d1 < d2 ? t->row_factor : t->col_factor);
   const int64_t n = d1 < d2 ? d1 : d2;
@@ -228,7 +230,7 @@ using namespace advopt;
 extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
   if (!L || !L->tensors || !L->pieces || !L->cta_offsets || L->grid <= 0)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: null table or empty grid");
-  if (L->precision < 0 || L->precision > 3 || L->algo < 0 || L->algo > 2 || L->param_dtype < 0 || L->param_dtype > 1)
+  if (L->precision < 0 || L->precision > 3 || L->algo < 0 || L->algo > 3 || L->param_dtype < 0 || L->param_dtype > 1)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: bad precision/algo/dtype code");
   if ((L->flags & (ADVOPT_F_PRODIGY_STATS | ADVOPT_F_FISHER_STATS)) && !L->piece_stats)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: statistics requested without piece_stats");
@@ -239,6 +241,9 @@ extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
   if (L->smem_floats < 0 || L->smem_floats > 56832)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: shared memory request above 227 KB (factored d2 too large)");
   if (L->stages < 0 || L->stages > 4) return set_error(ADVOPT_E_INVALID, "advopt_adam_step: stages must be 0..4");
+  if (L->algo == ADVOPT_ALGO_LION && (L->precision != ADVOPT_PREC_FP32 || !(L->flags & ADVOPT_F_FACT_M) ||
+                                      !(L->flags & ADVOPT_F_HAS_M) || L->stages != 0))
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: Lion launches are float32, factored, general-kernel only");
   if ((L->flags & ADVOPT_F_FACT_M) && L->precision != ADVOPT_PREC_FP32)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: factored momentum needs ADVOPT_PREC_FP32");
   if ((L->flags & ADVOPT_F_EMIT_UPDATE) && (L->flags & (ADVOPT_F_FISHER | ADVOPT_F_FISHER_STATS)))

@@ -279,7 +279,9 @@ __device__ __forceinline__ void load_raw(const TensorRegs& T, const ChunkPos& cp
     ld_words<SB>(T.m, k0, nv, v8, R.m);
     if (kStore == 2) R.ms = T.m_scale[blk];
   }
-  if (fact) {
+  if (ALGO == ADVOPT_ALGO_LION) {
+    // Lion: no second moment
+  } else if (fact) {
     if (ffast) {
       const int64_t cc = cp.c0 + tid * kVec;
       const bool second = cc >= T.d2;
@@ -455,6 +457,8 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
     const bool vec = T.flags & ADVOPT_T_VEC;
     const bool has_anchor = EXT && (((T.flags >> ADVOPT_T_ANCHOR_SHIFT) & 7u) != 0);
     const bool fact_sums = fact && !fstats;   // factored row/column sums (skipped by the Fisher pass)
+    constexpr bool kHasV = ALGO != ADVOPT_ALGO_LION;
+    const bool v_sums = fact_sums && kHasV;
     // signed rank-1 momentum (state_precision='factored', AdamW_adv.py:342-399)
     const bool factm = kFM && has_m && fact && (T.flags & ADVOPT_T_FACT_M);
     const bool fm_sums = factm && !fstats;
@@ -469,7 +473,8 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
     const float rcp_sbc2 = __frcp_rn(T.sqrt_bc2);
     const float step_size = T.step_size, eps = T.eps, sbc2 = T.sqrt_bc2, wd = T.wd, cwd = T.cwd;
     if (fact_sums) {
-      for (int j = tid; j < (int)d2; j += kThreads) colacc[j] = 0.0f;
+      if (kHasV)
+        for (int j = tid; j < (int)d2; j += kThreads) colacc[j] = 0.0f;
       if (fm_sums)
         for (int j = tid; j < (int)d2; j += kThreads) colacc_m[j] = 0.0f;
       __syncthreads();
@@ -553,7 +558,10 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
           for (int e = 0; e < 8; ++e) m[e] = __fmul_rn(m[e], cur.ms);
         }
       }
-      if (fact) {
+      if (!kHasV) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) vh[e] = 0.0f;
+      } else if (fact) {
         if (ffast) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) vh[e] = __fmul_rn(cur.mu, cur.mv[e]);   // outer(mu, mv)
@@ -605,8 +613,17 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
       for (int e = 0; e < 8; ++e) {
         const bool ok = e < nv;
         float gi = g[e];
+        float vi = 0.0f, du = 1.0f, ui;
+        if constexpr (ALGO == ADVOPT_ALGO_LION) {
+          // Lion_adv.py:236-247 on the float32 grad: c = lerp(g, m, beta1),
+          // m = lerp(m, g, 1 - beta2), update = sign(c) (lion_k.py:23-24)
+          const float c = lerp_t(gi, m[e], beta1);
+          m_new[e] = ok ? lerp_t(m[e], gi, w_m) : 0.0f;
+          v[e] = 0.0f;
+          ui = c > 0.0f ? 1.0f : (c < 0.0f ? -1.0f : c);
+        } else {
         // v = v*beta2 + c_v*g*g   (mul_ then addcmul_, AdamW_adv.py:417, Prodigy_adv.py:469)
-        float vi = __fmul_rn(vh[e], beta2);
+        vi = __fmul_rn(vh[e], beta2);
         if (vbf) vi = round_bf16(vi);
         vi = __fmaf_rn(__fmul_rn(c_v, gi), gi, vi);
         if (vbf) vi = round_bf16(vi);
@@ -623,10 +640,9 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
           den = __fadd_rn(den, eps);   // Prodigy: eps holds d*eps
           if (vbf) den = round_bf16(den);
         }
-        const float du = kMBF ? round_bf16(den) : den;   // denom.to(update.dtype)
+        du = kMBF ? round_bf16(den) : den;   // denom.to(update.dtype)
         if (normed) gi = atan2m ? Rm(atan2f(gi, du)) : Rm(__fdiv_rn(gi, du));
         // first moment and the update direction
-        float ui;
         if (has_m) {
           float mi;
           if (ALGO == ADVOPT_ALGO_PRODIGY) {
@@ -641,6 +657,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
           ui = (ALGO == ADVOPT_ALGO_PRODIGY) ? Rm(__fmul_rn(gi, d_f)) : gi;
         }
         if (!normed) ui = atan2m ? Rm(atan2f(ui, du)) : Rm(__fdiv_rn(ui, du));
+        }
         if (emit) uemit[e] = ui;   // the update before its scaling (AdamW_adv.py:459-461)
         ui = Rm(__fmul_rn(ui, step_size));
         amax_m = fmaxf(amax_m, fabsf(m_new[e]));
@@ -728,7 +745,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
 
       // ---- factored second moment: row sums and column partials ----
       float rsum0 = 0.0f, rsum1 = 0.0f;
-      if (fact_sums) {
+      if (v_sums) {
         if (ffast) {
           const int64_t cc = c0 + tid * kVec;
           const bool second = cc >= d2;
@@ -824,7 +841,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
               s1 = __fadd_rn(s1, red[parity][w][3]);
             }
             row_carry += (double)s0;
-            if (clen >= d2 - c0) {         // row r0 completes in this chunk
+            if (kHasV && clen >= d2 - c0) {         // row r0 completes in this chunk
               T.row[r0] = (float)row_carry;
               row_carry = (double)s1;
             }
@@ -876,7 +893,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
             }
             __syncthreads();
           };
-          gen_sums(vbuf, colacc, segs, T.row, row_carry);
+          if (kHasV) gen_sums(vbuf, colacc, segs, T.row, row_carry);
           if (fm_sums) gen_sums(mbuf, colacc_m, msegs, T.mrow, row_carry_m);
         }
       }
@@ -941,8 +958,10 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
     // ---- end of piece: flush column partials and statistics ----
     if (fact_sums) {
       __syncthreads();
-      float* dst = T.colpart + (int64_t)pc.slot * d2;
-      for (int j = tid; j < (int)d2; j += kThreads) dst[j] = colacc[j];
+      if (kHasV) {
+        float* dst = T.colpart + (int64_t)pc.slot * d2;
+        for (int j = tid; j < (int)d2; j += kThreads) dst[j] = colacc[j];
+      }
       if (fm_sums) {
         float* dm = T.mcolpart + (int64_t)pc.slot * d2;
         for (int j = tid; j < (int)d2; j += kThreads) dm[j] = colacc_m[j];
@@ -1028,7 +1047,8 @@ cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
   const bool nin = L.flags & ADVOPT_F_NOISE_IN;
   const size_t smem = (size_t)L.smem_floats * sizeof(float);
   // signed rank-1 momentum and update emission live in the general kernel only
-  const bool general_only = L.flags & (ADVOPT_F_FACT_M | ADVOPT_F_EMIT_UPDATE);
+  const bool general_only = ALGO == ADVOPT_ALGO_LION || (L.flags & (ADVOPT_F_FACT_M | ADVOPT_F_EMIT_UPDATE));
+  if constexpr (ALGO != ADVOPT_ALGO_LION) {
   if (!ext && !general_only && L.stages > 0) {
     if (nin) {
       auto kf = adam_fast_kernel<PREC, PBF, ALGO, true, kCfDyn>;
@@ -1048,6 +1068,7 @@ cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
       }
     }
     return launch_fast<PREC, PBF, ALGO, kCfDyn>(L, smem, s);
+  }
   }
   auto k = ext ? (nin ? adam_kernel<PREC, PBF, ALGO, true, true> : adam_kernel<PREC, PBF, ALGO, true, false>)
                : (nin ? adam_kernel<PREC, PBF, ALGO, false, true> : adam_kernel<PREC, PBF, ALGO, false, false>);
@@ -1080,6 +1101,11 @@ cudaError_t launch_adam_prec(const advopt_adam_launch& L, cudaStream_t s) {
       return pbf ? launch_adam_algo<PREC, true, ADVOPT_ALGO_ADAMW>(L, s) : launch_adam_algo<PREC, false, ADVOPT_ALGO_ADAMW>(L, s);
     case ADVOPT_ALGO_AUXADAM:
       return pbf ? launch_adam_algo<PREC, true, ADVOPT_ALGO_AUXADAM>(L, s) : launch_adam_algo<PREC, false, ADVOPT_ALGO_AUXADAM>(L, s);
+    case ADVOPT_ALGO_LION:
+      // factored Lion: float32 launches only (checked by advopt_adam_step)
+      if constexpr (PREC == ADVOPT_PREC_FP32)
+        return pbf ? launch_adam_algo<PREC, true, ADVOPT_ALGO_LION>(L, s) : launch_adam_algo<PREC, false, ADVOPT_ALGO_LION>(L, s);
+      return cudaErrorInvalidValue;
     default:
       return pbf ? launch_adam_algo<PREC, true, ADVOPT_ALGO_PRODIGY>(L, s) : launch_adam_algo<PREC, false, ADVOPT_ALGO_PRODIGY>(L, s);
   }

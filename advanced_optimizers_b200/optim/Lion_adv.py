@@ -2,9 +2,11 @@
 
 One elementwise launch per group (csrc/lion.cu): update = sign(lerp(g, m,
 beta1)) * lr, m = lerp(m, g, 1 - beta2), then the reference's weight decay
-and bf16 stochastic rounding.  kappa_p = 1 (sign) only; the other Lion-K
-geometries need a global norm and are rejected, as are the options listed
-in reject() calls below.
+and bf16 stochastic rounding.  Under nnmf_factor the 2-D params keep m as
+signed rank-1 factors (Lion_adv.py:161-176, 232-254) and step in the
+Adam-family general kernel (ADVOPT_ALGO_LION, float32).  kappa_p = 1 (sign)
+only; the other Lion-K geometries need a global norm and are rejected, as are
+the options listed in reject() calls below.
 """
 from __future__ import annotations
 
@@ -17,7 +19,8 @@ import torch
 from .. import _lib as L
 from .._device import DeviceTable, aligned16, dtype_code, ptr, require_cuda_tensor, stream_handle, upload_static
 from .._plan import plan as plan_pieces
-from ._adam_family import adjust_wds, f32
+from .._plan import effective_shape
+from ._adam_family import SHIFTER, AdamCfg, AdamFamilyRunner, adjust_wds, f32, sign_storage
 from ._common import load_state_dict_exact, reject
 
 
@@ -78,7 +81,6 @@ class Lion_adv(torch.optim.Optimizer):
         reject(stochastic_sign, "stochastic_sign")
         reject(centered_wd, "centered_wd for Lion_adv")
         reject(spectral_normalization, "spectral_normalization")
-        reject(nnmf_factor, "nnmf_factor")
         reject(kappa_p != 1.0 and not auto_kappa_p, f"kappa_p={kappa_p}")
         defaults = dict(lr=lr, betas=betas, weight_decay=weight_decay, cautious_wd=cautious_wd,
                         vector_reshape=vector_reshape, orthogonal_gradient=orthogonal_gradient, kappa_p=kappa_p,
@@ -92,11 +94,13 @@ class Lion_adv(torch.optim.Optimizer):
         self._ids = {}
         self._test_noise = None
         self.seed = 42
+        self._fruner = AdamFamilyRunner(seed=42)     # factored tensors
         self.init_step()
 
     def load_state_dict(self, state_dict: dict) -> None:
         load_state_dict_exact(self, state_dict)
         self._plans.clear()
+        self._fruner.invalidate()
 
     @property
     def supports_fused_back_pass(self) -> bool:
@@ -120,12 +124,23 @@ class Lion_adv(torch.optim.Optimizer):
 
     @torch.no_grad()
     def _init_state(self, p, group):
-        """Lion_adv.py:156-181 (non-factored)."""
+        """Lion_adv.py:156-181: signed rank-1 m (float32 factors, 1-bit signs)
+        for params of two or more dims under nnmf_factor, else m in the
+        param dtype."""
         state = self.state[p]
         if "step" not in state:
             state["step"] = 0
-            state["factored"] = False
-            state["exp_avg"] = torch.zeros_like(p, device=p.device, dtype=p.dtype)
+            state["factored"] = bool(group["nnmf_factor"] and
+                                     not (p.dim() == 1 and not group["vector_reshape"]))
+            if state["factored"]:
+                d1, d2 = effective_shape(p.numel())
+                state["effective_shape"] = (d1, d2)
+                state["mu_m_nmf"] = torch.zeros(d1, device=p.device, dtype=torch.float32)
+                state["mv_m_nmf"] = torch.zeros(d2, device=p.device, dtype=torch.float32)
+                state["sign"] = sign_storage(d1, (d2 + 7) // 8, p.device)
+                state["shifter"] = torch.tensor(SHIFTER, device=p.device, dtype=torch.uint8)
+            else:
+                state["exp_avg"] = torch.zeros_like(p, device=p.device, dtype=p.dtype)
 
     def _tid(self, p):
         t = self._ids.get(id(p))
@@ -139,6 +154,10 @@ class Lion_adv(torch.optim.Optimizer):
             self._init_state(p, group)
             require_cuda_tensor(p, "param")
             require_cuda_tensor(p.grad, "grad")
+        fac = [p for p in params if self.state[p]["factored"]]
+        if fac:
+            self._run_factored(gi, group, fac)
+        params = [p for p in params if not self.state[p]["factored"]]
         by_dtype = {}
         for p in params:
             if group.get("auto_kappa_p", False) and p.ndim >= 4:
@@ -185,6 +204,29 @@ class Lion_adv(torch.optim.Optimizer):
                                              stream_handle(pl.device)), "advopt_lion_step")
             if keep:
                 torch.cuda.current_stream(pl.device).synchronize()
+
+    def _run_factored(self, gi, group, params):
+        """The factored params of a group: one float32 general-kernel launch
+        per dtype (Lion_adv.py:214-254)."""
+        cfg = AdamCfg(algo=L.ALGO_LION, lr=group["lr"], betas=group["betas"], eps=1.0,
+                      weight_decay=group["weight_decay"], precision="factored", use_bias_correction=False,
+                      cautious_wd=group.get("cautious_wd", False), stochastic_rounding=self.stochastic_rounding)
+        by_dtype = {}
+        for p in params:
+            if group.get("auto_kappa_p", False) and p.ndim >= 4:
+                raise NotImplementedError("Lion-K with kappa_p=2 (4-D params under auto_kappa_p) is not supported")
+            by_dtype.setdefault((p.dtype, p.device), []).append(p)
+        if self._test_noise is not None:
+            self._fruner.test_noise = {id(p): {"param": self._test_noise[id(p)]["param"]}
+                                       for p in params if "param" in self._test_noise.get(id(p), {})}
+        for (dt, dev), ps in by_dtype.items():
+            key = (gi, dt, dev, tuple(id(p) for p in ps))
+            self._fruner.run(key, ps, [self.state[p] for p in ps], [self._tid(p) for p in ps], cfg)
+        self._fruner.test_noise = None
+
+    def check_errors(self):
+        """Synchronise and raise if a factored step's kernel reported a bounded wait that gave up."""
+        self._fruner.check_errors()
 
     @torch.no_grad()
     def step_parameter(self, p: torch.Tensor, group: dict, i: Optional[int] = None):

@@ -265,13 +265,14 @@ class GroupPlan:
                 d1, d2 = st["effective_shape"]
                 flags |= L.T_FACTORED
                 d["d1"][i], d["d2"][i] = d1, d2
-                d["row_factor"][i] = ptr(st["mu_v_nmf"])
-                d["col_factor"][i] = ptr(st["mv_v_nmf"])
+                # (factored Lion has no second moment)
+                d["row_factor"][i] = ptr(st.get("mu_v_nmf"))
+                d["col_factor"][i] = ptr(st.get("mv_v_nmf"))
                 d2s.append(d2)
                 max_d2 = max(max_d2, d2)
                 if d2 < 2048 or d2 % 8 != 0:
                     any_generic = True
-                tensors += [st["mu_v_nmf"], st["mv_v_nmf"]]
+                tensors += [t for t in (st.get("mu_v_nmf"), st.get("mv_v_nmf")) if t is not None]
             else:
                 d2s.append(0)
             d["param"][i] = ptr(p)
@@ -308,7 +309,7 @@ class GroupPlan:
         # fast path: no extended options and only wide factored tensors
         ext = cfg.use_atan2 or cfg.normed or cfg.fisher or self.has_anchor
         factors_aligned = all(aligned16(st["mu_v_nmf"], st["mv_v_nmf"]) for st in self.states
-                              if st.get("factored_2nd", False) or st.get("factored", False))
+                              if "mu_v_nmf" in st)
         # the fast kernel keeps element offsets in 32 bits (tensors below 2^34
         # elements); signed rank-1 momentum runs in the general kernel
         self.fast = (not ext) and (not any_generic) and factors_aligned and max(numels, default=0) < (1 << 34) \
@@ -350,9 +351,10 @@ class GroupPlan:
         for i in range(n):
             if d["flags"][i] & L.T_FACTORED:
                 d2 = int(d["d2"][i])
-                buf = torch.empty(max(1, n_slots[i]) * d2, dtype=torch.float32, device=self.device)
-                self.scratch.append(buf)
-                d["col_partial"][i] = ptr(buf)
+                if d["row_factor"][i]:
+                    buf = torch.empty(max(1, n_slots[i]) * d2, dtype=torch.float32, device=self.device)
+                    self.scratch.append(buf)
+                    d["col_partial"][i] = ptr(buf)
                 d["n_slots"][i] = n_slots[i]
                 if d["flags"][i] & L.T_FACT_M:
                     mbuf = torch.empty(max(1, n_slots[i]) * d2, dtype=torch.float32, device=self.device)
@@ -472,6 +474,8 @@ class AdamFamilyRunner:
                 ss = dlr * A_ATAN2 if cfg.use_atan2 else dlr
                 sbc2 = 1.0
                 lr_wd = dlr
+            elif cfg.algo == L.ALGO_LION:
+                ss, sbc2, lr_wd = lr, 1.0, lr      # update.mul_(lr) (Lion_adv.py:273-276)
             else:
                 sc = step_cache.get(t)
                 if sc is None:
@@ -499,7 +503,7 @@ class AdamFamilyRunner:
             d["cwd"][i] = cwd * lr_wd if cwd != 0 else 0.0
             d["step"][i] = t & 0xFFFFFFFF
         flags = 0
-        if cfg.beta1 > 0:
+        if cfg.beta1 > 0 or cfg.algo == L.ALGO_LION:
             flags |= L.F_HAS_M
         if cfg.nesterov:
             flags |= L.F_NESTEROV
@@ -573,7 +577,8 @@ class AdamFamilyRunner:
         nv_coef = cfg.beta1 if nc is None else nc
         s.beta1 = f32(cfg.beta1)
         s.beta2 = f32(cfg.beta2)
-        s.w_m = f32(1.0 - cfg.beta1)
+        # Lion: torch.lerp(grad, m, beta1) for the update, m.lerp_(grad, 1 - beta2)
+        s.w_m = f32(1.0 - cfg.beta2) if cfg.algo == L.ALGO_LION else f32(1.0 - cfg.beta1)
         s.w_nest = f32(1 - nv_coef)
         if cfg.algo == L.ALGO_PRODIGY:
             pd = cfg.prodigy

@@ -49,6 +49,9 @@ extern "C" {
 #define ADVOPT_ALGO_ADAMW 0    /* AdamW_adv._step_parameter (v before m)           */
 #define ADVOPT_ALGO_AUXADAM 1  /* Muon_AuxAdam._adam_step_parameter (m before v)   */
 #define ADVOPT_ALGO_PRODIGY 2  /* Prodigy_adv._step_parameter (d-scaled moments)   */
+#define ADVOPT_ALGO_LION 3     /* Lion_adv factored tensors (Lion_adv.py:232-254): no second moment,
+                                  every tensor ADVOPT_T_FACTORED | ADVOPT_T_FACT_M, ADVOPT_PREC_FP32;
+                                  beta1 = the lerp weight of the update, w_m = 1 - beta2 */
 
 /* launch flags */
 #define ADVOPT_F_NESTEROV (1u << 0)

@@ -75,3 +75,49 @@ def test_matches_reference_golden(name):
             assert g0["k"] == int(ref[3])
             for j, key in enumerate(("d", "d_max", "d_numerator")):
                 np.testing.assert_allclose(g0[key], ref[j], rtol=1e-4, err_msg=f"{name} step {s} {key}")
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f32"])
+def test_lion_factored_matches_oracle_large(dt):
+    """Lion_adv(nnmf_factor=True) at sizes that take the one-sign-byte-per-thread
+    path (effective d2 = 2048, 4096) beside ragged rows ((777, 3) -> (63, 37))
+    and a 1-D param, against the oracle; each step starts from the device's
+    factors.  Tolerances as above (factors 2e-6, signs exact)."""
+    import advanced_optimizers_b200 as A
+    from _replay import O
+    shapes = [(4096, 1024), (2048, 2048), (96,), (777, 3)]
+    g = torch.Generator().manual_seed(3)
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float32
+    p_host = [(torch.randn(sh, generator=g) * 0.02).to(tdt) for sh in shapes]
+    params = [torch.nn.Parameter(t.cuda()) for t in p_host]
+    kw = dict(lr=1e-4, weight_decay=0.01, nnmf_factor=True, cautious_wd=(dt == "f32"))
+    opt = A.Lion_adv(params, **kw)
+    hp = dict(lr=1e-4, betas=(0.9, 0.99), weight_decay=0.01, cautious_wd=kw["cautious_wd"], stochastic_rounding=True)
+    ostate = [{k: (to_numpy(v) if torch.is_tensor(v) else v) for k, v in opt.state[p].items()} for p in params]
+    p_o = [O.from_bf16_bits(to_numpy(t)) if dt == "bf16" else to_numpy(t) for t in p_host]
+    for s in range(2):
+        grads = [(torch.randn(sh, generator=g) * 1e-3).to(tdt) for sh in shapes]
+        noise = {p: {"param": torch.randint(0, 65536, (math.prod(sh),), generator=g, dtype=torch.int32)}
+                 for p, sh in zip(params, shapes)}
+        for p, gr in zip(params, grads):
+            p.grad = gr.cuda()
+        opt.set_test_noise({p: {k: v.cuda() for k, v in nz.items()} for p, nz in noise.items()})
+        opt.step()
+        torch.cuda.synchronize()
+        for i, (p, sh) in enumerate(zip(params, shapes)):
+            gnp = to_numpy(grads[i])
+            gv = O.from_bf16_bits(gnp).reshape(sh) if dt == "bf16" else gnp
+            prev = p_o[i].copy()
+            p_o[i] = O.lion_step(p_o[i], dt, gv, ostate[i], hp, {"param": noise[p]["param"].numpy()})
+            what = f"{sh} step {s}"
+            if dt == "bf16":
+                check_bf16_param(to_numpy(p), O.bf16_bits(p_o[i]), what)
+            else:
+                check_fp32(to_numpy(p), p_o[i], 1e-6, what, prev)
+            for key, val in opt.state[p].items():
+                if torch.is_tensor(val) and isinstance(ostate[i].get(key), np.ndarray):
+                    check_state(key, to_numpy(val), ostate[i][key], f"{what} {key}")
+            for key in ("mu_m_nmf", "mv_m_nmf", "sign", "exp_avg"):
+                if key in ostate[i]:
+                    ostate[i][key] = to_numpy(opt.state[p][key])
+            p_o[i] = O.from_bf16_bits(to_numpy(p)).reshape(sh) if dt == "bf16" else to_numpy(p).reshape(sh)
