@@ -59,6 +59,12 @@ ADAM_TENSOR_DT = np.dtype([
     ("slot_base", "<i4"), ("n_slots", "<i4"),
 ])
 PIECE_DT = np.dtype([("begin", "<i8"), ("end", "<i8"), ("tensor", "<i4"), ("slot", "<i4")])
+# advopt_spectral_tensor (80 bytes)
+S_UPD_BF16, S_VEC_BF16, S_MAXABS = 1, 2, 4
+SPECTRAL_TENSOR_DT = np.dtype([
+    ("update", "<u8"), ("u", "<u8"), ("v", "<u8"), ("v_partial", "<u8"), ("u_raw", "<u8"), ("scalars", "<u8"),
+    ("d_out", "<i8"), ("d_in", "<i8"), ("target", "<f4"), ("flags", "<u4"), ("n_slabs", "<i4"), ("pad", "<i4"),
+])
 LION_TENSOR_DT = np.dtype([
     ("param", "<u8"), ("grad", "<u8"), ("exp_avg", "<u8"), ("noise_p", "<u8"), ("numel", "<i8"),
     ("lr", "<f4"), ("wd", "<f4"), ("tensor_id", "<u4"), ("step", "<u4"), ("flags", "<u4"), ("pad", "<u4"),
@@ -203,6 +209,7 @@ def lib():
             "advopt_ipc_close": ([P], ctypes.c_int),
             "advopt_enable_peer": ([I32], ctypes.c_int),
             "advopt_copy_async": ([P, P, U64, P], ctypes.c_int),
+            "advopt_spectral_step": ([ctypes.POINTER(AdamLaunch), P, P, I32, P, I32, P], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -214,7 +221,7 @@ def lib():
                             (2, ctypes.sizeof(AdamLaunch)), (3, LION_TENSOR_DT.itemsize),
                             (4, ctypes.sizeof(MuonArgs)), (5, ctypes.sizeof(KourkoutasArgs)),
                             (6, PRODIGY_DEV_BYTES), (7, ctypes.sizeof(ProdigyScalarArgs)),
-                            (8, ctypes.sizeof(ProdigyDArgs))):
+                            (8, ctypes.sizeof(ProdigyDArgs)), (9, SPECTRAL_TENSOR_DT.itemsize)):
             got = L.advopt_sizeof(which)
             if got != size:
                 raise AdvOptError(f"struct layout mismatch (#{which}: C {got} bytes, Python {size})")
@@ -236,7 +243,7 @@ def exported_symbols():
             "advopt_noise_fill", "advopt_ns_chain", "advopt_kourkoutas_prepare", "advopt_kourkoutas_accumulate",
             "advopt_prodigy_scalars", "advopt_prodigy_update_d", "advopt_lr_sketch", "advopt_lr_gemm",
             "advopt_lr_qr_work", "advopt_lr_qr", "advopt_ipc_get_handle", "advopt_ipc_open", "advopt_ipc_close",
-            "advopt_enable_peer", "advopt_copy_async"]
+            "advopt_enable_peer", "advopt_copy_async", "advopt_spectral_step"]
 
 
 _OCC_CACHE = {}

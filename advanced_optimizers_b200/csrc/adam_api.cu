@@ -241,9 +241,10 @@ extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
   if (L->smem_floats < 0 || L->smem_floats > 56832)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: shared memory request above 227 KB (factored d2 too large)");
   if (L->stages < 0 || L->stages > 4) return set_error(ADVOPT_E_INVALID, "advopt_adam_step: stages must be 0..4");
-  if (L->algo == ADVOPT_ALGO_LION && (L->precision != ADVOPT_PREC_FP32 || !(L->flags & ADVOPT_F_FACT_M) ||
-                                      !(L->flags & ADVOPT_F_HAS_M) || L->stages != 0))
-    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: Lion launches are float32, factored, general-kernel only");
+  if (L->algo == ADVOPT_ALGO_LION &&
+      ((L->precision != ADVOPT_PREC_FP32 && L->precision != ADVOPT_PREC_AUTO) || !(L->flags & ADVOPT_F_HAS_M) ||
+       L->stages != 0 || (L->flags & (ADVOPT_F_ATAN2 | ADVOPT_F_NORMED | ADVOPT_F_FISHER | ADVOPT_F_FISHER_STATS))))
+    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: Lion launches are float32 or 'auto', general-kernel only");
   if ((L->flags & ADVOPT_F_FACT_M) && L->precision != ADVOPT_PREC_FP32)
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: factored momentum needs ADVOPT_PREC_FP32");
   if ((L->flags & ADVOPT_F_EMIT_UPDATE) && (L->flags & (ADVOPT_F_FISHER | ADVOPT_F_FISHER_STATS)))

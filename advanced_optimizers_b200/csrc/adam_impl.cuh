@@ -617,8 +617,8 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
         if constexpr (ALGO == ADVOPT_ALGO_LION) {
           // Lion_adv.py:236-247 on the float32 grad: c = lerp(g, m, beta1),
           // m = lerp(m, g, 1 - beta2), update = sign(c) (lion_k.py:23-24)
-          const float c = lerp_t(gi, m[e], beta1);
-          m_new[e] = ok ? lerp_t(m[e], gi, w_m) : 0.0f;
+          const float c = Rm(lerp_t(gi, m[e], beta1));
+          m_new[e] = ok ? Rm(lerp_t(m[e], gi, w_m)) : 0.0f;
           v[e] = 0.0f;
           ui = c > 0.0f ? 1.0f : (c < 0.0f ? -1.0f : c);
         } else {
@@ -740,7 +740,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
       U4 nzm{0u, 0u, 0u, 0u}, nzv{0u, 0u, 0u, 0u};
       if (!fstats && TR::kStore != 0 && (kStore == 2 || TR::kSRStates)) {
         if (has_m) nzm = noise_words<NOISE_IN>(L, T, T.nz_m, kNoiseM, k0, nv);
-        if (!fact) nzv = noise_words<NOISE_IN>(L, T, T.nz_v, kNoiseV, k0, nv);
+        if (!fact && kHasV) nzv = noise_words<NOISE_IN>(L, T, T.nz_v, kNoiseV, k0, nv);
       }
 
       // ---- factored second moment: row sums and column partials ----
@@ -924,7 +924,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
             store8_f32(T.m, k0, nv, v8, m_new);
           }
         }
-        if (!fact) {
+        if (!fact && kHasV) {        // (Lion has no second moment)
           if (kStore == 2) {
             float bmax = 0.0f;
 #pragma unroll
@@ -1102,8 +1102,9 @@ cudaError_t launch_adam_prec(const advopt_adam_launch& L, cudaStream_t s) {
     case ADVOPT_ALGO_AUXADAM:
       return pbf ? launch_adam_algo<PREC, true, ADVOPT_ALGO_AUXADAM>(L, s) : launch_adam_algo<PREC, false, ADVOPT_ALGO_AUXADAM>(L, s);
     case ADVOPT_ALGO_LION:
-      // factored Lion: float32 launches only (checked by advopt_adam_step)
-      if constexpr (PREC == ADVOPT_PREC_FP32)
+      // Lion: float32 (factored, or float32 params) and 'auto' launches
+      // (checked by advopt_adam_step)
+      if constexpr (PREC == ADVOPT_PREC_FP32 || PREC == ADVOPT_PREC_AUTO)
         return pbf ? launch_adam_algo<PREC, true, ADVOPT_ALGO_LION>(L, s) : launch_adam_algo<PREC, false, ADVOPT_ALGO_LION>(L, s);
       return cudaErrorInvalidValue;
     default:

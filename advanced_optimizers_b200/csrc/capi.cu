@@ -35,6 +35,7 @@ extern "C" size_t advopt_sizeof(int which) {
     case 6: return sizeof(advopt_prodigy_dev);
     case 7: return sizeof(advopt_prodigy_scalar_args);
     case 8: return sizeof(advopt_prodigy_d_args);
+    case 9: return sizeof(advopt_spectral_tensor);
     default: return 0;
   }
 }

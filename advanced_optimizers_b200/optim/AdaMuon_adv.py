@@ -101,7 +101,7 @@ class AdaMuon_adv(MuonFamilyBase):
         # spectral normalisation of the orthogonalised update: the reference
         # calls it without its target_scale argument and fails
         reject(spectral_normalization, "spectral_normalization")
-        reject(adam_spectral_normalization, "adam_spectral_normalization")
+        reject(adam_spectral_normalization and adam_fisher_wd, "adam_spectral_normalization with adam_fisher_wd")
         reject(centered_wd, "centered_wd for AdaMuon_adv")
         reject(not auto_projection and kappa_p not in (1.0, 2.0), f"kappa_p={kappa_p}")
         defaults = {

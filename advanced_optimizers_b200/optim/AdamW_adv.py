@@ -13,7 +13,7 @@ from typing import Callable, Optional
 import torch
 
 from .. import _lib as L
-from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, init_adam_state
+from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, SpectralInit, init_adam_state
 from ._common import load_state_dict_exact, reject
 from ._kourkoutas import KourkoutasBeta
 
@@ -73,7 +73,7 @@ class AdamW_adv(torch.optim.Optimizer):
         if nnmf_factor:
             state_precision = "factored"
         reject(orthogonal_gradient != "disabled", "orthogonal_gradient")
-        reject(spectral_normalization, "spectral_normalization")
+        reject(spectral_normalization and fisher_wd, "spectral_normalization with fisher_wd")
         reject(state_precision not in SUPPORTED_PRECISIONS, f"state_precision='{state_precision}'")
         reject(centered_wd and centered_wd_mode not in ("full", "float8", "int8", "int4"),
                f"centered_wd_mode='{centered_wd_mode}'")
@@ -97,6 +97,7 @@ class AdamW_adv(torch.optim.Optimizer):
         self._init_lr = lr if lr > 0 else 1
         super().__init__(params, defaults)
         self._runner = AdamFamilyRunner(seed=42)
+        self._spectral_init = SpectralInit()
         self._ids = {}
         # Kourkoutas-beta's layer map is built once, before the first step
         # (Kourkoutas.py:25-57)
@@ -150,6 +151,8 @@ class AdamW_adv(torch.optim.Optimizer):
                         centered_wd=group.get("centered_wd", 0.0),
                         centered_wd_mode=group.get("centered_wd_mode", "float8"),
                         fisher_wd=group.get("fisher_wd", False))
+        if group.get("spectral_normalization", False):
+            self._spectral_init(state, p)       # AdamW_adv.py:272-273
 
     def _cfg(self, group):
         return AdamCfg(algo=L.ALGO_ADAMW, lr=group["lr"], betas=group["betas"], eps=group["eps"],
@@ -160,7 +163,8 @@ class AdamW_adv(torch.optim.Optimizer):
                        fisher_wd=group.get("fisher_wd", False), centered_wd=group.get("centered_wd", 0.0),
                        centered_wd_mode=group.get("centered_wd_mode", "float8"),
                        stochastic_rounding=self.stochastic_rounding,
-                       kourkoutas=self.kourkoutas_helper if group.get("kourkoutas_beta", False) else None)
+                       kourkoutas=self.kourkoutas_helper if group.get("kourkoutas_beta", False) else None,
+                       spectral=group.get("spectral_normalization", False))
 
     def _step_params(self, gi, group, params):
         for p in params:

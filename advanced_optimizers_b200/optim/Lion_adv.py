@@ -20,7 +20,7 @@ from .. import _lib as L
 from .._device import DeviceTable, aligned16, dtype_code, ptr, require_cuda_tensor, stream_handle, upload_static
 from .._plan import plan as plan_pieces
 from .._plan import effective_shape
-from ._adam_family import SHIFTER, AdamCfg, AdamFamilyRunner, adjust_wds, f32, sign_storage
+from ._adam_family import SHIFTER, AdamCfg, AdamFamilyRunner, SpectralInit, adjust_wds, f32, sign_storage
 from ._common import load_state_dict_exact, reject
 
 
@@ -80,7 +80,6 @@ class Lion_adv(torch.optim.Optimizer):
         reject(orthogonal_gradient != "disabled", "orthogonal_gradient")
         reject(stochastic_sign, "stochastic_sign")
         reject(centered_wd, "centered_wd for Lion_adv")
-        reject(spectral_normalization, "spectral_normalization")
         reject(kappa_p != 1.0 and not auto_kappa_p, f"kappa_p={kappa_p}")
         defaults = dict(lr=lr, betas=betas, weight_decay=weight_decay, cautious_wd=cautious_wd,
                         vector_reshape=vector_reshape, orthogonal_gradient=orthogonal_gradient, kappa_p=kappa_p,
@@ -94,7 +93,8 @@ class Lion_adv(torch.optim.Optimizer):
         self._ids = {}
         self._test_noise = None
         self.seed = 42
-        self._fruner = AdamFamilyRunner(seed=42)     # factored tensors
+        self._fruner = AdamFamilyRunner(seed=42)     # factored / spectral-normalised tensors
+        self._spectral_init = SpectralInit()
         self.init_step()
 
     def load_state_dict(self, state_dict: dict) -> None:
@@ -141,6 +141,8 @@ class Lion_adv(torch.optim.Optimizer):
                 state["shifter"] = torch.tensor(SHIFTER, device=p.device, dtype=torch.uint8)
             else:
                 state["exp_avg"] = torch.zeros_like(p, device=p.device, dtype=p.dtype)
+            if group.get("spectral_normalization", False):
+                self._spectral_init(state, p)             # Lion_adv.py:179-180
 
     def _tid(self, p):
         t = self._ids.get(id(p))
@@ -154,10 +156,13 @@ class Lion_adv(torch.optim.Optimizer):
             self._init_state(p, group)
             require_cuda_tensor(p, "param")
             require_cuda_tensor(p.grad, "grad")
-        fac = [p for p in params if self.state[p]["factored"]]
+        # factored tensors, and every tensor of a spectral-normalised group,
+        # step in the Adam-family general kernel (ADVOPT_ALGO_LION)
+        spectral = group.get("spectral_normalization", False)
+        fac = [p for p in params if self.state[p]["factored"] or spectral]
         if fac:
             self._run_factored(gi, group, fac)
-        params = [p for p in params if not self.state[p]["factored"]]
+        params = [p for p in params if not (self.state[p]["factored"] or spectral)]
         by_dtype = {}
         for p in params:
             if group.get("auto_kappa_p", False) and p.ndim >= 4:
@@ -206,21 +211,25 @@ class Lion_adv(torch.optim.Optimizer):
                 torch.cuda.current_stream(pl.device).synchronize()
 
     def _run_factored(self, gi, group, params):
-        """The factored params of a group: one float32 general-kernel launch
-        per dtype (Lion_adv.py:214-254)."""
-        cfg = AdamCfg(algo=L.ALGO_LION, lr=group["lr"], betas=group["betas"], eps=1.0,
-                      weight_decay=group["weight_decay"], precision="factored", use_bias_correction=False,
-                      cautious_wd=group.get("cautious_wd", False), stochastic_rounding=self.stochastic_rounding)
-        by_dtype = {}
+        """Params stepped by the general kernel: one launch per (dtype,
+        factored) — float32 for factored m, the param dtype otherwise
+        (Lion_adv.py:214-278) — with the spectral scaling when the group
+        asks for it."""
+        by_kind = {}
         for p in params:
             if group.get("auto_kappa_p", False) and p.ndim >= 4:
                 raise NotImplementedError("Lion-K with kappa_p=2 (4-D params under auto_kappa_p) is not supported")
-            by_dtype.setdefault((p.dtype, p.device), []).append(p)
+            by_kind.setdefault((p.dtype, p.device, bool(self.state[p]["factored"])), []).append(p)
         if self._test_noise is not None:
             self._fruner.test_noise = {id(p): {"param": self._test_noise[id(p)]["param"]}
                                        for p in params if "param" in self._test_noise.get(id(p), {})}
-        for (dt, dev), ps in by_dtype.items():
-            key = (gi, dt, dev, tuple(id(p) for p in ps))
+        for (dt, dev, fac), ps in by_kind.items():
+            cfg = AdamCfg(algo=L.ALGO_LION, lr=group["lr"], betas=group["betas"], eps=1.0,
+                          weight_decay=group["weight_decay"], precision="factored" if fac else "auto",
+                          use_bias_correction=False, cautious_wd=group.get("cautious_wd", False),
+                          stochastic_rounding=self.stochastic_rounding,
+                          spectral=group.get("spectral_normalization", False))
+            key = (gi, dt, dev, fac, tuple(id(p) for p in ps))
             self._fruner.run(key, ps, [self.state[p] for p in ps], [self._tid(p) for p in ps], cfg)
         self._fruner.test_noise = None
 

@@ -103,7 +103,7 @@ class Muon_adv(MuonFamilyBase):
         # spectral normalisation of the orthogonalised update: the reference
         # calls it without its target_scale argument and fails
         reject(spectral_normalization, "spectral_normalization")
-        reject(adam_spectral_normalization, "adam_spectral_normalization")
+        reject(adam_spectral_normalization and adam_fisher_wd, "adam_spectral_normalization with adam_fisher_wd")
         reject(centered_wd, "centered_wd for Muon_adv")
         defaults = {
             "lr": lr, "beta1": beta1, "weight_decay": weight_decay, "cautious_wd": cautious_wd,

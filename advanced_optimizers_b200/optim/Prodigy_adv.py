@@ -25,7 +25,7 @@ import torch.distributed as dist
 
 from .. import _lib as L
 from .._device import stream_handle
-from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, init_adam_state
+from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, SpectralInit, init_adam_state
 from ._common import load_state_dict_exact, reject
 from ._kourkoutas import KourkoutasBeta
 
@@ -290,6 +290,12 @@ class Prodigy_adv(torch.optim.Optimizer):
                         centered_wd=group.get("centered_wd", 0.0),
                         centered_wd_mode=group.get("centered_wd_mode", "float8"),
                         fisher_wd=group.get("fisher_wd", False))
+        if group.get("spectral_normalization", False):
+            # a param-group key only: the constructor takes no such argument
+            # (Prodigy_adv.py:319-320, 490-493)
+            if not hasattr(self, "_spectral_init"):
+                self._spectral_init = SpectralInit()
+            self._spectral_init(state, p)
         sp = group["slice_p"]
         state["s"] = torch.zeros_like(p.flatten()[::sp]).detach().contiguous()
         if p.any():
@@ -307,7 +313,8 @@ class Prodigy_adv(torch.optim.Optimizer):
                        fisher_wd=group.get("fisher_wd", False), centered_wd=group.get("centered_wd", 0.0),
                        centered_wd_mode=group.get("centered_wd_mode", "float8"),
                        stochastic_rounding=self.stochastic_rounding, prodigy=pd,
-                       kourkoutas=self.kourkoutas_helper if group.get("kourkoutas_beta", False) else None)
+                       kourkoutas=self.kourkoutas_helper if group.get("kourkoutas_beta", False) else None,
+                       spectral=group.get("spectral_normalization", False))
 
     def _step_params(self, gi, group, params):
         for p in params:

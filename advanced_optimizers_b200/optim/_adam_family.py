@@ -182,6 +182,132 @@ def init_adam_state(p, state, *, precision, factored_2nd, beta1, vector_reshape,
 
 
 # ---------------------------------------------------------------------------
+# spectral normalisation state (scaled_optm.py:108-142)
+# ---------------------------------------------------------------------------
+
+def is_spectral(p) -> bool:
+    """scaled_optm.is_spectral (scaled_optm.py:108-116)."""
+    if getattr(p, "_is_oft", False):
+        return True
+    if p.ndim < 2:
+        return False
+    if getattr(p, "_is_dora_scale", False) or getattr(p, "is_vector", False):
+        return False
+    return bool(getattr(p, "is_hidden", True))
+
+
+def spectral_kind(p) -> str:
+    """How scale_update treats p's update (scaled_optm.py:54-72): 'maxabs'
+    (1-D, DoRA magnitudes) or 'spectral' (2-D and larger)."""
+    if getattr(p, "_is_oft", False):
+        raise NotImplementedError("spectral normalisation of OFT blocks is not supported by the B200 kernels")
+    if p.ndim < 2 or getattr(p, "_is_dora_scale", False):
+        return "maxabs"
+    if not is_spectral(p):
+        # the reference has no singular vectors for it and fails in scale_update
+        raise NotImplementedError("spectral normalisation of a 2-D param marked is_vector / not is_hidden")
+    return "spectral"
+
+
+@torch.no_grad()
+def init_spectral_norm(state, p, generator):
+    """init_spectral_norm (scaled_optm.py:118-142), non-OFT: unit Gaussian v
+    (d_in) then u (d_out) in the param dtype, drawn on the param's device."""
+    if not is_spectral(p) or "spectral_u" in state:
+        return
+    d_out = p.shape[0]
+    d_in = p.numel() // d_out
+    v = torch.randn(d_in, device=p.device, dtype=p.dtype, generator=generator)
+    state["spectral_v"] = v.div_(v.norm().add_(1e-12))
+    u = torch.randn(d_out, device=p.device, dtype=p.dtype, generator=generator)
+    state["spectral_u"] = u.div_(u.norm().add_(1e-12))
+
+
+class SpectralInit:
+    """Creates spectral_u / spectral_v for params that get spectral
+    normalisation, from one seeded torch generator per device (the
+    reference draws them from its own per-device generator)."""
+
+    def __init__(self, seed: int = 42):
+        self.seed = int(seed)
+        self.gens = {}
+
+    def __call__(self, state, p):
+        spectral_kind(p)            # raises for updates the kernels do not scale
+        g = self.gens.get(p.device)
+        if g is None:
+            g = torch.Generator(device=p.device)
+            g.manual_seed(self.seed)
+            self.gens[p.device] = g
+        init_spectral_norm(state, p, g)
+
+
+class SpectralPlan:
+    """Scratch, descriptor table and work lists of advopt_spectral_step for
+    one group plan: per tensor the unscaled update (param dtype for 2-D
+    updates, which the reference casts to the singular vectors' dtype; the
+    update's own dtype for 1-D ones), the U^T u column partials per row slab,
+    U v and two scalars."""
+
+    def __init__(self, gp):
+        n = gp.n
+        sd = np.zeros(n, L.SPECTRAL_TENSOR_DT)
+        self.bufs = []
+        kinds = [spectral_kind(p) for p in gp.params]
+        rows_2d = sum(p.shape[0] for p, k in zip(gp.params, kinds) if k == "spectral")
+        # row slabs of the U^T u pass: about 600 work items, 8..64 rows each
+        slab = int(min(64, max(8, ((-(-rows_2d // 600) + 7) // 8) * 8)))
+        col_items, row_items = [], []
+        for i, (p, st, kind) in enumerate(zip(gp.params, gp.states, kinds)):
+            numel = p.numel()
+            if kind == "spectral":
+                if "spectral_u" not in st:
+                    raise RuntimeError("spectral normalisation state missing (spectral_u / spectral_v)")
+                vbf = st["spectral_u"].dtype == torch.bfloat16
+                d_out = p.shape[0]
+                d_in = numel // d_out
+                n_slabs = -(-d_out // slab)
+                vpart = torch.empty(n_slabs * d_in, dtype=torch.float32, device=gp.device)
+                uraw = torch.empty(d_out, dtype=torch.float32, device=gp.device)
+                self.bufs += [vpart, uraw]
+                flags = (L.S_UPD_BF16 | L.S_VEC_BF16) if vbf else 0
+                target = 1.0 if getattr(p, "_is_lora_A", False) else math.sqrt(d_out / d_in)
+                sd["u"][i], sd["v"][i] = ptr(st["spectral_u"]), ptr(st["spectral_v"])
+                sd["v_partial"][i], sd["u_raw"][i] = ptr(vpart), ptr(uraw)
+                sd["d_out"][i], sd["d_in"][i], sd["n_slabs"][i], sd["target"][i] = d_out, d_in, n_slabs, target
+                for s in range(n_slabs):
+                    col_items.append((s * slab, min((s + 1) * slab, d_out), i, s))
+                for r0 in range(0, d_out, 64):
+                    row_items.append((r0, min(r0 + 64, d_out), i, 0))
+                ubf = vbf
+            else:
+                # max-abs scaling in the update's own dtype: bf16 under bf16 math
+                ubf = gp.math_bf16 and not st.get("factored", False)
+                flags = L.S_MAXABS | (L.S_UPD_BF16 if ubf else 0)
+                sd["d_out"][i], sd["d_in"][i], sd["n_slabs"][i], sd["target"][i] = 1, numel, 0, 1.0
+                for k in range(0, numel, 65536):
+                    row_items.append((k, min(k + 65536, numel), i, 0))
+            upd = torch.empty(numel, dtype=torch.bfloat16 if ubf else torch.float32, device=gp.device)
+            scal = torch.zeros(2, dtype=torch.float32, device=gp.device)
+            self.bufs += [upd, scal]
+            sd["update"][i], sd["scalars"][i], sd["flags"][i] = ptr(upd), ptr(scal), flags
+            gp.descs["update_out"][i] = ptr(upd)
+            gp.vec_ok[i] = gp.vec_ok[i] and ptr(upd) % 16 == 0
+            if ubf:
+                gp.descs["flags"][i] |= L.T_UPD_BF16
+        self.table = upload_static(sd, gp.device)
+
+        def pieces(items):
+            a = np.zeros(max(1, len(items)), L.PIECE_DT)
+            for j, (b, e, t, s) in enumerate(items):
+                a[j] = (b, e, t, s)
+            return upload_static(a, gp.device), len(items)
+
+        self.col_dev, self.n_col = pieces(col_items)
+        self.row_dev, self.n_row = pieces(row_items)
+
+
+# ---------------------------------------------------------------------------
 # launch configuration
 # ---------------------------------------------------------------------------
 
@@ -192,7 +318,7 @@ class AdamCfg:
     def __init__(self, *, algo, lr, betas, eps, weight_decay, precision, nesterov=False, nesterov_coef=None,
                  use_bias_correction=True, use_atan2=False, normed_momentum=False, cautious_wd=False,
                  fisher_wd=False, centered_wd=0.0, centered_wd_mode="float8", stochastic_rounding=True,
-                 prodigy=None, kourkoutas=None, kourkoutas_apply=True):
+                 prodigy=None, kourkoutas=None, kourkoutas_apply=True, spectral=False):
         self.algo = algo
         self.lr = float(lr)
         self.beta1, self.beta2 = float(betas[0]), float(betas[1])
@@ -216,6 +342,11 @@ class AdamCfg:
         # False: the grads' squared norms are pooled but the v update keeps
         # beta2 (the hybrid optimizers' auxiliary Adam under bias correction)
         self.kourkoutas_apply = bool(kourkoutas_apply)
+        # spectral_normalization: the step emits the unscaled update and
+        # advopt_spectral_step scales and applies it (scaled_optm.py:35-72)
+        self.spectral = bool(spectral)
+        if self.spectral and self.fisher:
+            raise NotImplementedError("spectral_normalization with fisher_wd is not supported by the B200 kernels")
 
 
 class GroupPlan:
@@ -313,7 +444,7 @@ class GroupPlan:
         # the fast kernel keeps element offsets in 32 bits (tensors below 2^34
         # elements); signed rank-1 momentum runs in the general kernel
         self.fast = (not ext) and (not any_generic) and factors_aligned and max(numels, default=0) < (1 << 34) \
-            and not self.any_fact_m
+            and not self.any_fact_m and not cfg.spectral and cfg.algo != L.ALGO_LION
         if self.fast:
             bpp = 2 if self.pdt == L.DT_BF16 else 4
             bps = {0: 4, 1: 2, 2: 1, 3: 2 if self.pdt == L.DT_BF16 else 4}[self.precision]
@@ -379,6 +510,7 @@ class GroupPlan:
         # Prodigy with d on the device: per-tensor (eps_t, wd_t, cwd_t) in double
         self.pconsts_host = None
         self.pconsts_dev = None
+        self.spectral = SpectralPlan(self) if cfg.spectral else None
 
     def kourkoutas_tables(self, kk):
         if self.layer_dev is None:
@@ -438,7 +570,8 @@ class AdamFamilyRunner:
 
     def get_plan(self, key, params, states, ids, cfg):
         pl = self.plans.get(key)
-        if pl is None or any(pl.descs["param"][i] != ptr(p) for i, p in enumerate(params)):
+        if pl is None or (pl.spectral is not None) != cfg.spectral or \
+                any(pl.descs["param"][i] != ptr(p) for i, p in enumerate(params)):
             pl = GroupPlan(params, states, ids, cfg, self.reserve_sms)
             pl.err = self.errors.word(pl.device)
             self.plans[key] = pl
@@ -521,6 +654,8 @@ class AdamFamilyRunner:
             flags |= L.F_NO_WD
         if pl.any_fact_m:
             flags |= L.F_FACT_M
+        if cfg.spectral:
+            flags |= L.F_EMIT_UPDATE
         noise_keep = []
         if self.test_noise is not None:
             flags |= L.F_NOISE_IN
@@ -626,6 +761,12 @@ class AdamFamilyRunner:
             L.check(lib.advopt_prodigy_finish(ctypes.byref(s), int(prodigy_sums.data_ptr()), coef, s_bf16, stream),
                     "advopt_prodigy_finish")
             self.launch_count += 1
+        if cfg.spectral:
+            sp = pl.spectral
+            L.check(lib.advopt_spectral_step(ctypes.byref(s), int(sp.table.data_ptr()), int(sp.col_dev.data_ptr()),
+                                             sp.n_col, int(sp.row_dev.data_ptr()), sp.n_row, stream),
+                    "advopt_spectral_step")
+            self.launch_count += 3 + (1 if sp.n_col else 0) + (1 if sp.n_row else 0)
         self.errors.after_launch(pl.device)
         for st in states:
             st["step"] += 1

@@ -6,7 +6,7 @@ from __future__ import annotations
 import torch
 
 from .. import _lib as L
-from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, init_adam_state
+from ._adam_family import AdamCfg, AdamFamilyRunner, SUPPORTED_PRECISIONS, SpectralInit, init_adam_state
 from ._common import load_state_dict_exact, reject
 from ._kourkoutas import KourkoutasBeta
 from ._muon_family import MuonMatrixRunner, init_muon_state, is_suitable_for_muon
@@ -18,6 +18,7 @@ class MuonFamilyBase(torch.optim.Optimizer):
     def _setup(self):
         self.device = self.param_groups[0]["params"][0].device if self.param_groups[0]["params"] else None
         self._adam_runner = AdamFamilyRunner(seed=42)
+        self._spectral_init = SpectralInit()
         self._muon_runner = MuonMatrixRunner(seed=42)
         self._ids = {}
         self._mstep = {}
@@ -95,6 +96,8 @@ class MuonFamilyBase(torch.optim.Optimizer):
                             centered_wd=group.get("centered_wd", 0.0),
                             centered_wd_mode=group.get("centered_wd_mode", "float8"),
                             fisher_wd=group.get("adam_fisher_wd", False))
+            if group.get("adam_spectral_normalization", False):
+                self._spectral_init(state, p)            # Muon_AuxAdam.py:63-64
             state["is_muon"] = False
 
     def _adam_cfg(self, group, factored=False):
@@ -123,7 +126,8 @@ class MuonFamilyBase(torch.optim.Optimizer):
                        fisher_wd=group.get("adam_fisher_wd", False), centered_wd=group.get("centered_wd", 0.0),
                        centered_wd_mode=group.get("centered_wd_mode", "float8"),
                        stochastic_rounding=self.stochastic_rounding,
-                       kourkoutas=kk, kourkoutas_apply=not bc)
+                       kourkoutas=kk, kourkoutas_apply=not bc,
+                       spectral=group.get("adam_spectral_normalization", False))
 
     def _muon_hp(self, group, p):
         raise NotImplementedError

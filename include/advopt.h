@@ -49,8 +49,9 @@ extern "C" {
 #define ADVOPT_ALGO_ADAMW 0    /* AdamW_adv._step_parameter (v before m)           */
 #define ADVOPT_ALGO_AUXADAM 1  /* Muon_AuxAdam._adam_step_parameter (m before v)   */
 #define ADVOPT_ALGO_PRODIGY 2  /* Prodigy_adv._step_parameter (d-scaled moments)   */
-#define ADVOPT_ALGO_LION 3     /* Lion_adv factored tensors (Lion_adv.py:232-254): no second moment,
-                                  every tensor ADVOPT_T_FACTORED | ADVOPT_T_FACT_M, ADVOPT_PREC_FP32;
+#define ADVOPT_ALGO_LION 3     /* Lion_adv in the general kernel (Lion_adv.py:214-278): no second
+                                  moment; ADVOPT_PREC_FP32 (factored tensors: ADVOPT_T_FACTORED |
+                                  ADVOPT_T_FACT_M) or ADVOPT_PREC_AUTO (m in the param dtype);
                                   beta1 = the lerp weight of the update, w_m = 1 - beta2 */
 
 /* launch flags */
@@ -206,6 +207,48 @@ typedef struct advopt_adam_launch {
  * (Prodigy_adv.py:372-519), and param_update.apply_parameter_update
  * (param_update.py:77-156) for every tensor of the group. */
 int advopt_adam_step(const advopt_adam_launch* launch, void* stream);
+
+/*
+ * Spectral normalisation (scaled_optm.py:35-72, 160-168, 255-295), the step's
+ * last part when a group sets spectral_normalization: advopt_adam_step with
+ * ADVOPT_F_EMIT_UPDATE writes each tensor's unscaled update U to update_out;
+ * advopt_spectral_step then
+ *   - for a 2-D update (d_out x d_in, in the singular vectors' dtype): one
+ *     power-iteration step v = norm(U^T u), u = norm(U v), sigma = u . (U v),
+ *     scale = lr * (target / max(sigma, 1/(sqrt(d_out)+sqrt(d_in)))), with
+ *     each torch op's rounding to that dtype; u and v are updated in place;
+ *   - for a 1-D update: scale = lr / max(max|U|, 1e-12) in the update's dtype;
+ * and applies p = apply_parameter_update(p, U * scale) (param_update.py:77-156)
+ * with the launch's weight decay, cautious mask, centered anchors and bf16
+ * stochastic rounding.  lr is each tensor's step_size in the launch's table.
+ */
+#define ADVOPT_S_UPD_BF16 (1u << 0)    /* update_out holds bf16 (else float32) */
+#define ADVOPT_S_VEC_BF16 (1u << 1)    /* u, v are bf16 (else float32) */
+#define ADVOPT_S_MAXABS (1u << 2)      /* 1-D update: max-abs scaling, no u / v */
+
+typedef struct advopt_spectral_tensor {
+  const void* update;        /* U [d_out][d_in] (the adam table's update_out)     */
+  void* u;                   /* spectral_u [d_out]                               */
+  void* v;                   /* spectral_v [d_in]                                */
+  float* v_partial;          /* scratch [n_slabs][d_in]                          */
+  float* u_raw;              /* scratch [d_out]                                  */
+  float* scalars;            /* scratch [2]: the step's scale, max|U| (1-D)      */
+  int64_t d_out;             /* 1-D: 1                                           */
+  int64_t d_in;              /* 1-D: numel                                       */
+  float target;              /* sqrt(d_out / d_in) (1 for LoRA A factors)        */
+  uint32_t flags;            /* ADVOPT_S_*                                       */
+  int32_t n_slabs;           /* row slabs of the U^T u pass                      */
+  int32_t pad;
+} advopt_spectral_tensor;
+
+/* `launch` is the step's launch (its table, pieces, grid, flags, seed);
+ * `tensors` has launch->n_tensors entries in the same order.  col_items: one
+ * advopt_piece per row slab of each 2-D update (begin/end = rows, slot = slab
+ * index, at most 64 rows); row_items: pieces of rows (2-D, at most 64 rows)
+ * or of elements (1-D) for the U v and max|U| passes. */
+int advopt_spectral_step(const advopt_adam_launch* launch, const advopt_spectral_tensor* tensors,
+                         const advopt_piece* col_items, int32_t n_col_items,
+                         const advopt_piece* row_items, int32_t n_row_items, void* stream);
 
 /* Second half of factored_2nd / 'factored': reduce the column partials into
  * mv_v_nmf (and mv_m_nmf for ADVOPT_T_FACT_M tensors) and normalise one factor

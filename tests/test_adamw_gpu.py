@@ -88,6 +88,14 @@ def _oracle_state_from_torch(st):
                   dict(state_precision="factored", nesterov=True, weight_decay=0.01)), id="factored_bf16"),
     pytest.param(([(4096, 4096), (4096,), (333, 12)], "f32",
                   dict(state_precision="factored", cautious_wd=True, weight_decay=0.05)), id="factored_f32"),
+    # spectral normalisation: one power-iteration step per 2-D update (bf16
+    # singular vectors), max-abs scaling of the 1-D update
+    pytest.param(([(2048, 1024), (1024,), (512, 1536), (96, 40, 3)], "bf16",
+                  dict(state_precision="auto", spectral_normalization=True, weight_decay=0.01, nesterov=True)),
+                 id="spectral_bf16"),
+    pytest.param(([(4096, 1024), (1024,)], "bf16",
+                  dict(state_precision="factored", spectral_normalization=True, cautious_wd=True,
+                       weight_decay=0.05)), id="spectral_factored_bf16"),
 ])
 def test_adamw_matches_oracle_large(case):
     import advanced_optimizers_b200 as A
@@ -101,6 +109,7 @@ def test_adamw_matches_oracle_large(case):
     hp = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, nesterov=False, use_bias_correction=True,
               stochastic_rounding=True, precision=kw.get("state_precision", "auto"))
     hp.update({k: v for k, v in kw.items() if k != "state_precision"})
+    hp["spectral"] = kw.get("spectral_normalization", False)
     p_o = [to_numpy(t) for t in p_host]
     p_o = [O.from_bf16_bits(x) if dt == "bf16" else x for x in p_o]
     for s in range(2):
@@ -139,7 +148,7 @@ def test_adamw_matches_oracle_large(case):
                 if torch.is_tensor(val) and key in ostate[i] and isinstance(ostate[i][key], np.ndarray):
                     check_state(key, to_numpy(val), ostate[i][key], f"{what} {key}")
             # keep the oracle on the device's factors so later steps compare one step each
-            for key in ("mu_v_nmf", "mv_v_nmf", "mu_m_nmf", "mv_m_nmf", "sign"):
+            for key in ("mu_v_nmf", "mv_v_nmf", "mu_m_nmf", "mv_m_nmf", "sign", "spectral_u", "spectral_v"):
                 if key in ostate[i]:
                     ostate[i][key] = to_numpy(opt.state[p][key])
             p_o[i] = O.from_bf16_bits(to_numpy(p)).reshape(sh) if dt == "bf16" else to_numpy(p).reshape(sh)
