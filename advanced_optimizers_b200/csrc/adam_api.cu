@@ -245,8 +245,11 @@ extern "C" int advopt_adam_step(const advopt_adam_launch* L, void* stream) {
       ((L->precision != ADVOPT_PREC_FP32 && L->precision != ADVOPT_PREC_AUTO) || !(L->flags & ADVOPT_F_HAS_M) ||
        L->stages != 0 || (L->flags & (ADVOPT_F_ATAN2 | ADVOPT_F_NORMED | ADVOPT_F_FISHER | ADVOPT_F_FISHER_STATS))))
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: Lion launches are float32 or 'auto', general-kernel only");
-  if ((L->flags & ADVOPT_F_FACT_M) && L->precision != ADVOPT_PREC_FP32)
-    return set_error(ADVOPT_E_INVALID, "advopt_adam_step: factored momentum needs ADVOPT_PREC_FP32");
+  if ((L->flags & ADVOPT_F_FACT_M) && (L->precision != ADVOPT_PREC_FP32 || !(L->flags & ADVOPT_F_HAS_M) ||
+                                       (L->smem_floats % 2) != 0))
+    return set_error(ADVOPT_E_INVALID,
+                     "advopt_adam_step: factored momentum needs ADVOPT_PREC_FP32, ADVOPT_F_HAS_M and an even "
+                     "shared-memory split");
   if ((L->flags & ADVOPT_F_EMIT_UPDATE) && (L->flags & (ADVOPT_F_FISHER | ADVOPT_F_FISHER_STATS)))
     return set_error(ADVOPT_E_INVALID, "advopt_adam_step: update emission with Fisher weight decay");
   return check_cuda(run_adam(*L, static_cast<cudaStream_t>(stream)), "advopt_adam_step");

@@ -391,7 +391,7 @@ __device__ __forceinline__ void slice_apply(const TensorRegs& T, const SliceAt& 
   st1 += (double)fabsf(s2);
 }
 
-template <int PREC, bool PBF, int ALGO, bool EXT, bool NOISE_IN>
+template <int PREC, bool PBF, int ALGO, bool EXT, bool NOISE_IN, bool FM = false>
 __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_launch L) {
   using TR = StateTraits<PREC, PBF>;
   constexpr int kStore = TR::kStore;
@@ -404,10 +404,10 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
   float* colacc = reinterpret_cast<float*>(dsm4);
   float* vbuf = colacc + L.gen_offset;
   float* segs = vbuf + kChunk;
-  // signed rank-1 momentum ('factored' launches, fp32 only): the same three
-  // areas again for |m|, after the second moment's
-  constexpr bool kFM = PREC == ADVOPT_PREC_FP32;
-  float* colacc_m = colacc + L.gen_offset + 2 * kChunk + 4;
+  // FM: a launch of signed rank-1 momentum tensors only ('factored', fp32);
+  // the same areas again for |m| in the second half of shared memory
+  static_assert(!FM || PREC == ADVOPT_PREC_FP32, "factored momentum is float32");
+  float* colacc_m = colacc + (FM ? L.smem_floats / 2 : 0);
   float* mbuf = colacc_m + L.gen_offset;
   float* msegs = mbuf + kChunk;
   __shared__ float red[2][kWarps][6];         // per-chunk block reductions (double-buffered)
@@ -453,14 +453,14 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
       c_v = l >= 0 ? L.layer_beta2[2 * l + 1] : c_v0;
     }
     double gacc = 0.0;     // Kourkoutas-beta: this thread's sum of g*g over the piece
-    const bool fact = T.flags & ADVOPT_T_FACTORED;
+    const bool fact = FM || (T.flags & ADVOPT_T_FACTORED);
     const bool vec = T.flags & ADVOPT_T_VEC;
     const bool has_anchor = EXT && (((T.flags >> ADVOPT_T_ANCHOR_SHIFT) & 7u) != 0);
     const bool fact_sums = fact && !fstats;   // factored row/column sums (skipped by the Fisher pass)
     constexpr bool kHasV = ALGO != ADVOPT_ALGO_LION;
     const bool v_sums = fact_sums && kHasV;
     // signed rank-1 momentum (state_precision='factored', AdamW_adv.py:342-399)
-    const bool factm = kFM && has_m && fact && (T.flags & ADVOPT_T_FACT_M);
+    const bool factm = FM && has_m;
     const bool fm_sums = factm && !fstats;
     const int64_t d2 = fact ? T.d2 : 1;
     const int64_t pd2 = (d2 + 7) >> 3;        // sign bytes per row
@@ -1069,6 +1069,18 @@ cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
     }
     return launch_fast<PREC, PBF, ALGO, kCfDyn>(L, smem, s);
   }
+  }
+  if (L.flags & ADVOPT_F_FACT_M) {
+    // every tensor of the launch holds signed rank-1 momentum
+    if constexpr (PREC == ADVOPT_PREC_FP32) {
+      auto kf = ext ? (nin ? adam_kernel<PREC, PBF, ALGO, true, true, true> : adam_kernel<PREC, PBF, ALGO, true, false, true>)
+                    : (nin ? adam_kernel<PREC, PBF, ALGO, false, true, true> : adam_kernel<PREC, PBF, ALGO, false, false, true>);
+      cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      kf<<<L.grid, kThreads, smem, s>>>(L);
+      return cudaGetLastError();
+    }
+    return cudaErrorInvalidValue;
   }
   auto k = ext ? (nin ? adam_kernel<PREC, PBF, ALGO, true, true> : adam_kernel<PREC, PBF, ALGO, true, false>)
                : (nin ? adam_kernel<PREC, PBF, ALGO, false, true> : adam_kernel<PREC, PBF, ALGO, false, false>);

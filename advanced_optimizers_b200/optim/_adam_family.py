@@ -401,7 +401,10 @@ class GroupPlan:
                 d["col_factor"][i] = ptr(st.get("mv_v_nmf"))
                 d2s.append(d2)
                 max_d2 = max(max_d2, d2)
-                if d2 < 2048 or d2 % 8 != 0:
+                # the kernel takes its generic path for these rows (and then
+                # needs the staging area in shared memory)
+                cols = [t for t in (st.get("mv_v_nmf"), st.get("mv_m_nmf") if smmf else None) if t is not None]
+                if d2 < 2048 or d2 % 8 != 0 or not aligned16(*cols):
                     any_generic = True
                 tensors += [t for t in (st.get("mu_v_nmf"), st.get("mv_v_nmf")) if t is not None]
             else:
@@ -458,9 +461,12 @@ class GroupPlan:
             self.stages = int(max(2, min(4, budget // stage)))
             self.smem_floats = self.gen_offset + self.stages * stage // 4
         elif self.any_fact_m:
-            # the second-moment and |m| areas: column sums + generic staging each
+            # two equal halves: the second-moment and the |m| column sums, with
+            # the generic path's staging when a row is not on the fast layout
+            if not all(st.get("factored", False) and "mu_m_nmf" in st for st in self.states):
+                raise RuntimeError("a factored-momentum launch holds only factored-momentum tensors")
             self.stages = 0
-            self.smem_floats = 2 * (self.gen_offset + 2 * 2048 + 4)
+            self.smem_floats = 2 * (self.gen_offset + (2 * 2048 + 4 if any_generic else 0))
             if self.smem_floats > 56832:
                 raise NotImplementedError(
                     f"state_precision='factored' with an effective row of {max_d2} columns: the B200 kernel keeps "
@@ -579,7 +585,17 @@ class AdamFamilyRunner:
 
     @torch.no_grad()
     def run(self, key, params, states, ids, cfg: AdamCfg, prodigy_sums=None):
-        """One launch over `params` (same dtype and device, all with grads)."""
+        """One launch over `params` (same dtype and device, all with grads);
+        under 'factored' two, when the group mixes signed rank-1 momentum
+        tensors with others (1-D params keep float32 m and v)."""
+        if cfg.precision == "factored":
+            fm = [bool(st.get("factored", False) and "mu_m_nmf" in st) for st in states]
+            if any(fm) and not all(fm):
+                for sel in (True, False):
+                    idx = [i for i, f in enumerate(fm) if f == sel]
+                    self.run(key + (sel,), [params[i] for i in idx], [states[i] for i in idx],
+                             [ids[i] for i in idx], cfg, prodigy_sums)
+                return
         for p in params:
             require_cuda_tensor(p, "param")
             require_cuda_tensor(p.grad, "grad")

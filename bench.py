@@ -396,7 +396,8 @@ def run_ours(args):
     if not args.no_e2e:
         e2e = run_e2e(args, owned, step, world, dev, opt if world == 1 else None, sharded)
     ns = prodigy = None
-    if not (args.no_ns and args.no_prodigy and (world < 4 or args.no_70b)):
+    modes = world == 1 and not args.no_modes
+    if not (args.no_ns and args.no_prodigy and (world < 4 or args.no_70b) and not modes):
         # the other legs need the memory of the AdamW leg
         del opt, opts, owned, params, step, sharded
         torch.cuda.empty_cache()
@@ -407,9 +408,13 @@ def run_ours(args):
     adamuon70 = None
     if world >= 4 and not args.no_70b:
         adamuon70 = run_adamuon70b_leg(args, world, rank, dev)
+    mode_legs = {}
+    if modes:
+        mode_legs["factored_step"] = run_mode_leg(args, dev, "factored")
+        mode_legs["spectral_step"] = run_mode_leg(args, dev, "spectral")
     if rank == 0:
         emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, launches, clocks, e2e, ns,
-             prodigy, adamuon70, split)
+             prodigy, adamuon70, split, mode_legs)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -650,6 +655,67 @@ def run_prodigy_leg(args, world, rank, dev):
                          "kernel_ms": kernel_ms, "algorithmic_bytes": alg}}
 
 
+# algorithmic HBM bytes per element of the two optional-mode AdamW steps
+# (bf16 params and grads):
+#  factored: grad 2 + param 2 + 2 + sign bits 1/8 + 1/8 (factors and column
+#            partials are per row / column, below 0.1%)
+#  spectral ('auto' bf16 states): step kernel grad 2 + param 2 + m 2+2 +
+#            v 2+2 + update written 2; U^T u and U v read the update twice
+#            (2 + 2); the apply pass reads update 2 and param 2, writes param 2
+MODE_BYTES_PER_ELEMENT = {"factored": 6.25, "spectral": 24.0}
+
+
+def run_mode_leg(args, dev, mode):
+    """AdamW_adv(state_precision='factored', nesterov=True) or
+    AdamW_adv(state_precision='auto', spectral_normalization=True,
+    nesterov=True) over the hidden weights and norms of args.mode_layers
+    Llama-3-8B decoder layers (no embeddings), bf16; params ~N(0, 0.02^2),
+    grads ~N(0, 1e-3^2).  Timed with CUDA events around whole steps (every
+    launch of the step)."""
+    import advanced_optimizers_b200 as A
+    shapes = llama3_8b_shapes(args.mode_layers, embed=False)
+    gen = torch.Generator(device=dev).manual_seed(4242)
+    params = [torch.nn.Parameter(torch.empty(sh, dtype=torch.bfloat16, device=dev)) for sh in shapes]
+    with torch.no_grad():
+        for p in params:
+            p.normal_(0, 0.02, generator=gen)
+            p.grad = torch.empty_like(p).normal_(0, 1e-3, generator=gen)
+    if mode == "factored":
+        kw = dict(state_precision="factored", nesterov=True, weight_decay=0.01)
+        kernel = "adam_kernel<FP32, bf16, AdamW, factored momentum> + factored finish"
+    else:
+        kw = dict(state_precision="auto", spectral_normalization=True, nesterov=True, weight_decay=0.01)
+        kernel = "adam_kernel<AUTO, bf16, AdamW> emitting U + spec_vpart/vfinish/rows/ufinish/apply"
+    opt = A.AdamW_adv(params, **kw)
+    warm, steps = 3, 10
+    for _ in range(warm):
+        opt.step()
+    torch.cuda.synchronize()
+    opt.check_errors()
+    l0 = opt._runner.launch_count
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        opt.step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    launches = (opt._runner.launch_count - l0) // steps
+    numel = sum(math.prod(s) for s in shapes)
+    alg = MODE_BYTES_PER_ELEMENT[mode] * numel
+    peak, peak_kind = measured_peaks()
+    achieved = alg / (ms * 1e-3) / 1e9
+    del opt, params
+    torch.cuda.empty_cache()
+    return {"workload": f"AdamW_adv({', '.join(f'{k}={v!r}' for k, v in kw.items())}), Llama-3-8B hidden "
+                        f"weights and norms of {args.mode_layers} layers, bf16 (inputs larger than L2)",
+            "params": numel, "tensors": len(shapes), "steps": steps, "warmup": warm, "ms_per_step": ms,
+            "value": 1000.0 / ms, "unit": "optimizer steps/s", "launches_per_step": launches,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "kernel": kernel, "algorithmic_bytes": alg,
+                         "bytes_per_element": MODE_BYTES_PER_ELEMENT[mode]}}
+
+
 def llama3_70b_matrices(layers=80):
     """Llama-3-70B 2-D weights: per layer q/o 8192x8192, k/v 1024x8192,
     gate/up 28672x8192, down 8192x28672, plus the 128256x8192 embedding; 561
@@ -818,7 +884,7 @@ def run_e2e(args, owned, step, world, dev, opt=None, sharded=None):
 
 
 def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, launches, clocks, e2e, ns=None,
-         prodigy=None, adamuon70=None, split=None):
+         prodigy=None, adamuon70=None, split=None, mode_legs=None):
     if True:
         alg = algorithmic_bytes([shapes[i] for i in mine])
         peak, peak_kind = measured_peaks()
@@ -853,6 +919,8 @@ def emit(args, shapes, mine, total, world, value, ms_per_step, kernel_avg_ms, la
             out["adamuon_70b_step"] = adamuon70
         if split is not None:
             out["sharded"] = split
+        for k, v in (mode_legs or {}).items():
+            out[k] = v
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline()
         print(json.dumps(out), flush=True)
@@ -873,6 +941,9 @@ def main():
     ap.add_argument("--prodigy-layers", type=int, default=24,
                     help="layers of the 1.3B GPT shapes in the Prodigy_adv leg (24 = the full model; fewer for profiling)")
     ap.add_argument("--no-70b", action="store_true", help="skip the AdaMuon Llama-3-70B leg (4+ GPUs)")
+    ap.add_argument("--no-modes", action="store_true",
+                    help="skip the 'factored' state and spectral-normalisation AdamW legs (1 GPU)")
+    ap.add_argument("--mode-layers", type=int, default=8, help="Llama-3-8B decoder layers of those legs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

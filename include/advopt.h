@@ -70,7 +70,9 @@ extern "C" {
 #define ADVOPT_F_GRAD_SQ (1u << 12)    /* also write each piece's sum of g*g to piece_gsq (Kourkoutas-beta) */
 #define ADVOPT_F_EMIT_UPDATE (1u << 13)/* write each tensor's unscaled update to update_out and leave the
                                           param alone (spectral normalisation finishes the step) */
-#define ADVOPT_F_FACT_M (1u << 14)     /* some tensor carries ADVOPT_T_FACT_M (needs ADVOPT_PREC_FP32) */
+#define ADVOPT_F_FACT_M (1u << 14)     /* every tensor carries ADVOPT_T_FACT_M and ADVOPT_T_FACTORED
+                                          (needs ADVOPT_PREC_FP32 and ADVOPT_F_HAS_M; dynamic shared
+                                          memory: two equal halves, the second for the |m| sums) */
 
 /* per-tensor flags */
 #define ADVOPT_T_FACTORED (1u << 0)    /* second moment as rank-1 factors (factored_2nd) */
