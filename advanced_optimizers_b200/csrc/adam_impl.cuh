@@ -168,6 +168,34 @@ __device__ __forceinline__ float fisher_den(float v, float den_u, const TensorRe
 
 
 // ---------------------------------------------------------------------------
+// Correctly rounded square root and division for the general kernel: the
+// Newton–Markstein sequences of the fast kernel (Markstein 1990; Muller et
+// al., Handbook of Floating-Point Arithmetic, ch. 5), used inside the ranges
+// where they were checked against __fsqrt_rn / __fdiv_rn on B200
+// (v in [2^-100, FLT_MAX]; 2^-50 <= d <= 2^24 and 2^-100 <= |u| <= 2^64),
+// IEEE division / square root outside them.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float sqrt_cr(float v) {
+  if (!(v >= 0x1p-100f && v <= 3.402823466e38f)) return __fsqrt_rn(v);
+  float y;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(v));
+  const float s = __fmul_rn(v, y);
+  const float r = __fmaf_rn(-s, s, v);
+  return __fmaf_rn(r, __fmul_rn(y, 0.5f), s);
+}
+__device__ __forceinline__ float div_cr(float u, float d) {
+  const float au = fabsf(u);
+  if (!(d >= 0x1p-50f && d <= 0x1p24f && au >= 0x1p-100f && au <= 0x1p64f)) return __fdiv_rn(u, d);
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+  const float e = __fmaf_rn(-d, y, 1.0f);
+  const float y1 = __fmaf_rn(e, y, y);
+  const float q = __fmul_rn(u, y1);
+  const float r = __fmaf_rn(-q, d, u);
+  return __fmaf_rn(r, y1, q);
+}
+
+// ---------------------------------------------------------------------------
 // Raw words of one thread's 8 elements of one chunk, as loaded from HBM; the
 // next chunk's words are loaded while the current chunk is computed.
 // ---------------------------------------------------------------------------
@@ -630,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
         if (fact) vi = fabsf(vi);       // _factorize_state's abs_ (factorization_util.py:35)
         v[e] = ok ? vi : 0.0f;
         // denominator (AdamW_adv.py:424-431, Prodigy_adv.py:477-482)
-        float den = __fsqrt_rn(vi);
+        float den = sqrt_cr(vi);
         if (vbf) den = round_bf16(den);
         if (ALGO != ADVOPT_ALGO_PRODIGY) {
           den = div_rcp(den, sbc2, rcp_sbc2);   // den >= 2^-75 or 0: always in div_rcp's exact range
@@ -641,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
           if (vbf) den = round_bf16(den);
         }
         du = kMBF ? round_bf16(den) : den;   // denom.to(update.dtype)
-        if (normed) gi = atan2m ? Rm(atan2f(gi, du)) : Rm(__fdiv_rn(gi, du));
+        if (normed) gi = atan2m ? Rm(atan2f(gi, du)) : Rm(div_cr(gi, du));
         // first moment and the update direction
         if (has_m) {
           float mi;
@@ -656,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
           m_new[e] = 0.0f;
           ui = (ALGO == ADVOPT_ALGO_PRODIGY) ? Rm(__fmul_rn(gi, d_f)) : gi;
         }
-        if (!normed) ui = atan2m ? Rm(atan2f(ui, du)) : Rm(__fdiv_rn(ui, du));
+        if (!normed) ui = atan2m ? Rm(atan2f(ui, du)) : Rm(div_cr(ui, du));
         }
         if (emit) uemit[e] = ui;   // the update before its scaling (AdamW_adv.py:459-461)
         ui = Rm(__fmul_rn(ui, step_size));
