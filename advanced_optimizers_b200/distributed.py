@@ -201,9 +201,11 @@ class PeerPull:
             for j, (flat, seg) in enumerate(self.flats[k].buffers):
                 es = flat.element_size()
                 nbytes = seg * es
-                for q in range(self.world):
-                    if q == self.rank:
-                        continue
+                # rank r pulls from r+1, r+2, ... (mod N): at each phase every
+                # source GPU feeds exactly one reader, so no peer's outgoing
+                # NVLink bandwidth is shared by several pulls
+                for dq in range(1, self.world):
+                    q = (self.rank + dq) % self.world
                     L.check(lib.advopt_copy_async(flat.data_ptr() + q * nbytes, self.peer[(k, j, q)] + q * nbytes,
                                                   nbytes, sh), "advopt_copy_async")
 
