@@ -446,7 +446,8 @@ __device__ __forceinline__ void fast_update(const Words<FastLayout<PREC, PBF>::B
         const float2 mask = make_float2(prod.x >= 0.0f ? 1.0f : 0.0f, prod.y >= 0.0f ? 1.0f : 0.0f);
         pc2 = fma2(mul2(splat2(-S.wd), pc2), mask, pc2);
       } else {
-        pc2 = fma2(pc2, splat2(-S.wd), pc2);
+        // add_(p, alpha=-wd): alpha rounded to bf16 on a bf16 tensor (no SR)
+        pc2 = fma2(pc2, splat2(-((PBF && !cf_sr<CF>(S)) ? round_bf16(S.wd) : S.wd)), pc2);
       }
       if (PBF && !cf_sr<CF>(S)) pc2 = make_float2(round_bf16(pc2.x), round_bf16(pc2.y));
     }
@@ -513,6 +514,8 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
   const float s_alpha = pdev ? L.prodigy->s_alpha : L.s_alpha;
   SC.c_v = c_v0;
   SC.c_m = pdev ? L.prodigy->c_m : L.c_m;
+  // Prodigy's m.add_(grad, alpha=...) rounds alpha to bf16 under bf16 math
+  if (StateTraits<PREC, PBF>::kMathBF) SC.c_m = round_bf16(SC.c_m);
   SC.w_m = L.w_m;
   SC.w_m1 = __fsub_rn(L.w_m, 1.0f);
   SC.w_n = L.w_nest;

@@ -111,7 +111,9 @@ __device__ __forceinline__ float anchor_value(const TensorRegs& T, int64_t k, bo
 // _apply_weight_decay for one element (param_update.py:15-75).  `pc` is the
 // working param value; `rb` rounds to the working dtype (bf16 for the
 // non-SR bf16 path).  wd/cwd are already scaled by lr (and by the Fisher
-// scaler `ws` when ws_on).
+// scaler `ws` when ws_on).  The non-cautious decay is add_(target, alpha=-wd),
+// which on a bf16 tensor rounds alpha to bf16 first; addcmul_'s value stays
+// float32.
 template <bool RB>
 __device__ __forceinline__ float weight_decay(float pc, float u, float wd, float cwd, bool cautious, bool has_anchor,
                                               float anchor, bool ws_on, float ws) {
@@ -130,7 +132,7 @@ __device__ __forceinline__ float weight_decay(float pc, float u, float wd, float
       if (ws_on) {
         pc = R(__fmaf_rn(__fmul_rn(-1.0f, tgt), __fmul_rn(ws, wd), pc));
       } else {
-        pc = R(__fmaf_rn(tgt, -wd, pc));
+        pc = R(__fmaf_rn(tgt, -R(wd), pc));
       }
     }
   }
@@ -148,7 +150,7 @@ __device__ __forceinline__ float weight_decay(float pc, float u, float wd, float
       if (ws_on) {
         pc = R(__fmaf_rn(__fmul_rn(-1.0f, tgt), __fmul_rn(ws, cwd), pc));
       } else {
-        pc = R(__fmaf_rn(tgt, -cwd, pc));
+        pc = R(__fmaf_rn(tgt, -R(cwd), pc));
       }
     }
   }
@@ -459,7 +461,9 @@ __global__ void __launch_bounds__(kThreads, 2) adam_kernel(const advopt_adam_lau
   const float c_v0 = pdev ? L.prodigy->c_v : L.c_v;
   const float d_f = pdev ? L.prodigy->d_f : L.d;
   const float s_alpha = pdev ? L.prodigy->s_alpha : L.s_alpha;
-  const float beta1 = L.beta1, w_m = L.w_m, w_nest = L.w_nest, c_m = pdev ? L.prodigy->c_m : L.c_m;
+  // Prodigy's m.add_(grad, alpha=d*(1-beta1)): alpha rounded to bf16 under bf16 math
+  const float c_m_raw = pdev ? L.prodigy->c_m : L.c_m;
+  const float beta1 = L.beta1, w_m = L.w_m, w_nest = L.w_nest, c_m = kMBF ? round_bf16(c_m_raw) : c_m_raw;
   float beta2 = L.beta2, c_v = c_v0;      // per tensor under Kourkoutas-beta
   const bool gsq = (F & ADVOPT_F_GRAD_SQ) && !fstats;
   const bool emit = F & ADVOPT_F_EMIT_UPDATE;

@@ -60,7 +60,8 @@ __global__ void __launch_bounds__(kThreads) lion_kernel(const advopt_lion_tensor
               const float mask = (sr ? __fmul_rn(u[e], pcv) : round_bf16(__fmul_rn(u[e], pcv))) >= 0.0f ? 1.0f : 0.0f;
               pcv = __fmaf_rn(__fmul_rn(-T.wd, pcv), mask, pcv);
             } else {
-              pcv = __fmaf_rn(pcv, -T.wd, pcv);
+              // add_(p, alpha=-wd) on a bf16 tensor rounds alpha to bf16
+              pcv = __fmaf_rn(pcv, -(sr ? T.wd : round_bf16(T.wd)), pcv);
             }
             if (!sr) pcv = round_bf16(pcv);
           }

@@ -477,7 +477,8 @@ __device__ __forceinline__ void apply_one(const Args& a, int64_t k, float u, uin
       const float mask = __fmul_rn(u, p) >= 0.0f ? 1.0f : 0.0f;
       p = __fmaf_rn(__fmul_rn(-a.wd, p), mask, p);
     } else {
-      p = __fmaf_rn(p, -a.wd, p);
+      // add_(p, alpha=-wd) on a bf16 tensor rounds alpha to bf16
+      p = __fmaf_rn(p, -((pbf && !sr) ? round_bf16(a.wd) : a.wd), p);
     }
     if (pbf && !sr) p = round_bf16(p);
   }
@@ -535,7 +536,7 @@ __global__ void __launch_bounds__(256) apply_vec_kernel(const Args a) {
           const float mask = __fmul_rn(ue, pe) >= 0.0f ? 1.0f : 0.0f;
           pe = __fmaf_rn(__fmul_rn(-a.wd, pe), mask, pe);
         } else {
-          pe = __fmaf_rn(pe, -a.wd, pe);
+          pe = __fmaf_rn(pe, -(sr ? a.wd : round_bf16(a.wd)), pe);
         }
         if (!sr) pe = round_bf16(pe);
       }

@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(1024) spec_ufinish_kernel(const advopt_adam_te
     } else {
       nu = ld_val(T.u, i, vb);
     }
-    dot += (double)nu * (double)T.u_raw[i];
+    dot += (double)rnd(__fmul_rn(nu, T.u_raw[i]), vb);   // vecdot = (u * u_raw).sum(): products in the dtype
   }
   dot = block_sum_d(dot, red);
   if (threadIdx.x == 0) {

@@ -197,9 +197,14 @@ class T:
         return T(out, dt or self.dt)
 
     def add_alpha(self, other, alpha, dt=None):
+        """self + alpha * other (add_ with alpha): between two bf16 tensors
+        ATen first rounds alpha to bf16; otherwise alpha is float32."""
         a, b = _c(self.v), _c(other.v)
         out = np.empty_like(a)
-        _lib().orc_add_alpha(_ptr(out), _ptr(a), _ptr(b), f32(alpha), a.size)
+        al = f32(alpha)
+        if self.dt == "bf16" and other.dt == "bf16":
+            al = f32(round_bf16(np.array([al], np.float32))[0])
+        _lib().orc_add_alpha(_ptr(out), _ptr(a), _ptr(b), al, a.size)
         return T(out, dt or self.dt)
 
 
@@ -539,7 +544,8 @@ def spectral_normalization(upd: T, state, lr, target_scale) -> T:
     cand_u = rnd(u_raw / np.maximum(u_norm, rnd(1e-8)[0]))
     next_u = cand_u if u_norm >= 1e-6 else u0
     state["spectral_u"] = _store_like(state["spectral_u"], next_u)
-    sigma = rnd(np.dot(next_u.astype(np.float64), u_raw.astype(np.float64)))[0]
+    # linalg.vecdot is (u * u_raw).sum(): each product rounded to the dtype
+    sigma = rnd(np.sum(rnd(next_u * u_raw).astype(np.float64)))[0]
     eps = 1.0 / (math.sqrt(d_out) + math.sqrt(d_in))
     sig = T(np.array([sigma if sigma >= eps else eps], np.float32), sdt)     # clamp_min_(eps)
     scale = _rdiv(target_scale, sig).mul_s(lr)

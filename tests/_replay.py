@@ -188,7 +188,8 @@ def replay(name, steps=None, pin_d=False, teacher=False):
                               hp["k_warmup_steps"])
         hp["betas"] = tuple(hp["betas"])
         hp["precision"] = "factored" if hp.get("nnmf_factor") else hp["state_precision"]
-        hp["spectral"] = hp.get("spectral_normalization", False)
+        hp["spectral"] = hp.get("spectral_normalization", False) or \
+            bool((meta.get("group_kw") or {}).get("spectral_normalization", False))
         group = dict(d=hp["d0"], d0=hp["d0"], d_max=hp["d0"], d_numerator=0.0, d_coef=hp["d_coef"],
                      growth_rate=hp["growth_rate"], d_limiter=hp["d_limiter"], k=0,
                      prodigy_steps=hp["prodigy_steps"],

@@ -288,6 +288,23 @@ CASES = {
     "adamw_spectral_factored_f32": dict(cls="AdamW_adv", dtype="f32", shapes=[(64, 48), (50,)],
                                         kw=dict(state_precision="factored", spectral_normalization=True,
                                                 cautious_wd=True, weight_decay=0.05), steps=3),
+    # bf16 params without stochastic rounding: decoupled and centered decay run
+    # as add_(target, alpha=-wd*lr) on the bf16 param, which rounds alpha to bf16
+    "adamw_bf16_nosr_wd": dict(cls="AdamW_adv", dtype="bf16", shapes=[(64, 33), (50,)],
+                               kw=dict(state_precision="auto", weight_decay=0.37, centered_wd=0.21,
+                                       centered_wd_mode="full", stochastic_rounding=False, lr=3e-3), steps=3),
+    "lion_bf16_nosr_wd": dict(cls="Lion_adv", dtype="bf16", shapes=[(64, 32), (32,)],
+                              kw=dict(lr=3e-4, weight_decay=0.37, stochastic_rounding=False), steps=3),
+    "muon_nosr_wd": dict(cls="Muon_adv", dtype="bf16",
+                         groups=[dict(shapes=[(64, 48)], optim_type="muon"),
+                                 dict(shapes=[(100, 32), (48,)], optim_type="adam")],
+                         kw=dict(lr=3e-3, weight_decay=0.37, adam_weight_decay=0.29, stochastic_rounding=False,
+                                 adam_state_precision="auto"), steps=2),
+    # Prodigy_adv has no spectral_normalization argument; its step reads the
+    # param-group key (Prodigy_adv.py:319-320, 490-493)
+    "prodigy_spectral_group_key": dict(cls="Prodigy_adv", dtype="bf16", shapes=[(120, 40), (40,), (24, 5, 6)],
+                                       kw=dict(state_precision="auto", d0=1e-4, slice_p=7, weight_decay=0.01),
+                                       group_kw=dict(spectral_normalization=True), steps=3, log_scale=True),
     "lion_spectral_bf16": dict(cls="Lion_adv", dtype="bf16", shapes=[(64, 32), (32,)],
                                kw=dict(lr=1e-4, weight_decay=0.01, spectral_normalization=True), steps=3),
     "muon_aux_spectral": dict(cls="Muon_adv", dtype="bf16",
@@ -314,6 +331,9 @@ def run_case(name, spec, adv_optm, pu):
                 grp["optim_type"] = gspec["optim_type"]
             groups.append(grp)
             k += n
+    elif "group_kw" in spec:
+        # keys the constructor does not take but a param group may carry
+        groups = [dict(params=params, **spec["group_kw"])]
     else:
         groups = params
     cls = getattr(adv_optm, spec["cls"])
@@ -321,6 +341,17 @@ def run_case(name, spec, adv_optm, pu):
     rec = DrawRecorder(pu)
     rec.param_index = {id(p): i for i, p in enumerate(params)}
     out = {}
+    # the initial spectral singular vectors, recorded where they are drawn
+    # (Prodigy_adv creates its states at the first step)
+    mod = sys.modules[cls.__module__]
+    orig_init_sn = getattr(mod, "init_spectral_norm", None)
+    init_sn = {}
+    if orig_init_sn is not None:
+        def rec_init_sn(state, p):
+            orig_init_sn(state, p)
+            i = rec.param_index.get(id(p), -1)
+            init_sn[i] = {k: bits(state[k]) for k in ("spectral_u", "spectral_v") if k in state}
+        mod.init_spectral_norm = rec_init_sn
     try:
         # the optimizer's constructor reseeds the per-device generator to 42
         opt = cls(groups, **spec["kw"])
@@ -328,7 +359,8 @@ def run_case(name, spec, adv_optm, pu):
                                                 shapes=[list(s) for s in shapes],
                                                 groups=[dict(n=len(g["shapes"]), optim_type=g["optim_type"])
                                                         for g in spec["groups"]] if "groups" in spec else None,
-                                                kw=spec["kw"], steps=spec["steps"])))
+                                                kw=spec["kw"], steps=spec["steps"],
+                                                group_kw=spec.get("group_kw"))))
         for i, p in enumerate(params):
             out[f"p0_{i}"] = bits(p)
             st = opt.state.get(p, {})
@@ -372,6 +404,11 @@ def run_case(name, spec, adv_optm, pu):
                 out[f"d_{s}"] = np.array([g0["d"], g0["d_max"], g0["d_numerator"], g0["k"]], np.float64)
     finally:
         rec.restore()
+        if orig_init_sn is not None:
+            mod.init_spectral_norm = orig_init_sn
+    for i, d in init_sn.items():
+        for k, v in d.items():
+            out.setdefault(f"st0_{i}_{k}", v)
     return out
 
 

@@ -88,6 +88,10 @@ def _oracle_state_from_torch(st):
                   dict(state_precision="factored", nesterov=True, weight_decay=0.01)), id="factored_bf16"),
     pytest.param(([(4096, 4096), (4096,), (333, 12)], "f32",
                   dict(state_precision="factored", cautious_wd=True, weight_decay=0.05)), id="factored_f32"),
+    # 'factored' without momentum (betas[0] = 0): rank-1 v only; the
+    # reference fails here (its v reconstruction reads a shifter it never made)
+    pytest.param(([(2048, 2048), (96,), (333, 12)], "bf16",
+                  dict(state_precision="factored", betas=(0.0, 0.99), weight_decay=0.01)), id="factored_no_momentum"),
     # spectral normalisation: one power-iteration step per 2-D update (bf16
     # singular vectors), max-abs scaling of the 1-D update
     pytest.param(([(2048, 1024), (1024,), (512, 1536), (96, 40, 3)], "bf16",

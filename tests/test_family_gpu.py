@@ -34,8 +34,15 @@ def test_matches_reference_golden(name):
     shapes = [tuple(s) for s in meta["shapes"]]
     params = [torch.nn.Parameter(to_torch(z[f"p0_{i}"], dt).reshape(sh)) for i, sh in enumerate(shapes)]
     cls = getattr(A, meta["cls"])
-    opt = cls(params, **meta["kw"])
+    # keys only a param group carries (Prodigy_adv's spectral_normalization)
+    opt = cls([dict(params=params, **meta["group_kw"])] if meta.get("group_kw") else params, **meta["kw"])
     prodigy = meta["cls"] == "Prodigy_adv"
+    if prodigy and any(f"st0_{i}_spectral_u" in z.files for i in range(len(shapes))):
+        # Prodigy creates its states at the first step; create them now so
+        # that the reference's initial singular vectors can be loaded
+        for g in opt.param_groups:
+            for p in g["params"]:
+                opt._init_state(p, g)
     for s in range(meta["steps"]):
         for i, p in enumerate(params):
             if s > 0:
