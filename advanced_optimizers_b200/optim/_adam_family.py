@@ -288,7 +288,7 @@ class SpectralPlan:
                 for k in range(0, numel, 65536):
                     row_items.append((k, min(k + 65536, numel), i, 0))
             upd = torch.empty(numel, dtype=torch.bfloat16 if ubf else torch.float32, device=gp.device)
-            scal = torch.zeros(2, dtype=torch.float32, device=gp.device)
+            scal = torch.zeros(4, dtype=torch.float32, device=gp.device)
             self.bufs += [upd, scal]
             sd["update"][i], sd["scalars"][i], sd["flags"][i] = ptr(upd), ptr(scal), flags
             gp.descs["update_out"][i] = ptr(upd)

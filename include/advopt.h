@@ -234,7 +234,8 @@ typedef struct advopt_spectral_tensor {
   void* v;                   /* spectral_v [d_in]                                */
   float* v_partial;          /* scratch [n_slabs][d_in]                          */
   float* u_raw;              /* scratch [d_out]                                  */
-  float* scalars;            /* scratch [2]: the step's scale, max|U| (1-D)      */
+  float* scalars;            /* scratch [4], 8-byte aligned: the step's scale, max|U| (1-D),
+                                then |U^T u|^2 as a double                       */
   int64_t d_out;             /* 1-D: 1                                           */
   int64_t d_in;              /* 1-D: numel                                       */
   float target;              /* sqrt(d_out / d_in) (1 for LoRA A factors)        */
