@@ -94,6 +94,7 @@ struct FastLayout {
 // 32-bit offsets).
 struct PieceRegs {
   unsigned char* p;     // param bytes of the piece
+  unsigned char* u;     // emitted update of the piece (ADVOPT_F_EMIT_UPDATE: the param dtype)
   unsigned char* m;     // first-moment storage of the piece
   float* ms;            // block scales of m from the piece's first block
   float* vs;            // block scales of v
@@ -107,6 +108,7 @@ template <int PREC, bool PBF>
 __device__ __forceinline__ void piece_regs(const TensorRegs& T, int64_t pb, PieceRegs& P) {
   using LY = FastLayout<PREC, PBF>;
   P.p = static_cast<unsigned char*>(T.param) + pb * LY::BPP;
+  P.u = T.upd ? static_cast<unsigned char*>(T.upd) + pb * LY::BPP : nullptr;
   P.m = T.m ? static_cast<unsigned char*>(T.m) + pb * LY::BPS : nullptr;
   P.ms = T.m_scale ? T.m_scale + (pb >> 11) : nullptr;
   P.vs = T.v_scale ? T.v_scale + (pb >> 11) : nullptr;
@@ -337,7 +339,11 @@ struct FastScalars {
 // picks such a kernel only when the launch matches it exactly).  Compiled-in
 // flags remove a uniform branch per element pair and let the scheduler
 // interleave the pairs.
-enum : int { kCfDyn = -1, kCfHasM = 1, kCfNest = 2, kCfWd = 4, kCfSR = 8, kCfMSmall = 16, kCfNSmall = 32 };
+// kCfDynEmit: the dynamic-flag kernel that also writes the unscaled update
+// (ADVOPT_F_EMIT_UPDATE) instead of the param; a variant of its own, so that
+// the other kernels carry none of that code
+enum : int { kCfDynEmit = -2, kCfDyn = -1, kCfHasM = 1, kCfNest = 2, kCfWd = 4, kCfSR = 8, kCfMSmall = 16,
+             kCfNSmall = 32 };
 template <int CF> __device__ __forceinline__ bool cf_has_m(const FastScalars& S) { return CF < 0 ? S.has_m : (CF & kCfHasM) != 0; }
 template <int CF> __device__ __forceinline__ bool cf_nest(const FastScalars& S) { return CF < 0 ? S.nest : (CF & kCfNest) != 0; }
 template <int CF> __device__ __forceinline__ bool cf_wd(const FastScalars& S) { return CF < 0 ? S.wd != 0.0f : (CF & kCfWd) != 0 && S.wd != 0.0f; }
@@ -398,7 +404,7 @@ template <int PREC, bool PBF, int ALGO, int CF, bool FACT, bool FAST>
 __device__ __forceinline__ void fast_update(const Words<FastLayout<PREC, PBF>::BPP>& g,
                                             const Words<FastLayout<PREC, PBF>::BPP>& p, const float2 (&m_new)[4],
                                             const float2 (&v)[4], const FastScalars& S, const uint32_t (&npw)[4],
-                                            uint32_t (&pw)[PBF ? 4 : 8], bool& hard) {
+                                            uint32_t (&pw)[PBF ? 4 : 8], bool& hard, bool emit) {
   using TR = StateTraits<PREC, PBF>;
   using LY = FastLayout<PREC, PBF>;
   constexpr bool kMBF = TR::kMathBF;
@@ -436,6 +442,17 @@ __device__ __forceinline__ void fast_update(const Words<FastLayout<PREC, PBF>::B
     if (FAST) hi = max3f(hi, du.x, du.y);
     ui = FAST ? div_nm2(ui, du) : make_float2(__fdiv_rn(ui.x, du.x), __fdiv_rn(ui.y, du.y));
     ui = Rm2(ui);
+    if (emit) {
+      // spectral normalisation: the update before its scaling, in the param
+      // dtype (AdamW_adv.py:459-461; scaled_optm.py:269 casts it there)
+      if (PBF) {
+        pw[i] = f_to_bf16_rne(ui.x) | (f_to_bf16_rne(ui.y) << 16);
+      } else {
+        pw[2 * i] = __float_as_uint(ui.x);
+        pw[2 * i + 1] = __float_as_uint(ui.y);
+      }
+      continue;
+    }
     ui = Rm2(mul2(ui, splat2(S.step_size)));
     // parameter update (param_update.py:77-156)
     float2 pc2 = pair_of<LY::BPP, true>(p, i);
@@ -504,6 +521,9 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
   const uint32_t F = L.flags;
   const bool has_m = CF < 0 ? (F & ADVOPT_F_HAS_M) != 0 : (CF & kCfHasM) != 0;
   const bool pstats = (ALGO == ADVOPT_ALGO_PRODIGY) && (F & ADVOPT_F_PRODIGY_STATS);
+  // spectral normalisation (the kCfDynEmit variant): write the unscaled
+  // update where the param would be written, and leave the param alone
+  constexpr bool emit = CF == kCfDynEmit;
   const bool gsq = F & ADVOPT_F_GRAD_SQ;
   FastScalars SC;
   SC.beta1 = L.beta1;
@@ -689,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
       {
         const uint32_t npw[4] = {nzp.x, nzp.y, nzp.z, nzp.w};
         bool hard = false;
-        fast_update<PREC, PBF, ALGO, CF, fact, true>(in.g, in.p, m_new, v, SC, npw, pw, hard);
+        fast_update<PREC, PBF, ALGO, CF, fact, true>(in.g, in.p, m_new, v, SC, npw, pw, hard, emit);
         if (__any_sync(0xffffffffu, hard)) {
           // some lane of the warp is outside the Newton–Markstein ranges:
           // redo the warp's parameter update with the IEEE operations (the
@@ -701,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
           if (cf_sr<CF>(SC)) nz2 = noise(T.nz_p, kNoiseP);
           const uint32_t npw2[4] = {nz2.x, nz2.y, nz2.z, nz2.w};
           bool h2;
-          fast_update<PREC, PBF, ALGO, CF, fact, false>(in2.g, in2.p, m_new, v, SC, npw2, pw, h2);
+          fast_update<PREC, PBF, ALGO, CF, fact, false>(in2.g, in2.p, m_new, v, SC, npw2, pw, h2, emit);
         }
       }
       if (!kFull) {
@@ -735,7 +755,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
 
       // param store
       if (PBF) {
-        uint16_t* dst = reinterpret_cast<uint16_t*>(P.p) + toff;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(emit ? P.u : P.p) + toff;
         if (v8) {
           *reinterpret_cast<uint4*>(dst) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
         } else {
@@ -744,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
             if (e < nv) dst[e] = (uint16_t)(pw[e >> 1] >> (16 * (e & 1)));
         }
       } else {
-        float* dst = reinterpret_cast<float*>(P.p) + toff;
+        float* dst = reinterpret_cast<float*>(emit ? P.u : P.p) + toff;
         if (v8) {
           reinterpret_cast<uint4*>(dst)[0] = make_uint4(pw[0], pw[1], pw[2], pw[3]);
           reinterpret_cast<uint4*>(dst)[1] = make_uint4(pw[4], pw[5], pw[6], pw[7]);

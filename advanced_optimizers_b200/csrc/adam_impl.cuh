@@ -1049,7 +1049,8 @@ template <int PREC, bool PBF, int ALGO>
 int fast_config(const advopt_adam_launch& L) {
   if (!(PREC == ADVOPT_PREC_INT8_SR && PBF && ALGO == ADVOPT_ALGO_ADAMW)) return kCfDyn;
   const uint32_t F = L.flags;
-  if (!(F & ADVOPT_F_HAS_M) || !(F & ADVOPT_F_SR) || (F & (ADVOPT_F_CAUTIOUS | ADVOPT_F_NOISE_IN))) return kCfDyn;
+  if (!(F & ADVOPT_F_HAS_M) || !(F & ADVOPT_F_SR) || (F & (ADVOPT_F_CAUTIOUS | ADVOPT_F_NOISE_IN | ADVOPT_F_EMIT_UPDATE)))
+    return kCfDyn;
   if (!(fabsf(L.w_m) < 0.5f)) return kCfDyn;
   int cf = kCfHasM | kCfSR | kCfMSmall;
   if (F & ADVOPT_F_NESTEROV) {
@@ -1078,12 +1079,14 @@ cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
                               ADVOPT_F_ANCHORS);
   const bool nin = L.flags & ADVOPT_F_NOISE_IN;
   const size_t smem = (size_t)L.smem_floats * sizeof(float);
-  // signed rank-1 momentum and update emission live in the general kernel only
-  const bool general_only = ALGO == ADVOPT_ALGO_LION || (L.flags & (ADVOPT_F_FACT_M | ADVOPT_F_EMIT_UPDATE));
+  // signed rank-1 momentum and Lion live in the general kernel only; update
+  // emission runs in either (the fast kernel's only when the planner chose it)
+  const bool general_only = ALGO == ADVOPT_ALGO_LION || (L.flags & ADVOPT_F_FACT_M);
   if constexpr (ALGO != ADVOPT_ALGO_LION) {
   if (!ext && !general_only && L.stages > 0) {
+    const bool emit = L.flags & ADVOPT_F_EMIT_UPDATE;
     if (nin) {
-      auto kf = adam_fast_kernel<PREC, PBF, ALGO, true, kCfDyn>;
+      auto kf = emit ? adam_fast_kernel<PREC, PBF, ALGO, true, kCfDynEmit> : adam_fast_kernel<PREC, PBF, ALGO, true, kCfDyn>;
       cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
       kf<<<L.grid, kThreads, smem, s>>>(L, philox_keys(L.seed));
@@ -1099,6 +1102,7 @@ cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
         default: break;
       }
     }
+    if (emit) return launch_fast<PREC, PBF, ALGO, kCfDynEmit>(L, smem, s);
     return launch_fast<PREC, PBF, ALGO, kCfDyn>(L, smem, s);
   }
   }

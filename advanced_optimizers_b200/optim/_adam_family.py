@@ -446,8 +446,20 @@ class GroupPlan:
                               if "mu_v_nmf" in st)
         # the fast kernel keeps element offsets in 32 bits (tensors below 2^34
         # elements); signed rank-1 momentum runs in the general kernel
+        # spectral normalisation: the fast kernel emits the update in the param
+        # dtype, so it runs when every tensor's update has that dtype (the
+        # singular vectors' dtype for 2-D updates; the math dtype for 1-D ones)
+        spectral_fast = True
+        if cfg.spectral:
+            math_bf16 = cfg.precision == "auto" and self.pdt == L.DT_BF16
+            for p, st in zip(self.params, self.states):
+                if spectral_kind(p) == "spectral":
+                    same = "spectral_u" in st and st["spectral_u"].dtype == p.dtype
+                else:
+                    same = self.pdt == L.DT_F32 or math_bf16
+                spectral_fast = spectral_fast and same
         self.fast = (not ext) and (not any_generic) and factors_aligned and max(numels, default=0) < (1 << 34) \
-            and not self.any_fact_m and not cfg.spectral and cfg.algo != L.ALGO_LION
+            and not self.any_fact_m and spectral_fast and cfg.algo != L.ALGO_LION
         if self.fast:
             bpp = 2 if self.pdt == L.DT_BF16 else 4
             bps = {0: 4, 1: 2, 2: 1, 3: 2 if self.pdt == L.DT_BF16 else 4}[self.precision]

@@ -69,7 +69,8 @@ extern "C" {
 #define ADVOPT_F_NO_WD (1u << 11)      /* no tensor of the launch has weight decay (optional hint) */
 #define ADVOPT_F_GRAD_SQ (1u << 12)    /* also write each piece's sum of g*g to piece_gsq (Kourkoutas-beta) */
 #define ADVOPT_F_EMIT_UPDATE (1u << 13)/* write each tensor's unscaled update to update_out and leave the
-                                          param alone (spectral normalisation finishes the step) */
+                                          param alone (spectral normalisation finishes the step); with
+                                          stages > 0 (fast kernel) every update_out has the param dtype */
 #define ADVOPT_F_FACT_M (1u << 14)     /* every tensor carries ADVOPT_T_FACT_M and ADVOPT_T_FACTORED
                                           (needs ADVOPT_PREC_FP32 and ADVOPT_F_HAS_M; dynamic shared
                                           memory: two equal halves, the second for the |m| sums) */
