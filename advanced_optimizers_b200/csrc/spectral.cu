@@ -1,7 +1,7 @@
 // Spectral normalisation of Adam-family and Lion updates (scaled_optm.py:35-72,
 // 160-168, 255-295) and the parameter update that follows it
 // (param_update.py:77-156).  The step kernel has written each tensor's
-// unscaled update U (ADVOPT_F_EMIT_UPDATE); five launches finish the step:
+// unscaled update U (ADVOPT_F_EMIT_UPDATE); six launches finish the step:
 //   1. spec_vpart_kernel   U^T u per row slab (column partials, float32)
 //   2. spec_vsum_kernel    U^T u from the slabs, column-parallel (float64),
 //      and its squared norm; spec_vfinish_kernel v = U^T u / |U^T u|
