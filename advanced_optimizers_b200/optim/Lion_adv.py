@@ -161,7 +161,7 @@ class Lion_adv(torch.optim.Optimizer):
         spectral = group.get("spectral_normalization", False)
         fac = [p for p in params if self.state[p]["factored"] or spectral]
         if fac:
-            self._run_factored(gi, group, fac)
+            self._run_general(gi, group, fac)
         params = [p for p in params if not (self.state[p]["factored"] or spectral)]
         by_dtype = {}
         for p in params:
@@ -210,7 +210,7 @@ class Lion_adv(torch.optim.Optimizer):
             if keep:
                 torch.cuda.current_stream(pl.device).synchronize()
 
-    def _run_factored(self, gi, group, params):
+    def _run_general(self, gi, group, params):
         """Params stepped by the general kernel: one launch per (dtype,
         factored) — float32 for factored m, the param dtype otherwise
         (Lion_adv.py:214-278) — with the spectral scaling when the group
