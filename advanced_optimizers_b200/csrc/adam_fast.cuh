@@ -100,6 +100,9 @@ struct PieceRegs {
   float* vs;            // block scales of v
   float* row;           // factored row factor
   const float* col;     // factored column factor
+  float* mrow;          // signed rank-1 momentum (FM): row factor, column factor, sign bytes
+  const float* mcol;
+  uint8_t* msign;
   uint32_t gbase;       // Philox element group of the piece's first element
   uint32_t tensor_id, step;
 };
@@ -114,6 +117,9 @@ __device__ __forceinline__ void piece_regs(const TensorRegs& T, int64_t pb, Piec
   P.vs = T.v_scale ? T.v_scale + (pb >> 11) : nullptr;
   P.row = T.row;
   P.col = T.col;
+  P.mrow = T.mrow;
+  P.mcol = T.mcol;
+  P.msign = T.msign;
   P.gbase = (uint32_t)((uint64_t)pb >> 3);
   P.tensor_id = T.tensor_id;
   P.step = T.step;
@@ -290,6 +296,10 @@ struct FastIn {
   Words<LY::BPS> m, v;
   float ms, vs, mu;
   float4 mva, mvb;
+  // FM: the momentum's row factor, eight column factors and the sign byte
+  float fmu;
+  float4 fma, fmb;
+  uint32_t fsg;
 };
 
 template <int PREC, bool PBF>
@@ -356,7 +366,7 @@ template <int CF> __device__ __forceinline__ bool cf_nsmall(const FastScalars& S
 // Muon_AuxAdam.py:148-175, Prodigy_adv.py:430-470): the new m and the new v
 // (factored: before the factor rebuild).  No square root or division is
 // involved, so these are exact whichever update path follows.
-template <int PREC, bool PBF, int ALGO, int CF, bool FACT>
+template <int PREC, bool PBF, int ALGO, int CF, bool FACT, bool FM = false>
 __device__ __forceinline__ void fast_moments(const FastIn<PREC, PBF>& in, const FastScalars& S, float2 (&m_new)[4],
                                              float2 (&v)[4]) {
   using TR = StateTraits<PREC, PBF>;
@@ -384,8 +394,18 @@ __device__ __forceinline__ void fast_moments(const FastIn<PREC, PBF>& in, const 
     if (vbf) vi = make_float2(round_bf16(vi.x), round_bf16(vi.y));
     v[i] = vi;
     if (cf_has_m<CF>(S)) {
-      float2 m0 = pair_of<LY::BPS, true>(in.m, i);
-      if (kStore == 2) m0 = mul2(m0, splat2(in.ms));
+      float2 m0;
+      if (FM) {
+        // _reconstruct_state(signed=True): outer(mu, mv), negated where the
+        // sign bit is clear (factorization_util.py:9-19)
+        const float2 mv = (i == 0) ? make_float2(in.fma.x, in.fma.y) : (i == 1) ? make_float2(in.fma.z, in.fma.w)
+                        : (i == 2) ? make_float2(in.fmb.x, in.fmb.y) : make_float2(in.fmb.z, in.fmb.w);
+        const float2 a = mul2(splat2(in.fmu), mv);
+        m0 = make_float2(((in.fsg >> (2 * i)) & 1u) ? a.x : -a.x, ((in.fsg >> (2 * i + 1)) & 1u) ? a.y : -a.y);
+      } else {
+        m0 = pair_of<LY::BPS, true>(in.m, i);
+        if (kStore == 2) m0 = mul2(m0, splat2(in.ms));
+      }
       if (ALGO == ADVOPT_ALGO_PRODIGY) m_new[i] = Rm2(fma2(gi, splat2(S.c_m), Rm2(mul2(m0, splat2(S.beta1)))));
       else m_new[i] = Rm2(lerp2(m0, gi, S.w_m, S.w_m1, cf_msmall<CF>(S)));
     } else {
@@ -494,7 +514,11 @@ struct FastOcc {
   static constexpr int v = (PREC == ADVOPT_PREC_INT8_SR && PBF && ALGO != ADVOPT_ALGO_PRODIGY) ? 3 : 2;
 };
 
-template <int PREC, bool PBF, int ALGO, bool NOISE_IN, int CF>
+// FM: a launch of signed rank-1 momentum tensors only ('factored', float32
+// launches): m is rebuilt from its factors and sign bytes instead of being
+// streamed through the ring, and its |m| row sums and column partials use a
+// second accumulator area after the second moment's.
+template <int PREC, bool PBF, int ALGO, bool NOISE_IN, int CF, bool FM = false>
 __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
     adam_fast_kernel(const advopt_adam_launch L, const PhiloxKeys K) {
   using TR = StateTraits<PREC, PBF>;
@@ -503,12 +527,15 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
   constexpr int kMaxStages = 4;
   extern __shared__ float4 dsm4[];
   float* colacc = reinterpret_cast<float*>(dsm4);
-  unsigned char* stages = reinterpret_cast<unsigned char*>(colacc + L.gen_offset);
+  static_assert(!FM || PREC == ADVOPT_PREC_FP32, "factored momentum is float32");
+  float* colacc_m = colacc + (FM ? L.gen_offset : 0);
+  unsigned char* stages = reinterpret_cast<unsigned char*>(colacc + (FM ? 2 : 1) * L.gen_offset);
   __shared__ uint64_t bars[kMaxStages];
   __shared__ int direct[kMaxStages];
   __shared__ int abort_flag;
   __shared__ uint32_t redm[2][kWarps], redv[2][kWarps];
   __shared__ float redr[2][kWarps];
+  __shared__ float redrm[2][kWarps];
   __shared__ double dred[kWarps][2];
   __shared__ double gred[kWarps];
   __shared__ TensorRegs Ts;
@@ -520,6 +547,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
   const int S = L.stages;
   const uint32_t F = L.flags;
   const bool has_m = CF < 0 ? (F & ADVOPT_F_HAS_M) != 0 : (CF & kCfHasM) != 0;
+  const bool ring_m = has_m && !FM;    // m streamed through the stage ring
   const bool pstats = (ALGO == ADVOPT_ALGO_PRODIGY) && (F & ADVOPT_F_PRODIGY_STATS);
   // spectral normalisation (the kCfDynEmit variant): write the unscaled
   // update where the param would be written, and leave the param alone
@@ -560,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
     cur.tensor = -1;
     cur_valid = cursor_seek<PREC, PBF>(L, cur, pend);
     for (int s = 0; s < S && cur_valid; ++s) {
-      issue_chunk<PREC, PBF>(cur, stages + (size_t)s * LY::BYTES, &bars[s], &direct[s], has_m);
+      issue_chunk<PREC, PBF>(cur, stages + (size_t)s * LY::BYTES, &bars[s], &direct[s], ring_m);
       cur_valid = cursor_next<PREC, PBF>(L, cur, pend);
     }
   }
@@ -585,6 +613,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
     // column partials in their own global slot row (read-modify-write)
     const bool col_global = fact && d2 > (int64_t)L.gen_offset;
     float* colrow = fact ? (col_global ? T.colpart + (int64_t)pc.slot * d2 : colacc) : nullptr;
+    float* colrow_m = FM ? (col_global ? T.mcolpart + (int64_t)pc.slot * d2 : colacc_m) : nullptr;
     if (L.layer_beta2) {
       // Kourkoutas-beta: the tensor's layer's dynamic beta2 (Kourkoutas.py:249-257)
       const int l = L.layer_of_tensor[pc.tensor];
@@ -600,6 +629,9 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
     if (fact) {
       for (int j2 = tid * 4; j2 < (int)d2; j2 += kThreads * 4)
         *reinterpret_cast<float4*>(colrow + j2) = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (FM)
+        for (int j2 = tid * 4; j2 < (int)d2; j2 += kThreads * 4)
+          *reinterpret_cast<float4*>(colrow_m + j2) = make_float4(0.f, 0.f, 0.f, 0.f);
       __syncthreads();
     }
     // Per-piece constants: the descriptor fields the chunks use, read once
@@ -613,6 +645,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
     int r0 = fact ? (int)(pb / d2) : 0;
     int c0 = fact ? (int)(pb - (int64_t)r0 * d2) : 0;
     float racc0 = 0.0f, racc1 = 0.0f;   // this thread's part of rows r0 and r0 + 1
+    float raccm0 = 0.0f, raccm1 = 0.0f; // FM: the same for |m|
     double st0 = 0.0, st1 = 0.0;
     const uint32_t slice_p = T.slice_p ? T.slice_p : 1u;
     // Prodigy: this thread's first element's remainder mod slice_p, advanced
@@ -626,6 +659,9 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
     // loaded one chunk ahead so their L2 latency overlaps the current chunk.
     float pre_mu = 0.0f, pre_ms = 0.0f, pre_vs = 0.0f;
     float4 pre_a = make_float4(0.f, 0.f, 0.f, 0.f), pre_b = pre_a;
+    float pre_fmu = 0.0f;
+    float4 pre_fa = pre_a, pre_fb = pre_a;
+    uint32_t pre_sg = 0u;
     auto prefetch = [&](int off, int c0n, int r0n, auto fact_tag) {
       constexpr bool fct = decltype(fact_tag)::value;
       if (fct) {
@@ -636,6 +672,13 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
         pre_mu = nvn > 0 ? P.row[r0n + (sec ? 1 : 0)] : 0.0f;
         pre_a = *reinterpret_cast<const float4*>(P.col + col);
         pre_b = *(reinterpret_cast<const float4*>(P.col + col) + 1);
+        if (FM) {
+          pre_fmu = nvn > 0 ? P.mrow[r0n + (sec ? 1 : 0)] : 0.0f;
+          pre_fa = *reinterpret_cast<const float4*>(P.mcol + col);
+          pre_fb = *(reinterpret_cast<const float4*>(P.mcol + col) + 1);
+          // the thread's 8 elements are one sign byte (8-aligned columns)
+          pre_sg = nvn > 0 ? (uint32_t)P.msign[(pb + off + tid * kVec) >> 3] : 0u;
+        }
       }
       if (kStore == 2 && has_m) pre_ms = P.ms[off >> 11];
       if (kStore == 2 && !fct) pre_vs = P.vs[off >> 11];
@@ -678,6 +721,10 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
       in.mvb = pre_b;
       in.ms = pre_ms;
       in.vs = pre_vs;
+      in.fmu = pre_fmu;
+      in.fma = pre_fa;
+      in.fmb = pre_fb;
+      in.fsg = pre_sg;
       if (!mbar_wait(&bars[slot], par)) {
         // the copies never arrived: report, finish this chunk on whatever is
         // in the stage, and leave uniformly after the next barrier
@@ -686,7 +733,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
       }
       const unsigned char* st = stages + (size_t)slot * LY::BYTES;
       const bool dir = kFull ? false : (direct[slot] != 0);
-      fast_load<PREC, PBF>(T, st, dir, k0, nv, v8, has_m, fact, in);
+      fast_load<PREC, PBF>(T, st, dir, k0, nv, v8, ring_m, fact, in);
       U4 nzp{0u, 0u, 0u, 0u};
       if (cf_sr<CF>(SC)) nzp = noise(T.nz_p, kNoiseP);
       if (gsq) {
@@ -705,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
       }
       float2 m_new[4], v[4];
       uint32_t pw[PBF ? 4 : 8];
-      fast_moments<PREC, PBF, ALGO, CF, fact>(in, SC, m_new, v);
+      fast_moments<PREC, PBF, ALGO, CF, fact, FM>(in, SC, m_new, v);
       {
         const uint32_t npw[4] = {nzp.x, nzp.y, nzp.z, nzp.w};
         bool hard = false;
@@ -808,22 +855,50 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
         if (second) racc1 = __fadd_rn(racc1, sum);
         else racc0 = __fadd_rn(racc0, sum);
         row_done = clen >= d2i - c0;   // row r0 ends inside this chunk (uniform)
+        if (FM) {
+          // _factorize_state(signed=True) (factorization_util.py:25-32): the
+          // sign bits of m > 0, |m| row sums and column partials
+          float2 am[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) am[i] = make_float2(fabsf(m_new[i].x), fabsf(m_new[i].y));
+          if (nv > 0) {
+            uint32_t sb = 0u;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              sb |= ((m_new[i].x > 0.0f ? 1u : 0u) << (2 * i)) | ((m_new[i].y > 0.0f ? 1u : 0u) << (2 * i + 1));
+            P.msign[k0 >> 3] = (uint8_t)sb;
+            float4* cm = reinterpret_cast<float4*>(colrow_m + col);
+            float4 a = cm[0], b = cm[1];
+            const float2 a01 = add2(make_float2(a.x, a.y), am[0]), a23 = add2(make_float2(a.z, a.w), am[1]);
+            const float2 b01 = add2(make_float2(b.x, b.y), am[2]), b23 = add2(make_float2(b.z, b.w), am[3]);
+            cm[0] = make_float4(a01.x, a01.y, a23.x, a23.y);
+            cm[1] = make_float4(b01.x, b01.y, b23.x, b23.y);
+          }
+          const float2 t = add2(add2(am[0], am[1]), add2(am[2], am[3]));
+          const float tsum = __fadd_rn(t.x, t.y);
+          if (second) raccm1 = __fadd_rn(raccm1, tsum);
+          else raccm0 = __fadd_rn(raccm0, tsum);
+        }
         if (row_done) {
           const float w = warp_sum(racc0);
           if (lane == 0) redr[parity][warp] = w;
+          if (FM) {
+            const float wm = warp_sum(raccm0);
+            if (lane == 0) redrm[parity][warp] = wm;
+          }
         }
       }
       __syncthreads();
       if (abort_flag) return false;   // every thread reads the same flag after the barrier
       // every thread is done with this stage: refill it with the chunk S ahead
       if (tid == 0 && cur_valid) {
-        issue_chunk<PREC, PBF>(cur, stages + (size_t)slot * LY::BYTES, &bars[slot], &direct[slot], has_m);
+        issue_chunk<PREC, PBF>(cur, stages + (size_t)slot * LY::BYTES, &bars[slot], &direct[slot], ring_m);
         cur_valid = cursor_next<PREC, PBF>(L, cur, pend);
       }
       // noise of the quantised states
       U4 nzm{0u, 0u, 0u, 0u}, nzv{0u, 0u, 0u, 0u};
       if (kStore == 2 || TR::kSRStates) {
-        if (has_m) nzm = noise(T.nz_m, kNoiseM);
+        if (ring_m) nzm = noise(T.nz_m, kNoiseM);
         if (!fact) nzv = noise(T.nz_v, kNoiseV);
       }
       if (row_done) {
@@ -832,11 +907,19 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
 #pragma unroll
           for (int w = 0; w < kWarps; ++w) t += (double)redr[parity][w];
           P.row[r0] = (float)t;
+          if (FM) {
+            double tm = 0.0;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) tm += (double)redrm[parity][w];
+            P.mrow[r0] = (float)tm;
+          }
         }
         racc0 = racc1;
         racc1 = 0.0f;
+        raccm0 = raccm1;
+        raccm1 = 0.0f;
       }
-      if (has_m) {
+      if (ring_m) {
         if (kStore == 2) {
           const float bmax = __uint_as_float(__reduce_max_sync(0xffffffffu, redm[parity][lane & (kWarps - 1)]));
           const float scale = block_scale<true>(bmax);
@@ -923,6 +1006,11 @@ __global__ void __launch_bounds__(kThreads, (FastOcc<PREC, PBF, ALGO>::v))
         float* dstp = T.colpart + (int64_t)pc.slot * d2;
         for (int j2 = tid * 4; j2 < (int)d2; j2 += kThreads * 4)
           *reinterpret_cast<float4*>(dstp + j2) = *reinterpret_cast<const float4*>(colacc + j2);
+        if (FM) {
+          float* dstm = T.mcolpart + (int64_t)pc.slot * d2;
+          for (int j2 = tid * 4; j2 < (int)d2; j2 += kThreads * 4)
+            *reinterpret_cast<float4*>(dstm + j2) = *reinterpret_cast<const float4*>(colacc_m + j2);
+        }
       }
       __syncthreads();
     }

@@ -1079,8 +1079,20 @@ cudaError_t launch_adam_algo(const advopt_adam_launch& L, cudaStream_t s) {
                               ADVOPT_F_ANCHORS);
   const bool nin = L.flags & ADVOPT_F_NOISE_IN;
   const size_t smem = (size_t)L.smem_floats * sizeof(float);
-  // signed rank-1 momentum and Lion live in the general kernel only; update
-  // emission runs in either (the fast kernel's only when the planner chose it)
+  // signed rank-1 momentum on the fast layout (planned with stages > 0):
+  // the fast kernel's FM variant
+  if constexpr (PREC == ADVOPT_PREC_FP32 && ALGO != ADVOPT_ALGO_LION) {
+    if ((L.flags & ADVOPT_F_FACT_M) && !ext && L.stages > 0 && !(L.flags & ADVOPT_F_EMIT_UPDATE)) {
+      auto kf = nin ? adam_fast_kernel<PREC, PBF, ALGO, true, kCfDyn, true>
+                    : adam_fast_kernel<PREC, PBF, ALGO, false, kCfDyn, true>;
+      cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      kf<<<L.grid, kThreads, smem, s>>>(L, philox_keys(L.seed));
+      return cudaGetLastError();
+    }
+  }
+  // Lion, and signed rank-1 momentum otherwise, live in the general kernel;
+  // update emission runs in either (the fast kernel's only when planned)
   const bool general_only = ALGO == ADVOPT_ALGO_LION || (L.flags & ADVOPT_F_FACT_M);
   if constexpr (ALGO != ADVOPT_ALGO_LION) {
   if (!ext && !general_only && L.stages > 0) {

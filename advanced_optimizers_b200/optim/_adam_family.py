@@ -458,8 +458,13 @@ class GroupPlan:
                 else:
                     same = self.pdt == L.DT_F32 or math_bf16
                 spectral_fast = spectral_fast and same
+        # signed rank-1 momentum takes the fast kernel's FM variant when every
+        # row is on the fast layout (no generic rows) and nothing needs the
+        # general kernel (update emission, Lion)
+        fm_ok = (not self.any_fact_m) or (not cfg.spectral and all(
+            aligned16(st["mv_m_nmf"]) for st in self.states if "mv_m_nmf" in st))
         self.fast = (not ext) and (not any_generic) and factors_aligned and max(numels, default=0) < (1 << 34) \
-            and not self.any_fact_m and spectral_fast and cfg.algo != L.ALGO_LION
+            and fm_ok and spectral_fast and cfg.algo != L.ALGO_LION
         if self.fast:
             bpp = 2 if self.pdt == L.DT_BF16 else 4
             bps = {0: 4, 1: 2, 2: 1, 3: 2 if self.pdt == L.DT_BF16 else 4}[self.precision]
@@ -469,9 +474,11 @@ class GroupPlan:
             self.gen_offset = min(self.gen_offset, FAST_COLS)
             three = self.precision == L.PREC["int8_sr"] and self.pdt == L.DT_BF16 and cfg.algo != L.ALGO_PRODIGY
             per_cta = (227 * 1024) // (3 if three else 2) - 2048
-            budget = per_cta - self.gen_offset * 4
+            # FM: a second column-sum area for |m|
+            areas = 2 if self.any_fact_m else 1
+            budget = per_cta - areas * self.gen_offset * 4
             self.stages = int(max(2, min(4, budget // stage)))
-            self.smem_floats = self.gen_offset + self.stages * stage // 4
+            self.smem_floats = areas * self.gen_offset + self.stages * stage // 4
         elif self.any_fact_m:
             # two equal halves: the second-moment and the |m| column sums, with
             # the generic path's staging when a row is not on the fast layout

@@ -72,8 +72,11 @@ extern "C" {
                                           param alone (spectral normalisation finishes the step); with
                                           stages > 0 (fast kernel) every update_out has the param dtype */
 #define ADVOPT_F_FACT_M (1u << 14)     /* every tensor carries ADVOPT_T_FACT_M and ADVOPT_T_FACTORED
-                                          (needs ADVOPT_PREC_FP32 and ADVOPT_F_HAS_M; dynamic shared
-                                          memory: two equal halves, the second for the |m| sums) */
+                                          (needs ADVOPT_PREC_FP32 and ADVOPT_F_HAS_M).  General kernel
+                                          (stages 0): dynamic shared memory in two equal halves, the
+                                          second for the |m| sums; fast kernel (stages > 0, every row
+                                          on the fast layout): 2 x gen_offset floats of column sums,
+                                          then the stage ring */
 
 /* per-tensor flags */
 #define ADVOPT_T_FACTORED (1u << 0)    /* second moment as rank-1 factors (factored_2nd) */
