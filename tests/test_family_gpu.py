@@ -128,3 +128,67 @@ def test_lion_factored_matches_oracle_large(dt):
                 if key in ostate[i]:
                     ostate[i][key] = to_numpy(opt.state[p][key])
             p_o[i] = O.from_bf16_bits(to_numpy(p)).reshape(sh) if dt == "bf16" else to_numpy(p).reshape(sh)
+
+
+@pytest.mark.parametrize("which", ["prodigy", "auxadam"])
+def test_factored_fast_layout_matches_oracle(which):
+    """state_precision='factored' at sizes whose effective rows take the fast
+    kernel's factored-momentum variant (d2 = 1024 / 2048 -> fast layout for
+    (4096, 1024) as (2048, 2048), (2048, 2048)), beside a 1-D param, for
+    Prodigy_adv (slice statistics and the d estimate on top) and Muon_adv's
+    auxiliary Adam, one step against the oracle.  Tolerances: params within 1
+    bf16 ulp; sign bits exact; rank-1 factors 2e-6 relative; Prodigy's s bf16
+    within 1 ulp and d within 1e-4 relative."""
+    import advanced_optimizers_b200 as A
+    from _replay import O, PRODIGY_DEFAULTS
+    shapes = [(4096, 1024), (2048, 2048), (96,)]
+    g = torch.Generator().manual_seed(11)
+    p_host = [(torch.randn(sh, generator=g) * 0.02).bfloat16() for sh in shapes]
+    params = [torch.nn.Parameter(t.cuda()) for t in p_host]
+    if which == "prodigy":
+        kw = dict(state_precision="factored", d0=1e-4, slice_p=11, nesterov=True, weight_decay=0.01)
+        opt = A.Prodigy_adv(params, **kw)
+        for p in params:
+            opt._init_state(p, opt.param_groups[0])
+        hp = dict(PRODIGY_DEFAULTS)
+        hp.update(kw)
+        hp["betas"] = tuple(hp["betas"])
+        hp["precision"] = "factored"
+        beta3 = math.sqrt(hp["betas"][1])
+        group = dict(d=1e-4, d0=1e-4, d_max=1e-4, d_numerator=0.0, d_coef=1.0, growth_rate=float("inf"),
+                     d_limiter=False, k=0, prodigy_steps=0, beta3=beta3)
+        hp = dict(hp, d=group["d"], k=0, beta3=beta3)
+        algo = "prodigy"
+    else:
+        kw = dict(lr=1e-3, adam_state_precision="factored", adam_nesterov=True, adam_weight_decay=0.01)
+        opt = A.Muon_adv([dict(params=params, optim_type="adam")], **kw)
+        hp = dict(lr=1e-3, betas=(0.9, 0.99), eps=1e-8, weight_decay=0.01, use_bias_correction=True,
+                  stochastic_rounding=True, nesterov=True, precision="factored")
+        algo = "auxadam"
+    ostate = [{k: (to_numpy(v) if torch.is_tensor(v) else v) for k, v in opt.state[p].items()} for p in params]
+    grads = [(torch.randn(sh, generator=g) * 1e-3).bfloat16() for sh in shapes]
+    noise = {p: {"param": torch.randint(0, 65536, (math.prod(sh),), generator=g, dtype=torch.int32)}
+             for p, sh in zip(params, shapes)}
+    for p, gr in zip(params, grads):
+        p.grad = gr.cuda()
+    opt.set_test_noise({p: {k: v.cuda() for k, v in nz.items()} for p, nz in noise.items()})
+    opt.step()
+    torch.cuda.synchronize()
+    d_num, d_den = np.float32(0.0), np.float32(0.0)
+    from _replay import O as _O
+    for i, (p, sh) in enumerate(zip(params, shapes)):
+        gv = _O.from_bf16_bits(to_numpy(grads[i])).reshape(sh)
+        pv = _O.from_bf16_bits(to_numpy(p_host[i])).reshape(sh)
+        out = _O.adam_family_step(pv, "bf16", gv, ostate[i], hp, {"param": noise[p]["param"].numpy()}, algo=algo)
+        if algo == "prodigy":
+            out, stats = out
+            d_num = np.float32(d_num + np.float32(stats[0]))
+            d_den = np.float32(d_den + np.float32(stats[1]))
+        what = f"{which} {sh}"
+        check_bf16_param(to_numpy(p), _O.bf16_bits(out), what)
+        for key, val in opt.state[p].items():
+            if torch.is_tensor(val) and isinstance(ostate[i].get(key), np.ndarray):
+                check_state(key, to_numpy(val), ostate[i][key], f"{what} {key}")
+    if algo == "prodigy":
+        _O.prodigy_calculate_d(group, d_num, d_den)
+        np.testing.assert_allclose(opt.param_groups[0]["d"], group["d"], rtol=1e-4, err_msg="prodigy d")
